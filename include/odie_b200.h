@@ -1,0 +1,144 @@
+/*
+ * odie_b200 C-ABI: the drop-in boundary of the ODIE hot path on B200 (sm_100a).
+ *
+ * Plain C types only.  Every pointer argument is a device pointer unless its
+ * name ends in _host; `stream` is a cudaStream_t passed as uint64.  Integer
+ * returns are 0 on success; on failure they are -1 (runtime calls, with the
+ * message in odie_error()) or a nonzero cudaError_t (selection/residual calls,
+ * as in the reference).  Each entry point cites the reference interface it
+ * replaces (paths relative to the ODIE project root).
+ */
+#ifndef ODIE_B200_H
+#define ODIE_B200_H
+#include <stdbool.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ODIE_API __attribute__((visibility("default")))
+#else
+#define ODIE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * Native training runtime.  Replaces odie/native/runtime.cu:318-331 (the
+ * odie_* symbols bound by odie/native_backend.py:32-44) with the same JSON
+ * contract (odie/native_backend.py:50-59), plus the keys that the reference
+ * bakes in at compile time (odie/build.py:26-30): "levels", "raw_width",
+ * "router", "gate_k", "softplus", "rgb8", and "batch" (maximum coordinates per
+ * step; the reference fixes 65536).
+ * ------------------------------------------------------------------------ */
+/* Thread-local message of the last failure. runtime.cu:320 */
+ODIE_API const char* odie_error(void);
+/* Create a runtime for one stream; NULL on failure. runtime.cu:321 */
+ODIE_API void* odie_create(const char* json);
+/* One fwd/bwd(/Adam when update) step over n int64 pixel ids. runtime.cu:322 */
+ODIE_API int odie_step(void* handle, uint64_t ids, int n, int update);
+/* JSON of internal device buffers ("squares", "grid_grad", "head_grad", ...). runtime.cu:323 */
+ODIE_API const char* odie_pointers(void* handle);
+/* {"pristine": bool} for a grid range, or {"hash_fnv1a64", "bytes"} of all
+ * optimizer state when begin < 0. runtime.cu:324 */
+ODIE_API const char* odie_state(void* handle, int begin, int end);
+/* Change active prefix, layout pointers and learning rates. runtime.cu:325 */
+ODIE_API int odie_configure(void* handle, const char* json);
+/* No TCNN contexts exist here; kept for the binding. runtime.cu:326,328 */
+ODIE_API void odie_release_contexts(void* handle);
+ODIE_API void odie_pin_contexts(void* handle);
+/* Refresh every fp16 copy from the caller's fp32 masters. runtime.cu:327 */
+ODIE_API int odie_sync_weights(void* handle);
+/* cudaMemcpyAsync device-to-device. runtime.cu:329 */
+ODIE_API int odie_copy(uint64_t dst, uint64_t src, uint64_t bytes, uint64_t stream);
+/* Destroy the runtime. runtime.cu:330 */
+ODIE_API void odie_destroy(void* handle);
+
+/* Split step for data-parallel training (no reference counterpart; the
+ * reference is single-GPU): odie_step_grads runs the forward/backward, the
+ * grid update (when update) and leaves the summed fp32 head gradient in the
+ * "head_grad" buffer; the caller all-reduces it; odie_step_heads applies the
+ * head update.  odie_step == odie_step_grads + odie_step_heads.  update: 0
+ * discards the gradients, 1 applies the grid update, 2 keeps the fp32 grid
+ * gradient ("grid_grad", loss scale 128) for inspection; odie_grid_update then
+ * applies the grid update to it. */
+ODIE_API int odie_step_grads(void* handle, uint64_t ids, int n, int update);
+ODIE_API int odie_step_heads(void* handle);
+ODIE_API int odie_grid_update(void* handle);
+
+/* Stage timers (no reference counterpart): enable/disable CUDA-event timing of
+ * every stage launch on the runtime's stream (resets the record), and a JSON
+ * report {stage: {"launches": k, "ms": total}} of what was recorded. */
+ODIE_API int odie_profile(void* handle, int enable);
+ODIE_API const char* odie_profile_report(void* handle);
+
+/* Full-image decode of pixel ids [begin, begin+n) through the model: fp32 RGB
+ * [n][3] and/or uint8 RGB rint(clip(x,0,1)*255) (scripts/reconstruct.py:39-44,
+ * odie/evaluation.py:12-36; either output may be NULL). */
+ODIE_API int odie_decode(void* handle, int64_t begin, int64_t n, float* rgb, uint8_t* rgb8);
+
+/* ------------------------------------------------------------------------
+ * Packed-plane query.  Replaces the pybind extension odie/packed_bindings.cpp:4-12
+ * (packed_forward_cuda / packed_backward_cuda, odie/packed_kernels.cu:107-145).
+ * coords f32[n][2]; grid f32[P]; descriptors i32[levels][8]; node_bitmap
+ * u64[words]; node_prefix i32[words]; bitmap u8[bytes].
+ * ------------------------------------------------------------------------ */
+/* features f16 bits [n][width], visible u8 [n][levels]. packed_kernels.cu:107-125 */
+ODIE_API int odie_query_forward(const float* coords, int64_t n, const float* grid, const int32_t* descriptors, int levels,
+                       const uint64_t* node_bitmap, const int32_t* node_prefix, const uint8_t* bitmap, int width,
+                       uint16_t* features, uint8_t* visible, uint64_t stream);
+/* gradient f32[parameter_count], zeroed then scatter-added. packed_kernels.cu:127-145 */
+ODIE_API int odie_query_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
+                        const int32_t* descriptors, int levels, const uint64_t* node_bitmap,
+                        const int32_t* node_prefix, const uint8_t* bitmap, float* gradient,
+                        int64_t parameter_count, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Hashed multiresolution grid (the TCNN HashGrid encoding used by
+ * odie/hash_grid.py:27-34 and odie/native/runtime.cu:184-193,260,287; TCNN is
+ * not vendored in the reference).  Level table on the host.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+    float scale;          /* fp32 grid scale of odie/config.py:92 */
+    int32_t resolution;   /* ceil(scale) + 1 */
+    int32_t capacity;     /* table entries: min(align8(resolution^2), 2^log2_hashmap_size) */
+    int32_t offset;       /* first parameter of the level */
+    int32_t features;     /* features per entry */
+    int32_t column;       /* first output column */
+    int32_t hashed;       /* 1: spatial hash, 0: dense x + y*resolution (both modulo capacity) */
+} odie_hash_level;
+ODIE_API int odie_hash_forward(const float* coords, int64_t n, const float* table, const odie_hash_level* levels_host,
+                      int levels, int width, uint16_t* features, uint64_t stream);
+ODIE_API int odie_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
+                       const odie_hash_level* levels_host, int levels, float* gradient, int64_t parameter_count,
+                       uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Live residual scoring.  Replaces odie/residual_cuda.cu:45-52 (same arguments).
+ * ------------------------------------------------------------------------ */
+ODIE_API int score_chunk(const float* prediction, const void* target, int64_t begin, int64_t end, int width, int resolution,
+                int first_y, int active_cells, const int* xb, const int* yb, double* totals, bool rgb8,
+                uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Exact greedy selection.  Replaces odie/native/selection_cuda.cu:208-230
+ * (same arguments and buffer sizes, bound at odie/selection_cuda.py:43-46).
+ * ------------------------------------------------------------------------ */
+ODIE_API int selection_init(const double* scores, int n, int points, int* missing, uint8_t* chosen, uint8_t* nodes, int* tree,
+                   int64_t* stats, const int* host_offsets, const int* host_sizes, int levels, uint64_t stream);
+ODIE_API int selection_chunk(const double* scores, int n, int points, int resolution, int cap, bool normalized, int* missing,
+                    uint8_t* chosen, uint8_t* nodes, int* tree, const int* offsets, const int* sizes, int levels,
+                    int chunk, int64_t* stats, int* trace, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tile top-k allocation (no reference counterpart).
+ * prediction f32[H*W][3], target u8[H*W][3]; row_sums f64[tiles*tile] scratch;
+ * scores f64[tiles]; chosen i64[k] (tile ids by rank); selected u8[tiles].
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_tile_topk(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
+                   double* row_sums, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,123 @@
+// Shared device helpers for the ODIE B200 library (sm_100a only).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <string>
+#include <stdexcept>
+
+#if !defined(__CUDA_ARCH__) || __CUDA_ARCH__ >= 1000
+#else
+#error "odie_b200 is built for sm_100a only"
+#endif
+
+namespace odie {
+
+// ---------------------------------------------------------------- errors
+struct CudaError : std::runtime_error {
+    explicit CudaError(const std::string& what) : std::runtime_error(what) {}
+};
+#define ODIE_CUDA(expr)                                                                  \
+    do {                                                                                 \
+        cudaError_t odie_status_ = (expr);                                               \
+        if (odie_status_ != cudaSuccess)                                                 \
+            throw ::odie::CudaError(std::string(#expr) + ": " + cudaGetErrorString(odie_status_)); \
+    } while (0)
+#define ODIE_REQUIRE(cond, msg)                          \
+    do {                                                 \
+        if (!(cond)) throw std::invalid_argument(msg);   \
+    } while (0)
+
+void set_error(const std::string& message);  // thread-local, read by odie_error()
+int sm_count();                              // cached multiprocessor count of the current device
+
+inline unsigned blocks_for(long long n, int threads) { return unsigned((n + threads - 1) / threads); }
+
+// ---------------------------------------------------------------- levels
+// One encoding level as the kernels see it (built on the host from the
+// reference's int32 descriptor rows [R, points, plane offset, node word offset,
+// cell bitmap offset, F, feature offset, direct] or from a hash-grid layout).
+enum LevelKind : int { PLANE = 0, HASH_DENSE = 1, HASH_HASHED = 2 };
+struct __align__(16) Level {
+    float scale;     // coordinate scale: R-1 for planes, the fp32 grid scale for hash levels
+    int res;         // row stride of cells / integer corners
+    int points;      // node universe: modulo for node indices
+    int offset;      // first parameter of the level (elements)
+    int words;       // first node-index word of a packed plane, -1 for direct addressing
+    int cells;       // first byte of the level's cell bitmap, -1 for no bitmap (always visible)
+    int F;           // features per node: 1, 2 or 4
+    int col;         // first output feature column
+    int kind;        // LevelKind
+    int pad[3];
+};
+constexpr int MAX_LEVELS = 32;
+
+// geometry, the reference's packed_kernels.cu:12-22: p = fmaf(scale, x, 0.5),
+// integer cell = floor(p), bilinear weights of the 4 corners (x-fastest).
+struct Corner4 {
+    int ix, iy;
+    float w[4];
+};
+__device__ __forceinline__ Corner4 geometry(float x, float y, float scale) {
+    Corner4 c;
+    const float px = __fmaf_rn(scale, x, 0.5f), py = __fmaf_rn(scale, y, 0.5f);
+    c.ix = int(floorf(px));
+    c.iy = int(floorf(py));
+    const float fx = __fsub_rn(px, float(c.ix)), fy = __fsub_rn(py, float(c.iy));
+    const float gx = __fsub_rn(1.0f, fx), gy = __fsub_rn(1.0f, fy);
+    c.w[0] = __fmul_rn(gx, gy);
+    c.w[1] = __fmul_rn(fx, gy);
+    c.w[2] = __fmul_rn(gx, fy);
+    c.w[3] = __fmul_rn(fx, fy);
+    return c;
+}
+
+__device__ __forceinline__ bool cell_visible(const Level& d, const uint8_t* __restrict__ bitmap, int cell) {
+    if (d.cells < 0) return true;
+    return (__ldg(bitmap + d.cells + (cell >> 3)) >> (cell & 7)) & 1;
+}
+
+// Row of a node in a packed plane: exclusive popcount rank over a 64-bit
+// presence word plus the word's prefix (node-bitmap64-exclusive-prefix32).
+__device__ __forceinline__ int packed_row(const Level& d, const uint64_t* __restrict__ node_bitmap,
+                                          const int* __restrict__ prefix, int node) {
+    if (d.words < 0) return node;
+    const int word = d.words + (node >> 6);
+    const uint64_t mask = (uint64_t(1) << (node & 63)) - 1;
+    return __ldg(prefix + word) + __popcll(__ldg(reinterpret_cast<const unsigned long long*>(node_bitmap) + word) & mask);
+}
+
+// Parameter row of corner k (0: x0y0, 1: x1y0, 2: x0y1, 3: x1y1) of a level.
+__device__ __forceinline__ int corner_row(const Level& d, const Corner4& g, int k,
+                                          const uint64_t* __restrict__ node_bitmap, const int* __restrict__ prefix) {
+    const int dx = k & 1, dy = k >> 1;
+    if (d.kind == PLANE) {
+        const int cell = g.ix + g.iy * d.res;
+        const int node = (cell + dx + dy * d.res) % d.points;
+        return packed_row(d, node_bitmap, prefix, node);
+    }
+    const uint32_t cx = uint32_t(g.ix + dx), cy = uint32_t(g.iy + dy);
+    uint32_t idx;
+    if (d.kind == HASH_HASHED) idx = cx ^ (cy * 2654435761u);
+    else idx = cx + cy * uint32_t(d.res);
+    return int(idx % uint32_t(d.points));
+}
+
+__device__ __forceinline__ int level_cell(const Level& d, const Corner4& g) { return g.ix + g.iy * d.res; }
+
+// ---------------------------------------------------------------- fp16 bits
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+    return uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
+}
+__device__ __forceinline__ __half lo_half(uint32_t v) { return __ushort_as_half(uint16_t(v & 0xffff)); }
+__device__ __forceinline__ __half hi_half(uint32_t v) { return __ushort_as_half(uint16_t(v >> 16)); }
+
+// 8-byte vector reduction into global memory (sm_90+).
+__device__ __forceinline__ void red_add_v2(float* address, float a, float b) {
+    asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(address), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void red_add_f32(float* address, float a) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(address), "f"(a) : "memory");
+}
+
+}  // namespace odie

@@ -1,0 +1,226 @@
+// Multiresolution 2-D grid encoding: forward gather and backward scatter.
+//
+// One thread per (coordinate, level); grid = (ceil(n/256), levels).  The
+// forward interpolates the 4 corners with the fp16 fused-multiply-add chain of
+// the reference (odie/packed_kernels.cu:38-64), reading either the fp32 master
+// table (module path) or the library's fp16 mirror (training step; the values
+// are bit-identical because the reference rounds every fp32 corner value to
+// fp16 before the chain).  The backward scatter-adds w_k * g into an fp32
+// gradient (odie/packed_kernels.cu:66-88, odie/native/runtime.cu:111-143) with
+// 8-byte vector reductions for F=2 and warp aggregation of equal addresses on
+// coarse levels.
+#include "encode.cuh"
+
+namespace odie {
+
+namespace {
+
+__device__ __forceinline__ Level level_from_descriptor(const int* __restrict__ d) {
+    // Reference descriptor row [R, points, plane offset, node word offset,
+    // cell bitmap offset, F, feature offset, direct] (odie/model.py:100-101).
+    Level L;
+    L.scale = float(__ldg(d + 0) - 1);
+    L.res = __ldg(d + 0);
+    L.points = __ldg(d + 1);
+    L.offset = __ldg(d + 2);
+    L.words = __ldg(d + 7) ? -1 : __ldg(d + 3);
+    L.cells = __ldg(d + 4);
+    L.F = __ldg(d + 5);
+    L.col = __ldg(d + 6);
+    L.kind = PLANE;
+    return L;
+}
+
+template <bool FROM_DESC>
+__device__ __forceinline__ Level fetch_level(const int* desc, const LevelTable& table, int l) {
+    if (FROM_DESC) return level_from_descriptor(desc + 8 * l);
+    return table.level[l];
+}
+
+// A plane cell outside the R x R grid (coordinates outside [0, 1], which the
+// reference never produces) is treated as hidden instead of reading outside the
+// bitmap.
+__device__ __forceinline__ bool level_on(const Level& d, const Corner4& g, const uint8_t* __restrict__ bitmap) {
+    if (d.kind != PLANE) return true;
+    if (g.ix < 0 || g.iy < 0 || g.ix >= d.res || g.iy >= d.res) return false;
+    return cell_visible(d, bitmap, level_cell(d, g));
+}
+
+__device__ __forceinline__ __half2 load_pair(const float* __restrict__ t, long long index) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(t + index));
+    return __floats2half2_rn(v.x, v.y);
+}
+__device__ __forceinline__ __half2 load_pair(const __half* __restrict__ t, long long index) {
+    return __ldg(reinterpret_cast<const __half2*>(t + index));
+}
+__device__ __forceinline__ __half load_one(const float* __restrict__ t, long long index) {
+    return __float2half_rn(__ldg(t + index));
+}
+__device__ __forceinline__ __half load_one(const __half* __restrict__ t, long long index) { return __ldg(t + index); }
+
+__device__ __forceinline__ void store_feature(__half* out, bool row_major, long long i, int col, int width,
+                                              long long stride, __half v) {
+    if (row_major) out[i * width + col] = v;
+    else out[((long long)(col >> 1) * stride + i) * 2 + (col & 1)] = v;
+}
+
+template <typename T, bool FROM_DESC>
+__global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a, const int* desc,
+                                                             const __grid_constant__ LevelTable table,
+                                                             const T* __restrict__ params, __half* __restrict__ out,
+                                                             uint8_t* __restrict__ vis) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int l = blockIdx.y;
+    if (i >= a.n) return;
+    const Level d = fetch_level<FROM_DESC>(desc, table, l);
+    const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+    const Corner4 g = geometry(p.x, p.y, d.scale);
+    const bool on = l < a.active && level_on(d, g, a.bitmap);
+    if (vis) {
+        if (a.row_major) vis[i * a.levels + l] = on;
+        else vis[(long long)l * a.stride + i] = on;
+    }
+    if (d.F == 2) {
+        __half2 acc = __float2half2_rn(0.0f);
+        if (on) {
+            int rows[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+            __half2 t[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) t[k] = load_pair(params, (long long)d.offset + 2LL * rows[k]);
+            // __hfma2 rounds each lane once, exactly as the reference's per-channel __hfma chain.
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc = __hfma2(__float2half2_rn(g.w[k]), t[k], acc);
+        }
+        if (!a.row_major && (d.col & 1) == 0) {
+            reinterpret_cast<__half2*>(out)[(long long)(d.col >> 1) * a.stride + i] = acc;
+        } else {
+            store_feature(out, a.row_major, i, d.col, a.width, a.stride, __low2half(acc));
+            store_feature(out, a.row_major, i, d.col + 1, a.width, a.stride, __high2half(acc));
+        }
+        return;
+    }
+    int rows[4] = {0, 0, 0, 0};
+    if (on) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+    }
+    for (int c = 0; c < d.F; ++c) {
+        __half acc = __float2half_rn(0.0f);
+        if (on) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                acc = __hfma(__float2half_rn(g.w[k]), load_one(params, (long long)d.offset + (long long)rows[k] * d.F + c), acc);
+        }
+        store_feature(out, a.row_major, i, d.col + c, a.width, a.stride, acc);
+    }
+}
+
+__device__ __forceinline__ float upstream_value(const __half* __restrict__ up, const EncodeArgs& a, long long i, int col) {
+    if (a.row_major) return __half2float(up[i * a.width + col]);
+    return __half2float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
+}
+
+// Sum the values of lanes that target the same address; the lowest lane issues
+// one reduction for the group (the reference's labeled_partition + reduce,
+// odie/native/runtime.cu:137-139).
+__device__ __forceinline__ void aggregated_red2(float* address, float a, float b) {
+    const unsigned active = __activemask();
+    const unsigned peers = __match_any_sync(active, reinterpret_cast<unsigned long long>(address));
+    float sa = 0.0f, sb = 0.0f;
+    unsigned m = peers;
+    while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        sa += __shfl_sync(peers, a, src);
+        sb += __shfl_sync(peers, b, src);
+    }
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) red_add_v2(address, sa, sb);
+}
+__device__ __forceinline__ void aggregated_red1(float* address, float a) {
+    const unsigned active = __activemask();
+    const unsigned peers = __match_any_sync(active, reinterpret_cast<unsigned long long>(address));
+    float sa = 0.0f;
+    unsigned m = peers;
+    while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        sa += __shfl_sync(peers, a, src);
+    }
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) red_add_f32(address, sa);
+}
+
+template <bool FROM_DESC>
+__global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
+                                                              const __grid_constant__ LevelTable table,
+                                                              const __half* __restrict__ upstream,
+                                                              float* __restrict__ grad, int warp_limit) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int l = blockIdx.y;
+    if (i >= a.n || l >= a.active) return;
+    const Level d = fetch_level<FROM_DESC>(desc, table, l);
+    const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+    const Corner4 g = geometry(p.x, p.y, d.scale);
+    if (!level_on(d, g, a.bitmap)) return;
+    const bool aggregate = d.res <= warp_limit;
+    if (d.F == 2) {
+        const float v0 = upstream_value(upstream, a, i, d.col);
+        const float v1 = upstream_value(upstream, a, i, d.col + 1);
+        if (v0 == 0.0f && v1 == 0.0f) return;
+        int rows[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float* address = grad + d.offset + 2LL * rows[k];
+            const float x = __fmul_rn(g.w[k], v0), y = __fmul_rn(g.w[k], v1);
+            if (aggregate) aggregated_red2(address, x, y);
+            else red_add_v2(address, x, y);
+        }
+        return;
+    }
+    int rows[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+    for (int c = 0; c < d.F; ++c) {
+        const float v = upstream_value(upstream, a, i, d.col + c);
+        if (v == 0.0f) continue;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float* address = grad + d.offset + (long long)rows[k] * d.F + c;
+            const float x = __fmul_rn(g.w[k], v);
+            if (aggregate) aggregated_red1(address, x);
+            else red_add_f32(address, x);
+        }
+    }
+}
+
+}  // namespace
+
+void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const float* table32, const __half* table16,
+                           __half* out, uint8_t* vis, cudaStream_t stream) {
+    if (a.n <= 0 || a.levels <= 0) return;
+    ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
+    const dim3 grid(blocks_for(a.n, 256), a.levels);
+    if (src.descriptors) {
+        if (table32) encode_forward_kernel<float, true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, table32, out, vis);
+        else encode_forward_kernel<__half, true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, table16, out, vis);
+    } else {
+        if (table32) encode_forward_kernel<float, false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, table32, out, vis);
+        else encode_forward_kernel<__half, false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, table16, out, vis);
+    }
+}
+
+void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
+                            int warp_limit, cudaStream_t stream) {
+    if (a.n <= 0 || a.levels <= 0) return;
+    ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
+    const dim3 grid(blocks_for(a.n, 256), a.levels);
+    if (src.descriptors)
+        encode_backward_kernel<true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, upstream, grad, warp_limit);
+    else
+        encode_backward_kernel<false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, warp_limit);
+}
+
+}  // namespace odie

@@ -1,0 +1,766 @@
+// Training runtime behind the odie_* C-ABI (the reference's Probe,
+// odie/native/runtime.cu:163-317, re-designed for B200).
+//
+// Ownership follows the reference: the caller owns the target image, the fp32
+// grid master and the fp32 head masters (updated in place); the library owns
+// gradients, fp16 copies, Adam state, per-batch activations and scratch.
+// One step on one stream, every launch capturable in a CUDA graph (no host
+// synchronisation, no allocation after creation):
+//   input_batch -> encode forward (fp16 mirror gather) -> fused MLP heads
+//   (gate, decoder, loss, backward, weight-gradient partials) -> encode
+//   backward (scatter) -> partial reduction -> Adam (grid, gate, decoder).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <sstream>
+#include <vector>
+
+#include "encode.cuh"
+#include "odie_b200.h"
+#include "json_lite.hpp"
+#include "step.cuh"
+
+namespace odie {
+
+namespace {
+thread_local std::string g_error, g_reply;
+}
+
+void set_error(const std::string& message) { g_error = message; }
+
+int sm_count() {
+    static int cached[64] = {0};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+    if (!cached[device]) {
+        int count = 0;
+        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || count <= 0) count = 148;
+        cached[device] = count;
+    }
+    return cached[device];
+}
+
+template <typename T>
+struct DeviceArray {
+    T* ptr = nullptr;
+    long long count = 0;
+    DeviceArray() = default;
+    DeviceArray(const DeviceArray&) = delete;
+    DeviceArray& operator=(const DeviceArray&) = delete;
+    ~DeviceArray() { release(); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        count = 0;
+    }
+    void allocate(long long n) {
+        release();
+        if (n <= 0) return;
+        ODIE_CUDA(cudaMalloc(&ptr, size_t(n) * sizeof(T)));
+        count = n;
+    }
+    void zero(cudaStream_t stream) {
+        if (count) ODIE_CUDA(cudaMemsetAsync(ptr, 0, size_t(count) * sizeof(T), stream));
+    }
+};
+
+template <typename T>
+T* pointer_of(const Json& j, const char* key) {
+    return reinterpret_cast<T*>(j.at(key).as_u64());
+}
+
+constexpr double BETA1 = 0.9, BETA2 = 0.999, EPS = 1e-15;
+constexpr long long TABLE_STEPS = 1LL << 22;  // Adam bias-correction tables (steps per parameter)
+
+struct Runtime {
+    cudaStream_t stream = nullptr;
+    int device = 0;
+    long long total = 0, capacity = 65536;
+    int image_width = 0, image_height = 0, mode = 0, warp_limit = 128;
+    int levels = 16, raw_width = 32, input_width = 32, gate_k = 0, active = 16;
+    bool router = true, softplus = false, rgb8 = true, hash_mode = false;
+    double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
+    // caller-owned
+    float* grid = nullptr;
+    const uint8_t* rgb = nullptr;
+    float* gate_master = nullptr;
+    float* decoder_master = nullptr;
+    const int* descriptors = nullptr;
+    const uint64_t* node_bitmap = nullptr;
+    const int* node_prefix = nullptr;
+    const uint8_t* cell_bitmap = nullptr;
+    float* external_head_grad = nullptr;
+    // layout
+    LevelTable table{};
+    FeatureMap fmap{};
+    int gate_count = 0, decoder_count = 0, head_count = 0;
+    // library-owned
+    DeviceArray<__half> grid_half, head_half;
+    DeviceArray<float> grid_grad, grid_m, grid_v, head_grad_own, head_m, head_v, partials;
+    DeviceArray<uint32_t> grid_steps, head_steps;
+    DeviceArray<float> table_bc2, table_step[3];
+    DeviceArray<float> xy, target, squares;
+    DeviceArray<__half> raw, gvals;
+    DeviceArray<uint8_t> vis;
+    DeviceArray<int> error_flag;
+    std::vector<double> host_bc1, host_bc2;
+    int partial_blocks = 0;
+
+    float* head_grad() { return external_head_grad ? external_head_grad : head_grad_own.ptr; }
+
+    explicit Runtime(const Json& j) {
+        ODIE_CUDA(cudaGetDevice(&device));
+        stream = reinterpret_cast<cudaStream_t>(j.at("stream").as_u64());
+        total = j.at("total").as_int();
+        image_width = int(j.at("width").as_int());
+        image_height = int(j.at("height").as_int());
+        mode = int(j.value("mode", 20));
+        warp_limit = int(j.value("warp_limit", 128));
+        capacity = j.value("batch", 65536);
+        router = j.value("router", 1) != 0;
+        gate_k = int(j.value("gate_k", 0));
+        softplus = j.value("softplus", 0) != 0;
+        rgb8 = j.value("rgb8", 1) != 0;
+        ODIE_REQUIRE(total > 0 && total <= 0x7fffffffLL, "total must fit int32 addressing");
+        ODIE_REQUIRE(image_width >= 2 && image_height >= 2, "image axes must be >= 2");
+        ODIE_REQUIRE(capacity >= 1 && capacity <= (1LL << 26), "batch capacity must be in [1, 2^26]");
+        grid = pointer_of<float>(j, "grid");
+        rgb = pointer_of<uint8_t>(j, "rgb");
+        decoder_master = pointer_of<float>(j, "decoder");
+        if (router) gate_master = pointer_of<float>(j, "gate");
+        if (j.contains("head_grad")) external_head_grad = pointer_of<float>(j, "head_grad");
+        hash_mode = j.contains("hash_encoding");
+        if (hash_mode) build_hash_table(j.at("hash_encoding"));
+        else levels = int(j.value("levels", 16));
+        ODIE_REQUIRE(levels >= 2 && levels <= 16, "the fused heads support 2..16 levels");
+        ODIE_REQUIRE(gate_k >= 0 && gate_k <= levels, "gate_k outside [0, levels]");
+        active = levels;
+        for (int g = 0; g < 3; ++g) lr[g] = 0.0;
+        host_bc1.resize(TABLE_STEPS);
+        host_bc2.resize(TABLE_STEPS);
+        for (long long s = 0; s < TABLE_STEPS; ++s) {
+            host_bc1[s] = 1.0 - std::pow(BETA1, double(s + 1));
+            host_bc2[s] = 1.0 - std::pow(BETA2, double(s + 1));
+        }
+        table_bc2.allocate(TABLE_STEPS);
+        for (int g = 0; g < 3; ++g) table_step[g].allocate(TABLE_STEPS);
+        {
+            std::vector<float> bc2(TABLE_STEPS);
+            for (long long s = 0; s < TABLE_STEPS; ++s) bc2[s] = float(std::sqrt(host_bc2[s]));
+            ODIE_CUDA(cudaMemcpy(table_bc2.ptr, bc2.data(), TABLE_STEPS * sizeof(float), cudaMemcpyHostToDevice));
+        }
+        configure(j);
+        gate_count = router ? gate_params(input_width) : 0;
+        decoder_count = decoder_params(input_width);
+        head_count = gate_count + decoder_count;
+        // library-owned buffers
+        grid_half.allocate(total);
+        grid_grad.allocate(total);
+        grid_m.allocate(total);
+        grid_v.allocate(total);
+        grid_steps.allocate(total);
+        head_half.allocate(head_count);
+        head_grad_own.allocate(head_count);
+        head_m.allocate(head_count);
+        head_v.allocate(head_count);
+        head_steps.allocate(head_count);
+        partial_blocks = mlp_train_blocks(capacity);
+        partials.allocate((long long)partial_blocks * head_count);
+        xy.allocate(2 * capacity);
+        target.allocate(3 * capacity);
+        squares.allocate(capacity);
+        raw.allocate((long long)input_width * capacity);
+        gvals.allocate((long long)input_width * capacity);
+        vis.allocate((long long)levels * capacity);
+        error_flag.allocate(1);
+        for (auto* a : {&grid_grad, &grid_m, &grid_v, &head_grad_own, &head_m, &head_v})
+            a->zero(stream);
+        grid_steps.zero(stream);
+        head_steps.zero(stream);
+        raw.zero(stream);
+        gvals.zero(stream);
+        squares.zero(stream);
+        error_flag.zero(stream);
+        sync_weights();
+        ODIE_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    // TCNN-style HashGrid layout restated from odie/config.py:83-94.
+    void build_hash_table(const Json& enc) {
+        levels = int(enc.at("n_levels").as_int());
+        const int F = int(enc.at("n_features_per_level").as_int());
+        const int log2t = int(enc.at("log2_hashmap_size").as_int());
+        const int base = int(enc.at("base_resolution").as_int());
+        const double growth = double(float(enc.at("per_level_scale").as_double()));
+        ODIE_REQUIRE(levels >= 2 && levels <= MAX_LEVELS, "hash grid levels in [2, 32]");
+        ODIE_REQUIRE(F == 1 || F == 2 || F == 4, "hash grid features per level must be 1, 2 or 4");
+        const float log_growth = float(std::log2(growth));
+        long long offset = 0;
+        for (int l = 0; l < levels; ++l) {
+            const float e = float(double(l) * double(log_growth));
+            const float p = float(std::pow(2.0, double(e)));
+            const float scale = float(double(float(double(p) * double(base))) - 1.0);
+            const int res = int(std::ceil(double(scale))) + 1;
+            const long long dense = ((long long)res * res + 7) / 8 * 8;
+            const long long cap = std::min(dense, 1LL << log2t);
+            Level& L = table.level[l];
+            L.scale = scale;
+            L.res = res;
+            L.points = int(cap);
+            L.offset = int(offset);
+            L.words = -1;
+            L.cells = -1;
+            L.F = F;
+            L.col = l * F;
+            L.kind = (long long)res * res > cap ? HASH_HASHED : HASH_DENSE;
+            offset += cap * F;
+        }
+        ODIE_REQUIRE(offset == total, "hash grid allocation differs from the resolved layout total");
+        raw_width = levels * F;
+        input_width = (raw_width + 15) / 16 * 16;
+        build_feature_map();
+    }
+
+    void build_feature_map() {
+        std::memset(&fmap, 0, sizeof(fmap));
+        for (int c = 0; c < 64; ++c) fmap.level_of_col[c] = -1;
+        for (int l = 0; l < levels; ++l) {
+            const Level& L = table.level[l];
+            fmap.col_of_level[l] = int8_t(L.col);
+            fmap.dim_of_level[l] = int8_t(L.F);
+            for (int c = L.col; c < L.col + L.F; ++c) fmap.level_of_col[c] = int8_t(l);
+        }
+    }
+
+    void configure(const Json& j) {
+        active = int(j.at("active").as_int());
+        ODIE_REQUIRE(active >= 2 && active <= levels, "invalid active prefix");
+        if (!hash_mode) {
+            descriptors = pointer_of<const int>(j, "descriptors");
+            node_bitmap = pointer_of<const uint64_t>(j, "node_bitmap");
+            node_prefix = pointer_of<const int>(j, "node_prefix");
+            cell_bitmap = pointer_of<const uint8_t>(j, "bitmap");
+            std::vector<int> host(levels * 8);
+            ODIE_CUDA(cudaMemcpy(host.data(), descriptors, host.size() * sizeof(int), cudaMemcpyDeviceToHost));
+            int width = 0;
+            for (int l = 0; l < levels; ++l) {
+                const int* d = host.data() + 8 * l;
+                Level& L = table.level[l];
+                L.scale = float(d[0] - 1);
+                L.res = d[0];
+                L.points = d[1];
+                L.offset = d[2];
+                L.words = d[7] ? -1 : d[3];
+                L.cells = d[4];
+                L.F = d[5];
+                L.col = d[6];
+                L.kind = PLANE;
+                ODIE_REQUIRE(L.F == 1 || L.F == 2 || L.F == 4, "plane features must be 1, 2 or 4");
+                width = std::max(width, L.col + L.F);
+            }
+            raw_width = width;
+            input_width = (raw_width + 15) / 16 * 16;
+            ODIE_REQUIRE(input_width <= 64, "decoder input width must be <= 64");
+            build_feature_map();
+        }
+        lr[0] = j.at("grid_lr").as_double();
+        if (router) lr[1] = j.at("gate_lr").as_double();
+        lr[2] = j.at("decoder_lr").as_double();
+        upload_step_tables();
+        if (grid_half.count) sync_weights();
+    }
+
+    void upload_step_tables() {
+        std::vector<float> host(TABLE_STEPS);
+        for (int g = 0; g < 3; ++g) {
+            if (!table_step[g].ptr) continue;
+            for (long long s = 0; s < TABLE_STEPS; ++s) host[s] = float(lr[g] / host_bc1[s]);
+            ODIE_CUDA(cudaMemcpy(table_step[g].ptr, host.data(), TABLE_STEPS * sizeof(float), cudaMemcpyHostToDevice));
+        }
+    }
+
+    void sync_weights() {
+        launch_cast_half(grid, grid_half.ptr, total, stream);
+        if (router) launch_cast_half(gate_master, head_half.ptr, gate_count, stream);
+        launch_cast_half(decoder_master, head_half.ptr + gate_count, decoder_count, stream);
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    EncodeArgs encode_args(long long n) const {
+        EncodeArgs a;
+        a.coords = xy.ptr;
+        a.n = n;
+        a.levels = levels;
+        a.active = active;
+        a.node_bitmap = node_bitmap;
+        a.node_prefix = node_prefix;
+        a.bitmap = cell_bitmap;
+        a.row_major = false;
+        a.width = input_width;
+        a.stride = capacity;
+        return a;
+    }
+
+    MlpArgs mlp_args(long long n) {
+        MlpArgs m{};
+        m.n = n;
+        m.stride = capacity;
+        m.raw = raw.ptr;
+        m.vis = vis.ptr;
+        m.target = target.ptr;
+        m.gate_w = router ? head_half.ptr : nullptr;
+        m.decoder_w = head_half.ptr + gate_count;
+        m.levels = levels;
+        m.raw_width = raw_width;
+        m.k_fixed = gate_k;
+        m.softplus = softplus;
+        m.three_real = float(3 * n);
+        m.fmap = fmap;
+        m.gvals = gvals.ptr;
+        m.squares = squares.ptr;
+        m.partials = partials.ptr;
+        return m;
+    }
+
+    // ---- optional stage timers (CUDA events on the runtime's stream; off by default)
+    enum Stage { S_INPUT, S_ENCODE_FWD, S_MLP, S_ENCODE_BWD, S_REDUCE, S_ADAM_GRID, S_ADAM_HEADS, S_COUNT };
+    static constexpr const char* STAGE_NAMES[S_COUNT] = {"input_batch", "encode_forward", "mlp_train",
+                                                         "encode_backward", "reduce_partials", "adam_grid", "adam_heads"};
+    static constexpr int EVENT_PAIRS = 4096;
+    bool profiling = false;
+    std::vector<cudaEvent_t> events;            // 2 per recorded stage launch
+    std::vector<int> event_stage;
+    int recorded = 0;
+
+    void profile(bool enable) {
+        ODIE_CUDA(cudaStreamSynchronize(stream));
+        if (enable && events.empty()) {
+            events.resize(2 * EVENT_PAIRS);
+            for (auto& e : events) ODIE_CUDA(cudaEventCreate(&e));
+            event_stage.assign(EVENT_PAIRS, -1);
+        }
+        profiling = enable;
+        recorded = 0;
+    }
+    int stage_begin(Stage s) {
+        if (!profiling || recorded >= EVENT_PAIRS) return -1;
+        const int slot = recorded++;
+        event_stage[slot] = s;
+        ODIE_CUDA(cudaEventRecord(events[2 * slot], stream));
+        return slot;
+    }
+    void stage_end(int slot) {
+        if (slot >= 0) ODIE_CUDA(cudaEventRecord(events[2 * slot + 1], stream));
+    }
+    std::string profile_report() {
+        ODIE_CUDA(cudaStreamSynchronize(stream));
+        double ms[S_COUNT] = {0};
+        int launches[S_COUNT] = {0};
+        for (int i = 0; i < recorded; ++i) {
+            float t = 0.0f;
+            ODIE_CUDA(cudaEventElapsedTime(&t, events[2 * i], events[2 * i + 1]));
+            ms[event_stage[i]] += t;
+            launches[event_stage[i]] += 1;
+        }
+        std::ostringstream o;
+        o << "{";
+        for (int s = 0; s < S_COUNT; ++s)
+            o << (s ? "," : "") << "\"" << STAGE_NAMES[s] << "\":{\"launches\":" << launches[s] << ",\"ms\":" << ms[s] << "}";
+        o << "}";
+        return o.str();
+    }
+
+    void step_grads(const int64_t* ids, int n, int update) {
+        ODIE_REQUIRE(n > 0 && n <= capacity, "invalid batch size for this runtime");
+        int slot = stage_begin(S_INPUT);
+        launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, xy.ptr, target.ptr, stream);
+        stage_end(slot);
+        LevelSource src;
+        src.table = table;
+        const EncodeArgs ea = encode_args(n);
+        slot = stage_begin(S_ENCODE_FWD);
+        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, vis.ptr, stream);
+        stage_end(slot);
+        const MlpArgs ma = mlp_args(n);
+        const int blocks = mlp_train_blocks(n);
+        slot = stage_begin(S_MLP);
+        launch_mlp_train(ma, input_width, router, blocks, stream);
+        stage_end(slot);
+        slot = stage_begin(S_ENCODE_BWD);
+        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, warp_limit, stream);
+        stage_end(slot);
+        slot = stage_begin(S_REDUCE);
+        launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), stream);
+        stage_end(slot);
+        if (update == 1) grid_update();
+        else if (update == 0) launch_zero(grid_grad.ptr, total, stream);
+        // update == 2 keeps the grid gradient for inspection; grid_update() consumes it
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    void grid_update() {
+        AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
+        const int slot = stage_begin(S_ADAM_GRID);
+        launch_adam(grid, grid_half.ptr, grid_m.ptr, grid_v.ptr, grid_steps.ptr, grid_grad.ptr, total, 1.0f / 128.0f, t,
+                    float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), true, error_flag.ptr, stream);
+        stage_end(slot);
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    void step_heads(bool update) {
+        if (!update) return;
+        const int slot = stage_begin(S_ADAM_HEADS);
+        // head gradients carry the 128 x 128 loss scale (odie/native/runtime.cu:59,300-309)
+        const float inv = 1.0f / 16384.0f;
+        if (router) {
+            AdamTables t{table_step[1].ptr, table_bc2.ptr, TABLE_STEPS};
+            launch_adam(gate_master, head_half.ptr, head_m.ptr, head_v.ptr, head_steps.ptr, head_grad(), gate_count, inv,
+                        t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
+        }
+        AdamTables t{table_step[2].ptr, table_bc2.ptr, TABLE_STEPS};
+        launch_adam(decoder_master, head_half.ptr + gate_count, head_m.ptr + gate_count, head_v.ptr + gate_count,
+                    head_steps.ptr + gate_count, head_grad() + gate_count, decoder_count, inv, t, float(1.0 - BETA1),
+                    float(BETA2), float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
+        stage_end(slot);
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    ~Runtime() {
+        for (auto& e : events) cudaEventDestroy(e);
+    }
+
+    void decode(long long begin, long long n, float* out_rgb, uint8_t* out_rgb8) {
+        LevelSource src;
+        src.table = table;
+        for (long long done = 0; done < n; done += capacity) {
+            const long long count = std::min(capacity, n - done);
+            launch_coords_range(begin + done, count, image_width, image_height, xy.ptr, stream);
+            const EncodeArgs ea = encode_args(count);
+            launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, vis.ptr, stream);
+            MlpArgs ma = mlp_args(count);
+            ma.rgb = out_rgb ? out_rgb + 3 * done : nullptr;
+            ma.rgb8 = out_rgb8 ? out_rgb8 + 3 * done : nullptr;
+            launch_mlp_decode(ma, input_width, router, stream);
+        }
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    std::string pointers() {
+        std::ostringstream o;
+        o << "{\"squares\":" << (unsigned long long)squares.ptr << ",\"grid_grad\":" << (unsigned long long)grid_grad.ptr
+          << ",\"half_grad\":0,\"gate_grad\":" << (unsigned long long)(router ? head_grad() : nullptr)
+          << ",\"decoder_grad\":" << (unsigned long long)(head_grad() + gate_count)
+          << ",\"head_grad\":" << (unsigned long long)head_grad() << ",\"head_count\":" << head_count
+          << ",\"gate_count\":" << gate_count << ",\"output\":0,\"raw\":" << (unsigned long long)raw.ptr
+          << ",\"dirty_count\":0,\"grid_half\":" << (unsigned long long)grid_half.ptr
+          << ",\"head_half\":" << (unsigned long long)head_half.ptr << ",\"error_flag\":" << (unsigned long long)error_flag.ptr
+          << ",\"capacity\":" << capacity << ",\"input_width\":" << input_width
+          << ",\"gvals\":" << (unsigned long long)gvals.ptr << ",\"vis\":" << (unsigned long long)vis.ptr
+          << ",\"xy\":" << (unsigned long long)xy.ptr << ",\"target\":" << (unsigned long long)target.ptr
+          << ",\"grid_m\":" << (unsigned long long)grid_m.ptr << ",\"grid_v\":" << (unsigned long long)grid_v.ptr
+          << ",\"grid_steps\":" << (unsigned long long)grid_steps.ptr << ",\"head_m\":" << (unsigned long long)head_m.ptr
+          << ",\"head_v\":" << (unsigned long long)head_v.ptr << ",\"head_steps\":" << (unsigned long long)head_steps.ptr
+          << "}";
+        return o.str();
+    }
+
+    std::string state(int begin, int end) {
+        ODIE_CUDA(cudaStreamSynchronize(stream));
+        int flag = 0;
+        ODIE_CUDA(cudaMemcpy(&flag, error_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+        ODIE_REQUIRE(flag == 0, "optimizer step table exhausted");
+        if (begin >= 0) {
+            ODIE_REQUIRE(begin <= end && end <= total, "state range outside the grid");
+            const long long count = end - begin;
+            bool pristine = true;
+            if (count > 0) {
+                std::vector<uint32_t> host(count);
+                const void* arrays[3] = {grid_m.ptr + begin, grid_v.ptr + begin, grid_steps.ptr + begin};
+                for (const void* src : arrays) {
+                    ODIE_CUDA(cudaMemcpy(host.data(), src, count * 4, cudaMemcpyDeviceToHost));
+                    for (uint32_t x : host) if (x) { pristine = false; break; }
+                    if (!pristine) break;
+                }
+            }
+            return std::string("{\"pristine\":") + (pristine ? "true" : "false") + "}";
+        }
+        // FNV-1a-64 over the raw bytes of every optimizer state array
+        unsigned long long hash = 14695981039346656037ull, bytes = 0;
+        auto mix = [&](const void* src, long long count) {
+            std::vector<unsigned char> host(size_t(count) * 4);
+            if (count) ODIE_CUDA(cudaMemcpy(host.data(), src, host.size(), cudaMemcpyDeviceToHost));
+            for (unsigned char b : host) { hash ^= b; hash *= 1099511628211ull; }
+            bytes += host.size();
+        };
+        mix(grid_m.ptr, total); mix(grid_v.ptr, total); mix(grid_steps.ptr, total);
+        mix(head_m.ptr, head_count); mix(head_v.ptr, head_count); mix(head_steps.ptr, head_count);
+        std::ostringstream o;
+        o << "{\"hash_fnv1a64\":\"" << hash << "\",\"bytes\":" << bytes << "}";
+        return o.str();
+    }
+};
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+LevelTable hash_levels_table(const odie_hash_level* host, int levels) {
+    ODIE_REQUIRE(host && levels >= 1 && levels <= MAX_LEVELS, "1..32 hash levels required");
+    LevelTable t{};
+    for (int l = 0; l < levels; ++l) {
+        Level& L = t.level[l];
+        L.scale = host[l].scale;
+        L.res = host[l].resolution;
+        L.points = host[l].capacity;
+        L.offset = host[l].offset;
+        L.words = -1;
+        L.cells = -1;
+        L.F = host[l].features;
+        L.col = host[l].column;
+        L.kind = host[l].hashed ? HASH_HASHED : HASH_DENSE;
+        ODIE_REQUIRE(L.points > 0 && (L.F == 1 || L.F == 2 || L.F == 4), "invalid hash level");
+    }
+    return t;
+}
+
+}  // namespace odie
+
+// ---------------------------------------------------------------- residual / selection (residual.cu, selection.cu)
+namespace odie {
+void launch_score_chunk(const float* prediction, const void* target, long long begin, long long end, int width,
+                        int resolution, int first_y, int active_cells, const int* xb, const int* yb, double* totals,
+                        bool rgb8, cudaStream_t stream);
+void launch_tile_scores(const float* prediction, const uint8_t* target, int height, int width, int tile, double* row_sums,
+                        double* scores, cudaStream_t stream);
+void launch_topk(const double* scores, int count, int k, long long* chosen, uint8_t* selected, cudaStream_t stream);
+int launch_selection_init(const double* scores, int n, int points, int* missing, uint8_t* chosen, uint8_t* nodes,
+                          int* tree, long long* stats, const int* host_offsets, const int* host_sizes, int levels,
+                          cudaStream_t stream);
+int launch_selection_chunk(const double* scores, int n, int points, int resolution, int cap, bool normalized, int* missing,
+                           uint8_t* chosen, uint8_t* nodes, int* tree, const int* offsets, const int* sizes, int levels,
+                           int chunk, long long* stats, int* trace, cudaStream_t stream);
+}  // namespace odie
+
+using odie::guarded;
+using odie::Runtime;
+
+extern "C" {
+
+const char* odie_error(void) { return odie::g_error.c_str(); }
+
+void* odie_create(const char* json) {
+    try {
+        return new Runtime(odie::parse_json(json));
+    } catch (const std::exception& e) {
+        odie::set_error(e.what());
+        return nullptr;
+    }
+}
+
+int odie_step(void* handle, uint64_t ids, int n, int update) {
+    return guarded([&] {
+        auto* r = static_cast<Runtime*>(handle);
+        r->step_grads(reinterpret_cast<const int64_t*>(ids), n, update != 0 ? 1 : 0);
+        r->step_heads(update != 0);
+    });
+}
+
+int odie_step_grads(void* handle, uint64_t ids, int n, int update) {
+    return guarded([&] { static_cast<Runtime*>(handle)->step_grads(reinterpret_cast<const int64_t*>(ids), n, update); });
+}
+
+int odie_step_heads(void* handle) {
+    return guarded([&] { static_cast<Runtime*>(handle)->step_heads(true); });
+}
+
+int odie_grid_update(void* handle) {
+    return guarded([&] { static_cast<Runtime*>(handle)->grid_update(); });
+}
+
+int odie_profile(void* handle, int enable) {
+    return guarded([&] { static_cast<Runtime*>(handle)->profile(enable != 0); });
+}
+
+const char* odie_profile_report(void* handle) {
+    try {
+        odie::g_reply = static_cast<Runtime*>(handle)->profile_report();
+        return odie::g_reply.c_str();
+    } catch (const std::exception& e) {
+        odie::set_error(e.what());
+        return nullptr;
+    }
+}
+
+const char* odie_pointers(void* handle) {
+    odie::g_reply = static_cast<Runtime*>(handle)->pointers();
+    return odie::g_reply.c_str();
+}
+
+const char* odie_state(void* handle, int begin, int end) {
+    try {
+        odie::g_reply = static_cast<Runtime*>(handle)->state(begin, end);
+        return odie::g_reply.c_str();
+    } catch (const std::exception& e) {
+        odie::set_error(e.what());
+        return nullptr;
+    }
+}
+
+int odie_configure(void* handle, const char* json) {
+    return guarded([&] { static_cast<Runtime*>(handle)->configure(odie::parse_json(json)); });
+}
+
+void odie_release_contexts(void*) {}
+void odie_pin_contexts(void*) {}
+
+int odie_sync_weights(void* handle) {
+    return guarded([&] { static_cast<Runtime*>(handle)->sync_weights(); });
+}
+
+int odie_copy(uint64_t dst, uint64_t src, uint64_t bytes, uint64_t stream) {
+    return int(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes,
+                               cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+void odie_destroy(void* handle) { delete static_cast<Runtime*>(handle); }
+
+int odie_decode(void* handle, int64_t begin, int64_t n, float* rgb, uint8_t* rgb8) {
+    return guarded([&] {
+        ODIE_REQUIRE(n >= 0 && begin >= 0, "invalid decode range");
+        static_cast<Runtime*>(handle)->decode(begin, n, rgb, rgb8);
+    });
+}
+
+int odie_query_forward(const float* coords, int64_t n, const float* grid, const int32_t* descriptors, int levels,
+                       const uint64_t* node_bitmap, const int32_t* node_prefix, const uint8_t* bitmap, int width,
+                       uint16_t* features, uint8_t* visible, uint64_t stream) {
+    return guarded([&] {
+        ODIE_REQUIRE(levels >= 2 && levels <= 32, "descriptor must hold 2..32 levels");
+        ODIE_REQUIRE(width >= 2 && width <= 128, "feature width must be within 2..128");
+        ODIE_REQUIRE(n >= 0, "negative coordinate count");
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.node_bitmap = node_bitmap;
+        a.node_prefix = node_prefix;
+        a.bitmap = bitmap;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        odie::LevelSource src;
+        src.descriptors = descriptors;
+        odie::launch_encode_forward(a, src, grid, nullptr, reinterpret_cast<__half*>(features), visible,
+                                    reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_query_backward(const float* coords, int64_t n, const uint16_t* upstream, int width, const int32_t* descriptors,
+                        int levels, const uint64_t* node_bitmap, const int32_t* node_prefix, const uint8_t* bitmap,
+                        float* gradient, int64_t parameter_count, uint64_t stream) {
+    return guarded([&] {
+        ODIE_REQUIRE(levels >= 2 && levels <= 32, "descriptor must hold 2..32 levels");
+        ODIE_REQUIRE(width >= 2 && width <= 128, "upstream width must be within 2..128");
+        ODIE_REQUIRE(parameter_count >= 0 && n >= 0, "negative sizes");
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (parameter_count) ODIE_CUDA(cudaMemsetAsync(gradient, 0, size_t(parameter_count) * 4, s));
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.node_bitmap = node_bitmap;
+        a.node_prefix = node_prefix;
+        a.bitmap = bitmap;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        odie::LevelSource src;
+        src.descriptors = descriptors;
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_hash_forward(const float* coords, int64_t n, const float* table, const odie_hash_level* levels_host, int levels,
+                      int width, uint16_t* features, uint64_t stream) {
+    return guarded([&] {
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        odie::LevelSource src;
+        src.table = odie::hash_levels_table(levels_host, levels);
+        odie::launch_encode_forward(a, src, table, nullptr, reinterpret_cast<__half*>(features), nullptr,
+                                    reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
+                       const odie_hash_level* levels_host, int levels, float* gradient, int64_t parameter_count,
+                       uint64_t stream) {
+    return guarded([&] {
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (parameter_count) ODIE_CUDA(cudaMemsetAsync(gradient, 0, size_t(parameter_count) * 4, s));
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        odie::LevelSource src;
+        src.table = odie::hash_levels_table(levels_host, levels);
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int score_chunk(const float* prediction, const void* target, int64_t begin, int64_t end, int width, int resolution,
+                int first_y, int active_cells, const int* xb, const int* yb, double* totals, bool rgb8, uint64_t stream) {
+    odie::launch_score_chunk(prediction, target, begin, end, width, resolution, first_y, active_cells, xb, yb, totals, rgb8,
+                             reinterpret_cast<cudaStream_t>(stream));
+    return int(cudaGetLastError());
+}
+
+int selection_init(const double* scores, int n, int points, int* missing, uint8_t* chosen, uint8_t* nodes, int* tree,
+                   int64_t* stats, const int* host_offsets, const int* host_sizes, int levels, uint64_t stream) {
+    return odie::launch_selection_init(scores, n, points, missing, chosen, nodes, tree, reinterpret_cast<long long*>(stats),
+                                       host_offsets, host_sizes, levels, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int selection_chunk(const double* scores, int n, int points, int resolution, int cap, bool normalized, int* missing,
+                    uint8_t* chosen, uint8_t* nodes, int* tree, const int* offsets, const int* sizes, int levels, int chunk,
+                    int64_t* stats, int* trace, uint64_t stream) {
+    return odie::launch_selection_chunk(scores, n, points, resolution, cap, normalized, missing, chosen, nodes, tree,
+                                        offsets, sizes, levels, chunk, reinterpret_cast<long long*>(stats), trace,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+int odie_tile_topk(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
+                   double* row_sums, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (height < 1 || width < 1 || tile < 1 || k < 0) return int(cudaErrorInvalidValue);
+    odie::launch_tile_scores(prediction, target, height, width, tile, row_sums, scores, s);
+    const int tiles = ((width + tile - 1) / tile) * ((height + tile - 1) / tile);
+    odie::launch_topk(scores, tiles, k, reinterpret_cast<long long*>(chosen), selected, s);
+    return int(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+// Training/decoding step kernels (step.cu).
+#pragma once
+#include "common.cuh"
+
+namespace odie {
+
+// Head network shapes (the reference's TCNN FullyFusedMLP heads,
+// odie/native/runtime.cu:155-157, odie/model.py:186-188): no biases, ReLU hidden
+// layers, linear output, fp16 weights with fp32 masters, parameters row-major
+// [out][in] per layer in the order gate W1, gate W2 | decoder W1, W2, W3.
+constexpr int GATE_HIDDEN = 32, GATE_OUT = 16, DEC_HIDDEN = 64, DEC_OUT = 16;
+__host__ __device__ constexpr int gate_params(int w) { return GATE_HIDDEN * w + GATE_OUT * GATE_HIDDEN; }
+__host__ __device__ constexpr int decoder_params(int w) { return DEC_HIDDEN * w + DEC_HIDDEN * DEC_HIDDEN + DEC_OUT * DEC_HIDDEN; }
+
+struct FeatureMap {
+    int8_t level_of_col[64];  // level of each decoder-input column, -1 for pad columns (constant 1)
+    int8_t col_of_level[32];  // first column of each level
+    int8_t dim_of_level[32];  // features of each level
+};
+
+struct MlpArgs {
+    long long n;          // coordinates of this launch
+    long long stride;     // pair-major stride of raw/gvals and level stride of vis
+    const __half* raw;    // [W/2][stride] half2 features
+    const uint8_t* vis;   // [levels][stride]
+    const float* target;  // [n][3] fp32 (training) or nullptr
+    const __half* gate_w;     // fp16 gate weights (may be null without router)
+    const __half* decoder_w;  // fp16 decoder weights
+    int levels, raw_width, k_fixed, softplus;
+    float three_real;     // fp32(3 * real) of the loss gradient
+    FeatureMap fmap;
+    __half* gvals;        // [W/2][stride] grid-gradient values (training)
+    float* squares;       // [n] per-sample mean-RGB squared error (training)
+    float* partials;      // [gridDim.x][head params] weight-gradient partials (training)
+    float* rgb;           // [n][3] fp32 decode output (decode)
+    uint8_t* rgb8;        // [n][3] u8 decode output (decode)
+};
+
+size_t mlp_train_smem(int width);
+void launch_mlp_train(const MlpArgs& args, int width, bool router, int blocks, cudaStream_t stream);
+void launch_mlp_decode(const MlpArgs& args, int width, bool router, cudaStream_t stream);
+int mlp_train_blocks(long long n);
+
+void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
+                        float* xy, float* target, cudaStream_t stream);
+void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream);
+
+// Sum of the per-block weight-gradient partials in block order (deterministic).
+void launch_reduce_partials(const float* partials, int blocks, int count, float* out, cudaStream_t stream);
+
+struct AdamTables {
+    const float* step_size;  // fp32(lr / (1 - beta1^s)) for s = 1..size (index s-1), evaluated in double
+    const float* bc2_sqrt;   // fp32(sqrt(1 - beta2^s)), evaluated in double
+    long long size;
+};
+// Adam over one parameter group with device-side per-parameter step counters
+// (so a captured CUDA graph replays correct bias corrections).  skip_zero:
+// entries whose gradient is exactly zero keep their state and step (the native
+// grid optimizer, odie/native/runtime.cu:212-213); without it every entry steps
+// (torch.optim.Adam on a dense tensor).  The gradient is consumed (zeroed) and
+// the fp16 copy refreshed for every updated entry.
+void launch_adam(float* master, __half* copy, float* m, float* v, uint32_t* steps, float* grad, long long count,
+                 float inv_scale, AdamTables tables, float beta1w, float beta2, float beta2w, float eps, bool skip_zero,
+                 int* error_flag, cudaStream_t stream);
+void launch_zero(float* p, long long count, cudaStream_t stream);
+void launch_cast_half(const float* in, __half* out, long long count, cudaStream_t stream);
+
+}  // namespace odie

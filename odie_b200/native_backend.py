@@ -1,0 +1,156 @@
+"""Optimizer-like wrapper of the native training runtime (odie/native_backend.py).
+
+Same public surface as the reference's NativeOptimizer: param_groups, state,
+prepare_epoch, train_batch, release_graph, recaptures, build_manifest,
+state_summary, native_state_digest, close.  The step is one C-ABI call
+(odie_step) captured in a CUDA graph and replayed for every full batch.
+Differences from the reference: the batch is the configured batch size (not
+fixed at 65536) and the compile-time specialisation of the reference build
+(odie/build.py:26-30) is passed as JSON keys.
+"""
+import json
+
+import torch
+
+from . import _lib
+
+
+class PlaneState:
+    """Per-plane view of the native optimizer state (odie/native_backend.py:7-20)."""
+
+    def __init__(self, backend, planes):
+        self.backend = backend
+        self.ranges = {}
+        offset = 0
+        for plane in planes:
+            self.ranges[plane] = (offset, offset + plane.numel())
+            offset += plane.numel()
+
+    def get(self, plane, default=None):
+        if plane not in self.ranges:
+            return default
+        value = self.backend.state_summary(*self.ranges[plane])
+        return {} if value['pristine'] else {'native_adam_state': True}
+
+
+def target_bytes(target):
+    data = getattr(target, 'data', target)
+    return data
+
+
+class NativeOptimizer:
+    def __init__(self, model, target, shape, config, planes, half=True, batch=None, head_grad=None):
+        self.lib = _lib.library()
+        self.model, self.target, self.config = model, target, config
+        self.half = half
+        self.graph = self.key = None
+        self.recaptures = 0
+        self.batch = int(batch or config.get('batch_size', 65536))
+        self.build_manifest = {'library': str(_lib.LIBRARY), 'arch': 'sm_100a',
+                               'levels': model.n_levels, 'router': model.gate is not None}
+        self.stream = torch.cuda.current_stream()
+        self.param_groups = [dict(name='grid', params=planes, lr=config['grid_lr'])]
+        if model.gate is not None:
+            self.param_groups.append(dict(name='gate', params=list(model.gate.parameters()), lr=config['gate_lr']))
+        self.param_groups.append(dict(name='decoder', params=list(model.decoder.parameters()), lr=config['decoder_lr']))
+        data = target_bytes(target)
+        settings = dict(stream=self.stream.cuda_stream, total=model.grid.numel(), width=shape[1], height=shape[0],
+                        mode=20 if half else 16, warp_limit=128, rgb=data.data_ptr(), grid=model.grid.data_ptr(),
+                        decoder=model.decoder.params.data_ptr(), levels=model.n_levels,
+                        router=int(model.gate is not None), gate_k=int(model.gate_coarse_levels_K),
+                        softplus=int(config.get('router_output_activation', 'sigmoid') == 'softplus'),
+                        rgb8=int(data.dtype == torch.uint8), batch=self.batch, **self.current_settings())
+        if model.gate is not None:
+            settings['gate'] = model.gate.params.data_ptr()
+        if head_grad is not None:
+            settings['head_grad'] = head_grad.data_ptr()
+        if config['representation'] == 'hash_grid':
+            settings['hash_encoding'] = config['hash_encoding']
+        self.handle = self.lib.odie_create(json.dumps(settings).encode())
+        if not self.handle:
+            raise RuntimeError(_lib.error())
+        self.pointers = json.loads(self.lib.odie_pointers(self.handle))
+        self.fixed = torch.zeros(self.batch, device='cuda', dtype=torch.int64)
+        self.squares = torch.empty(self.batch, device='cuda', dtype=torch.float32)
+        self.state = PlaneState(self, planes)
+
+    def current_settings(self):
+        rates = {g['name'] + '_lr': float(g['lr']) for g in self.param_groups}
+        if self.config['representation'] == 'hash_grid':
+            return dict(active=self.model.active_prefix, **rates)
+        return dict(active=self.model.active_prefix,
+                    **{k: getattr(self.model, k).data_ptr() for k in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap')},
+                    **rates)
+
+    def check(self, code):
+        if code:
+            raise RuntimeError(_lib.error())
+
+    def step_raw(self, ids, update=True):
+        self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), int(update)))
+
+    def copied(self, name, shape, dtype):
+        result = torch.empty(shape, device='cuda', dtype=dtype)
+        self.check(self.lib.odie_copy(result.data_ptr(), self.pointers[name], result.numel() * result.element_size(),
+                                      self.stream.cuda_stream))
+        return result
+
+    def release_graph(self):
+        torch.cuda.synchronize()
+        self.graph = self.key = None
+        self.lib.odie_release_contexts(self.handle)
+
+    def prepare_epoch(self):
+        settings = self.current_settings()
+        key = tuple(settings.items())
+        if key == self.key:
+            return
+        self.release_graph()
+        self.check(self.lib.odie_configure(self.handle, json.dumps(settings).encode()))
+        for _ in range(3):
+            self.step_raw(self.fixed, update=False)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            self.step_raw(self.fixed)
+            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], self.batch * 4,
+                                          self.stream.cuda_stream))
+            self.graph_loss = self.squares.double().mean()
+        self.lib.odie_pin_contexts(self.handle)
+        self.graph, self.key = graph, key
+        self.recaptures += 1
+
+    def train_batch(self, ids):
+        if ids.numel() == self.batch and self.graph is not None:
+            self.fixed.copy_(ids)
+            self.graph.replay()
+            return self.graph_loss
+        self.step_raw(ids)
+        self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], ids.numel() * 4,
+                                      self.stream.cuda_stream))
+        return self.squares[:ids.numel()].double().mean()
+
+    def state_summary(self, begin=-1, end=-1):
+        data = self.lib.odie_state(self.handle, begin, end)
+        if data is None:
+            raise RuntimeError(_lib.error())
+        return json.loads(data)
+
+    def native_state_digest(self):
+        return json.dumps(self.state_summary(), sort_keys=True)
+
+    def close(self):
+        if self.handle:
+            self.release_graph()
+            self.lib.odie_destroy(self.handle)
+            self.handle = None
+
+    def decode(self, begin, count, rgb=None, rgb8=None):
+        """Decode pixel ids [begin, begin+count) into fp32 and/or u8 RGB device tensors."""
+        self.check(self.lib.odie_decode(self.handle, begin, count, _lib.ptr(rgb), _lib.ptr(rgb8)))
+
+
+def make_native_optimizer(model, target, shape, config):
+    planes = [torch.nn.Parameter(model.grid[level['plane_offset']:level['plane_offset'] +
+              level['plane_node_capacity'] * level['plane_dim']].detach()) for level in model.layout['levels']]
+    return NativeOptimizer(model, target, shape, config, planes), planes

@@ -1,0 +1,75 @@
+"""Benchmark workloads: seeded synthetic images plus the model layouts they train.
+
+c2-planes: the reference's own method (packed multiresolution planes with a
+per-level sigmoid router, odie/model.py) at BASELINE config 2's image shape
+(2040 x 1356 u8, blobs + gratings + 1/f^2 noise) and batch (2^20 coords).  The
+layout is the reference's DIV2K plan (odie/config.py:resolve at this image
+class; resolutions 8..1020, 13 full-cover levels, 3 on-demand levels with
+caps 181112/181112/181120, results/div2k_50/0028/odie/metrics.json), with the
+on-demand supports chosen as the top cells of a seeded smooth residual field,
+trimmed to their node caps.
+"""
+import numpy as np
+import torch
+
+from . import layout as host_layout
+from .data import ByteTarget, pink_noise, synthetic_image
+from .model import PackedXYPlanes
+
+DIV2K_RESOLUTIONS = [8, 11, 15, 21, 29, 40, 56, 77, 106, 147, 203, 280, 387, 534, 738, 1020]
+DIV2K_SPARSE_CAPS = {13: 181112, 14: 181112, 15: 181120}
+
+
+def plane_model_config(resolutions, dims, initial, seed=1729, batch=1 << 20):
+    width = (sum(dims) + 15) // 16 * 16
+    return dict(resolutions=list(resolutions), n_levels=len(resolutions), representation='xy_planes', coarse_levels=0,
+                gate_coarse_levels_K=0, gate_topology='shared', gate_position='feature', initial_active_prefix=initial,
+                router_enabled=True, router_output_activation='sigmoid', seed=seed, feature_init_std=1e-3,
+                gate_parameters=width * 32 + 32 * 16, decoder_parameters=width * 64 + 64 * 64 + 64 * 16,
+                grid_lr=1e-2, gate_lr=1e-3, decoder_lr=1e-3, batch_size=batch)
+
+
+def capped_support(resolution, cap, seed):
+    """Cells above a threshold of a smooth seeded field, the threshold raised until the closure fits the cap."""
+    field = pink_noise(resolution, resolution, seed)[..., 0].reshape(-1).numpy()
+    lo, hi = float(field.min()), float(field.max())
+    best = np.zeros(resolution * resolution, dtype=bool)
+    for _ in range(40):
+        mid = (lo + hi) / 2
+        support = field > mid
+        if host_layout.plane_closure(support, resolution).numel() <= cap:
+            best, hi = support, mid
+        else:
+            lo = mid
+    return best
+
+
+def c2_planes(seed=1729, batch=1 << 20, band=(0, 1)):
+    """(config, supports, dims, caps, rgb u8 [H*W, 3] on CPU, shape) of rank band[0] of band[1] (row bands)."""
+    rgb, (height, width) = synthetic_image('c2', seed=seed)
+    rank, ranks = band
+    if ranks > 1:
+        rows = np.array_split(np.arange(height), ranks)[rank]
+        rgb = rgb.reshape(height, width, 3)[rows[0]:rows[-1] + 1].reshape(-1, 3).contiguous()
+        height = len(rows)
+    dims = [2] * 16
+    supports, caps = [], []
+    for level, r in enumerate(DIV2K_RESOLUTIONS):
+        points = host_layout.align8(r * r)
+        if level in DIV2K_SPARSE_CAPS:
+            cap = DIV2K_SPARSE_CAPS[level]
+            supports.append(torch.from_numpy(capped_support(r, cap, seed + 31 * level + rank)))
+            caps.append(cap)
+        else:
+            supports.append(torch.ones(r * r, dtype=torch.bool))
+            caps.append(points)
+    config = plane_model_config(DIV2K_RESOLUTIONS, dims, 13, seed=seed + rank, batch=batch)
+    return config, supports, dims, caps, rgb, (height, width)
+
+
+def build_plane_model(config, supports, dims, caps, rgb, device='cuda'):
+    model = PackedXYPlanes(config, supports, dims, caps)
+    target = ByteTarget(rgb.to(device))
+    planes = [torch.nn.Parameter(model.grid[l['plane_offset']:l['plane_offset'] + l['plane_node_capacity'] *
+                                            l['plane_dim']].detach()) for l in model.layout['levels']]
+    return model, target, planes

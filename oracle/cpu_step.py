@@ -1,0 +1,135 @@
+"""PyTorch-CPU restatement of the reference training step -- TEST/BENCH INFRASTRUCTURE ONLY.
+
+Used only by bench.py as the CPU baseline and as the `--impl reference` arm:
+the reference has no CPU path (its "reference" backend still needs CUDA and
+TCNN, odie/optimizer.py:54-89), so its native step (odie/native/runtime.cu:
+253-312) is restated here with vectorised torch CPU ops: index_select gathers
+of the fp16-rounded corner values, autograd's index_add scatter, F.linear heads
+with fp16 activations, the L2 loss with the reference's 128 x 128 loss scaling
+and torch.optim.Adam (betas 0.9/0.999, eps 1e-15).  It runs on all the host
+threads torch is given.
+"""
+import time
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+class CpuStep:
+    def __init__(self, shape, rgb_u8, levels, grid, gate, decoder, width, router=True, lr=(1e-2, 1e-3, 1e-3)):
+        """levels: list of dicts {scale, res, points, offset, F, col, kind, row_map (int64 node->row or None),
+        cells (bool [R*R] visibility or None)}; grid/gate/decoder: fp32 numpy masters."""
+        self.shape = shape
+        self.rgb = torch.from_numpy(np.ascontiguousarray(rgb_u8))
+        self.levels = levels
+        self.width = width
+        self.router = router
+        self.grid = torch.nn.Parameter(torch.from_numpy(grid.copy()))
+        self.gate = torch.nn.Parameter(torch.from_numpy(gate.copy())) if router else None
+        self.decoder = torch.nn.Parameter(torch.from_numpy(decoder.copy()))
+        groups = [{'params': [self.grid], 'lr': lr[0]}, {'params': [self.decoder], 'lr': lr[2]}]
+        if router:
+            groups.append({'params': [self.gate], 'lr': lr[1]})
+        self.optimizer = torch.optim.Adam(groups, betas=(.9, .999), eps=1e-15, foreach=False)
+
+    def _mats(self, params, shapes):
+        out, offset = [], 0
+        for o, i in shapes:
+            out.append(params[offset:offset + o * i].view(o, i))
+            offset += o * i
+        return out
+
+    def encode(self, xy):
+        n = xy.shape[0]
+        cols = []
+        vis_all = []
+        for lv in self.levels:
+            p = xy * lv['scale'] + 0.5
+            i = torch.floor(p)
+            f = p - i
+            ix, iy = i[:, 0].long(), i[:, 1].long()
+            fx, fy = f[:, 0], f[:, 1]
+            w = torch.stack(((1 - fx) * (1 - fy), fx * (1 - fy), (1 - fx) * fy, fx * fy), 1)
+            if lv['kind'] == 'plane':
+                cell = ix + iy * lv['res']
+                nodes = torch.stack((cell, cell + 1, cell + lv['res'], cell + lv['res'] + 1), 1) % lv['points']
+                vis = lv['cells'][cell.clamp(0, lv['res'] ** 2 - 1)] if lv['cells'] is not None else torch.ones(n, dtype=torch.bool)
+                rows = lv['row_map'][nodes] if lv['row_map'] is not None else nodes
+            else:
+                cx = torch.stack((ix, ix + 1, ix, ix + 1), 1)
+                cy = torch.stack((iy, iy, iy + 1, iy + 1), 1)
+                if lv['kind'] == 'hashed':
+                    idx = (cx ^ ((cy * 2654435761) & 0xffffffff)) & 0xffffffff
+                else:
+                    idx = cx + cy * lv['res']
+                rows = idx % lv['points']
+                vis = torch.ones(n, dtype=torch.bool)
+            rows = torch.where(vis.unsqueeze(1), rows, torch.zeros_like(rows)).clamp(min=0)  # hidden cells read row 0
+            for c in range(lv['F']):
+                values = self.grid.index_select(0, (lv['offset'] + rows * lv['F'] + c).reshape(-1)).view(n, 4)
+                values = values.half().float() + (values - values.detach())  # fp16-rounded corners, fp32 gradient
+                cols.append((w.half().float() * values).sum(1) * vis)
+            vis_all.append(vis)
+        raw = torch.stack(cols, 1)
+        if raw.shape[1] < self.width:
+            raw = torch.cat((raw, torch.ones((n, self.width - raw.shape[1]))), 1)
+        return raw.half().float() + (raw - raw.detach()), torch.stack(vis_all, 1)
+
+    def step(self, ids):
+        height, width = self.shape
+        xy = torch.stack(((ids % width).float() * (1.0 / (width - 1)), (ids // width).float() * (1.0 / (height - 1))), 1)
+        target = self.rgb[ids].float() / 255.
+        self.optimizer.zero_grad(set_to_none=True)
+        raw, vis = self.encode(xy)
+        W = self.width
+        if self.router:
+            g1, g2 = self._mats(self.gate, [(32, W), (16, 32)])
+            gh = F.relu(F.linear(raw, g1.half().float())).half().float()
+            logits = F.linear(gh, g2.half().float()).half().float()
+            gates = torch.sigmoid(logits[:, :len(self.levels)]) * vis.float()
+            per_col = torch.cat([gates[:, l:l + 1].expand(-1, lv['F']) for l, lv in enumerate(self.levels)], 1)
+            if per_col.shape[1] < W:
+                per_col = torch.cat((per_col, torch.ones((raw.shape[0], W - per_col.shape[1]))), 1)
+            x = (raw * per_col.half().float()).half().float()
+        else:
+            x = raw
+        d1, d2, d3 = self._mats(self.decoder, [(64, W), (64, 64), (16, 64)])
+        h1 = F.relu(F.linear(x, d1.half().float())).half().float()
+        h2 = F.relu(F.linear(h1, d2.half().float())).half().float()
+        out = F.linear(h2, d3.half().float()).half().float()[:, :3]
+        loss = (out - target).square().mean()
+        (loss * 128.).backward()
+        for p in (self.grid, self.decoder, self.gate):
+            if p is not None and p.grad is not None:
+                p.grad.div_(128.)
+        self.optimizer.step()
+        return float(loss.detach())
+
+
+def plane_levels_for_cpu(descriptors, node_bitmap, node_prefix, bitmap):
+    """Per-level dicts for CpuStep from the reference descriptor tables (dense node->row maps for packed planes)."""
+    levels = []
+    nb = np.asarray(node_bitmap).view(np.uint64)
+    for d in np.asarray(descriptors):
+        r, points, offset, words, cells_off, f, col, direct = (int(v) for v in d)
+        cells = np.unpackbits(np.asarray(bitmap)[cells_off:cells_off + (points // 8)], bitorder='little')[:r * r]
+        row_map = None
+        if not direct:
+            bits = np.unpackbits(nb[words:words + (points + 63) // 64].view(np.uint8), bitorder='little')[:points]
+            row_map = torch.from_numpy((np.cumsum(bits) - bits).astype(np.int64))
+        levels.append(dict(scale=float(r - 1), res=r, points=points, offset=offset, F=f, col=col, kind='plane',
+                           row_map=row_map, cells=torch.from_numpy(cells.astype(bool))))
+    return levels
+
+
+def time_steps(step, ids_batches, budget_seconds=20.0):
+    """Run steps until the batches or the time budget run out; returns (coords, seconds)."""
+    started = time.perf_counter()
+    coords = 0
+    for ids in ids_batches:
+        step.step(ids)
+        coords += ids.numel()
+        if time.perf_counter() - started > budget_seconds:
+            break
+    return coords, time.perf_counter() - started

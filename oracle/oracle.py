@@ -1,0 +1,348 @@
+"""CPU oracle of the ODIE hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline leg and the
+--impl reference arm) may import this module.  The product (odie_b200) never
+does; it has no CPU fallback.
+
+Two layers:
+  * liboracle.so (oracle.c): the reference's arithmetic restated in strict C,
+    one function per reference function, each citing the file:line it follows;
+  * this module: ctypes wrappers, and `reference_step`, the reference's native
+    training step (odie/native/runtime.cu:253-312) restated on the CPU from
+    those functions plus fp64 matrix products for the fully fused MLP heads
+    (whose fp16 rounding points follow the reference's fp16 network:
+    activations stored in fp16, products accumulated at higher precision).
+
+Pinning: the C oracle's selection/scoring/layout functions are checked bit-for-
+bit against golden vectors produced by the reference's own CPU code
+(tests/golden/make_golden.py); the packed query against the reference's own
+CUDA kernels compiled from source (oracle/build_ref.py) on the GPU box.  The
+TCNN heads and TCNN Adam of the reference are third-party code that is not
+vendored (instant-ngp abe236ee -> tiny-cuda-nn 2e757bb): their arithmetic is
+parity-unpinned; the heads follow the fully fused MLP's published structure
+and Adam follows torch.optim.Adam, the reference backend's optimizer.
+"""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / 'liboracle.so'
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / 'oracle.c').stat().st_mtime:
+            subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
+        _lib = C.CDLL(str(LIB_PATH))
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class HashLevelC(C.Structure):
+    _fields_ = [('scale', C.c_float), ('res', C.c_int), ('capacity', C.c_int), ('offset', C.c_int),
+                ('F', C.c_int), ('feature_offset', C.c_int), ('hashed', C.c_int), ('pad', C.c_int)]
+
+
+def _hash_levels(records):
+    arr = (HashLevelC * len(records))()
+    for i, r in enumerate(records):
+        arr[i] = HashLevelC(r['scale'], r['resolution'], r['capacity'], r['offset'], r['features'], r['column'],
+                            r['hashed'], 0)
+    return arr
+
+
+# ---------------------------------------------------------------- wrappers
+def coords(ids, width, height):
+    ids = np.ascontiguousarray(ids, dtype=np.int64)
+    xy = np.empty((ids.size, 2), dtype=np.float32)
+    lib().oracle_coords(_p(ids), C.c_int64(ids.size), width, height, _p(xy))
+    return xy
+
+
+def rows(xy, descriptors, node_bitmap, prefix, bitmap):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    desc = np.ascontiguousarray(descriptors, dtype=np.int32)
+    n, levels = xy.shape[0], desc.shape[0]
+    vis = np.empty((n, levels), dtype=np.uint8)
+    out = np.empty((n, levels, 4), dtype=np.int32)
+    nb = np.ascontiguousarray(node_bitmap).view(np.uint64) if node_bitmap.size else np.zeros(1, np.uint64)
+    pf = np.ascontiguousarray(prefix, dtype=np.int32) if prefix.size else np.zeros(1, np.int32)
+    lib().oracle_rows(_p(xy), C.c_int64(n), _p(desc), levels, _p(nb), _p(pf), _p(np.ascontiguousarray(bitmap)),
+                      _p(vis), _p(out))
+    return vis, out
+
+
+def query(xy, grid, descriptors, node_bitmap, prefix, bitmap, width, active=None, raw_width=None, pad_ones=False):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    grid = np.ascontiguousarray(grid, dtype=np.float32)
+    desc = np.ascontiguousarray(descriptors, dtype=np.int32)
+    n, levels = xy.shape[0], desc.shape[0]
+    out = np.zeros((n, width), dtype=np.uint16)
+    vis = np.empty((n, levels), dtype=np.uint8)
+    nb = np.ascontiguousarray(node_bitmap).view(np.uint64) if node_bitmap.size else np.zeros(1, np.uint64)
+    pf = np.ascontiguousarray(prefix, dtype=np.int32) if prefix.size else np.zeros(1, np.int32)
+    lib().oracle_query(_p(xy), C.c_int64(n), _p(grid), _p(desc), levels, _p(nb), _p(pf),
+                       _p(np.ascontiguousarray(bitmap)), width, levels if active is None else active,
+                       width if raw_width is None else raw_width, int(pad_ones), _p(out), _p(vis))
+    return out.view(np.float16), vis
+
+
+def query_backward(xy, upstream, descriptors, node_bitmap, prefix, bitmap, params):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    up = np.ascontiguousarray(upstream, dtype=np.float16).view(np.uint16)
+    desc = np.ascontiguousarray(descriptors, dtype=np.int32)
+    grad = np.zeros(params, dtype=np.float64)
+    nb = np.ascontiguousarray(node_bitmap).view(np.uint64) if node_bitmap.size else np.zeros(1, np.uint64)
+    pf = np.ascontiguousarray(prefix, dtype=np.int32) if prefix.size else np.zeros(1, np.int32)
+    lib().oracle_query_backward(_p(xy), C.c_int64(xy.shape[0]), _p(up), up.shape[1], _p(desc), desc.shape[0],
+                                _p(nb), _p(pf), _p(np.ascontiguousarray(bitmap)), _p(grad))
+    return grad
+
+
+def hash_indices(xy, records):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    n, levels = xy.shape[0], len(records)
+    idx = np.empty((n, levels, 4), dtype=np.int32)
+    w = np.empty((n, levels, 4), dtype=np.float32)
+    lib().oracle_hash_indices(_p(xy), C.c_int64(n), _hash_levels(records), levels, _p(idx), _p(w))
+    return idx, w
+
+
+def hash_query(xy, table16, records, width):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    table = np.ascontiguousarray(table16, dtype=np.float16).view(np.uint16)
+    out = np.zeros((xy.shape[0], width), dtype=np.uint16)
+    lib().oracle_hash_query(_p(xy), C.c_int64(xy.shape[0]), _p(table), _hash_levels(records), len(records), width,
+                            _p(out))
+    return out.view(np.float16)
+
+
+def hash_backward(xy, upstream, records, params):
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    up = np.ascontiguousarray(upstream, dtype=np.float16).view(np.uint16)
+    grad = np.zeros(params, dtype=np.float64)
+    lib().oracle_hash_backward(_p(xy), C.c_int64(xy.shape[0]), _p(up), up.shape[1], _hash_levels(records),
+                               len(records), _p(grad))
+    return grad
+
+
+def gate_forward(raw, logits, vis, feature_level, k_fixed=0, softplus=False):
+    raw = np.ascontiguousarray(raw, dtype=np.float16).view(np.uint16)
+    lg = np.ascontiguousarray(logits, dtype=np.float16).view(np.uint16)
+    vis = np.ascontiguousarray(vis, dtype=np.uint8)
+    fl = np.ascontiguousarray(feature_level, dtype=np.int32)
+    n, width = raw.shape
+    levels = vis.shape[1]
+    weighted = np.empty_like(raw)
+    sig = np.empty((n, levels), dtype=np.float32)
+    lib().oracle_gate_forward(_p(raw), _p(lg), _p(vis), C.c_int64(n), levels, width, lg.shape[1], _p(fl), k_fixed,
+                              int(softplus), _p(weighted), _p(sig))
+    return weighted.view(np.float16), sig
+
+
+def gate_backward(raw, sig, vis, dz, level_offset, level_dim, gate_width=16, k_fixed=0, softplus=False):
+    raw = np.ascontiguousarray(raw, dtype=np.float16).view(np.uint16)
+    dz = np.ascontiguousarray(dz, dtype=np.float16).view(np.uint16)
+    sig = np.ascontiguousarray(sig, dtype=np.float32)
+    vis = np.ascontiguousarray(vis, dtype=np.uint8)
+    n, width = raw.shape
+    levels = vis.shape[1]
+    direct = np.empty_like(raw)
+    da = np.empty((n, gate_width), dtype=np.uint16)
+    lib().oracle_gate_backward(_p(raw), _p(sig), _p(vis), _p(dz), C.c_int64(n), levels, width, gate_width,
+                               _p(np.ascontiguousarray(level_offset, dtype=np.int32)),
+                               _p(np.ascontiguousarray(level_dim, dtype=np.int32)), k_fixed, int(softplus),
+                               _p(direct), _p(da))
+    return direct.view(np.float16), da.view(np.float16)
+
+
+def grid_values(direct, dr, router=True):
+    d = np.ascontiguousarray(direct, dtype=np.float16).view(np.uint16)
+    r = np.ascontiguousarray(dr if dr is not None else direct, dtype=np.float16).view(np.uint16)
+    out = np.empty(d.shape, dtype=np.float32)
+    lib().oracle_grid_values(_p(d), _p(r), C.c_int64(d.size), int(router), _p(out))
+    return out
+
+
+def loss_grad(output16, target, real=None):
+    out = np.ascontiguousarray(output16, dtype=np.float16).view(np.uint16)
+    target = np.ascontiguousarray(target, dtype=np.float32)
+    n = out.shape[0]
+    dy = np.empty((n, 16), dtype=np.uint16)
+    squares = np.empty(n, dtype=np.float32)
+    lib().oracle_loss_grad(_p(out), _p(target), C.c_int64(n), C.c_int64(n if real is None else real), _p(dy),
+                           _p(squares))
+    return dy.view(np.float16), squares
+
+
+def target_u8(rgb, ids):
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    ids = np.ascontiguousarray(ids, dtype=np.int64)
+    out = np.empty((ids.size, 3), dtype=np.float32)
+    lib().oracle_target_u8(_p(rgb), _p(ids), C.c_int64(ids.size), _p(out))
+    return out
+
+
+def adam(p, m, v, steps, grad, loss_scale, lr, skip_zero, beta1=0.9, beta2=0.999, eps=1e-15):
+    """In place on copies; returns (p, m, v, steps, half_copy)."""
+    p, m, v = (np.array(x, dtype=np.float32, copy=True) for x in (p, m, v))
+    steps = np.array(steps, dtype=np.uint32, copy=True)
+    grad = np.ascontiguousarray(grad, dtype=np.float32)
+    half = np.empty(p.size, dtype=np.uint16)
+    lib().oracle_adam(_p(p), _p(m), _p(v), _p(steps), _p(grad), C.c_int64(p.size), C.c_float(loss_scale),
+                      C.c_double(lr), C.c_double(beta1), C.c_double(beta2), C.c_double(eps), int(skip_zero), _p(half))
+    return p, m, v, steps, half.view(np.float16)
+
+
+def score_chunk(prediction, target, begin, end, width, resolution, first_y, active_cells, xb, yb, totals, rgb8):
+    pred = np.ascontiguousarray(prediction, dtype=np.float32)
+    tgt = np.ascontiguousarray(target)
+    lib().oracle_score_chunk(_p(pred), _p(tgt), C.c_int64(begin), C.c_int64(end), width, resolution, first_y,
+                             active_cells, _p(np.ascontiguousarray(xb, dtype=np.int32)),
+                             _p(np.ascontiguousarray(yb, dtype=np.int32)), _p(totals), int(rgb8))
+    return totals
+
+
+def select_benefit_cost(scores, resolution, cap, normalize=True):
+    scores = np.ascontiguousarray(scores, dtype=np.float64)
+    cells = resolution * resolution
+    selected = np.empty(cells, dtype=np.uint8)
+    nodes = np.empty((cells + 7) // 8 * 8, dtype=np.uint8)
+    used = C.c_int64(0)
+    lib().oracle_select_benefit_cost.restype = C.c_int64
+    iterations = lib().oracle_select_benefit_cost(_p(scores), resolution, C.c_int64(cap), int(normalize),
+                                                  _p(selected), _p(nodes), C.byref(used))
+    return selected.astype(bool), nodes.astype(bool), int(iterations), int(used.value)
+
+
+def select_mean_rank(scores, resolution, cap):
+    scores = np.ascontiguousarray(scores, dtype=np.float64)
+    cells = resolution * resolution
+    selected = np.empty(cells, dtype=np.uint8)
+    nodes = np.empty((cells + 7) // 8 * 8, dtype=np.uint8)
+    lib().oracle_select_mean_rank(_p(scores), resolution, C.c_int64(cap), _p(selected), _p(nodes))
+    return selected.astype(bool), nodes.astype(bool)
+
+
+def tile_scores(prediction, target_u8_img, height, width, tile):
+    tiles = ((width + tile - 1) // tile) * ((height + tile - 1) // tile)
+    out = np.empty(tiles, dtype=np.float64)
+    lib().oracle_tile_scores(_p(np.ascontiguousarray(prediction, dtype=np.float32)),
+                             _p(np.ascontiguousarray(target_u8_img, dtype=np.uint8)), height, width, tile, _p(out))
+    return out
+
+
+def topk(scores, k):
+    scores = np.ascontiguousarray(scores, dtype=np.float64)
+    chosen = np.empty(k, dtype=np.int64)
+    lib().oracle_topk(_p(scores), C.c_int64(scores.size), C.c_int64(k), _p(chosen))
+    return chosen
+
+
+def router(x16, w1, w2, w3, hidden, experts):
+    x = np.ascontiguousarray(x16, dtype=np.float16).view(np.uint16)
+    n, in_width = x.shape
+    out_width = np.asarray(w3).size // hidden
+    expert = np.empty(n, dtype=np.int32)
+    prob = np.empty(n, dtype=np.float32)
+    logits = np.empty((n, out_width), dtype=np.uint16)
+    ws = [np.ascontiguousarray(w, dtype=np.float16).view(np.uint16) for w in (w1, w2, w3)]
+    lib().oracle_router(_p(x), C.c_int64(n), in_width, _p(ws[0]), hidden, _p(ws[1]), _p(ws[2]), out_width, experts,
+                        _p(expert), _p(prob), _p(logits))
+    return expert, prob, logits.view(np.float16)
+
+
+# ---------------------------------------------------------------- heads and the full step
+def head_matrices(params, shapes):
+    out, offset = [], 0
+    for o, i in shapes:
+        out.append(np.asarray(params[offset:offset + o * i], dtype=np.float32).reshape(o, i))
+        offset += o * i
+    return out
+
+
+def head_shapes(width, hidden, depth, out):
+    return [(hidden, width)] + [(hidden, hidden)] * (depth - 1) + [(out, hidden)]
+
+
+def _f16(x):
+    return np.asarray(x, dtype=np.float64).astype(np.float16)
+
+
+def _mm(a16, w16t):
+    """fp16 x fp16 products accumulated in fp64 (the network's higher-precision accumulation)."""
+    return a16.astype(np.float64) @ w16t.astype(np.float64)
+
+
+def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, levels, raw_width, router=True,
+                   k_fixed=0, softplus=False, active=None):
+    """One native training step of the reference, forward and backward, on the CPU.
+
+    rgb: u8 [H*W, 3]; ids: int64 [n]; grid: fp32 master; layout: dict with
+    descriptors/node_bitmap/node_prefix/bitmap (numpy).  Returns a dict of every
+    intermediate: xy, target, raw, vis, logits, sig, weighted, out, dy, squares,
+    dz, direct, da, dr, values (grid-gradient values, fp16-valued fp32),
+    grid_grad (fp64, scale 128), head_grad (fp64, scale 16384, gate | decoder).
+    """
+    height, width = shape
+    n = ids.size
+    W = (raw_width + 15) // 16 * 16
+    active = levels if active is None else active
+    xy = coords(ids, width, height)
+    target = target_u8(rgb, ids)
+    desc = layout['descriptors']
+    raw, vis = query(xy, grid, desc, layout['node_bitmap'], layout['node_prefix'], layout['bitmap'], W,
+                     active=active, raw_width=raw_width, pad_ones=True)
+    feature_level = np.full(W, -1, dtype=np.int32)
+    level_offset = desc[:, 6].astype(np.int32)
+    level_dim = desc[:, 5].astype(np.int32)
+    for l in range(levels):
+        feature_level[level_offset[l]:level_offset[l] + level_dim[l]] = l
+    gate = head_matrices(gate_params, head_shapes(W, 32, 1, 16)) if router else None
+    dec = head_matrices(decoder_params, head_shapes(W, 64, 2, 16))
+    result = dict(xy=xy, target=target, raw=raw, vis=vis)
+    if router:
+        g1, g2 = (_f16(w) for w in gate)
+        gh = _f16(np.maximum(_mm(raw, g1.T), 0))
+        logits = _f16(_mm(gh, g2.T))
+        weighted, sig = gate_forward(raw, logits, vis, feature_level, k_fixed, softplus)
+        result.update(gh=gh, logits=logits, sig=sig)
+    else:
+        weighted = raw
+    d1, d2, d3 = (_f16(w) for w in dec)
+    h1 = _f16(np.maximum(_mm(weighted, d1.T), 0))
+    h2 = _f16(np.maximum(_mm(h1, d2.T), 0))
+    out = _f16(_mm(h2, d3.T))
+    dy, squares = loss_grad(out, target)
+    dh2 = _f16(np.where(h2 > 0, _mm(dy, d3), 0))
+    dh1 = _f16(np.where(h1 > 0, _mm(dh2, d2), 0))
+    dz = _f16(_mm(dh1, d1))
+    dec_grad = [dy.astype(np.float64).T @ h2.astype(np.float64), dh2.astype(np.float64).T @ h1.astype(np.float64),
+                dh1.astype(np.float64).T @ weighted.astype(np.float64)]
+    result.update(weighted=weighted, h1=h1, h2=h2, out=out, dy=dy, squares=squares, dz=dz)
+    if router:
+        direct, da = gate_backward(raw, sig, vis, dz, level_offset, level_dim, 16, k_fixed, softplus)
+        dgh = _f16(np.where(gh > 0, _mm(da, g2), 0))
+        dr = _f16(_mm(dgh, g1))
+        values = grid_values(direct, dr, True)
+        gate_grad = [dgh.astype(np.float64).T @ raw.astype(np.float64), da.astype(np.float64).T @ gh.astype(np.float64)]
+        result.update(direct=direct, da=da, dgh=dgh, dr=dr)
+    else:
+        values = grid_values(dz, None, False)
+        gate_grad = []
+    result['values'] = values
+    upstream = values.astype(np.float16)
+    result['grid_grad'] = query_backward(xy, upstream, desc, layout['node_bitmap'], layout['node_prefix'],
+                                         layout['bitmap'], grid.size)
+    result['head_grad'] = np.concatenate([g.reshape(-1) for g in gate_grad + dec_grad]) if (gate_grad or dec_grad) \
+        else np.zeros(0)
+    return result

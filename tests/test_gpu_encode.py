@@ -1,0 +1,143 @@
+"""GPU parity of the grid encoding (a2-a7, a16) through the C-ABI.
+
+Forward features, visibility and packed rows are bit-exact against the CPU
+oracle (which is itself pinned against the reference's own CUDA query kernel,
+compiled from source, below).  The backward's fp32 reductions are order-
+nondeterministic, so it is compared with a relative tolerance of 1e-5 (fp32)
+against an fp64 accumulation of the same products.
+"""
+import importlib.util
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from odie_b200 import layout as host_layout
+from odie_b200.model import HashQuery, PackedQuery
+from tests.cases import close, coordinates_with_edges, plane_case, plane_config
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def reference_query_module():
+    path = ROOT / 'oracle' / '_ref' / 'query' / 'odie_ref_query.so'
+    if not path.exists():
+        pytest.skip('reference GPU oracle (oracle/_ref) was not built')
+    spec = importlib.util.spec_from_file_location('odie_ref_query', path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def build(seed=3, dims=None, levels=16, dense=10, packed=4):
+    resolutions, dims, supports, caps = plane_case(seed, levels=levels, dims=dims, dense=dense, packed=packed)
+    config = plane_config(resolutions, dims, dense)
+    lay = host_layout.make_layout(config, supports, dims, caps)
+    rng = np.random.default_rng(seed + 100)
+    grid = (rng.standard_normal(lay['params']) * .1).astype(np.float32)
+    return lay, grid
+
+
+def to_cuda(lay, grid):
+    return (torch.from_numpy(grid).cuda(), lay['descriptors'].cuda(), lay['node_bitmap'].cuda(),
+            lay['node_prefix'].cuda(), lay['bitmap'].cuda())
+
+
+@pytest.mark.parametrize('dims', [None, [2] * 12 + [4, 1, 2, 1]])
+def test_query_forward_bit_exact(cuda, dims):
+    lay, grid = build(dims=dims)
+    xy = coordinates_with_edges(20000, 11)
+    g, desc, nb, pf, bm = to_cuda(lay, grid)
+    width = lay['input_width']
+    features, visible = PackedQuery.apply(torch.from_numpy(xy).cuda(), g, desc, nb, pf, bm, width)
+    ref_features, ref_visible = oracle.query(xy, grid, lay['descriptors'].numpy(), lay['node_bitmap'].numpy(),
+                                             lay['node_prefix'].numpy(), lay['bitmap'].numpy(), width)
+    assert np.array_equal(visible.cpu().numpy().astype(np.uint8), ref_visible)
+    assert np.array_equal(features.cpu().numpy().view(np.uint16), ref_features.view(np.uint16))
+    assert ref_visible[:, 10:14].any() and not ref_visible[:, 10:14].all(), 'packed levels must be partly visible'
+
+
+def test_query_forward_matches_reference_kernel(cuda):
+    """Pin: the reference's own query_kernel (odie/packed_kernels.cu, built for sm_100a) == oracle == ours."""
+    ref = reference_query_module()
+    lay, grid = build(seed=5)
+    xy = coordinates_with_edges(30000, 12)
+    g, desc, nb, pf, bm = to_cuda(lay, grid)
+    coords = torch.from_numpy(xy).cuda()
+    width = lay['input_width']
+    ref_features, ref_visible = ref.forward(coords, g, desc, nb, pf, bm, width)
+    features, visible = PackedQuery.apply(coords, g, desc, nb, pf, bm, width)
+    orc_features, orc_visible = oracle.query(xy, grid, lay['descriptors'].numpy(), lay['node_bitmap'].numpy(),
+                                             lay['node_prefix'].numpy(), lay['bitmap'].numpy(), width)
+    assert np.array_equal(ref_features.cpu().numpy().view(np.uint16), orc_features.view(np.uint16))
+    assert np.array_equal(ref_visible.cpu().numpy().astype(np.uint8), orc_visible)
+    assert torch.equal(features.view(torch.int16), ref_features.view(torch.int16))
+    assert torch.equal(visible, ref_visible)
+
+
+def test_query_backward_vs_oracle_and_reference(cuda):
+    lay, grid = build(seed=9)
+    xy = coordinates_with_edges(20000, 13)
+    rng = np.random.default_rng(14)
+    width = lay['input_width']
+    upstream = (rng.standard_normal((xy.shape[0], width)) * .5).astype(np.float16)
+    upstream[rng.random(upstream.shape) < .1] = 0
+    g, desc, nb, pf, bm = to_cuda(lay, grid)
+    coords = torch.from_numpy(xy).cuda()
+    g.requires_grad_(True)
+    features, _ = PackedQuery.apply(coords, g, desc, nb, pf, bm, width)
+    features.backward(torch.from_numpy(upstream).cuda())
+    expected = oracle.query_backward(xy, upstream, lay['descriptors'].numpy(), lay['node_bitmap'].numpy(),
+                                     lay['node_prefix'].numpy(), lay['bitmap'].numpy(), grid.size)
+    close(g.grad.cpu().numpy(), expected, 1e-5, 1e-6, 'query backward vs fp64 oracle')
+    try:
+        ref = reference_query_module()
+    except pytest.skip.Exception:
+        return
+    ref_grad = ref.backward(coords, torch.from_numpy(upstream).cuda(), desc, nb, pf, bm, grid.size)
+    close(g.grad.cpu().numpy(), ref_grad.cpu().numpy(), 1e-5, 1e-6, 'query backward vs reference kernel')
+
+
+def test_query_empty_and_tiny_batches(cuda):
+    lay, grid = build(seed=1)
+    g, desc, nb, pf, bm = to_cuda(lay, grid)
+    for n in (0, 1, 33):
+        xy = coordinates_with_edges(max(n, 7), 2)[:n]
+        features, visible = PackedQuery.apply(torch.from_numpy(xy).cuda().reshape(n, 2), g, desc, nb, pf, bm,
+                                              lay['input_width'])
+        assert features.shape == (n, lay['input_width']) and visible.shape == (n, 16)
+        if n:
+            ref, _ = oracle.query(xy, grid, lay['descriptors'].numpy(), lay['node_bitmap'].numpy(),
+                                  lay['node_prefix'].numpy(), lay['bitmap'].numpy(), lay['input_width'])
+            assert np.array_equal(features.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def test_query_outside_unit_square_is_hidden(cuda):
+    """Coordinates outside [0, 1] (never produced by the reference) read nothing and return zeros."""
+    lay, grid = build(seed=4)
+    g, desc, nb, pf, bm = to_cuda(lay, grid)
+    xy = torch.tensor([[-0.5, 0.5], [1.5, 0.5], [0.5, 2.0], [-3.0, -3.0]], device='cuda')
+    features, visible = PackedQuery.apply(xy, g, desc, nb, pf, bm, lay['input_width'])
+    assert not visible.any() and not features.any()
+
+
+@pytest.mark.parametrize('log2t', [10, 16])
+def test_hash_forward_bit_exact_and_backward(cuda, log2t):
+    enc = dict(otype='HashGrid', n_levels=16, n_features_per_level=2, log2_hashmap_size=log2t, base_resolution=16,
+               per_level_scale=1.5)
+    records, total = host_layout.hash_levels(enc)
+    assert any(r['hashed'] for r in records) and any(not r['hashed'] for r in records)
+    rng = np.random.default_rng(log2t)
+    table = (rng.standard_normal(total) * .1).astype(np.float32)
+    xy = coordinates_with_edges(20000, log2t)
+    coords = torch.from_numpy(xy).cuda()
+    t = torch.from_numpy(table).cuda().requires_grad_(True)
+    features = HashQuery.apply(coords, t, records, 32)
+    expected = oracle.hash_query(xy, table.astype(np.float16), records, 32)
+    assert np.array_equal(features.detach().cpu().numpy().view(np.uint16), expected.view(np.uint16))
+    upstream = (rng.standard_normal((xy.shape[0], 32)) * .5).astype(np.float16)
+    features.backward(torch.from_numpy(upstream).cuda())
+    close(t.grad.cpu().numpy(), oracle.hash_backward(xy, upstream, records, total), 1e-5, 1e-6, 'hash backward')
