@@ -506,7 +506,10 @@ __global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n,
                                    bool rgb8, int width, int height, float* __restrict__ xy, float* __restrict__ target) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const uint32_t id = uint32_t(ids[i]);
+    uint32_t id = uint32_t(ids[i]);
+    // an id outside the image (never produced by the samplers) reads pixel 0
+    // instead of memory outside the target
+    if ((unsigned long long)id >= (unsigned long long)width * (unsigned long long)height) id = 0;
     // fp32(id % W) * fp32(1 / (W - 1)): the reciprocal in double rounded to fp32
     // (odie/native/runtime.cu:34-36).
     const float rx = float(1.0 / double(width - 1)), ry = float(1.0 / double(height - 1));
