@@ -155,10 +155,11 @@ template <bool FROM_DESC>
 __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
                                                               const __grid_constant__ LevelTable table,
                                                               const __half* __restrict__ upstream,
-                                                              float* __restrict__ grad, int warp_limit) {
+                                                              float* __restrict__ grad, int warp_limit,
+                                                              unsigned skip_levels) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int l = blockIdx.y;
-    if (i >= a.n || l >= a.active) return;
+    if (i >= a.n || l >= a.active || (skip_levels >> l & 1u)) return;
     const Level d = fetch_level<FROM_DESC>(desc, table, l);
     const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
     const Corner4 g = geometry(p.x, p.y, d.scale);
@@ -196,7 +197,56 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
     }
 }
 
+// Coarse levels: every block accumulates the gradient of one small level for a
+// contiguous chunk of coordinates in shared memory, then adds each non-zero
+// entry to global memory once.  This turns the heavy same-address contention
+// of coarse tables (2^20 coordinates into a few hundred nodes) into shared-
+// memory updates plus blocks x table-size global reductions.
+struct CoarseList {
+    int level[MAX_LEVELS];
+    int blocks[MAX_LEVELS];  // blocks working on each listed level (<= gridDim.x)
+};
+
+__global__ void __launch_bounds__(512) encode_backward_shared_kernel(const EncodeArgs a,
+                                                                     const __grid_constant__ LevelTable table,
+                                                                     const __grid_constant__ CoarseList list,
+                                                                     const __half* __restrict__ upstream,
+                                                                     float* __restrict__ grad) {
+    extern __shared__ float acc[];
+    const int l = list.level[blockIdx.y];
+    const int blocks = list.blocks[blockIdx.y];
+    if ((int)blockIdx.x >= blocks) return;  // uniform per block
+    const Level d = table.level[l];
+    const int count = d.points * d.F;
+    for (int j = threadIdx.x; j < count; j += blockDim.x) acc[j] = 0.0f;
+    __syncthreads();
+    const long long chunk = (a.n + blocks - 1) / blocks;
+    const long long begin = (long long)blockIdx.x * chunk;
+    const long long end = begin + chunk < a.n ? begin + chunk : a.n;
+    for (long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
+        const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+        const Corner4 g = geometry(p.x, p.y, d.scale);
+        if (!level_on(d, g, a.bitmap)) continue;
+        int rows[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+        for (int c = 0; c < d.F; ++c) {
+            const float v = upstream_value(upstream, a, i, d.col + c);
+            if (v == 0.0f) continue;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) atomicAdd(acc + rows[k] * d.F + c, __fmul_rn(g.w[k], v));
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < count; j += blockDim.x) {
+        const float v = acc[j];
+        if (v != 0.0f) red_add_f32(grad + d.offset + j, v);
+    }
+}
+
 }  // namespace
+
+constexpr int COARSE_SMEM_FLOATS = 24576;  // 96 KB of shared memory per block
 
 void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const float* table32, const __half* table16,
                            __half* out, uint8_t* vis, cudaStream_t stream) {
@@ -217,10 +267,43 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     if (a.n <= 0 || a.levels <= 0) return;
     ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
     const dim3 grid(blocks_for(a.n, 256), a.levels);
-    if (src.descriptors)
-        encode_backward_kernel<true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, upstream, grad, warp_limit);
-    else
-        encode_backward_kernel<false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, warp_limit);
+    if (src.descriptors) {
+        encode_backward_kernel<true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, upstream, grad, warp_limit, 0u);
+        return;
+    }
+    // Levels whose table fits in shared memory and whose global reductions the
+    // block-level pre-aggregation cuts by >= 4x take the shared-memory path.
+    CoarseList list{};
+    int coarse = 0, max_blocks = 0, max_floats = 0;
+    unsigned skip = 0;
+    const int cap_blocks = 2 * sm_count();
+    for (int l = 0; l < a.levels && l < a.active; ++l) {
+        const Level& d = src.table.level[l];
+        const long long floats = (long long)d.points * d.F;
+        if (floats > COARSE_SMEM_FLOATS) continue;
+        long long blocks = (a.n * d.F) / (floats > 0 ? floats : 1);  // flush <= 1/4 of the direct reductions
+        if (blocks < 1) continue;
+        if (blocks > cap_blocks) blocks = cap_blocks;
+        list.level[coarse] = l;
+        list.blocks[coarse] = int(blocks);
+        ++coarse;
+        skip |= 1u << l;
+        if (blocks > max_blocks) max_blocks = int(blocks);
+        if (floats > max_floats) max_floats = int(floats);
+    }
+    if (coarse) {
+        const int bytes = max_floats * 4;
+        static unsigned long long configured = 0;
+        int device = 0;
+        ODIE_CUDA(cudaGetDevice(&device));
+        if (!(configured >> device & 1ull)) {
+            ODIE_CUDA(cudaFuncSetAttribute(encode_backward_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           COARSE_SMEM_FLOATS * 4));
+            configured |= 1ull << device;
+        }
+        encode_backward_shared_kernel<<<dim3(max_blocks, coarse), 512, bytes, stream>>>(a, src.table, list, upstream, grad);
+    }
+    encode_backward_kernel<false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, warp_limit, skip);
 }
 
 }  // namespace odie

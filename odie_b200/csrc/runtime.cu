@@ -261,7 +261,7 @@ struct Runtime {
             }
             raw_width = width;
             input_width = (raw_width + 15) / 16 * 16;
-            ODIE_REQUIRE(input_width <= 64, "decoder input width must be <= 64");
+            ODIE_REQUIRE(input_width <= 32, "the fused heads take at most 32 input features (16 levels x F2)");
             build_feature_map();
         }
         lr[0] = j.at("grid_lr").as_double();

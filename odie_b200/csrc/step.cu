@@ -45,7 +45,7 @@ struct Smem {
     static constexpr int weight_bytes = (weight_halves * 2 + 15) / 16 * 16;
     static constexpr int fmap_bytes = 128;
     static constexpr int head_params = gate_params(W) + decoder_params(W);
-    static constexpr int acc_bytes = head_params * 4;
+    static constexpr int acc_bytes = WARPS * head_params * 4;  // one private accumulator per warp
     // per-warp staging
     static constexpr int xs_bytes = 16 * LDX * 2;
     static constexpr int tm_bytes = 16 * LD_TM * 2;
@@ -256,32 +256,40 @@ __device__ __forceinline__ void accumulate_dw(float* acc, int ld, const uint32_t
             mma::b_transposed(b0, b1, in, ni);
             float c[4] = {0, 0, 0, 0};
             mma::m16n8k16(c, at, b0, b1);
+            // the warp's private accumulator: plain read-modify-write, no atomics
             const int o0 = 16 * mo + g, col = 8 * ni + 2 * t;
             if (o0 < row_limit) {
-                atomicAdd(acc + o0 * ld + col, c[0]);
-                atomicAdd(acc + o0 * ld + col + 1, c[1]);
+                float2* p = reinterpret_cast<float2*>(acc + o0 * ld + col);
+                float2 v = *p;
+                v.x += c[0];
+                v.y += c[1];
+                *p = v;
             }
             if (o0 + 8 < row_limit) {
-                atomicAdd(acc + (o0 + 8) * ld + col, c[2]);
-                atomicAdd(acc + (o0 + 8) * ld + col + 1, c[3]);
+                float2* p = reinterpret_cast<float2*>(acc + (o0 + 8) * ld + col);
+                float2 v = *p;
+                v.x += c[2];
+                v.y += c[3];
+                *p = v;
             }
         }
     }
 }
 
 template <int W, bool ROUTER>
-__global__ void __launch_bounds__(THREADS, 2) mlp_train_kernel(const MlpArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) mlp_train_kernel(const MlpArgs a) {
     using S = Smem<W>;
-    constexpr int KW = W / 16, NW = W / 8;
+    constexpr int NW = W / 8;
     extern __shared__ __align__(16) unsigned char smem[];
     __half* ws = reinterpret_cast<__half*>(smem);
     int8_t* fmap = reinterpret_cast<int8_t*>(smem + S::weight_bytes);
-    float* acc = reinterpret_cast<float*>(smem + S::weight_bytes + S::fmap_bytes);
+    float* acc_all = reinterpret_cast<float*>(smem + S::weight_bytes + S::fmap_bytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     WarpBufs<W> wb(smem + S::weight_bytes + S::fmap_bytes + S::acc_bytes + warp * S::warp_bytes);
     stage_weights<W, ROUTER>(a, ws, fmap);
-    for (int i = threadIdx.x; i < S::head_params; i += blockDim.x) acc[i] = 0.0f;
+    for (int i = threadIdx.x; i < WARPS * S::head_params; i += blockDim.x) acc_all[i] = 0.0f;
     __syncthreads();
+    float* acc = acc_all + warp * S::head_params;  // this warp's weight-gradient accumulator
     float* dg1 = acc;                                   // [32][W]
     float* dg2 = dg1 + GATE_HIDDEN * W;                 // [16][32]
     float* dd1 = acc + gate_params(W);                  // [64][W]
@@ -465,7 +473,12 @@ __global__ void __launch_bounds__(THREADS, 2) mlp_train_kernel(const MlpArgs a) 
     }
     __syncthreads();
     float* out = a.partials + (long long)blockIdx.x * S::head_params;
-    for (int i = threadIdx.x; i < S::head_params; i += blockDim.x) out[i] = acc[i];
+    for (int i = threadIdx.x; i < S::head_params; i += blockDim.x) {
+        float s = acc_all[i];
+#pragma unroll
+        for (int w = 1; w < WARPS; ++w) s = __fadd_rn(s, acc_all[w * S::head_params + i]);
+        out[i] = s;
+    }
 }
 
 template <int W, bool ROUTER>
@@ -639,20 +652,20 @@ void launch_decode_t(const MlpArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
+// The training kernel keeps one fp32 weight-gradient accumulator per warp in
+// shared memory, which bounds the decoder input width to 32 (16 levels x F2).
 size_t mlp_train_smem(int width) {
     switch (width) {
         case 16: return Smem<16>::train_bytes;
         case 32: return Smem<32>::train_bytes;
-        case 48: return Smem<48>::train_bytes;
-        case 64: return Smem<64>::train_bytes;
     }
-    throw std::invalid_argument("decoder input width must be 16, 32, 48 or 64");
+    throw std::invalid_argument("decoder input width must be 16 or 32");
 }
 
 int mlp_train_blocks(long long n) {
     const long long tiles = (n + 15) / 16;
     long long blocks = (tiles + WARPS - 1) / WARPS;
-    const long long cap = 2LL * sm_count();
+    const long long cap = 1LL * sm_count();
     if (blocks > cap) blocks = cap;
     return blocks < 1 ? 1 : int(blocks);
 }
@@ -664,9 +677,9 @@ void launch_mlp_train(const MlpArgs& a, int width, bool router, int blocks, cuda
         if (router) launch_train_t<WV, true>(a, blocks, stream);     \
         else launch_train_t<WV, false>(a, blocks, stream);           \
         return;
-    switch (width) { ODIE_W(16) ODIE_W(32) ODIE_W(48) ODIE_W(64) }
+    switch (width) { ODIE_W(16) ODIE_W(32) }
 #undef ODIE_W
-    throw std::invalid_argument("decoder input width must be 16, 32, 48 or 64");
+    throw std::invalid_argument("decoder input width must be 16 or 32");
 }
 
 void launch_mlp_decode(const MlpArgs& a, int width, bool router, cudaStream_t stream) {
@@ -676,9 +689,9 @@ void launch_mlp_decode(const MlpArgs& a, int width, bool router, cudaStream_t st
         if (router) launch_decode_t<WV, true>(a, stream);         \
         else launch_decode_t<WV, false>(a, stream);               \
         return;
-    switch (width) { ODIE_W(16) ODIE_W(32) ODIE_W(48) ODIE_W(64) }
+    switch (width) { ODIE_W(16) ODIE_W(32) }
 #undef ODIE_W
-    throw std::invalid_argument("decoder input width must be 16, 32, 48 or 64");
+    throw std::invalid_argument("decoder input width must be 16 or 32");
 }
 
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,

@@ -143,10 +143,11 @@ def test_tile_topk_bit_exact(cuda):
     scores = torch.empty(tiles, dtype=torch.float64, device='cuda')
     chosen = torch.empty(k, dtype=torch.int64, device='cuda')
     selected = torch.empty(tiles, dtype=torch.uint8, device='cuda')
-    _lib.check(_lib.library().odie_tile_topk(torch.from_numpy(pred).cuda().data_ptr(),
-                                             torch.from_numpy(u8).cuda().data_ptr(), h, w, tile, k,
+    pred_d, u8_d = torch.from_numpy(pred).cuda(), torch.from_numpy(u8).cuda()  # keep both alive during the call
+    _lib.check(_lib.library().odie_tile_topk(pred_d.data_ptr(), u8_d.data_ptr(), h, w, tile, k,
                                              row_sums.data_ptr(), scores.data_ptr(), chosen.data_ptr(),
                                              selected.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
     expected = oracle.tile_scores(pred, u8, h, w, tile)
     assert np.array_equal(scores.cpu().numpy(), expected)
     assert np.array_equal(chosen.cpu().numpy(), oracle.topk(expected, k))
