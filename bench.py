@@ -191,6 +191,7 @@ def main():
     rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
     local = int(os.environ.get('LOCAL_RANK', 0))
     torch.cuda.set_device(local)
+    torch.cuda.set_stream(torch.cuda.Stream())  # a dedicated training stream, as odie/train.py:73-75
     dist = None
     if world > 1:
         import datetime

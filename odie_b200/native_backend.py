@@ -8,6 +8,7 @@ Differences from the reference: the batch is the configured batch size (not
 fixed at 65536) and the compile-time specialisation of the reference build
 (odie/build.py:26-30) is passed as JSON keys.
 """
+import contextlib
 import json
 
 import torch
@@ -48,7 +49,9 @@ class NativeOptimizer:
         self.batch = int(batch or config.get('batch_size', 65536))
         self.build_manifest = {'library': str(_lib.LIBRARY), 'arch': 'sm_100a',
                                'levels': model.n_levels, 'router': model.gate is not None}
-        self.stream = torch.cuda.current_stream()
+        # the reference trains on a dedicated stream (odie/train.py:73-75); CUDA graphs need a non-default one
+        current = torch.cuda.current_stream()
+        self.stream = torch.cuda.Stream() if current == torch.cuda.default_stream() else current
         self.param_groups = [dict(name='grid', params=planes, lr=config['grid_lr'])]
         if model.gate is not None:
             self.param_groups.append(dict(name='gate', params=list(model.gate.parameters()), lr=config['gate_lr']))
@@ -86,13 +89,27 @@ class NativeOptimizer:
         if code:
             raise RuntimeError(_lib.error())
 
+    @contextlib.contextmanager
+    def on_stream(self):
+        """Run on the runtime's stream, ordered after and before the caller's current stream."""
+        caller = torch.cuda.current_stream()
+        if caller == self.stream:
+            yield
+            return
+        self.stream.wait_stream(caller)
+        with torch.cuda.stream(self.stream):
+            yield
+        caller.wait_stream(self.stream)
+
     def step_raw(self, ids, update=True):
-        self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), int(update)))
+        with self.on_stream():
+            self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), int(update)))
 
     def copied(self, name, shape, dtype):
-        result = torch.empty(shape, device='cuda', dtype=dtype)
-        self.check(self.lib.odie_copy(result.data_ptr(), self.pointers[name], result.numel() * result.element_size(),
-                                      self.stream.cuda_stream))
+        with self.on_stream():
+            result = torch.empty(shape, device='cuda', dtype=dtype)
+            self.check(self.lib.odie_copy(result.data_ptr(), self.pointers[name],
+                                          result.numel() * result.element_size(), self.stream.cuda_stream))
         return result
 
     def release_graph(self):
@@ -112,7 +129,7 @@ class NativeOptimizer:
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=self.stream):
-            self.step_raw(self.fixed)
+            self.check(self.lib.odie_step(self.handle, self.fixed.data_ptr(), self.fixed.numel(), 1))
             self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], self.batch * 4,
                                           self.stream.cuda_stream))
             self.graph_loss = self.squares.double().mean()
@@ -121,14 +138,15 @@ class NativeOptimizer:
         self.recaptures += 1
 
     def train_batch(self, ids):
-        if ids.numel() == self.batch and self.graph is not None:
-            self.fixed.copy_(ids)
-            self.graph.replay()
-            return self.graph_loss
-        self.step_raw(ids)
-        self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], ids.numel() * 4,
-                                      self.stream.cuda_stream))
-        return self.squares[:ids.numel()].double().mean()
+        with self.on_stream():
+            if ids.numel() == self.batch and self.graph is not None:
+                self.fixed.copy_(ids)
+                self.graph.replay()
+                return self.graph_loss
+            self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), 1))
+            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], ids.numel() * 4,
+                                          self.stream.cuda_stream))
+            return self.squares[:ids.numel()].double().mean()
 
     def state_summary(self, begin=-1, end=-1):
         data = self.lib.odie_state(self.handle, begin, end)
@@ -147,7 +165,13 @@ class NativeOptimizer:
 
     def decode(self, begin, count, rgb=None, rgb8=None):
         """Decode pixel ids [begin, begin+count) into fp32 and/or u8 RGB device tensors."""
-        self.check(self.lib.odie_decode(self.handle, begin, count, _lib.ptr(rgb), _lib.ptr(rgb8)))
+        with self.on_stream():
+            self.check(self.lib.odie_decode(self.handle, begin, count, _lib.ptr(rgb), _lib.ptr(rgb8)))
+
+    def call(self, name, *args):
+        """Call a runtime entry point (odie_<name>) on this optimizer's stream."""
+        with self.on_stream():
+            self.check(getattr(self.lib, 'odie_' + name)(self.handle, *args))
 
 
 def make_native_optimizer(model, target, shape, config):

@@ -200,7 +200,7 @@ def adam(p, m, v, steps, grad, loss_scale, lr, skip_zero, beta1=0.9, beta2=0.999
     half = np.empty(p.size, dtype=np.uint16)
     lib().oracle_adam(_p(p), _p(m), _p(v), _p(steps), _p(grad), C.c_int64(p.size), C.c_float(loss_scale),
                       C.c_double(lr), C.c_double(beta1), C.c_double(beta2), C.c_double(eps), int(skip_zero), _p(half))
-    return p, m, v, steps, half.view(np.float16)
+    return p, m, v, steps, p.astype(np.float16)  # fp16 copy of every entry (updated or skipped)
 
 
 def score_chunk(prediction, target, begin, end, width, resolution, first_y, active_cells, xb, yb, totals, rgb8):
@@ -326,8 +326,9 @@ def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, l
     dh2 = _f16(np.where(h2 > 0, _mm(dy, d3), 0))
     dh1 = _f16(np.where(h1 > 0, _mm(dh2, d2), 0))
     dz = _f16(_mm(dh1, d1))
-    dec_grad = [dy.astype(np.float64).T @ h2.astype(np.float64), dh2.astype(np.float64).T @ h1.astype(np.float64),
-                dh1.astype(np.float64).T @ weighted.astype(np.float64)]
+    # parameter order of the decoder: W1 [64][W], W2 [64][64], W3 [16][64]
+    dec_grad = [dh1.astype(np.float64).T @ weighted.astype(np.float64), dh2.astype(np.float64).T @ h1.astype(np.float64),
+                dy.astype(np.float64).T @ h2.astype(np.float64)]
     result.update(weighted=weighted, h1=h1, h2=h2, out=out, dy=dy, squares=squares, dz=dz)
     if router:
         direct, da = gate_backward(raw, sig, vis, dz, level_offset, level_dim, 16, k_fixed, softplus)
