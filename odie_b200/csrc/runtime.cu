@@ -80,6 +80,7 @@ struct Runtime {
     int image_width = 0, image_height = 0, mode = 0, warp_limit = 128;
     int levels = 16, raw_width = 32, input_width = 32, gate_k = 0, active = 16;
     bool router = true, softplus = false, rgb8 = true, hash_mode = false;
+    bool tc_heads = true;  // tcgen05/TMEM heads (width 32); false: the mma.sync heads
     double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
     // caller-owned
     float* grid = nullptr;
@@ -122,6 +123,7 @@ struct Runtime {
         gate_k = int(j.value("gate_k", 0));
         softplus = j.value("softplus", 0) != 0;
         rgb8 = j.value("rgb8", 1) != 0;
+        tc_heads = j.value("mma_heads", 0) == 0;
         ODIE_REQUIRE(total > 0 && total <= 0x7fffffffLL, "total must fit int32 addressing");
         ODIE_REQUIRE(image_width >= 2 && image_height >= 2, "image axes must be >= 2");
         ODIE_REQUIRE(capacity >= 1 && capacity <= (1LL << 26), "batch capacity must be in [1, 2^26]");
@@ -165,7 +167,8 @@ struct Runtime {
         head_m.allocate(head_count);
         head_v.allocate(head_count);
         head_steps.allocate(head_count);
-        partial_blocks = mlp_train_blocks(capacity);
+        if (input_width != 32) tc_heads = false;
+        partial_blocks = std::max(mlp_train_blocks(capacity), mlp_tc_blocks(capacity));
         partials.allocate((long long)partial_blocks * head_count);
         xy.allocate(2 * capacity);
         target.allocate(3 * capacity);
@@ -383,9 +386,10 @@ struct Runtime {
         launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, vis.ptr, stream);
         stage_end(slot);
         const MlpArgs ma = mlp_args(n);
-        const int blocks = mlp_train_blocks(n);
+        const int blocks = tc_heads ? mlp_tc_blocks(n) : mlp_train_blocks(n);
         slot = stage_begin(S_MLP);
-        launch_mlp_train(ma, input_width, router, blocks, stream);
+        if (tc_heads) launch_mlp_tc_train(ma, input_width, router, blocks, error_flag.ptr, stream);
+        else launch_mlp_train(ma, input_width, router, blocks, stream);
         stage_end(slot);
         slot = stage_begin(S_ENCODE_BWD);
         launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, warp_limit, stream);
@@ -441,7 +445,8 @@ struct Runtime {
             MlpArgs ma = mlp_args(count);
             ma.rgb = out_rgb ? out_rgb + 3 * done : nullptr;
             ma.rgb8 = out_rgb8 ? out_rgb8 + 3 * done : nullptr;
-            launch_mlp_decode(ma, input_width, router, stream);
+            if (tc_heads) launch_mlp_tc_decode(ma, input_width, router, error_flag.ptr, stream);
+            else launch_mlp_decode(ma, input_width, router, stream);
         }
         ODIE_CUDA(cudaGetLastError());
     }

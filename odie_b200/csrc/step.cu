@@ -292,7 +292,10 @@ __global__ void __launch_bounds__(THREADS, 1) mlp_train_kernel(const MlpArgs a) 
     float* acc = acc_all + warp * S::head_params;  // this warp's weight-gradient accumulator
     float* dg1 = acc;                                   // [32][W]
     float* dg2 = dg1 + GATE_HIDDEN * W;                 // [16][32]
-    float* dd1 = acc + gate_params(W);                  // [64][W]
+    // head parameters of this launch: gate | decoder, or decoder only without the router
+    constexpr int GATE = ROUTER ? gate_params(W) : 0;
+    constexpr int P = GATE + decoder_params(W);
+    float* dd1 = acc + GATE;                            // [64][W]
     float* dd2 = dd1 + DEC_HIDDEN * W;                  // [64][64]
     float* dd3 = dd2 + DEC_HIDDEN * DEC_HIDDEN;         // [16][64]
     const FeatureMap* fm = reinterpret_cast<const FeatureMap*>(fmap);
@@ -472,8 +475,8 @@ __global__ void __launch_bounds__(THREADS, 1) mlp_train_kernel(const MlpArgs a) 
         __syncwarp();
     }
     __syncthreads();
-    float* out = a.partials + (long long)blockIdx.x * S::head_params;
-    for (int i = threadIdx.x; i < S::head_params; i += blockDim.x) {
+    float* out = a.partials + (long long)blockIdx.x * P;
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
         float s = acc_all[i];
 #pragma unroll
         for (int w = 1; w < WARPS; ++w) s = __fadd_rn(s, acc_all[w * S::head_params + i]);

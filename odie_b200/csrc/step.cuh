@@ -41,6 +41,12 @@ void launch_mlp_train(const MlpArgs& args, int width, bool router, int blocks, c
 void launch_mlp_decode(const MlpArgs& args, int width, bool router, cudaStream_t stream);
 int mlp_train_blocks(long long n);
 
+// tcgen05/TMEM fused heads (mlp_tc.cu), decoder input width 32.  A wait that
+// runs out sets *error_flag = 2 and the kernel returns.
+int mlp_tc_blocks(long long n);
+void launch_mlp_tc_train(const MlpArgs& args, int width, bool router, int blocks, int* error_flag, cudaStream_t stream);
+void launch_mlp_tc_decode(const MlpArgs& args, int width, bool router, int* error_flag, cudaStream_t stream);
+
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
                         float* xy, float* target, cudaStream_t stream);
 void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream);

@@ -65,6 +65,7 @@ def test_step_gradients_match_oracle(cuda, router, k, activation):
     lib = _lib.library()
     opt.call('step_grads', ids.data_ptr(), n, 2)
     torch.cuda.synchronize()
+    assert opt.copied('error_flag', (1,), torch.int32).item() == 0, 'a bounded device wait ran out'
     W = opt.pointers['input_width']
     ref = reference(model, rgb, ids.cpu().numpy(), grid, gate, dec, router, k, activation == 'softplus')
     # bit-exact integer/byte stages
