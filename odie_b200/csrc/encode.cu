@@ -71,15 +71,26 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
                                                              uint8_t* __restrict__ vis) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int l = blockIdx.y;
-    if (i >= a.n) return;
+    const bool inside = i < a.n;
     const Level d = fetch_level<FROM_DESC>(desc, table, l);
-    const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
-    const Corner4 g = geometry(p.x, p.y, d.scale);
-    const bool on = l < a.active && level_on(d, g, a.bitmap);
-    if (vis) {
-        if (a.row_major) vis[i * a.levels + l] = on;
-        else vis[(long long)l * a.stride + i] = on;
+    Corner4 g{};
+    bool on = false;
+    if (inside) {
+        const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+        g = geometry(p.x, p.y, d.scale);
+        on = l < a.active && level_on(d, g, a.bitmap);
     }
+    if (vis) {
+        if (a.row_major) {
+            if (inside) vis[i * a.levels + l] = on;
+        } else {
+            // bit-packed [levels][stride / 32] words: one ballot per warp of 32 consecutive coordinates
+            const unsigned bits = __ballot_sync(0xffffffffu, on);
+            if ((threadIdx.x & 31) == 0 && inside)
+                reinterpret_cast<uint32_t*>(vis)[(long long)l * (a.stride >> 5) + (i >> 5)] = bits;
+        }
+    }
+    if (!inside) return;
     if (d.F == 2) {
         __half2 acc = __float2half2_rn(0.0f);
         if (on) {

@@ -11,10 +11,14 @@
 // accumulators in TMEM) issued by one thread and tracked by one mbarrier; the
 // epilogues read TMEM rows with tcgen05.ld (thread = row) and write the next
 // operand to shared memory.  Weight gradients are products over the
-// coordinate dimension (K = 128 rows of a tile) whose accumulators stay in TMEM
-// across all tiles of the CTA and are written once as per-CTA partials.
+// coordinate dimension (K = the 128 rows of a tile) whose accumulators stay in
+// TMEM across all tiles of the CTA and are written once as per-CTA partials.
 // Activations are rounded to fp16 where the reference's fp16 network stores
 // them; every wait is bounded and reports through an error flag.
+//
+// UNIFORM: every level has 2 features at columns (2l, 2l+1) (the reference's
+// default layout); the per-level epilogues are then fully unrolled with
+// compile-time indices.  Other layouts take the generic per-column path.
 #include "step.cuh"
 #include "tc.cuh"
 
@@ -31,30 +35,32 @@ constexpr uint32_t TMEM_COLUMNS = 256;
 // gradient accumulators (M=64: lanes 0-15 of each 32-lane subpartition).
 constexpr uint32_t T_ACC = 0, T_DWD2 = 64, T_DWD1 = 128, T_DW3T = 160, T_DWG2T = 176, T_DWG1 = 192;
 
-// Shared memory (bytes), decoder input width 32: weights blocked [out x in],
+// Shared memory (bytes) for decoder input width W: weights blocked [out x in],
 // activations blocked [128 x cols].  GH and DGH are read 64 columns wide as
 // M=64 operands; their upper half aliases the following buffers and only
 // feeds accumulator rows that are never read.
+template <int W>
 struct TcSmem {
-    static constexpr int g1 = 0;                  // [32 x 32]
-    static constexpr int g2 = g1 + 32 * 32 * 2;   // [16 x 32]
-    static constexpr int d1 = g2 + 16 * 32 * 2;   // [64 x 32]
-    static constexpr int d2 = d1 + 64 * 32 * 2;   // [64 x 64]
-    static constexpr int d3 = d2 + 64 * 64 * 2;   // [16 x 64]
-    static constexpr int x = d3 + 16 * 64 * 2;    // [128 x 32] raw features
-    static constexpr int wx = x + 8192;           // [128 x 32] gated decoder input
-    static constexpr int gh = wx + 8192;          // [128 x 32] gate hidden
-    static constexpr int h1 = gh + 8192;          // [128 x 64] decoder hidden 1, then dh1
-    static constexpr int h2 = h1 + 16384;         // [128 x 64] decoder hidden 2, then dh2
-    static constexpr int dgh = h2 + 16384;        // [128 x 32] gate hidden gradient
-    static constexpr int dy = dgh + 8192;         // [128 x 16] output gradient
-    static constexpr int da = dy + 4096;          // [128 x 16] gate logit gradient
-    static constexpr int bar = da + 4096;         // mbarrier
-    static constexpr int tmem = bar + 8;          // TMEM base address
+    static constexpr int XB = 128 * W * 2;              // one [128 x W] buffer
+    static constexpr int g1 = 0;                        // [32 x W]
+    static constexpr int g2 = g1 + 32 * W * 2;          // [16 x 32]
+    static constexpr int d1 = g2 + 16 * 32 * 2;         // [64 x W]
+    static constexpr int d2 = d1 + 64 * W * 2;          // [64 x 64]
+    static constexpr int d3 = d2 + 64 * 64 * 2;         // [16 x 64]
+    static constexpr int x = d3 + 16 * 64 * 2;          // [128 x W] raw features
+    static constexpr int wx = x + XB;                   // [128 x W] gated decoder input
+    static constexpr int gh = wx + XB;                  // [128 x 32] gate hidden
+    static constexpr int h1 = gh + 8192;                // [128 x 64] decoder hidden 1, then dh1
+    static constexpr int h2 = h1 + 16384;               // [128 x 64] decoder hidden 2, then dh2
+    static constexpr int dgh = h2 + 16384;              // [128 x 32] gate hidden gradient
+    static constexpr int dy = dgh + 8192;               // [128 x 16] output gradient
+    static constexpr int da = dy + 4096;                // [128 x 16] gate logit gradient
+    static constexpr int bar = da + 4096;               // mbarrier
+    static constexpr int tmem = bar + 8;                // TMEM base address
     static constexpr int total = tmem + 8;
+    static_assert(gh + 16384 <= dgh, "GH read 64 wide stays inside the activation buffers");
+    static_assert(dgh + 16384 <= bar, "DGH read 64 wide stays inside the activation buffers");
 };
-static_assert(TcSmem::gh + 16384 <= TcSmem::dgh, "GH read 64 wide stays inside shared memory");
-static_assert(TcSmem::dgh + 16384 <= TcSmem::bar, "DGH read 64 wide stays inside the activation buffers");
 
 __device__ __forceinline__ uint4 pack8(const float* v) {
     uint4 q;
@@ -65,12 +71,11 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
     return q;
 }
 
-// Store 8 fp16 values (one 16-byte chunk) of row r, columns [8j, 8j+8) of a blocked [128 x cols] matrix.
+// Row r, columns [8j, 8j+8) of a blocked [128 x cols] matrix.
 __device__ __forceinline__ void store_chunk(unsigned char* smem, int base, int r, int j, uint4 q) {
     *reinterpret_cast<uint4*>(smem + base + tc::blocked(TC_TILE, r, 8 * j)) = q;
 }
 
-// Copy a global fp16 matrix [rows x cols] (row-major) into a blocked shared-memory matrix.
 __device__ void stage_blocked(const __half* __restrict__ src, int rows, int cols, unsigned char* smem, int base) {
     for (int idx = threadIdx.x; idx < rows * cols; idx += blockDim.x) {
         const int r = idx / cols, c = idx - r * cols;
@@ -82,8 +87,8 @@ struct Issuer {
     uint64_t* bar;
     uint32_t phase = 0;
     bool ok = true;
-    // Make this thread's shared-memory writes visible to the tensor cores and
-    // every thread's TMEM reads complete, then let thread 0 issue.
+    // Make every thread's shared-memory writes visible to the tensor cores and
+    // every TMEM read complete, then let thread 0 issue.
     __device__ void before_issue() {
         tc::fence_async_smem();
         tc::fence_before_sync();
@@ -101,22 +106,58 @@ struct Issuer {
     }
 };
 
-template <bool ROUTER, bool TRAIN>
+// Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
+__device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
+    float v[16];
+    tc::tmem_ld16(taddr, v);
+    uint32_t mask = 0;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
+        mask |= uint32_t(v[c] > 0.0f) << c;
+    }
+    store_chunk(smem, base, r, j0, pack8(v));
+    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
+    return mask;
+}
+// Load 16 TMEM columns, keep those whose forward activation was positive, store two chunks.
+__device__ __forceinline__ void masked_store16(uint32_t taddr, uint32_t mask, unsigned char* smem, int base, int r, int j0) {
+    float v[16];
+    tc::tmem_ld16(taddr, v);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) v[c] = (mask >> c & 1u) ? v[c] : 0.0f;
+    store_chunk(smem, base, r, j0, pack8(v));
+    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
+}
+
+__device__ __forceinline__ float gate_value(float z, int level, int k_fixed, int softplus) {
+    if (level < k_fixed) return 1.0f;
+    if (softplus) return z > 20.0f ? z : log1pf(expf(z));
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+}
+__device__ __forceinline__ float gate_derivative(float incoming, float s, int level, int k_fixed, int softplus) {
+    if (level < k_fixed) return 0.0f;
+    if (softplus) return incoming * (-expm1f(-s));
+    return __fmul_rn(__fmul_rn(incoming, __fsub_rn(1.0f, s)), s);
+}
+
+template <int W, bool ROUTER, bool TRAIN, bool UNIFORM>
 __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, int* error_flag) {
-    constexpr int W = 32;
+    using S = TcSmem<W>;
+    constexpr int PAIRS = W / 2, KW = W / 16;
     extern __shared__ __align__(128) unsigned char smem[];
     const int t = threadIdx.x, warp = t >> 5;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TcSmem::bar);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
     const uint32_t sbase = tc::smem_u32(smem);
 
     if (ROUTER) {
-        stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, TcSmem::g1);
-        stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, TcSmem::g2);
+        stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, S::g1);
+        stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, S::g2);
     }
-    stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, TcSmem::d1);
-    stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, TcSmem::d2);
-    stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, TcSmem::d3);
+    stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
     if (t == 0) {
         tc::bar_init(bar, 1);
         tc::fence_bar_init();
@@ -134,134 +175,109 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 
     const FeatureMap& fm = a.fmap;
     const int L = a.levels;
+    const long long vis_words = a.stride >> 5;
     Issuer is{bar};
     uint32_t dw_accumulate = 0;  // 0 until the first tile's weight-gradient products
     const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_G2 = tc::idesc(128, 16, 0, 0);
-    constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D2 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
+    constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
+    const int in_buf = ROUTER ? S::wx : S::x;
 
     for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
         const long long i = tile * TC_TILE + t;
         const bool valid = i < a.n;
         // ---- inputs: raw features (pad columns 1.0), visibility bits, target
-        uint32_t raw[W / 2];
+        uint32_t raw[PAIRS];
         const __half one = __float2half_rn(1.0f);
 #pragma unroll
-        for (int p = 0; p < W / 2; ++p) {
+        for (int p = 0; p < PAIRS; ++p) {
             uint32_t v = valid ? __ldg(reinterpret_cast<const uint32_t*>(a.raw) + (long long)p * a.stride + i) : 0u;
             if (2 * p >= a.raw_width) v = pack_half2(one, one);
             else if (2 * p + 1 >= a.raw_width) v = (v & 0xffffu) | (uint32_t(__half_as_ushort(one)) << 16);
             raw[p] = v;
         }
         uint32_t visbits = 0;
-        if (valid)
-            for (int l = 0; l < L; ++l) visbits |= uint32_t(__ldg(a.vis + (long long)l * a.stride + i) != 0) << l;
+        if (ROUTER) {
+            const long long word = tile * (TC_TILE / 32) + warp;  // this warp's 32 rows
+            for (int l = 0; l < L; ++l)
+                visbits |= ((__ldg(reinterpret_cast<const uint32_t*>(a.vis) + l * vis_words + word) >> (t & 31)) & 1u) << l;
+            if (!valid) visbits = 0;
+        }
 #pragma unroll
         for (int j = 0; j < W / 8; ++j)
-            store_chunk(smem, TcSmem::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
+            store_chunk(smem, S::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
 
         float sig[16];
         uint32_t gh_mask = 0;
-        uint32_t wx[W / 2];
         if (ROUTER) {
             // ---- gate hidden = relu(X Wg1^T)
             is.before_issue();
             if (t == 0)
-                for (int s = 0; s < W / 16; ++s)
-                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::x, 128, s), tc::kmajor(sbase + TcSmem::g1, 32, s), ID_G1, s > 0);
+                for (int s = 0; s < KW; ++s)
+                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
             if (!is.complete()) break;
-            for (int q = 0; q < 2; ++q) {
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
-                    gh_mask |= uint32_t(v[c] > 0.0f) << (16 * q + c);
-                }
-                store_chunk(smem, TcSmem::gh, t, 2 * q, pack8(v));
-                store_chunk(smem, TcSmem::gh, t, 2 * q + 1, pack8(v + 8));
-            }
-            // ---- logits = GH Wg2^T; per-level gate s (1 below K, sigmoid or softplus)
+            gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
+            gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
+            // ---- logits = GH Wg2^T; gated decoder input raw * half(s_l * vis_l) (runtime.cu:66-75)
             is.before_issue();
             if (t == 0)
                 for (int s = 0; s < 2; ++s)
-                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::gh, 128, s), tc::kmajor(sbase + TcSmem::g2, 16, s), ID_G2, s > 0);
+                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
             if (!is.complete()) break;
-            {
-                float z[16];
-                tc::tmem_ld16(lane_addr + T_ACC, z);
+            float z[16];
+            tc::tmem_ld16(lane_addr + T_ACC, z);
+            uint32_t wx[PAIRS];
+            if (UNIFORM) {
 #pragma unroll
-                for (int l = 0; l < 16; ++l) {
-                    const float zl = __half2float(__float2half_rn(z[l]));
-                    float s;
-                    if (l < a.k_fixed) s = 1.0f;
-                    else if (a.softplus) s = zl > 20.0f ? zl : log1pf(expf(zl));
-                    else s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-zl)));
-                    sig[l] = s;
-                }
-            }
-            // gated input: raw * half(s_l * vis_l) (runtime.cu:72-73); pad columns 1.0
-#pragma unroll
-            for (int p = 0; p < W / 2; ++p) {
-                __half h[2] = {lo_half(raw[p]), hi_half(raw[p])};
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int lev = fm.level_of_col[2 * p + q];
-                    if (lev >= 0) {
-                        float sl = 0.0f;
-#pragma unroll
-                        for (int l = 0; l < 16; ++l) sl = (l == lev) ? sig[l] : sl;
-                        const __half weight = __float2half_rn(__fmul_rn(sl, float((visbits >> lev) & 1u)));
-                        h[q] = __hmul_rn(h[q], weight);
+                for (int l = 0; l < PAIRS; ++l) {
+                    sig[l] = gate_value(__half2float(__float2half_rn(z[l])), l, a.k_fixed, a.softplus);
+                    if (l < L) {
+                        const __half w = __float2half_rn(__fmul_rn(sig[l], float((visbits >> l) & 1u)));
+                        wx[l] = pack_half2(__hmul_rn(lo_half(raw[l]), w), __hmul_rn(hi_half(raw[l]), w));
+                    } else {
+                        wx[l] = raw[l];
                     }
                 }
-                wx[p] = pack_half2(h[0], h[1]);
+            } else {
+#pragma unroll
+                for (int l = 0; l < 16; ++l) sig[l] = gate_value(__half2float(__float2half_rn(z[l])), l, a.k_fixed, a.softplus);
+                for (int p = 0; p < PAIRS; ++p) {
+                    __half h[2] = {lo_half(raw[p]), hi_half(raw[p])};
+                    for (int q = 0; q < 2; ++q) {
+                        const int lev = fm.level_of_col[2 * p + q];
+                        if (lev < 0) continue;
+                        float sl = 0.0f;
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) sl = (k == lev) ? sig[k] : sl;
+                        h[q] = __hmul_rn(h[q], __float2half_rn(__fmul_rn(sl, float((visbits >> lev) & 1u))));
+                    }
+                    wx[p] = pack_half2(h[0], h[1]);
+                }
             }
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
-                store_chunk(smem, TcSmem::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
         }
-        const int in_buf = ROUTER ? TcSmem::wx : TcSmem::x;
-        // ---- decoder hidden 1
-        uint64_t h1_mask = 0, h2_mask = 0;
+        // ---- decoder hidden 1, hidden 2, output
+        uint32_t h1_mask[4], h2_mask[4];
         is.before_issue();
         if (t == 0)
-            for (int s = 0; s < W / 16; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + in_buf, 128, s), tc::kmajor(sbase + TcSmem::d1, 64, s), ID_D1, s > 0);
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + in_buf, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
         if (!is.complete()) break;
-        for (int q = 0; q < 4; ++q) {
-            float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
-                h1_mask |= uint64_t(v[c] > 0.0f) << (16 * q + c);
-            }
-            store_chunk(smem, TcSmem::h1, t, 2 * q, pack8(v));
-            store_chunk(smem, TcSmem::h1, t, 2 * q + 1, pack8(v + 8));
-        }
-        // ---- decoder hidden 2
+        for (int q = 0; q < 4; ++q) h1_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::h1, 128, s), tc::kmajor(sbase + TcSmem::d2, 64, s), ID_D2, s > 0);
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
         if (!is.complete()) break;
-        for (int q = 0; q < 4; ++q) {
-            float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
-                h2_mask |= uint64_t(v[c] > 0.0f) << (16 * q + c);
-            }
-            store_chunk(smem, TcSmem::h2, t, 2 * q, pack8(v));
-            store_chunk(smem, TcSmem::h2, t, 2 * q + 1, pack8(v + 8));
-        }
-        // ---- output
+        for (int q = 0; q < 4; ++q) h2_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::h2, 128, s), tc::kmajor(sbase + TcSmem::d3, 16, s), ID_D3, s > 0);
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
         if (!is.complete()) break;
         float out[16];
         tc::tmem_ld16(lane_addr + T_ACC, out);
@@ -293,150 +309,148 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 }
                 a.squares[i] = __fdiv_rn(s, 3.0f);
             }
-            store_chunk(smem, TcSmem::dy, t, 0, pack8(dy));
-            store_chunk(smem, TcSmem::dy, t, 1, pack8(dy + 8));
+            store_chunk(smem, S::dy, t, 0, pack8(dy));
+            store_chunk(smem, S::dy, t, 1, pack8(dy + 8));
         }
         // ---- dh2 = DY Wd3 (B: Wd3 as MN-major); dW3^T += H2^T DY
         is.before_issue();
         if (t == 0) {
-            tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::dy, 128, 0), tc::mnmajor(sbase + TcSmem::d3, 16, 0),
+            tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0),
                     tc::idesc(128, 64, 0, 1), 0);
             for (int s = 0; s < 8; ++s)
-                tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + TcSmem::h2, 128, s), tc::mnmajor(sbase + TcSmem::dy, 128, s),
+                tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::dy, 128, s),
                         tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
         }
         if (!is.complete()) break;
-        for (int q = 0; q < 4; ++q) {  // dh2 = relu'(h2) * (.), stored over H2 (dead after dW3)
-            float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) v[c] = (h2_mask >> (16 * q + c) & 1ull) ? v[c] : 0.0f;
-            store_chunk(smem, TcSmem::h2, t, 2 * q, pack8(v));
-            store_chunk(smem, TcSmem::h2, t, 2 * q + 1, pack8(v + 8));
-        }
+        for (int q = 0; q < 4; ++q) masked_store16(lane_addr + T_ACC + 16 * q, h2_mask[q], smem, S::h2, t, 2 * q);
         // ---- dh1 = DH2 Wd2; dWd2 += DH2^T H1
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::h2, 128, s), tc::mnmajor(sbase + TcSmem::d2, 64, s),
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s),
                         tc::idesc(128, 64, 0, 1), s > 0);
             for (int s = 0; s < 8; ++s)
-                tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + TcSmem::h2, 128, s), tc::mnmajor(sbase + TcSmem::h1, 128, s),
+                tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::h1, 128, s),
                         tc::idesc(64, 64, 1, 1), dw_accumulate | uint32_t(s > 0));
         }
         if (!is.complete()) break;
-        for (int q = 0; q < 4; ++q) {  // dh1 = relu'(h1) * (.), stored over H1 (dead after dWd2)
-            float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) v[c] = (h1_mask >> (16 * q + c) & 1ull) ? v[c] : 0.0f;
-            store_chunk(smem, TcSmem::h1, t, 2 * q, pack8(v));
-            store_chunk(smem, TcSmem::h1, t, 2 * q + 1, pack8(v + 8));
-        }
+        for (int q = 0; q < 4; ++q) masked_store16(lane_addr + T_ACC + 16 * q, h1_mask[q], smem, S::h1, t, 2 * q);
         // ---- dz = DH1 Wd1; dWd1 += DH1^T WX
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::h1, 128, s), tc::mnmajor(sbase + TcSmem::d1, 64, s),
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s),
                         tc::idesc(128, W, 0, 1), s > 0);
             for (int s = 0; s < 8; ++s)
-                tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + TcSmem::h1, 128, s), tc::mnmajor(sbase + in_buf, 128, s),
+                tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + in_buf, 128, s),
                         tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
         }
         if (!is.complete()) break;
-        __half dz[W];
-        for (int q = 0; q < W / 16; ++q) {
-            float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
+        float dzf[W];
 #pragma unroll
-            for (int c = 0; c < 16; ++c) dz[16 * q + c] = __float2half_rn(v[c]);
-        }
-        uint32_t gv[W / 2];
+        for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
+        uint32_t gv[PAIRS];
         if (!ROUTER) {
             // grid values without router: half(dz / 128) (runtime.cu:123)
 #pragma unroll
-            for (int p = 0; p < W / 2; ++p)
-                gv[p] = pack_half2(__float2half_rn(__fdiv_rn(__half2float(dz[2 * p]), 128.0f)),
-                                   __float2half_rn(__fdiv_rn(__half2float(dz[2 * p + 1]), 128.0f)));
+            for (int p = 0; p < PAIRS; ++p)
+                gv[p] = pack_half2(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * p])), 128.0f)),
+                                   __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * p + 1])), 128.0f)));
         } else {
             // ---- gate backward per level (runtime.cu:76-92): direct and logit gradients
-            __half direct[W];
+            uint32_t direct[PAIRS];
             float da[16];
 #pragma unroll
-            for (int c = 0; c < W; ++c) direct[c] = __float2half_rn(0.0f);
-#pragma unroll
             for (int l = 0; l < 16; ++l) da[l] = 0.0f;
-            for (int l = 0; l < L; ++l) {
-                float sl = 0.0f;
+            if (UNIFORM) {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) sl = (k == l) ? sig[k] : sl;
-                const float vis = float((visbits >> l) & 1u);
-                const __half weight = __float2half_rn(__fmul_rn(sl, vis));
-                __half reduced = __float2half_rn(0.0f);
-                const int c0 = fm.col_of_level[l], dim = fm.dim_of_level[l];
-#pragma unroll
-                for (int c = 0; c < W; ++c) {
-                    if (c < c0 || c >= c0 + dim) continue;
-                    const __half value = __float2half_rn(__fdiv_rn(__half2float(dz[c]), 128.0f));
-                    direct[c] = __hmul_rn(value, weight);
-                    const __half rawc = (c & 1) ? hi_half(raw[c >> 1]) : lo_half(raw[c >> 1]);
-                    reduced = __hadd_rn(reduced, __hmul_rn(value, rawc));
+                for (int l = 0; l < PAIRS; ++l) {
+                    direct[l] = 0u;
+                    if (l < L) {
+                        const float vis = float((visbits >> l) & 1u);
+                        const __half w = __float2half_rn(__fmul_rn(sig[l], vis));
+                        const __half v0 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * l])), 128.0f));
+                        const __half v1 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * l + 1])), 128.0f));
+                        direct[l] = pack_half2(__hmul_rn(v0, w), __hmul_rn(v1, w));
+                        __half reduced = __hadd_rn(__float2half_rn(0.0f), __hmul_rn(v0, lo_half(raw[l])));
+                        reduced = __hadd_rn(reduced, __hmul_rn(v1, hi_half(raw[l])));
+                        const float derivative =
+                            gate_derivative(__fmul_rn(__half2float(reduced), vis), sig[l], l, a.k_fixed, a.softplus);
+                        da[l] = __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f)));
+                    }
                 }
-                const float incoming = __fmul_rn(__half2float(reduced), vis);
-                float derivative;
-                if (l < a.k_fixed) derivative = 0.0f;
-                else if (a.softplus) derivative = incoming * (-expm1f(-sl));
-                else derivative = __fmul_rn(__fmul_rn(incoming, __fsub_rn(1.0f, sl)), sl);
-                const float dal = __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f)));
+            } else {
+                __half directh[W];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) da[k] = (k == l) ? dal : da[k];
+                for (int c = 0; c < W; ++c) directh[c] = __float2half_rn(0.0f);
+                for (int l = 0; l < L; ++l) {
+                    float sl = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) sl = (k == l) ? sig[k] : sl;
+                    const float vis = float((visbits >> l) & 1u);
+                    const __half weight = __float2half_rn(__fmul_rn(sl, vis));
+                    __half reduced = __float2half_rn(0.0f);
+                    const int c0 = fm.col_of_level[l], dim = fm.dim_of_level[l];
+#pragma unroll
+                    for (int c = 0; c < W; ++c) {
+                        if (c < c0 || c >= c0 + dim) continue;
+                        const __half value = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[c])), 128.0f));
+                        directh[c] = __hmul_rn(value, weight);
+                        const __half rawc = (c & 1) ? hi_half(raw[c >> 1]) : lo_half(raw[c >> 1]);
+                        reduced = __hadd_rn(reduced, __hmul_rn(value, rawc));
+                    }
+                    const float derivative =
+                        gate_derivative(__fmul_rn(__half2float(reduced), vis), sl, l, a.k_fixed, a.softplus);
+                    const float dal = __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f)));
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) da[k] = (k == l) ? dal : da[k];
+                }
+#pragma unroll
+                for (int p = 0; p < PAIRS; ++p) direct[p] = pack_half2(directh[2 * p], directh[2 * p + 1]);
             }
-            store_chunk(smem, TcSmem::da, t, 0, pack8(da));
-            store_chunk(smem, TcSmem::da, t, 1, pack8(da + 8));
+            store_chunk(smem, S::da, t, 0, pack8(da));
+            store_chunk(smem, S::da, t, 1, pack8(da + 8));
             // ---- dgh = DA Wg2; dWg2^T += GH^T DA
             is.before_issue();
             if (t == 0) {
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::da, 128, 0), tc::mnmajor(sbase + TcSmem::g2, 16, 0),
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
                         tc::idesc(128, 32, 0, 1), 0);
                 for (int s = 0; s < 8; ++s)
-                    tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + TcSmem::gh, 128, s), tc::mnmajor(sbase + TcSmem::da, 128, s),
+                    tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh, 128, s), tc::mnmajor(sbase + S::da, 128, s),
                             tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
             }
             if (!is.complete()) break;
-            for (int q = 0; q < 2; ++q) {
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
-#pragma unroll
-                for (int c = 0; c < 16; ++c) v[c] = (gh_mask >> (16 * q + c) & 1u) ? v[c] : 0.0f;
-                store_chunk(smem, TcSmem::dgh, t, 2 * q, pack8(v));
-                store_chunk(smem, TcSmem::dgh, t, 2 * q + 1, pack8(v + 8));
-            }
-            // ---- dr = DGH Wg1; dWg1 += DGH^T X
+            masked_store16(lane_addr + T_ACC, gh_mask & 0xffffu, smem, S::dgh, t, 0);
+            masked_store16(lane_addr + T_ACC + 16, gh_mask >> 16, smem, S::dgh, t, 2);
+            // ---- dr = DGH Wg1; dWg1 += DGH^T X; grid values v = hadd(direct, half(dr / 128)) (runtime.cu:121)
             is.before_issue();
             if (t == 0) {
                 for (int s = 0; s < 2; ++s)
-                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + TcSmem::dgh, 128, s), tc::mnmajor(sbase + TcSmem::g1, 32, s),
+                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
                             tc::idesc(128, W, 0, 1), s > 0);
                 for (int s = 0; s < 8; ++s)
-                    tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + TcSmem::dgh, 128, s), tc::mnmajor(sbase + TcSmem::x, 128, s),
+                    tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::x, 128, s),
                             tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
             }
             if (!is.complete()) break;
-            for (int q = 0; q < W / 16; ++q) {
+#pragma unroll
+            for (int q = 0; q < KW; ++q) {
                 float v[16];
                 tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
 #pragma unroll
                 for (int c = 0; c < 16; c += 2) {
-                    const int col = 16 * q + c;
+                    const int p = 8 * q + c / 2;
                     const __half r0 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(v[c])), 128.0f));
                     const __half r1 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(v[c + 1])), 128.0f));
-                    gv[col >> 1] = pack_half2(__hadd_rn(direct[col], r0), __hadd_rn(direct[col + 1], r1));
+                    gv[p] = pack_half2(__hadd_rn(lo_half(direct[p]), r0), __hadd_rn(hi_half(direct[p]), r1));
                 }
             }
         }
         if (valid) {
 #pragma unroll
-            for (int p = 0; p < W / 2; ++p) reinterpret_cast<uint32_t*>(a.gvals)[(long long)p * a.stride + i] = gv[p];
+            for (int p = 0; p < PAIRS; ++p) reinterpret_cast<uint32_t*>(a.gvals)[(long long)p * a.stride + i] = gv[p];
         }
         dw_accumulate = 1;
     }
@@ -452,20 +466,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         constexpr int GATE = ROUTER ? gate_params(W) : 0;
         constexpr int P = GATE + decoder_params(W);
         float* part = a.partials + (long long)blockIdx.x * P;
+        float* dec = part + GATE;
         const int row = 16 * warp + (t & 31);
         const bool holds = (t & 31) < 16;
         const bool any = dw_accumulate && is.ok;
         tc::fence_before_sync();
         __syncthreads();
         tc::fence_after_sync();
-        float* dec = part + GATE;
+#pragma unroll
         for (int q = 0; q < 4; ++q) {  // dWd2 [64][64]
             float v[16];
             tc::tmem_ld16(lane_addr + T_DWD2 + 16 * q, v);
             if (holds)
                 for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + row * DEC_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
         }
-        for (int q = 0; q < W / 16; ++q) {  // dWd1 [64][W]
+#pragma unroll
+        for (int q = 0; q < KW; ++q) {  // dWd1 [64][W]
             float v[16];
             tc::tmem_ld16(lane_addr + T_DWD1 + 16 * q, v);
             if (holds)
@@ -485,7 +501,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 if (holds && row < GATE_HIDDEN)
                     for (int c = 0; c < 16; ++c) part[GATE_HIDDEN * W + c * GATE_HIDDEN + row] = any ? v[c] : 0.0f;
             }
-            for (int q = 0; q < W / 16; ++q) {  // dWg1 [32][W] from [64 (32 valid)][W]
+#pragma unroll
+            for (int q = 0; q < KW; ++q) {  // dWg1 [32][W] from [64 (32 valid)][W]
                 float v[16];
                 tc::tmem_ld16(lane_addr + T_DWG1 + 16 * q, v);
                 if (holds && row < GATE_HIDDEN)
@@ -498,17 +515,27 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
 }
 
-template <bool ROUTER, bool TRAIN>
+template <int W, bool ROUTER, bool TRAIN, bool UNIFORM>
 void launch_tc(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
     static unsigned long long configured = 0;
     int device = 0;
     ODIE_CUDA(cudaGetDevice(&device));
     if (!(configured >> device & 1ull)) {
-        ODIE_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<ROUTER, TRAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       TcSmem::total));
+        ODIE_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<W, ROUTER, TRAIN, UNIFORM>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<W>::total));
         configured |= 1ull << device;
     }
-    mlp_tc_kernel<ROUTER, TRAIN><<<blocks, TC_THREADS, TcSmem::total, stream>>>(a, error_flag);
+    mlp_tc_kernel<W, ROUTER, TRAIN, UNIFORM><<<blocks, TC_THREADS, TcSmem<W>::total, stream>>>(a, error_flag);
+}
+
+template <bool TRAIN>
+void dispatch(const MlpArgs& a, int width, bool router, bool uniform, int blocks, int* error_flag, cudaStream_t stream) {
+#define ODIE_TC(WV, R, U) \
+    if (width == WV && router == R && uniform == U) return launch_tc<WV, R, TRAIN, U>(a, blocks, error_flag, stream);
+    ODIE_TC(32, true, true) ODIE_TC(32, true, false) ODIE_TC(32, false, true) ODIE_TC(32, false, false)
+    ODIE_TC(16, true, true) ODIE_TC(16, true, false) ODIE_TC(16, false, true) ODIE_TC(16, false, false)
+#undef ODIE_TC
+    throw std::invalid_argument("the fused heads take 16 or 32 input features");
 }
 
 }  // namespace
@@ -520,19 +547,17 @@ int mlp_tc_blocks(long long n) {
     return blocks < 1 ? 1 : int(blocks);
 }
 
-void launch_mlp_tc_train(const MlpArgs& a, int width, bool router, int blocks, int* error_flag, cudaStream_t stream) {
-    ODIE_REQUIRE(width == 32, "the tcgen05 heads take 32 input features");
+void launch_mlp_tc_train(const MlpArgs& a, int width, bool router, bool uniform, int blocks, int* error_flag,
+                         cudaStream_t stream) {
     if (a.n <= 0) return;
-    if (router) launch_tc<true, true>(a, blocks, error_flag, stream);
-    else launch_tc<false, true>(a, blocks, error_flag, stream);
+    ODIE_REQUIRE(a.stride % TC_TILE == 0, "the feature stride must be a multiple of 128");
+    dispatch<true>(a, width, router, uniform, blocks, error_flag, stream);
 }
 
-void launch_mlp_tc_decode(const MlpArgs& a, int width, bool router, int* error_flag, cudaStream_t stream) {
-    ODIE_REQUIRE(width == 32, "the tcgen05 heads take 32 input features");
+void launch_mlp_tc_decode(const MlpArgs& a, int width, bool router, bool uniform, int* error_flag, cudaStream_t stream) {
     if (a.n <= 0) return;
-    const int blocks = mlp_tc_blocks(a.n);
-    if (router) launch_tc<true, false>(a, blocks, error_flag, stream);
-    else launch_tc<false, false>(a, blocks, error_flag, stream);
+    ODIE_REQUIRE(a.stride % TC_TILE == 0, "the feature stride must be a multiple of 128");
+    dispatch<false>(a, width, router, uniform, mlp_tc_blocks(a.n), error_flag, stream);
 }
 
 }  // namespace odie

@@ -80,7 +80,7 @@ struct Runtime {
     int image_width = 0, image_height = 0, mode = 0, warp_limit = 128;
     int levels = 16, raw_width = 32, input_width = 32, gate_k = 0, active = 16;
     bool router = true, softplus = false, rgb8 = true, hash_mode = false;
-    bool tc_heads = true;  // tcgen05/TMEM heads (width 32); false: the mma.sync heads
+    bool uniform = true;   // every level F=2 at columns (2l, 2l+1)
     double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
     // caller-owned
     float* grid = nullptr;
@@ -103,7 +103,7 @@ struct Runtime {
     DeviceArray<float> table_bc2, table_step[3];
     DeviceArray<float> xy, target, squares;
     DeviceArray<__half> raw, gvals;
-    DeviceArray<uint8_t> vis;
+    DeviceArray<uint32_t> vis;
     DeviceArray<int> error_flag;
     std::vector<double> host_bc1, host_bc2;
     int partial_blocks = 0;
@@ -118,12 +118,12 @@ struct Runtime {
         image_height = int(j.at("height").as_int());
         mode = int(j.value("mode", 20));
         warp_limit = int(j.value("warp_limit", 128));
-        capacity = j.value("batch", 65536);
+        // coordinate capacity per step, padded to whole 128-row tiles (the feature stride)
+        capacity = (j.value("batch", 65536) + 127) / 128 * 128;
         router = j.value("router", 1) != 0;
         gate_k = int(j.value("gate_k", 0));
         softplus = j.value("softplus", 0) != 0;
         rgb8 = j.value("rgb8", 1) != 0;
-        tc_heads = j.value("mma_heads", 0) == 0;
         ODIE_REQUIRE(total > 0 && total <= 0x7fffffffLL, "total must fit int32 addressing");
         ODIE_REQUIRE(image_width >= 2 && image_height >= 2, "image axes must be >= 2");
         ODIE_REQUIRE(capacity >= 1 && capacity <= (1LL << 26), "batch capacity must be in [1, 2^26]");
@@ -167,15 +167,14 @@ struct Runtime {
         head_m.allocate(head_count);
         head_v.allocate(head_count);
         head_steps.allocate(head_count);
-        if (input_width != 32) tc_heads = false;
-        partial_blocks = std::max(mlp_train_blocks(capacity), mlp_tc_blocks(capacity));
+        partial_blocks = mlp_tc_blocks(capacity);
         partials.allocate((long long)partial_blocks * head_count);
         xy.allocate(2 * capacity);
         target.allocate(3 * capacity);
         squares.allocate(capacity);
         raw.allocate((long long)input_width * capacity);
         gvals.allocate((long long)input_width * capacity);
-        vis.allocate((long long)levels * capacity);
+        vis.allocate((long long)levels * capacity / 32);  // bit-packed [levels][capacity / 32]
         error_flag.allocate(1);
         for (auto* a : {&grid_grad, &grid_m, &grid_v, &head_grad_own, &head_m, &head_v})
             a->zero(stream);
@@ -226,6 +225,8 @@ struct Runtime {
     }
 
     void build_feature_map() {
+        uniform = raw_width == 2 * levels;
+        for (int l = 0; l < levels; ++l) uniform = uniform && table.level[l].F == 2 && table.level[l].col == 2 * l;
         std::memset(&fmap, 0, sizeof(fmap));
         for (int c = 0; c < 64; ++c) fmap.level_of_col[c] = -1;
         for (int l = 0; l < levels; ++l) {
@@ -383,13 +384,12 @@ struct Runtime {
         src.table = table;
         const EncodeArgs ea = encode_args(n);
         slot = stage_begin(S_ENCODE_FWD);
-        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, vis.ptr, stream);
+        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
         stage_end(slot);
         const MlpArgs ma = mlp_args(n);
-        const int blocks = tc_heads ? mlp_tc_blocks(n) : mlp_train_blocks(n);
+        const int blocks = mlp_tc_blocks(n);
         slot = stage_begin(S_MLP);
-        if (tc_heads) launch_mlp_tc_train(ma, input_width, router, blocks, error_flag.ptr, stream);
-        else launch_mlp_train(ma, input_width, router, blocks, stream);
+        launch_mlp_tc_train(ma, input_width, router, uniform, blocks, error_flag.ptr, stream);
         stage_end(slot);
         slot = stage_begin(S_ENCODE_BWD);
         launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, warp_limit, stream);
@@ -441,12 +441,11 @@ struct Runtime {
             const long long count = std::min(capacity, n - done);
             launch_coords_range(begin + done, count, image_width, image_height, xy.ptr, stream);
             const EncodeArgs ea = encode_args(count);
-            launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, vis.ptr, stream);
+            launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
             MlpArgs ma = mlp_args(count);
             ma.rgb = out_rgb ? out_rgb + 3 * done : nullptr;
             ma.rgb8 = out_rgb8 ? out_rgb8 + 3 * done : nullptr;
-            if (tc_heads) launch_mlp_tc_decode(ma, input_width, router, error_flag.ptr, stream);
-            else launch_mlp_decode(ma, input_width, router, stream);
+            launch_mlp_tc_decode(ma, input_width, router, uniform, error_flag.ptr, stream);
         }
         ODIE_CUDA(cudaGetLastError());
     }

@@ -22,7 +22,7 @@ struct MlpArgs {
     long long n;          // coordinates of this launch
     long long stride;     // pair-major stride of raw/gvals and level stride of vis
     const __half* raw;    // [W/2][stride] half2 features
-    const uint8_t* vis;   // [levels][stride]
+    const uint32_t* vis;  // bit-packed visibility [levels][stride / 32]
     const float* target;  // [n][3] fp32 (training) or nullptr
     const __half* gate_w;     // fp16 gate weights (may be null without router)
     const __half* decoder_w;  // fp16 decoder weights
@@ -36,16 +36,15 @@ struct MlpArgs {
     uint8_t* rgb8;        // [n][3] u8 decode output (decode)
 };
 
-size_t mlp_train_smem(int width);
-void launch_mlp_train(const MlpArgs& args, int width, bool router, int blocks, cudaStream_t stream);
-void launch_mlp_decode(const MlpArgs& args, int width, bool router, cudaStream_t stream);
-int mlp_train_blocks(long long n);
-
-// tcgen05/TMEM fused heads (mlp_tc.cu), decoder input width 32.  A wait that
-// runs out sets *error_flag = 2 and the kernel returns.
+// tcgen05/TMEM fused heads (mlp_tc.cu), decoder input width 16 or 32.  uniform:
+// every level has 2 features at columns (2l, 2l+1).  vis is bit-packed
+// [levels][stride / 32]; stride is a multiple of 128.  A wait that runs out
+// sets *error_flag = 2 and the kernel returns.
 int mlp_tc_blocks(long long n);
-void launch_mlp_tc_train(const MlpArgs& args, int width, bool router, int blocks, int* error_flag, cudaStream_t stream);
-void launch_mlp_tc_decode(const MlpArgs& args, int width, bool router, int* error_flag, cudaStream_t stream);
+void launch_mlp_tc_train(const MlpArgs& args, int width, bool router, bool uniform, int blocks, int* error_flag,
+                         cudaStream_t stream);
+void launch_mlp_tc_decode(const MlpArgs& args, int width, bool router, bool uniform, int* error_flag,
+                          cudaStream_t stream);
 
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
                         float* xy, float* target, cudaStream_t stream);

@@ -71,7 +71,8 @@ def test_step_gradients_match_oracle(cuda, router, k, activation):
     # bit-exact integer/byte stages
     xy = opt.copied('xy', (opt.pointers['capacity'], 2), torch.float32)[:n].cpu().numpy()
     assert np.array_equal(xy, ref['xy'])
-    vis = opt.copied('vis', (16, opt.pointers['capacity']), torch.uint8)[:, :n].T.cpu().numpy()
+    words = opt.copied('vis', (16, opt.pointers['capacity'] // 32), torch.int32).cpu().numpy().view(np.uint32)
+    vis = np.unpackbits(words.view(np.uint8), axis=1, bitorder='little')[:, :n].T  # bit-packed [levels][capacity/32]
     assert np.array_equal(vis, ref['vis'])
     raw = read_pair_major(opt, 'raw', n, W)
     diff = np.argwhere(raw.view(np.uint16) != ref['raw'].view(np.uint16))
