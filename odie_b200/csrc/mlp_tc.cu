@@ -55,8 +55,9 @@ struct TcSmem {
     static constexpr int dgh = h2 + 16384;              // [128 x 32] gate hidden gradient
     static constexpr int dy = dgh + 8192;               // [128 x 16] output gradient
     static constexpr int da = dy + 4096;                // [128 x 16] gate logit gradient
-    static constexpr int bar = da + 4096;               // mbarrier
-    static constexpr int tmem = bar + 8;                // TMEM base address
+    static constexpr int bar = da + 4096;               // mbarrier: data products of a phase
+    static constexpr int bar_dw = bar + 8;              // mbarrier: weight-gradient products of a phase
+    static constexpr int tmem = bar_dw + 8;             // TMEM base address
     static constexpr int total = tmem + 8;
     static_assert(gh + 16384 <= dgh, "GH read 64 wide stays inside the activation buffers");
     static_assert(dgh + 16384 <= bar, "DGH read 64 wide stays inside the activation buffers");
@@ -85,8 +86,9 @@ __device__ void stage_blocked(const __half* __restrict__ src, int rows, int cols
 
 struct Issuer {
     uint64_t* bar;
-    uint32_t phase = 0;
-    bool ok = true;
+    uint64_t* bar_dw;
+    uint32_t phase = 0, phase_dw = 0;
+    bool ok = true, data_ok = true;
     // Make every thread's shared-memory writes visible to the tensor cores and
     // every TMEM read complete, then let thread 0 issue.
     __device__ void before_issue() {
@@ -104,7 +106,57 @@ struct Issuer {
         tc::fence_after_sync();
         return ok;
     }
+    // Backward phases commit the data product (bar) and the weight-gradient
+    // products (bar_dw) separately: the epilogue reads the data product while
+    // the weight-gradient products still run, and waits for them only before
+    // overwriting an operand they read.
+    __device__ void wait_data() {
+        data_ok = tc::bar_wait(bar, phase, WAIT_LIMIT);
+        phase ^= 1u;
+        tc::fence_after_sync();
+    }
+    __device__ bool wait_dw() {
+        const bool done = tc::bar_wait(bar_dw, phase_dw, WAIT_LIMIT);
+        phase_dw ^= 1u;
+        ok = __syncthreads_and(done && data_ok) != 0;
+        tc::fence_after_sync();
+        return ok;
+    }
 };
+
+// Load 16 TMEM columns, keep those whose forward activation was positive, pack to fp16 pairs.
+__device__ __forceinline__ void masked_pack16(uint32_t taddr, uint32_t mask, uint32_t* out) {
+    float v[16];
+    tc::tmem_ld16(taddr, v);
+#pragma unroll
+    for (int c = 0; c < 16; c += 2)
+        out[c / 2] = pack_half2(__float2half_rn((mask >> c & 1u) ? v[c] : 0.0f),
+                                __float2half_rn((mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f));
+}
+
+// Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
+__device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
+    float v[16];
+    tc::tmem_ld16(taddr, v);
+    uint32_t mask = 0;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
+        mask |= uint32_t(v[c] > 0.0f) << c;
+    }
+    store_chunk(smem, base, r, j0, pack8(v));
+    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
+    return mask;
+}
+// Load 16 TMEM columns, keep those whose forward activation was positive, pack to fp16 pairs.
+__device__ __forceinline__ void masked_pack16(uint32_t taddr, uint32_t mask, uint32_t* out) {
+    float v[16];
+    tc::tmem_ld16(taddr, v);
+#pragma unroll
+    for (int c = 0; c < 16; c += 2)
+        out[c / 2] = pack_half2(__float2half_rn((mask >> c & 1u) ? v[c] : 0.0f),
+                                __float2half_rn((mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f));
+}
 
 // Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
 __device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
@@ -130,10 +182,13 @@ __device__ __forceinline__ void masked_store16(uint32_t taddr, uint32_t mask, un
     store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
 }
 
+// x / 128 as an exact multiply: both round the same real value x * 2^-7, underflow included.
+__device__ __forceinline__ float div128(float x) { return __fmul_rn(x, 0.0078125f); }
+
 __device__ __forceinline__ float gate_value(float z, int level, int k_fixed, int softplus) {
     if (level < k_fixed) return 1.0f;
     if (softplus) return z > 20.0f ? z : log1pf(expf(z));
-    return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+    return __frcp_rn(__fadd_rn(1.0f, expf(-z)));  // the correctly rounded 1 / (1 + e^-z)
 }
 __device__ __forceinline__ float gate_derivative(float incoming, float s, int level, int k_fixed, int softplus) {
     if (level < k_fixed) return 0.0f;
@@ -148,6 +203,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     extern __shared__ __align__(128) unsigned char smem[];
     const int t = threadIdx.x, warp = t >> 5;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
+    uint64_t* bar_dw = reinterpret_cast<uint64_t*>(smem + S::bar_dw);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
     const uint32_t sbase = tc::smem_u32(smem);
 
@@ -160,6 +216,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
     if (t == 0) {
         tc::bar_init(bar, 1);
+        tc::bar_init(bar_dw, 1);
         tc::fence_bar_init();
     }
     if (warp == 0) {
@@ -176,12 +233,47 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     const FeatureMap& fm = a.fmap;
     const int L = a.levels;
     const long long vis_words = a.stride >> 5;
-    Issuer is{bar};
+    Issuer is{bar, bar_dw};
     uint32_t dw_accumulate = 0;  // 0 until the first tile's weight-gradient products
     const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_G2 = tc::idesc(128, 16, 0, 0);
     constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
     const int in_buf = ROUTER ? S::wx : S::x;
+
+    // Inputs of a tile: raw feature pairs, this warp's visibility words, target.
+    // The next tile's inputs are loaded while the current tile runs its
+    // backward products, so their global-memory latency is off the chain.
+    uint32_t next_raw[PAIRS], next_vis = 0;
+    float next_target[3] = {0.0f, 0.0f, 0.0f};
+    auto load_inputs = [&](long long tile) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = tile < tiles && i < a.n;
+#pragma unroll
+        for (int p = 0; p < PAIRS; ++p)
+            next_raw[p] = valid ? __ldg(reinterpret_cast<const uint32_t*>(a.raw) + (long long)p * a.stride + i) : 0u;
+        if (TRAIN) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
+        }
+    };
+    // Visibility: lane l (< levels) loads this warp's word of level l; the
+    // words are broadcast with shuffles when the bits are folded per row.
+    uint32_t vis_word = 0;
+    auto issue_vis = [&](long long tile) {
+        const int lane = t & 31;
+        vis_word = (ROUTER && tile < tiles && lane < L)
+                       ? __ldg(reinterpret_cast<const uint32_t*>(a.vis) + lane * vis_words + tile * (TC_TILE / 32) + warp)
+                       : 0u;
+    };
+    auto fold_vis = [&](long long tile) {
+        next_vis = 0;
+#pragma unroll
+        for (int l = 0; l < 16; ++l) next_vis |= ((__shfl_sync(0xffffffffu, vis_word, l) >> (t & 31)) & 1u) << l;
+        if (tile * TC_TILE + t >= a.n) next_vis = 0;
+    };
+    load_inputs(blockIdx.x);
+    issue_vis(blockIdx.x);
+    fold_vis(blockIdx.x);
 
     for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
         const long long i = tile * TC_TILE + t;
@@ -191,18 +283,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         const __half one = __float2half_rn(1.0f);
 #pragma unroll
         for (int p = 0; p < PAIRS; ++p) {
-            uint32_t v = valid ? __ldg(reinterpret_cast<const uint32_t*>(a.raw) + (long long)p * a.stride + i) : 0u;
+            uint32_t v = next_raw[p];
             if (2 * p >= a.raw_width) v = pack_half2(one, one);
             else if (2 * p + 1 >= a.raw_width) v = (v & 0xffffu) | (uint32_t(__half_as_ushort(one)) << 16);
             raw[p] = v;
         }
-        uint32_t visbits = 0;
-        if (ROUTER) {
-            const long long word = tile * (TC_TILE / 32) + warp;  // this warp's 32 rows
-            for (int l = 0; l < L; ++l)
-                visbits |= ((__ldg(reinterpret_cast<const uint32_t*>(a.vis) + l * vis_words + word) >> (t & 31)) & 1u) << l;
-            if (!valid) visbits = 0;
-        }
+        const uint32_t visbits = next_vis;
+        const float target[3] = {next_target[0], next_target[1], next_target[2]};
+        const long long next_tile = tile + gridDim.x;
 #pragma unroll
         for (int j = 0; j < W / 8; ++j)
             store_chunk(smem, S::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
@@ -281,6 +369,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         if (!is.complete()) break;
         float out[16];
         tc::tmem_ld16(lane_addr + T_ACC, out);
+        load_inputs(next_tile);  // prefetch: consumed at the start of the next tile
+        issue_vis(next_tile);
         if (!TRAIN) {
             if (valid) {
 #pragma unroll
@@ -291,6 +381,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                         a.rgb8[3 * i + c] = (uint8_t)__float2int_rn(__fmul_rn(fminf(fmaxf(xo, 0.0f), 1.0f), 255.0f));
                 }
             }
+            fold_vis(next_tile);
             continue;
         }
         // ---- loss gradient (odie/native/runtime.cu:53-63)
@@ -302,7 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 float s = 0.0f;
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
-                    const float d = __fsub_rn(__half2float(__float2half_rn(out[c])), __ldg(a.target + 3 * i + c));
+                    const float d = __fsub_rn(__half2float(__float2half_rn(out[c])), target[c]);
                     s = __fadd_rn(s, __fmul_rn(d, d));
                     const float scaled = __fmul_rn(__fdiv_rn(__fmul_rn(2.0f, d), a.three_real), 128.0f);
                     dy[c] = __half2float(__hmul_rn(__float2half_rn(scaled), __float2half_rn(128.0f)));
@@ -317,47 +408,63 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         if (t == 0) {
             tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0),
                     tc::idesc(128, 64, 0, 1), 0);
+            tc::commit(bar);
             for (int s = 0; s < 8; ++s)
                 tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::dy, 128, s),
                         tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+            tc::commit(bar_dw);
         }
-        if (!is.complete()) break;
+        uint32_t packed[32];
+        is.wait_data();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) masked_store16(lane_addr + T_ACC + 16 * q, h2_mask[q], smem, S::h2, t, 2 * q);
+        for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h2_mask[q], packed + 8 * q);
+        if (!is.wait_dw()) break;  // dW3 has read H2: dh2 may overwrite it
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            store_chunk(smem, S::h2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
         // ---- dh1 = DH2 Wd2; dWd2 += DH2^T H1
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s),
                         tc::idesc(128, 64, 0, 1), s > 0);
+            tc::commit(bar);
             for (int s = 0; s < 8; ++s)
                 tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::h1, 128, s),
                         tc::idesc(64, 64, 1, 1), dw_accumulate | uint32_t(s > 0));
+            tc::commit(bar_dw);
         }
-        if (!is.complete()) break;
+        is.wait_data();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) masked_store16(lane_addr + T_ACC + 16 * q, h1_mask[q], smem, S::h1, t, 2 * q);
+        for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h1_mask[q], packed + 8 * q);
+        if (!is.wait_dw()) break;  // dWd2 has read H1: dh1 may overwrite it
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            store_chunk(smem, S::h1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
         // ---- dz = DH1 Wd1; dWd1 += DH1^T WX
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s),
                         tc::idesc(128, W, 0, 1), s > 0);
+            tc::commit(bar);
             for (int s = 0; s < 8; ++s)
                 tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + in_buf, 128, s),
                         tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+            tc::commit(bar_dw);
         }
-        if (!is.complete()) break;
+        is.wait_data();
         float dzf[W];
 #pragma unroll
         for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
         uint32_t gv[PAIRS];
         if (!ROUTER) {
+            if (!is.wait_dw()) break;  // dWd1 has read X: the next tile may overwrite it
             // grid values without router: half(dz / 128) (runtime.cu:123)
 #pragma unroll
             for (int p = 0; p < PAIRS; ++p)
-                gv[p] = pack_half2(__float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * p])), 128.0f)),
-                                   __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * p + 1])), 128.0f)));
+                gv[p] = pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p])))),
+                                   __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p + 1])))));
         } else {
             // ---- gate backward per level (runtime.cu:76-92): direct and logit gradients
             uint32_t direct[PAIRS];
@@ -371,8 +478,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     if (l < L) {
                         const float vis = float((visbits >> l) & 1u);
                         const __half w = __float2half_rn(__fmul_rn(sig[l], vis));
-                        const __half v0 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * l])), 128.0f));
-                        const __half v1 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[2 * l + 1])), 128.0f));
+                        const __half v0 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * l]))));
+                        const __half v1 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * l + 1]))));
                         direct[l] = pack_half2(__hmul_rn(v0, w), __hmul_rn(v1, w));
                         __half reduced = __hadd_rn(__float2half_rn(0.0f), __hmul_rn(v0, lo_half(raw[l])));
                         reduced = __hadd_rn(reduced, __hmul_rn(v1, hi_half(raw[l])));
@@ -396,7 +503,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
                     for (int c = 0; c < W; ++c) {
                         if (c < c0 || c >= c0 + dim) continue;
-                        const __half value = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(dzf[c])), 128.0f));
+                        const __half value = __float2half_rn(div128(__half2float(__float2half_rn(dzf[c]))));
                         directh[c] = __hmul_rn(value, weight);
                         const __half rawc = (c & 1) ? hi_half(raw[c >> 1]) : lo_half(raw[c >> 1]);
                         reduced = __hadd_rn(reduced, __hmul_rn(value, rawc));
@@ -410,6 +517,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
                 for (int p = 0; p < PAIRS; ++p) direct[p] = pack_half2(directh[2 * p], directh[2 * p + 1]);
             }
+            if (!is.wait_dw()) break;  // dWd1 done before the next products are queued
             store_chunk(smem, S::da, t, 0, pack8(da));
             store_chunk(smem, S::da, t, 1, pack8(da + 8));
             // ---- dgh = DA Wg2; dWg2^T += GH^T DA
@@ -417,24 +525,32 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             if (t == 0) {
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
                         tc::idesc(128, 32, 0, 1), 0);
+                tc::commit(bar);
                 for (int s = 0; s < 8; ++s)
                     tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh, 128, s), tc::mnmajor(sbase + S::da, 128, s),
                             tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+                tc::commit(bar_dw);
             }
-            if (!is.complete()) break;
-            masked_store16(lane_addr + T_ACC, gh_mask & 0xffffu, smem, S::dgh, t, 0);
-            masked_store16(lane_addr + T_ACC + 16, gh_mask >> 16, smem, S::dgh, t, 2);
+            is.wait_data();
+            masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
+            masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
+            if (!is.wait_dw()) break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
             // ---- dr = DGH Wg1; dWg1 += DGH^T X; grid values v = hadd(direct, half(dr / 128)) (runtime.cu:121)
             is.before_issue();
             if (t == 0) {
                 for (int s = 0; s < 2; ++s)
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
                             tc::idesc(128, W, 0, 1), s > 0);
+                tc::commit(bar);
                 for (int s = 0; s < 8; ++s)
                     tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::x, 128, s),
                             tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+                tc::commit(bar_dw);
             }
-            if (!is.complete()) break;
+            is.wait_data();
 #pragma unroll
             for (int q = 0; q < KW; ++q) {
                 float v[16];
@@ -442,17 +558,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
                 for (int c = 0; c < 16; c += 2) {
                     const int p = 8 * q + c / 2;
-                    const __half r0 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(v[c])), 128.0f));
-                    const __half r1 = __float2half_rn(__fdiv_rn(__half2float(__float2half_rn(v[c + 1])), 128.0f));
+                    const __half r0 = __float2half_rn(div128(__half2float(__float2half_rn(v[c]))));
+                    const __half r1 = __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1]))));
                     gv[p] = pack_half2(__hadd_rn(lo_half(direct[p]), r0), __hadd_rn(hi_half(direct[p]), r1));
                 }
             }
+            if (!is.wait_dw()) break;  // dWg1 has read X and DGH: the next tile may overwrite them
         }
         if (valid) {
 #pragma unroll
             for (int p = 0; p < PAIRS; ++p) reinterpret_cast<uint32_t*>(a.gvals)[(long long)p * a.stride + i] = gv[p];
         }
         dw_accumulate = 1;
+        fold_vis(next_tile);
     }
 
     if (!is.ok) {
