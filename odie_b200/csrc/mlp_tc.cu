@@ -148,40 +148,6 @@ __device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* 
     store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
     return mask;
 }
-// Load 16 TMEM columns, keep those whose forward activation was positive, pack to fp16 pairs.
-__device__ __forceinline__ void masked_pack16(uint32_t taddr, uint32_t mask, uint32_t* out) {
-    float v[16];
-    tc::tmem_ld16(taddr, v);
-#pragma unroll
-    for (int c = 0; c < 16; c += 2)
-        out[c / 2] = pack_half2(__float2half_rn((mask >> c & 1u) ? v[c] : 0.0f),
-                                __float2half_rn((mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f));
-}
-
-// Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
-__device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
-    float v[16];
-    tc::tmem_ld16(taddr, v);
-    uint32_t mask = 0;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
-        mask |= uint32_t(v[c] > 0.0f) << c;
-    }
-    store_chunk(smem, base, r, j0, pack8(v));
-    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
-    return mask;
-}
-// Load 16 TMEM columns, keep those whose forward activation was positive, store two chunks.
-__device__ __forceinline__ void masked_store16(uint32_t taddr, uint32_t mask, unsigned char* smem, int base, int r, int j0) {
-    float v[16];
-    tc::tmem_ld16(taddr, v);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) v[c] = (mask >> c & 1u) ? v[c] : 0.0f;
-    store_chunk(smem, base, r, j0, pack8(v));
-    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
-}
-
 // x / 128 as an exact multiply: both round the same real value x * 2^-7, underflow included.
 __device__ __forceinline__ float div128(float x) { return __fmul_rn(x, 0.0078125f); }
 
