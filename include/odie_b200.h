@@ -138,6 +138,23 @@ ODIE_API int selection_chunk(const double* scores, int n, int points, int resolu
 ODIE_API int odie_tile_topk(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
                    double* row_sums, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free tile top-k (no counterpart in the reference).
+ * Same arguments and results as odie_tile_topk minus row_sums: the row sums
+ * live in a fixed 2 MiB array inside this library (262144 f64 entries), so the
+ * call allocates no device memory.  It is for callers that may not allocate at
+ * all: a host whose device memory is owned by another allocator or held to a
+ * hard budget, and code running where an allocation would synchronise the
+ * device or is forbidden.  tiles * tile above 262144 returns
+ * cudaErrorInvalidValue with a message in odie_error().  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls on one device share the
+ * array: calls that can overlap on the GPU (different streams, or several host
+ * threads) race and must be serialised by the caller.
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_tile_topk_noalloc(const float* prediction, const uint8_t* target, int height, int width, int tile,
+                   int k, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream);
+
 #ifdef __cplusplus
 }
 #endif

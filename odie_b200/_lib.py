@@ -45,6 +45,7 @@ SIGNATURES = {
     'selection_init': (I32, [P, I32, I32, P, P, P, P, P, P, P, I32, U64]),
     'selection_chunk': (I32, [P, I32, I32, I32, I32, B, P, P, P, P, P, P, I32, I32, P, P, U64]),
     'odie_tile_topk': (I32, [P, P, I32, I32, I32, I32, P, P, P, P, U64]),
+    'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),
 }
 
 

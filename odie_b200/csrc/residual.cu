@@ -11,6 +11,8 @@
 // Tile scores (no reference counterpart): per tile of
 // tile x tile pixels, fp64 row sums in raster order, then the fp64 sum of the
 // row sums in row order; then an exact top-k by (score desc, tile id asc).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace odie {
@@ -107,6 +109,40 @@ void launch_tile_scores(const float* prediction, const uint8_t* target, int heig
 void launch_topk(const double* scores, int count, int k, long long* chosen, uint8_t* selected, cudaStream_t stream) {
     if (count <= 0) return;
     topk_rank_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(scores, count, k, chosen, selected);
+}
+
+// ---------------------------------------------------------------- allocation-free tile top-k
+// Row-sum scratch of odie_tile_topk_noalloc: a fixed device array that every GPU
+// loading this library holds until the process exits.  Every call on a device
+// shares it, so calls that overlap on the GPU race; each call writes every entry
+// it later reads (tiles x tile row sums), so nothing needs clearing.
+constexpr long long NOALLOC_TILE_ROWS = 1LL << 18;  // 262 144 fp64 row sums = 2 MiB
+static __device__ __align__(256) double g_noalloc_row_sums[NOALLOC_TILE_ROWS];
+
+long long noalloc_tile_rows_max() { return NOALLOC_TILE_ROWS; }
+
+// Device address of the scratch for the current device, resolved once per device
+// (host code must not pass the symbol itself: it is a host-side stand-in).
+double* noalloc_row_sums(std::string& error) {
+    static std::mutex lock;
+    static double* address[64] = {nullptr};
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess || device < 0 || device >= 64) {
+        error = std::string("cudaGetDevice: ") + cudaGetErrorString(status);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> guard(lock);
+    if (!address[device]) {
+        void* p = nullptr;
+        status = cudaGetSymbolAddress(&p, g_noalloc_row_sums);
+        if (status != cudaSuccess) {
+            error = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(status);
+            return nullptr;
+        }
+        address[device] = static_cast<double*>(p);
+    }
+    return address[device];
 }
 
 }  // namespace odie

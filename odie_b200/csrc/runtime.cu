@@ -545,6 +545,8 @@ void launch_score_chunk(const float* prediction, const void* target, long long b
 void launch_tile_scores(const float* prediction, const uint8_t* target, int height, int width, int tile, double* row_sums,
                         double* scores, cudaStream_t stream);
 void launch_topk(const double* scores, int count, int k, long long* chosen, uint8_t* selected, cudaStream_t stream);
+long long noalloc_tile_rows_max();
+double* noalloc_row_sums(std::string& error);
 int launch_selection_init(const double* scores, int n, int points, int* missing, uint8_t* chosen, uint8_t* nodes,
                           int* tree, long long* stats, const int* host_offsets, const int* host_sizes, int levels,
                           cudaStream_t stream);
@@ -764,6 +766,35 @@ int odie_tile_topk(const float* prediction, const uint8_t* target, int height, i
     odie::launch_tile_scores(prediction, target, height, width, tile, row_sums, scores, s);
     const int tiles = ((width + tile - 1) / tile) * ((height + tile - 1) / tile);
     odie::launch_topk(scores, tiles, k, reinterpret_cast<long long*>(chosen), selected, s);
+    return int(cudaGetLastError());
+}
+
+// odie_tile_topk without the caller-provided row-sum buffer.  Some callers cannot
+// hand over device memory: an embedding host whose GPU memory is all owned by its
+// own allocator or capped by a budget, or code that runs where a cudaMalloc would
+// synchronise the device or is not allowed.  The row sums go to the library's fixed
+// array instead (size limit checked here, before anything is launched).
+int odie_tile_topk_noalloc(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
+                           double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream) {
+    if (height < 1 || width < 1 || tile < 1 || k < 0) {
+        odie::set_error("odie_tile_topk_noalloc: height, width and tile must be >= 1 and k >= 0");
+        return int(cudaErrorInvalidValue);
+    }
+    const long long tiles = (long long)((width + tile - 1) / tile) * ((height + tile - 1) / tile);
+    if (tiles * tile > odie::noalloc_tile_rows_max()) {
+        odie::set_error("odie_tile_topk_noalloc: tiles x tile = " + std::to_string(tiles * tile) +
+                        " row sums exceed the fixed scratch of " + std::to_string(odie::noalloc_tile_rows_max()));
+        return int(cudaErrorInvalidValue);
+    }
+    std::string error;
+    double* row_sums = odie::noalloc_row_sums(error);
+    if (!row_sums) {
+        odie::set_error("odie_tile_topk_noalloc: " + error);
+        return int(cudaErrorInvalidValue);
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    odie::launch_tile_scores(prediction, target, height, width, tile, row_sums, scores, s);
+    odie::launch_topk(scores, int(tiles), k, reinterpret_cast<long long*>(chosen), selected, s);
     return int(cudaGetLastError());
 }
 
