@@ -30,6 +30,10 @@ extern "C" {
  * bakes in at compile time (odie/build.py:26-30): "levels", "raw_width",
  * "router", "gate_k", "softplus", "rgb8", and "batch" (maximum coordinates per
  * step; the reference fixes 65536).
+ * Routed experts (no reference counterpart): "experts" (1..16) with
+ * "hash_encoding" (one expert's grid; "grid" holds experts x its parameters,
+ * expert-major), "router_encoding" (the coarse shared grid; fp32 master in
+ * "router_grid") and "gate" (router MLP W1 | W2 | W3, fp32 master, "gate_lr").
  * ------------------------------------------------------------------------ */
 /* Thread-local message of the last failure. runtime.cu:320 */
 ODIE_API const char* odie_error(void);
@@ -129,6 +133,26 @@ ODIE_API int selection_init(const double* scores, int n, int points, int* missin
 ODIE_API int selection_chunk(const double* scores, int n, int points, int resolution, int cap, bool normalized, int* missing,
                     uint8_t* chosen, uint8_t* nodes, int* tree, const int* offsets, const int* sizes, int levels,
                     int chunk, int64_t* stats, int* trace, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Routed multi-expert encoding (no reference counterpart).
+ * odie_router_forward: features f16[n][width] (width 16 or 32, row-major),
+ * weights f16 [32*width | 32*32 | 16*32] (router W1, W2, W3, row-major
+ * [out][in]); writes expert i32[n] (first maximum of the fp16 logits over
+ * experts 1..16), prob f32[n] (softmax probability of that expert) and, when
+ * logits is non-NULL, f16[n][16].  Bit-exact: fp32 fma chains in input order.
+ * odie_expert_hash_forward/backward: odie_hash_forward/backward with one table
+ * per expert; coordinate i uses the table starting expert[i] * expert_stride
+ * parameters into `tables` / `gradient` (same level records for every expert).
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
+                   int32_t* expert, float* prob, uint16_t* logits, uint64_t stream);
+ODIE_API int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
+                   const int32_t* expert, const odie_hash_level* levels, int level_count, int width,
+                   uint16_t* features, uint64_t stream);
+ODIE_API int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
+                   int64_t expert_stride, const int32_t* expert, const odie_hash_level* levels, int level_count,
+                   float* gradient, int64_t parameter_count, uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * Tile top-k allocation (no reference counterpart).

@@ -45,6 +45,9 @@ SIGNATURES = {
     'selection_init': (I32, [P, I32, I32, P, P, P, P, P, P, P, I32, U64]),
     'selection_chunk': (I32, [P, I32, I32, I32, I32, B, P, P, P, P, P, P, I32, I32, P, P, U64]),
     'odie_tile_topk': (I32, [P, P, I32, I32, I32, I32, P, P, P, P, U64]),
+    'odie_router_forward': (I32, [P, I64, I32, P, I32, P, P, P, U64]),
+    'odie_expert_hash_forward': (I32, [P, I64, P, I64, P, C.POINTER(HashLevel), I32, I32, P, U64]),
+    'odie_expert_hash_backward': (I32, [P, I64, P, I32, I64, P, C.POINTER(HashLevel), I32, P, I64, U64]),
     'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),
 }
 

@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
         }
     }
     if (!inside) return;
+    const long long base = d.offset + (a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL);
     if (d.F == 2) {
         __half2 acc = __float2half2_rn(0.0f);
         if (on) {
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
             for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
             __half2 t[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) t[k] = load_pair(params, (long long)d.offset + 2LL * rows[k]);
+            for (int k = 0; k < 4; ++k) t[k] = load_pair(params, base + 2LL * rows[k]);
             // __hfma2 rounds each lane once, exactly as the reference's per-channel __hfma chain.
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc = __hfma2(__float2half2_rn(g.w[k]), t[k], acc);
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
         if (on) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-                acc = __hfma(__float2half_rn(g.w[k]), load_one(params, (long long)d.offset + (long long)rows[k] * d.F + c), acc);
+                acc = __hfma(__float2half_rn(g.w[k]), load_one(params, base + (long long)rows[k] * d.F + c), acc);
         }
         store_feature(out, a.row_major, i, d.col + c, a.width, a.stride, acc);
     }
@@ -176,6 +177,7 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
     const Corner4 g = geometry(p.x, p.y, d.scale);
     if (!level_on(d, g, a.bitmap)) return;
     const bool aggregate = d.res <= warp_limit;
+    float* const level_grad = grad + d.offset + (a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL);
     if (d.F == 2) {
         const float v0 = upstream_value(upstream, a, i, d.col);
         const float v1 = upstream_value(upstream, a, i, d.col + 1);
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
         for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            float* address = grad + d.offset + 2LL * rows[k];
+            float* address = level_grad + 2LL * rows[k];
             const float x = __fmul_rn(g.w[k], v0), y = __fmul_rn(g.w[k], v1);
             if (aggregate) aggregated_red2(address, x, y);
             else red_add_v2(address, x, y);
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
         if (v == 0.0f) continue;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            float* address = grad + d.offset + (long long)rows[k] * d.F + c;
+            float* address = level_grad + (long long)rows[k] * d.F + c;
             const float x = __fmul_rn(g.w[k], v);
             if (aggregate) aggregated_red1(address, x);
             else red_add_f32(address, x);
@@ -284,11 +286,12 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     }
     // Levels whose table fits in shared memory and whose global reductions the
     // block-level pre-aggregation cuts by >= 4x take the shared-memory path.
+    // (Routed experts split each level over several tables: direct path only.)
     CoarseList list{};
     int coarse = 0, max_blocks = 0, max_floats = 0;
     unsigned skip = 0;
     const int cap_blocks = 2 * sm_count();
-    for (int l = 0; l < a.levels && l < a.active; ++l) {
+    for (int l = 0; l < a.levels && l < a.active && !a.expert; ++l) {
         const Level& d = src.table.level[l];
         const long long floats = (long long)d.points * d.F;
         if (floats > COARSE_SMEM_FLOATS) continue;

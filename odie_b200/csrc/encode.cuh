@@ -28,6 +28,11 @@ struct EncodeArgs {
     bool row_major = true;
     int width = 0;
     long long stride = 0;
+    // Routed experts: coordinate i reads and updates the table of expert
+    // expert[i], which starts expert[i] * expert_stride parameters after the
+    // level offsets (every expert has the same level layout).  Null: one table.
+    const int* expert = nullptr;
+    long long expert_stride = 0;
 };
 
 // Forward: table is fp32 (master) or fp16 (mirror); vis may be null.

@@ -19,6 +19,16 @@
 // UNIFORM: every level has 2 features at columns (2l, 2l+1) (the reference's
 // default layout); the per-level epilogues are then fully unrolled with
 // compile-time indices.  Other layouts take the generic per-column path.
+//
+// GATE_EXPERTS (routed multi-expert encoding, no reference counterpart): the
+// decoder input is the routed expert's features times half(p), p the router
+// probability of that expert (chosen bit-exactly by router.cu).  Training
+// recomputes the router MLP on the tensor cores (R -> 32 -> 32 -> 16 logits)
+// for its backward: dp = sum_c v_c f_c, dz_j = dp p (delta_je - p_j), then the
+// router backward down to the router-grid gradient values.  The router
+// features of the next tile stream into a second shared-memory buffer with
+// cp.async while the current tile runs.
+#include "router.cuh"
 #include "step.cuh"
 #include "tc.cuh"
 
@@ -33,7 +43,7 @@ constexpr uint32_t TMEM_COLUMNS = 256;
 
 // TMEM columns: a per-tile accumulator (M=128) and the persistent weight-
 // gradient accumulators (M=64: lanes 0-15 of each 32-lane subpartition).
-constexpr uint32_t T_ACC = 0, T_DWD2 = 64, T_DWD1 = 128, T_DW3T = 160, T_DWG2T = 176, T_DWG1 = 192;
+constexpr uint32_t T_ACC = 0, T_DWD2 = 64, T_DWD1 = 128, T_DW3T = 160, T_DWG2T = 176, T_DWG1 = 192, T_DWR2 = 224;
 
 // Shared memory (bytes) for decoder input width W: weights blocked [out x in],
 // activations blocked [128 x cols].  GH and DGH are read 64 columns wide as
@@ -42,15 +52,17 @@ constexpr uint32_t T_ACC = 0, T_DWD2 = 64, T_DWD1 = 128, T_DW3T = 160, T_DWG2T =
 template <int W>
 struct TcSmem {
     static constexpr int XB = 128 * W * 2;              // one [128 x W] buffer
-    static constexpr int g1 = 0;                        // [32 x W]
-    static constexpr int g2 = g1 + 32 * W * 2;          // [16 x 32]
-    static constexpr int d1 = g2 + 16 * 32 * 2;         // [64 x W]
+    static constexpr int g1 = 0;                        // [32 x W] gate / router W1
+    static constexpr int g2 = g1 + 32 * W * 2;          // [16 x 32] gate W2 / router W3
+    static constexpr int r2 = g2 + 16 * 32 * 2;         // [32 x 32] router W2
+    static constexpr int d1 = r2 + 32 * 32 * 2;         // [64 x W]
     static constexpr int d2 = d1 + 64 * W * 2;          // [64 x 64]
     static constexpr int d3 = d2 + 64 * 64 * 2;         // [16 x 64]
     static constexpr int x = d3 + 16 * 64 * 2;          // [128 x W] raw features
     static constexpr int wx = x + XB;                   // [128 x W] gated decoder input
-    static constexpr int gh = wx + XB;                  // [128 x 32] gate hidden
-    static constexpr int h1 = gh + 8192;                // [128 x 64] decoder hidden 1, then dh1
+    static constexpr int gh = wx + XB;                  // [128 x 32] gate / router hidden 1
+    static constexpr int gh2 = gh + 8192;               // [128 x 32] router hidden 2
+    static constexpr int h1 = gh2 + 8192;               // [128 x 64] decoder hidden 1, then dh1
     static constexpr int h2 = h1 + 16384;               // [128 x 64] decoder hidden 2, then dh2
     static constexpr int dgh = h2 + 16384;              // [128 x 32] gate hidden gradient
     static constexpr int dy = dgh + 8192;               // [128 x 16] output gradient
@@ -58,7 +70,9 @@ struct TcSmem {
     static constexpr int bar = da + 4096;               // mbarrier: data products of a phase
     static constexpr int bar_dw = bar + 8;              // mbarrier: weight-gradient products of a phase
     static constexpr int tmem = bar_dw + 8;             // TMEM base address
+    static constexpr int x2 = (tmem + 8 + 127) / 128 * 128;  // [128 x W] second router-feature buffer (experts)
     static constexpr int total = tmem + 8;
+    static constexpr int total_experts = x2 + XB;
     static_assert(gh + 16384 <= dgh, "GH read 64 wide stays inside the activation buffers");
     static_assert(dgh + 16384 <= bar, "DGH read 64 wide stays inside the activation buffers");
 };
@@ -76,6 +90,13 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
 __device__ __forceinline__ void store_chunk(unsigned char* smem, int base, int r, int j, uint4 q) {
     *reinterpret_cast<uint4*>(smem + base + tc::blocked(TC_TILE, r, 8 * j)) = q;
 }
+
+// 4-byte asynchronous global -> shared copy; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_older() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 __device__ void stage_blocked(const __half* __restrict__ src, int rows, int cols, unsigned char* smem, int base) {
     for (int idx = threadIdx.x; idx < rows * cols; idx += blockDim.x) {
@@ -162,7 +183,7 @@ __device__ __forceinline__ float gate_derivative(float incoming, float s, int le
     return __fmul_rn(__fmul_rn(incoming, __fsub_rn(1.0f, s)), s);
 }
 
-template <int W, bool ROUTER, bool TRAIN, bool UNIFORM>
+template <int W, int GATE, bool TRAIN, bool UNIFORM>
 __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, int* error_flag) {
     using S = TcSmem<W>;
     constexpr int PAIRS = W / 2, KW = W / 16;
@@ -173,9 +194,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
     const uint32_t sbase = tc::smem_u32(smem);
 
+    constexpr bool ROUTER = GATE == GATE_LEVELS;   // the reference's per-level gate
+    constexpr bool EXPERTS = GATE == GATE_EXPERTS;  // routed experts
     if (ROUTER) {
         stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, S::g1);
         stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, S::g2);
+    }
+    if (EXPERTS && TRAIN) {
+        stage_blocked(a.gate_w, ROUTER_HIDDEN, W, smem, S::g1);
+        stage_blocked(a.gate_w + ROUTER_HIDDEN * W, ROUTER_HIDDEN, ROUTER_HIDDEN, smem, S::r2);
+        stage_blocked(a.gate_w + ROUTER_HIDDEN * W + ROUTER_HIDDEN * ROUTER_HIDDEN, ROUTER_OUT, ROUTER_HIDDEN, smem, S::g2);
     }
     stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
@@ -204,13 +232,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_G2 = tc::idesc(128, 16, 0, 0);
     constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
-    const int in_buf = ROUTER ? S::wx : S::x;
+    const int in_buf = GATE != GATE_NONE ? S::wx : S::x;
 
     // Inputs of a tile: raw feature pairs, this warp's visibility words, target.
     // The next tile's inputs are loaded while the current tile runs its
     // backward products, so their global-memory latency is off the chain.
     uint32_t next_raw[PAIRS], next_vis = 0;
     float next_target[3] = {0.0f, 0.0f, 0.0f};
+    float next_prob = 0.0f;
+    int next_expert = 0;
     auto load_inputs = [&](long long tile) {
         const long long i = tile * TC_TILE + t;
         const bool valid = tile < tiles && i < a.n;
@@ -221,6 +251,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
         }
+        if (EXPERTS) {
+            next_prob = valid ? __ldg(a.prob + i) : 0.0f;
+            if (TRAIN) next_expert = valid ? __ldg(a.expert + i) : 0;
+        }
+    };
+    // Router features of a tile (experts, training): cp.async into shared buffer `buf`.
+    auto prefetch_router = [&](long long tile, int buf) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = tile < tiles && i < a.n;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.router_in);
+#pragma unroll
+        for (int p = 0; p < PAIRS; ++p)
+            cp_async4(sbase + buf + tc::blocked(TC_TILE, t, 2 * p), valid ? src + (long long)p * a.stride + i : src,
+                      valid ? 4u : 0u);
+        cp_async_commit();
     };
     // Visibility: lane l (< levels) loads this warp's word of level l; the
     // words are broadcast with shuffles when the bits are folded per row.
@@ -240,10 +285,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     load_inputs(blockIdx.x);
     issue_vis(blockIdx.x);
     fold_vis(blockIdx.x);
+    int xbuf = S::x;  // router features of the current tile (experts: alternates with S::x2)
+    if (EXPERTS && TRAIN) prefetch_router(blockIdx.x, S::x);
 
     for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
         const long long i = tile * TC_TILE + t;
         const bool valid = i < a.n;
+        if (EXPERTS && TRAIN) {
+            // the other buffer was last read by the previous tile's router weight-gradient product, which has completed
+            prefetch_router(tile + gridDim.x, xbuf == S::x ? S::x2 : S::x);
+            cp_async_wait_older();  // this tile's features have landed
+        }
+        const float prob = next_prob;
+        const int expert = next_expert;
         // ---- inputs: raw features (pad columns 1.0), visibility bits, target
         uint32_t raw[PAIRS];
         const __half one = __float2half_rn(1.0f);
@@ -257,9 +311,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         const uint32_t visbits = next_vis;
         const float target[3] = {next_target[0], next_target[1], next_target[2]};
         const long long next_tile = tile + gridDim.x;
+        if (!EXPERTS) {
 #pragma unroll
-        for (int j = 0; j < W / 8; ++j)
-            store_chunk(smem, S::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
+            for (int j = 0; j < W / 8; ++j)
+                store_chunk(smem, S::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
+        }
 
         float sig[16];
         uint32_t gh_mask = 0;
@@ -311,6 +367,48 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
                 store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+        }
+        uint32_t gh2_mask = 0;
+        uint32_t zh[ROUTER_OUT / 2];  // fp16 router logits recomputed for the backward (experts, training)
+        if (EXPERTS) {
+            // ---- decoder input: the routed expert's features x half(p), one rounding per feature
+            const __half2 ph = __float2half2_rn(prob);
+            uint32_t wx[PAIRS];
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p) {
+                const __half2 f = __halves2half2(lo_half(raw[p]), hi_half(raw[p]));
+                const __half2 g = __hmul2(f, ph);
+                wx[p] = pack_half2(__low2half(g), __high2half(g));
+            }
+#pragma unroll
+            for (int j = 0; j < W / 8; ++j)
+                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+            if (TRAIN) {
+                // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T), Z = GH2 Wr3^T
+                is.before_issue();
+                if (t == 0)
+                    for (int s = 0; s < KW; ++s)
+                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
+                if (!is.complete()) break;
+                gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
+                gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
+                is.before_issue();
+                if (t == 0)
+                    for (int s = 0; s < 2; ++s)
+                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
+                if (!is.complete()) break;
+                gh2_mask = relu_store16(lane_addr + T_ACC, smem, S::gh2, t, 0);
+                gh2_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh2, t, 2) << 16;
+                is.before_issue();
+                if (t == 0)
+                    for (int s = 0; s < 2; ++s)
+                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh2, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
+                if (!is.complete()) break;
+                float z[ROUTER_OUT];
+                tc::tmem_ld16(lane_addr + T_ACC, z);
+#pragma unroll
+                for (int j = 0; j < ROUTER_OUT / 2; ++j) zh[j] = pack_half2(__float2half_rn(z[2 * j]), __float2half_rn(z[2 * j + 1]));
+            }
         }
         // ---- decoder hidden 1, hidden 2, output
         uint32_t h1_mask[4], h2_mask[4];
@@ -424,7 +522,106 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
         for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
         uint32_t gv[PAIRS];
-        if (!ROUTER) {
+        if (EXPERTS) {
+            // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
+            const __half ph = __float2half_rn(prob);
+            float dp = 0.0f;
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p) {
+                const __half v0 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p]))));
+                const __half v1 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p + 1]))));
+                gv[p] = pack_half2(__hmul_rn(v0, ph), __hmul_rn(v1, ph));
+                dp = __fmaf_rn(__half2float(v0), __half2float(lo_half(raw[p])), dp);
+                dp = __fmaf_rn(__half2float(v1), __half2float(hi_half(raw[p])), dp);
+            }
+            // ---- logit gradients: softmax of the recomputed fp16 logits over the live experts
+            float z[ROUTER_OUT], zmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < ROUTER_OUT; ++j) {
+                z[j] = __half2float((j & 1) ? hi_half(zh[j >> 1]) : lo_half(zh[j >> 1]));
+                if (j < a.experts) zmax = fmaxf(zmax, z[j]);
+            }
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < ROUTER_OUT; ++j) {
+                z[j] = j < a.experts ? expf(__fsub_rn(z[j], zmax)) : 0.0f;
+                sum = __fadd_rn(sum, z[j]);
+            }
+            const float dpp = __fmul_rn(dp, prob);
+            float da[ROUTER_OUT];
+#pragma unroll
+            for (int j = 0; j < ROUTER_OUT; ++j) {
+                const float pj = __fdiv_rn(z[j], sum);
+                const float derivative = __fmul_rn(dpp, __fsub_rn(j == expert ? 1.0f : 0.0f, pj));
+                da[j] = j < a.experts ? __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f))) : 0.0f;
+            }
+            if (!is.wait_dw()) break;  // dWd1 done before the next products are queued
+            store_chunk(smem, S::da, t, 0, pack8(da));
+            store_chunk(smem, S::da, t, 1, pack8(da + 8));
+            // ---- dgh2 = DA Wr3; dWr3^T += GH2^T DA
+            is.before_issue();
+            if (t == 0) {
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
+                        tc::idesc(128, 32, 0, 1), 0);
+                tc::commit(bar);
+                for (int s = 0; s < 8; ++s)
+                    tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh2, 128, s), tc::mnmajor(sbase + S::da, 128, s),
+                            tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+                tc::commit(bar_dw);
+            }
+            is.wait_data();
+            masked_pack16(lane_addr + T_ACC, gh2_mask & 0xffffu, packed);
+            masked_pack16(lane_addr + T_ACC + 16, gh2_mask >> 16, packed + 8);
+            if (!is.wait_dw()) break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+            // ---- dgh1 = DGH2 Wr2; dWr2 += DGH2^T GH1
+            is.before_issue();
+            if (t == 0) {
+                for (int s = 0; s < 2; ++s)
+                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::r2, 32, s),
+                            tc::idesc(128, 32, 0, 1), s > 0);
+                tc::commit(bar);
+                for (int s = 0; s < 8; ++s)
+                    tc::mma(tmem + T_DWR2, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::gh, 128, s),
+                            tc::idesc(64, 32, 1, 1), dw_accumulate | uint32_t(s > 0));
+                tc::commit(bar_dw);
+            }
+            is.wait_data();
+            masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
+            masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
+            if (!is.wait_dw()) break;  // dWr2 has read DGH2: dgh1 may overwrite it
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+            // ---- dR = DGH1 Wr1; dWr1 += DGH1^T R; router grid values half(dR / 128)
+            is.before_issue();
+            if (t == 0) {
+                for (int s = 0; s < 2; ++s)
+                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
+                            tc::idesc(128, W, 0, 1), s > 0);
+                tc::commit(bar);
+                for (int s = 0; s < 8; ++s)
+                    tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + xbuf, 128, s),
+                            tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+                tc::commit(bar_dw);
+            }
+            is.wait_data();
+#pragma unroll
+            for (int q = 0; q < KW; ++q) {
+                float v[16];
+                tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
+                if (valid) {
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2)
+                        reinterpret_cast<uint32_t*>(a.router_gvals)[(long long)(8 * q + c / 2) * a.stride + i] =
+                            pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(v[c])))),
+                                       __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1])))));
+                }
+            }
+            if (!is.wait_dw()) break;  // dWr1 has read R and DGH1
+        } else if (!ROUTER) {
             if (!is.wait_dw()) break;  // dWd1 has read X: the next tile may overwrite it
             // grid values without router: half(dz / 128) (runtime.cu:123)
 #pragma unroll
@@ -537,7 +734,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         }
         dw_accumulate = 1;
         fold_vis(next_tile);
+        if (EXPERTS && TRAIN) xbuf = xbuf == S::x ? S::x2 : S::x;
     }
+    if (EXPERTS && TRAIN) asm volatile("cp.async.wait_all;\n" ::: "memory");  // no copy outlives the block
 
     if (!is.ok) {
         if (t == 0) atomicExch(error_flag, 2);
@@ -547,10 +746,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     }
     if (TRAIN) {
         // ---- weight gradients: TMEM (M=64 layout: rows 16w..16w+15 in lanes 32w..32w+15) -> partials
-        constexpr int GATE = ROUTER ? gate_params(W) : 0;
-        constexpr int P = GATE + decoder_params(W);
+        constexpr int GP = ROUTER ? gate_params(W) : EXPERTS ? router_params(W) : 0;
+        constexpr int P = GP + decoder_params(W);
         float* part = a.partials + (long long)blockIdx.x * P;
-        float* dec = part + GATE;
+        float* dec = part + GP;
         const int row = 16 * warp + (t & 31);
         const bool holds = (t & 31) < 16;
         const bool any = dw_accumulate && is.ok;
@@ -593,31 +792,58 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     for (int c = 0; c < 16; ++c) part[row * W + 16 * q + c] = any ? v[c] : 0.0f;
             }
         }
+        if (EXPERTS) {
+            constexpr int R2 = ROUTER_HIDDEN * W, R3 = R2 + ROUTER_HIDDEN * ROUTER_HIDDEN;
+#pragma unroll
+            for (int q = 0; q < KW; ++q) {  // dWr1 [32][W] from [64 (32 valid)][W]
+                float v[16];
+                tc::tmem_ld16(lane_addr + T_DWG1 + 16 * q, v);
+                if (holds && row < ROUTER_HIDDEN)
+                    for (int c = 0; c < 16; ++c) part[row * W + 16 * q + c] = any ? v[c] : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {  // dWr2 [32][32] from [64 (32 valid)][32]
+                float v[16];
+                tc::tmem_ld16(lane_addr + T_DWR2 + 16 * q, v);
+                if (holds && row < ROUTER_HIDDEN)
+                    for (int c = 0; c < 16; ++c) part[R2 + row * ROUTER_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
+            }
+            {  // dWr3 [16][32] from its transpose [64 (32 valid) in][16 out]
+                float v[16];
+                tc::tmem_ld16(lane_addr + T_DWG2T, v);
+                if (holds && row < ROUTER_HIDDEN)
+                    for (int c = 0; c < 16; ++c) part[R3 + c * ROUTER_HIDDEN + row] = any ? v[c] : 0.0f;
+            }
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
 }
 
-template <int W, bool ROUTER, bool TRAIN, bool UNIFORM>
+template <int W, int GATE, bool TRAIN, bool UNIFORM>
 void launch_tc(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
     static unsigned long long configured = 0;
+    constexpr int bytes = (GATE == GATE_EXPERTS && TRAIN) ? TcSmem<W>::total_experts : TcSmem<W>::total;
     int device = 0;
     ODIE_CUDA(cudaGetDevice(&device));
     if (!(configured >> device & 1ull)) {
-        ODIE_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<W, ROUTER, TRAIN, UNIFORM>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<W>::total));
+        ODIE_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<W, GATE, TRAIN, UNIFORM>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
         configured |= 1ull << device;
     }
-    mlp_tc_kernel<W, ROUTER, TRAIN, UNIFORM><<<blocks, TC_THREADS, TcSmem<W>::total, stream>>>(a, error_flag);
+    mlp_tc_kernel<W, GATE, TRAIN, UNIFORM><<<blocks, TC_THREADS, bytes, stream>>>(a, error_flag);
 }
 
 template <bool TRAIN>
-void dispatch(const MlpArgs& a, int width, bool router, bool uniform, int blocks, int* error_flag, cudaStream_t stream) {
-#define ODIE_TC(WV, R, U) \
-    if (width == WV && router == R && uniform == U) return launch_tc<WV, R, TRAIN, U>(a, blocks, error_flag, stream);
-    ODIE_TC(32, true, true) ODIE_TC(32, true, false) ODIE_TC(32, false, true) ODIE_TC(32, false, false)
-    ODIE_TC(16, true, true) ODIE_TC(16, true, false) ODIE_TC(16, false, true) ODIE_TC(16, false, false)
+void dispatch(const MlpArgs& a, int width, GateMode gate, bool uniform, int blocks, int* error_flag, cudaStream_t stream) {
+#define ODIE_TC(WV, G, U) \
+    if (width == WV && gate == G && uniform == U) return launch_tc<WV, G, TRAIN, U>(a, blocks, error_flag, stream);
+    ODIE_TC(32, GATE_LEVELS, true) ODIE_TC(32, GATE_LEVELS, false) ODIE_TC(32, GATE_NONE, true) ODIE_TC(32, GATE_NONE, false)
+    ODIE_TC(16, GATE_LEVELS, true) ODIE_TC(16, GATE_LEVELS, false) ODIE_TC(16, GATE_NONE, true) ODIE_TC(16, GATE_NONE, false)
+    // routed experts: no per-level epilogue, so the column layout does not matter
+    if (gate == GATE_EXPERTS && width == 32) return launch_tc<32, GATE_EXPERTS, TRAIN, true>(a, blocks, error_flag, stream);
+    if (gate == GATE_EXPERTS && width == 16) return launch_tc<16, GATE_EXPERTS, TRAIN, true>(a, blocks, error_flag, stream);
 #undef ODIE_TC
     throw std::invalid_argument("the fused heads take 16 or 32 input features");
 }
@@ -631,17 +857,17 @@ int mlp_tc_blocks(long long n) {
     return blocks < 1 ? 1 : int(blocks);
 }
 
-void launch_mlp_tc_train(const MlpArgs& a, int width, bool router, bool uniform, int blocks, int* error_flag,
+void launch_mlp_tc_train(const MlpArgs& a, int width, GateMode gate, bool uniform, int blocks, int* error_flag,
                          cudaStream_t stream) {
     if (a.n <= 0) return;
     ODIE_REQUIRE(a.stride % TC_TILE == 0, "the feature stride must be a multiple of 128");
-    dispatch<true>(a, width, router, uniform, blocks, error_flag, stream);
+    dispatch<true>(a, width, gate, uniform, blocks, error_flag, stream);
 }
 
-void launch_mlp_tc_decode(const MlpArgs& a, int width, bool router, bool uniform, int* error_flag, cudaStream_t stream) {
+void launch_mlp_tc_decode(const MlpArgs& a, int width, GateMode gate, bool uniform, int* error_flag, cudaStream_t stream) {
     if (a.n <= 0) return;
     ODIE_REQUIRE(a.stride % TC_TILE == 0, "the feature stride must be a multiple of 128");
-    dispatch<false>(a, width, router, uniform, mlp_tc_blocks(a.n), error_flag, stream);
+    dispatch<false>(a, width, gate, uniform, mlp_tc_blocks(a.n), error_flag, stream);
 }
 
 }  // namespace odie

@@ -9,6 +9,10 @@
 //   input_batch -> encode forward (fp16 mirror gather) -> fused MLP heads
 //   (gate, decoder, loss, backward, weight-gradient partials) -> encode
 //   backward (scatter) -> partial reduction -> Adam (grid, gate, decoder).
+// Routed experts ("experts" in the settings; no reference counterpart): the
+// router grid is encoded first, router.cu picks one expert per coordinate, the
+// expert tables are encoded at that expert's offset, and the fused heads train
+// router and decoder together; both grids take the scatter and the Adam step.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -19,6 +23,7 @@
 #include "encode.cuh"
 #include "odie_b200.h"
 #include "json_lite.hpp"
+#include "router.cuh"
 #include "step.cuh"
 
 namespace odie {
@@ -81,6 +86,12 @@ struct Runtime {
     int levels = 16, raw_width = 32, input_width = 32, gate_k = 0, active = 16;
     bool router = true, softplus = false, rgb8 = true, hash_mode = false;
     bool uniform = true;   // every level F=2 at columns (2l, 2l+1)
+    // routed experts: `experts` tables of expert_total parameters each, plus the router grid
+    int experts = 0;
+    long long expert_total = 0, router_total = 0;
+    int router_levels = 0, router_width = 0;
+    LevelTable router_table{};
+    float* router_grid = nullptr;  // caller-owned fp32 master of the router grid
     double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
     // caller-owned
     float* grid = nullptr;
@@ -105,10 +116,15 @@ struct Runtime {
     DeviceArray<__half> raw, gvals;
     DeviceArray<uint32_t> vis;
     DeviceArray<int> error_flag;
+    DeviceArray<__half> router_half, router_in, router_gvals;
+    DeviceArray<float> router_grad, router_m, router_v, prob;
+    DeviceArray<uint32_t> router_steps;
+    DeviceArray<int> expert_ids;
     std::vector<double> host_bc1, host_bc2;
     int partial_blocks = 0;
 
     float* head_grad() { return external_head_grad ? external_head_grad : head_grad_own.ptr; }
+    GateMode gate_mode() const { return experts ? GATE_EXPERTS : router ? GATE_LEVELS : GATE_NONE; }
 
     explicit Runtime(const Json& j) {
         ODIE_CUDA(cudaGetDevice(&device));
@@ -133,8 +149,20 @@ struct Runtime {
         if (router) gate_master = pointer_of<float>(j, "gate");
         if (j.contains("head_grad")) external_head_grad = pointer_of<float>(j, "head_grad");
         hash_mode = j.contains("hash_encoding");
+        experts = int(j.value("experts", 0));
+        if (experts) {
+            ODIE_REQUIRE(experts >= 1 && experts <= ROUTER_OUT, "experts must be within 1..16");
+            ODIE_REQUIRE(hash_mode && j.contains("router_encoding"), "routed experts need hash_encoding and router_encoding");
+            router = false;
+            gate_master = pointer_of<float>(j, "gate");
+            router_grid = pointer_of<float>(j, "router_grid");
+            int rf = 0;
+            router_total = hash_layout(j.at("router_encoding"), router_table, router_levels, rf);
+            router_width = (router_levels * rf + 15) / 16 * 16;
+        }
         if (hash_mode) build_hash_table(j.at("hash_encoding"));
         else levels = int(j.value("levels", 16));
+        if (experts) ODIE_REQUIRE(router_width == input_width, "router and expert encodings must have the same width");
         ODIE_REQUIRE(levels >= 2 && levels <= 16, "the fused heads support 2..16 levels");
         ODIE_REQUIRE(gate_k >= 0 && gate_k <= levels, "gate_k outside [0, levels]");
         active = levels;
@@ -153,7 +181,7 @@ struct Runtime {
             ODIE_CUDA(cudaMemcpy(table_bc2.ptr, bc2.data(), TABLE_STEPS * sizeof(float), cudaMemcpyHostToDevice));
         }
         configure(j);
-        gate_count = router ? gate_params(input_width) : 0;
+        gate_count = router ? gate_params(input_width) : experts ? router_params(input_width) : 0;
         decoder_count = decoder_params(input_width);
         head_count = gate_count + decoder_count;
         // library-owned buffers
@@ -176,6 +204,22 @@ struct Runtime {
         gvals.allocate((long long)input_width * capacity);
         vis.allocate((long long)levels * capacity / 32);  // bit-packed [levels][capacity / 32]
         error_flag.allocate(1);
+        if (experts) {
+            router_half.allocate(router_total);
+            router_grad.allocate(router_total);
+            router_m.allocate(router_total);
+            router_v.allocate(router_total);
+            router_steps.allocate(router_total);
+            router_in.allocate((long long)router_width * capacity);
+            router_gvals.allocate((long long)router_width * capacity);
+            prob.allocate(capacity);
+            expert_ids.allocate(capacity);
+            for (auto* a : {&router_grad, &router_m, &router_v, &prob}) a->zero(stream);
+            router_steps.zero(stream);
+            router_in.zero(stream);
+            router_gvals.zero(stream);
+            expert_ids.zero(stream);
+        }
         for (auto* a : {&grid_grad, &grid_m, &grid_v, &head_grad_own, &head_m, &head_v})
             a->zero(stream);
         grid_steps.zero(stream);
@@ -188,15 +232,16 @@ struct Runtime {
         ODIE_CUDA(cudaStreamSynchronize(stream));
     }
 
-    // TCNN-style HashGrid layout restated from odie/config.py:83-94.
-    void build_hash_table(const Json& enc) {
+    // TCNN-style HashGrid layout restated from odie/config.py:83-94; returns the parameter count.
+    static long long hash_layout(const Json& enc, LevelTable& table, int& levels, int& F) {
         levels = int(enc.at("n_levels").as_int());
-        const int F = int(enc.at("n_features_per_level").as_int());
+        F = int(enc.at("n_features_per_level").as_int());
         const int log2t = int(enc.at("log2_hashmap_size").as_int());
         const int base = int(enc.at("base_resolution").as_int());
         const double growth = double(float(enc.at("per_level_scale").as_double()));
-        ODIE_REQUIRE(levels >= 2 && levels <= MAX_LEVELS, "hash grid levels in [2, 32]");
+        ODIE_REQUIRE(levels >= 2 && levels <= 16, "hash grid levels in [2, 16]");
         ODIE_REQUIRE(F == 1 || F == 2 || F == 4, "hash grid features per level must be 1, 2 or 4");
+        ODIE_REQUIRE(levels * F <= 32, "the fused heads take at most 32 input features");
         const float log_growth = float(std::log2(growth));
         long long offset = 0;
         for (int l = 0; l < levels; ++l) {
@@ -218,10 +263,25 @@ struct Runtime {
             L.kind = (long long)res * res > cap ? HASH_HASHED : HASH_DENSE;
             offset += cap * F;
         }
-        ODIE_REQUIRE(offset == total, "hash grid allocation differs from the resolved layout total");
+        return offset;
+    }
+
+    void build_hash_table(const Json& enc) {
+        int F = 0;
+        expert_total = hash_layout(enc, table, levels, F);
+        if (experts) {
+            ODIE_REQUIRE(expert_total * experts == total, "total must equal experts x the expert grid's parameters");
+            check_router_total();
+        } else {
+            ODIE_REQUIRE(expert_total == total, "hash grid allocation differs from the resolved layout total");
+        }
         raw_width = levels * F;
         input_width = (raw_width + 15) / 16 * 16;
         build_feature_map();
+    }
+
+    void check_router_total() const {
+        ODIE_REQUIRE(router_total > 0 && router_total <= 0x7fffffffLL, "router grid must fit int32 addressing");
     }
 
     void build_feature_map() {
@@ -269,7 +329,7 @@ struct Runtime {
             build_feature_map();
         }
         lr[0] = j.at("grid_lr").as_double();
-        if (router) lr[1] = j.at("gate_lr").as_double();
+        if (router || experts) lr[1] = j.at("gate_lr").as_double();
         lr[2] = j.at("decoder_lr").as_double();
         upload_step_tables();
         if (grid_half.count) sync_weights();
@@ -286,7 +346,8 @@ struct Runtime {
 
     void sync_weights() {
         launch_cast_half(grid, grid_half.ptr, total, stream);
-        if (router) launch_cast_half(gate_master, head_half.ptr, gate_count, stream);
+        if (experts) launch_cast_half(router_grid, router_half.ptr, router_total, stream);
+        if (gate_count) launch_cast_half(gate_master, head_half.ptr, gate_count, stream);
         launch_cast_half(decoder_master, head_half.ptr + gate_count, decoder_count, stream);
         ODIE_CUDA(cudaGetLastError());
     }
@@ -313,7 +374,7 @@ struct Runtime {
         m.raw = raw.ptr;
         m.vis = vis.ptr;
         m.target = target.ptr;
-        m.gate_w = router ? head_half.ptr : nullptr;
+        m.gate_w = gate_count ? head_half.ptr : nullptr;
         m.decoder_w = head_half.ptr + gate_count;
         m.levels = levels;
         m.raw_width = raw_width;
@@ -324,12 +385,54 @@ struct Runtime {
         m.gvals = gvals.ptr;
         m.squares = squares.ptr;
         m.partials = partials.ptr;
+        m.router_in = router_in.ptr;
+        m.prob = prob.ptr;
+        m.expert = expert_ids.ptr;
+        m.router_gvals = router_gvals.ptr;
+        m.experts = experts;
         return m;
     }
 
+    EncodeArgs router_encode_args(long long n) const {
+        EncodeArgs a = encode_args(n);
+        a.levels = router_levels;
+        a.active = router_levels;
+        a.width = router_width;
+        return a;
+    }
+
+    // Routed experts, forward part shared by training and decode: router grid
+    // features -> expert choice -> the chosen experts' features (raw).
+    void route_and_encode(long long n) {
+        LevelSource rsrc;
+        rsrc.table = router_table;
+        int slot = stage_begin(S_ENCODE_FWD);
+        launch_encode_forward(router_encode_args(n), rsrc, nullptr, router_half.ptr, router_in.ptr, nullptr, stream);
+        stage_end(slot);
+        RouterArgs ra;
+        ra.features = router_in.ptr;
+        ra.stride = capacity;
+        ra.n = n;
+        ra.weights = head_half.ptr;
+        ra.experts = experts;
+        ra.expert = expert_ids.ptr;
+        ra.prob = prob.ptr;
+        slot = stage_begin(S_ROUTER);
+        launch_router_forward(ra, router_width, stream);
+        stage_end(slot);
+        LevelSource src;
+        src.table = table;
+        EncodeArgs ea = encode_args(n);
+        ea.expert = expert_ids.ptr;
+        ea.expert_stride = expert_total;
+        slot = stage_begin(S_ENCODE_FWD);
+        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, nullptr, stream);
+        stage_end(slot);
+    }
+
     // ---- optional stage timers (CUDA events on the runtime's stream; off by default)
-    enum Stage { S_INPUT, S_ENCODE_FWD, S_MLP, S_ENCODE_BWD, S_REDUCE, S_ADAM_GRID, S_ADAM_HEADS, S_COUNT };
-    static constexpr const char* STAGE_NAMES[S_COUNT] = {"input_batch", "encode_forward", "mlp_train",
+    enum Stage { S_INPUT, S_ENCODE_FWD, S_ROUTER, S_MLP, S_ENCODE_BWD, S_REDUCE, S_ADAM_GRID, S_ADAM_HEADS, S_COUNT };
+    static constexpr const char* STAGE_NAMES[S_COUNT] = {"input_batch", "encode_forward", "router", "mlp_train",
                                                          "encode_backward", "reduce_partials", "adam_grid", "adam_heads"};
     static constexpr int EVENT_PAIRS = 4096;
     bool profiling = false;
@@ -382,23 +485,37 @@ struct Runtime {
         stage_end(slot);
         LevelSource src;
         src.table = table;
-        const EncodeArgs ea = encode_args(n);
-        slot = stage_begin(S_ENCODE_FWD);
-        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
-        stage_end(slot);
+        EncodeArgs ea = encode_args(n);
+        if (experts) {
+            route_and_encode(n);
+            ea.expert = expert_ids.ptr;
+            ea.expert_stride = expert_total;
+        } else {
+            slot = stage_begin(S_ENCODE_FWD);
+            launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
+            stage_end(slot);
+        }
         const MlpArgs ma = mlp_args(n);
         const int blocks = mlp_tc_blocks(n);
         slot = stage_begin(S_MLP);
-        launch_mlp_tc_train(ma, input_width, router, uniform, blocks, error_flag.ptr, stream);
+        launch_mlp_tc_train(ma, input_width, gate_mode(), uniform, blocks, error_flag.ptr, stream);
         stage_end(slot);
         slot = stage_begin(S_ENCODE_BWD);
         launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, warp_limit, stream);
+        if (experts) {
+            LevelSource rsrc;
+            rsrc.table = router_table;
+            launch_encode_backward(router_encode_args(n), rsrc, router_gvals.ptr, router_grad.ptr, warp_limit, stream);
+        }
         stage_end(slot);
         slot = stage_begin(S_REDUCE);
         launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), stream);
         stage_end(slot);
         if (update == 1) grid_update();
-        else if (update == 0) launch_zero(grid_grad.ptr, total, stream);
+        else if (update == 0) {
+            launch_zero(grid_grad.ptr, total, stream);
+            if (experts) launch_zero(router_grad.ptr, router_total, stream);
+        }
         // update == 2 keeps the grid gradient for inspection; grid_update() consumes it
         ODIE_CUDA(cudaGetLastError());
     }
@@ -408,6 +525,10 @@ struct Runtime {
         const int slot = stage_begin(S_ADAM_GRID);
         launch_adam(grid, grid_half.ptr, grid_m.ptr, grid_v.ptr, grid_steps.ptr, grid_grad.ptr, total, 1.0f / 128.0f, t,
                     float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), true, error_flag.ptr, stream);
+        if (experts)
+            launch_adam(router_grid, router_half.ptr, router_m.ptr, router_v.ptr, router_steps.ptr, router_grad.ptr,
+                        router_total, 1.0f / 128.0f, t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS),
+                        true, error_flag.ptr, stream);
         stage_end(slot);
         ODIE_CUDA(cudaGetLastError());
     }
@@ -417,7 +538,7 @@ struct Runtime {
         const int slot = stage_begin(S_ADAM_HEADS);
         // head gradients carry the 128 x 128 loss scale (odie/native/runtime.cu:59,300-309)
         const float inv = 1.0f / 16384.0f;
-        if (router) {
+        if (gate_count) {
             AdamTables t{table_step[1].ptr, table_bc2.ptr, TABLE_STEPS};
             launch_adam(gate_master, head_half.ptr, head_m.ptr, head_v.ptr, head_steps.ptr, head_grad(), gate_count, inv,
                         t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
@@ -440,12 +561,16 @@ struct Runtime {
         for (long long done = 0; done < n; done += capacity) {
             const long long count = std::min(capacity, n - done);
             launch_coords_range(begin + done, count, image_width, image_height, xy.ptr, stream);
-            const EncodeArgs ea = encode_args(count);
-            launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
+            if (experts) {
+                route_and_encode(count);
+            } else {
+                const EncodeArgs ea = encode_args(count);
+                launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
+            }
             MlpArgs ma = mlp_args(count);
             ma.rgb = out_rgb ? out_rgb + 3 * done : nullptr;
             ma.rgb8 = out_rgb8 ? out_rgb8 + 3 * done : nullptr;
-            launch_mlp_tc_decode(ma, input_width, router, uniform, error_flag.ptr, stream);
+            launch_mlp_tc_decode(ma, input_width, gate_mode(), uniform, error_flag.ptr, stream);
         }
         ODIE_CUDA(cudaGetLastError());
     }
@@ -465,6 +590,12 @@ struct Runtime {
           << ",\"grid_m\":" << (unsigned long long)grid_m.ptr << ",\"grid_v\":" << (unsigned long long)grid_v.ptr
           << ",\"grid_steps\":" << (unsigned long long)grid_steps.ptr << ",\"head_m\":" << (unsigned long long)head_m.ptr
           << ",\"head_v\":" << (unsigned long long)head_v.ptr << ",\"head_steps\":" << (unsigned long long)head_steps.ptr
+          << ",\"experts\":" << experts << ",\"expert_total\":" << expert_total << ",\"router_total\":" << router_total
+          << ",\"router_width\":" << router_width << ",\"router_half\":" << (unsigned long long)router_half.ptr
+          << ",\"router_grad\":" << (unsigned long long)router_grad.ptr << ",\"router_in\":" << (unsigned long long)router_in.ptr
+          << ",\"router_gvals\":" << (unsigned long long)router_gvals.ptr << ",\"prob\":" << (unsigned long long)prob.ptr
+          << ",\"expert_ids\":" << (unsigned long long)expert_ids.ptr << ",\"router_m\":" << (unsigned long long)router_m.ptr
+          << ",\"router_v\":" << (unsigned long long)router_v.ptr << ",\"router_steps\":" << (unsigned long long)router_steps.ptr
           << "}";
         return o.str();
     }
@@ -499,6 +630,7 @@ struct Runtime {
         };
         mix(grid_m.ptr, total); mix(grid_v.ptr, total); mix(grid_steps.ptr, total);
         mix(head_m.ptr, head_count); mix(head_v.ptr, head_count); mix(head_steps.ptr, head_count);
+        if (experts) { mix(router_m.ptr, router_total); mix(router_v.ptr, router_total); mix(router_steps.ptr, router_total); }
         std::ostringstream o;
         o << "{\"hash_fnv1a64\":\"" << hash << "\",\"bytes\":" << bytes << "}";
         return o.str();
@@ -731,6 +863,72 @@ int odie_hash_backward(const float* coords, int64_t n, const uint16_t* upstream,
         a.row_major = true;
         a.width = width;
         a.stride = n;
+        odie::LevelSource src;
+        src.table = odie::hash_levels_table(levels_host, levels);
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
+                        int32_t* expert, float* prob, uint16_t* logits, uint64_t stream) {
+    return guarded([&] {
+        ODIE_REQUIRE(n >= 0, "negative coordinate count");
+        odie::RouterArgs a;
+        a.features = reinterpret_cast<const __half*>(features);
+        a.row_major = true;
+        a.stride = n;
+        a.n = n;
+        a.weights = reinterpret_cast<const __half*>(weights);
+        a.experts = experts;
+        a.expert = expert;
+        a.prob = prob;
+        a.logits = reinterpret_cast<__half*>(logits);
+        odie::launch_router_forward(a, width, reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
+                             const int32_t* expert, const odie_hash_level* levels_host, int levels, int width,
+                             uint16_t* features, uint64_t stream) {
+    return guarded([&] {
+        ODIE_REQUIRE(n >= 0 && expert_stride > 0, "invalid sizes");
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        a.expert = expert;
+        a.expert_stride = expert_stride;
+        odie::LevelSource src;
+        src.table = odie::hash_levels_table(levels_host, levels);
+        odie::launch_encode_forward(a, src, tables, nullptr, reinterpret_cast<__half*>(features), nullptr,
+                                    reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width, int64_t expert_stride,
+                              const int32_t* expert, const odie_hash_level* levels_host, int levels, float* gradient,
+                              int64_t parameter_count, uint64_t stream) {
+    return guarded([&] {
+        ODIE_REQUIRE(n >= 0 && expert_stride > 0 && parameter_count >= 0, "invalid sizes");
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (parameter_count) ODIE_CUDA(cudaMemsetAsync(gradient, 0, size_t(parameter_count) * 4, s));
+        odie::EncodeArgs a;
+        a.coords = coords;
+        a.n = n;
+        a.levels = levels;
+        a.active = levels;
+        a.row_major = true;
+        a.width = width;
+        a.stride = n;
+        a.expert = expert;
+        a.expert_stride = expert_stride;
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
         odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);

@@ -18,6 +18,11 @@ struct FeatureMap {
     int8_t dim_of_level[32];  // features of each level
 };
 
+// Gating of the decoder input: none, the reference's per-level gate
+// (odie/native/runtime.cu:66-75), or a routed expert scaled by its router
+// probability.
+enum GateMode : int { GATE_NONE = 0, GATE_LEVELS = 1, GATE_EXPERTS = 2 };
+
 struct MlpArgs {
     long long n;          // coordinates of this launch
     long long stride;     // pair-major stride of raw/gvals and level stride of vis
@@ -34,6 +39,12 @@ struct MlpArgs {
     float* partials;      // [gridDim.x][head params] weight-gradient partials (training)
     float* rgb;           // [n][3] fp32 decode output (decode)
     uint8_t* rgb8;        // [n][3] u8 decode output (decode)
+    // GATE_EXPERTS: raw holds the routed expert's features; gate_w the router weights
+    const __half* router_in;  // [W/2][stride] half2 router-grid features
+    const float* prob;        // [n] router probability of the chosen expert
+    const int* expert;        // [n] chosen expert
+    __half* router_gvals;     // [W/2][stride] router-grid gradient values (training)
+    int experts;              // live experts
 };
 
 // tcgen05/TMEM fused heads (mlp_tc.cu), decoder input width 16 or 32.  uniform:
@@ -41,9 +52,9 @@ struct MlpArgs {
 // [levels][stride / 32]; stride is a multiple of 128.  A wait that runs out
 // sets *error_flag = 2 and the kernel returns.
 int mlp_tc_blocks(long long n);
-void launch_mlp_tc_train(const MlpArgs& args, int width, bool router, bool uniform, int blocks, int* error_flag,
+void launch_mlp_tc_train(const MlpArgs& args, int width, GateMode gate, bool uniform, int blocks, int* error_flag,
                          cudaStream_t stream);
-void launch_mlp_tc_decode(const MlpArgs& args, int width, bool router, bool uniform, int* error_flag,
+void launch_mlp_tc_decode(const MlpArgs& args, int width, GateMode gate, bool uniform, int* error_flag,
                           cudaStream_t stream);
 
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,

@@ -19,7 +19,8 @@ from .layout import (ADDRESSING_VERSION, COORDINATE_VERSION, LAYOUT_VERSION, ali
                      make_layout, make_node_index, plane_closure)
 
 __all__ = ['router_weights', 'align8', 'plane_closure', 'make_node_index', 'make_layout', 'PackedQuery',
-           'HashQuery', 'Head', 'PackedXYPlanes', 'HashGrid', 'build_model']
+           'HashQuery', 'ExpertHashQuery', 'route', 'Head', 'PackedXYPlanes', 'HashGrid', 'RoutedExperts',
+           'build_model']
 
 
 def router_weights(logits, activation):
@@ -103,6 +104,47 @@ class HashQuery(torch.autograd.Function):
                                                      upstream.shape[1], _hash_table(ctx.records), len(ctx.records),
                                                      gradient.data_ptr(), ctx.count, _stream()), 'odie_hash_backward')
         return None, gradient, None, None
+
+
+class ExpertHashQuery(torch.autograd.Function):
+    """Hashed encoding with one table per expert: row i reads expert[i]'s table (routed experts)."""
+
+    @staticmethod
+    def forward(ctx, coordinates, tables, expert, expert_stride, records, width):
+        n = coordinates.shape[0]
+        features = torch.empty((n, width), dtype=torch.float16, device=coordinates.device)
+        _lib.check(_lib.library().odie_expert_hash_forward(
+            coordinates.data_ptr(), n, tables.data_ptr(), expert_stride, expert.data_ptr(), _hash_table(records),
+            len(records), width, features.data_ptr(), _stream()), 'odie_expert_hash_forward')
+        ctx.save_for_backward(coordinates, expert)
+        ctx.records, ctx.count, ctx.stride = records, tables.numel(), expert_stride
+        ctx.mark_non_differentiable(expert)
+        return features
+
+    @staticmethod
+    def backward(ctx, feature_gradient):
+        coordinates, expert = ctx.saved_tensors
+        upstream = feature_gradient.to(torch.float16).contiguous()
+        gradient = torch.empty(ctx.count, dtype=torch.float32, device=coordinates.device)
+        _lib.check(_lib.library().odie_expert_hash_backward(
+            coordinates.data_ptr(), coordinates.shape[0], upstream.data_ptr(), upstream.shape[1], ctx.stride,
+            expert.data_ptr(), _hash_table(ctx.records), len(ctx.records), gradient.data_ptr(), ctx.count, _stream()),
+            'odie_expert_hash_backward')
+        return None, gradient, None, None, None, None
+
+
+def route(features, router_weights16, experts):
+    """Top-1 routing: (expert int32 [N], probability fp32 [N], fp16 logits [N, 16]), bit-exact (router.cu)."""
+    features = features.to(torch.float16).contiguous()
+    n, width = features.shape
+    expert = torch.empty(n, dtype=torch.int32, device=features.device)
+    prob = torch.empty(n, dtype=torch.float32, device=features.device)
+    logits = torch.empty((n, 16), dtype=torch.float16, device=features.device)
+    weights = router_weights16.to(torch.float16).contiguous()
+    _lib.check(_lib.library().odie_router_forward(features.data_ptr(), n, width, weights.data_ptr(), int(experts),
+                                                  expert.data_ptr(), prob.data_ptr(), logits.data_ptr(), _stream()),
+               'odie_router_forward')
+    return expert, prob, logits
 
 
 class Head(nn.Module):
@@ -351,7 +393,70 @@ class HashGrid(nn.Module):
                     layout_version='hash-grid-v1', addressing_version='instant-ngp-spatial-hash')
 
 
+class RoutedExperts(nn.Module):
+    """Routed multi-expert hash-grid encoding with a shared decoder (no reference counterpart).
+
+    A coarse shared hash grid (``router_encoding``) feeds the router MLP
+    (W -> 32 -> 32 -> 16 logits, top-1 over ``experts``); coordinate i is then
+    encoded by its expert's own hash grid (``hash_encoding``; the tables of all
+    experts are one flat fp32 parameter, expert-major) and the features, scaled
+    by the router probability rounded to fp16, go through the shared decoder
+    (W -> 64 -> 64 -> 3).  Training runs in the native runtime; this module's
+    forward is the evaluation/decode path.
+    """
+
+    def __init__(self, config):
+        super().__init__()
+        self.config = deepcopy(config)
+        self.experts = int(config['experts'])
+        if not 1 <= self.experts <= 16:
+            raise ValueError('experts must be within 1..16')
+        encoding, router_encoding = config['hash_encoding'], config['router_encoding']
+        self.records, self.expert_total = hash_levels(encoding)
+        self.router_records, router_total = hash_levels(router_encoding)
+        self.n_levels = self.active_prefix = int(encoding['n_levels'])
+        self.gate_coarse_levels_K = 0
+        self.input_width = (self.n_levels * int(encoding['n_features_per_level']) + 15) // 16 * 16
+        router_width = (int(router_encoding['n_levels']) * int(router_encoding['n_features_per_level']) + 15) // 16 * 16
+        if router_width != self.input_width:
+            raise ValueError('router and expert encodings must have the same width')
+        seed = int(config['seed'])
+        generator = torch.Generator().manual_seed(seed)
+        self.grid = nn.Parameter(((torch.rand(self.experts * self.expert_total, generator=generator) * 2 - 1)
+                                  * float(config.get('grid_init', 1e-4))).cuda())
+        self.router_grid = nn.Parameter(((torch.rand(router_total, generator=generator) * 2 - 1)
+                                         * float(config.get('router_init', 1e-1))).cuda())
+        self.gate = Head(self.input_width, 16, 32, 2, (seed + 2000003) % 2**31)  # the router MLP
+        self.decoder = Head(self.input_width, 3, 64, 2, (seed + 4000037) % 2**31)
+        self.supports = []
+
+    def set_active_prefix(self, prefix):
+        if prefix != self.n_levels:
+            raise ValueError('routed experts always train every level')
+
+    def route(self, coordinates):
+        with torch.no_grad():
+            features = HashQuery.apply(coordinates.contiguous(), self.router_grid, self.router_records, self.input_width)
+            return route(features, self.gate.params, self.experts)
+
+    def forward(self, coordinates):
+        expert, prob, _ = self.route(coordinates)
+        features = ExpertHashQuery.apply(coordinates.contiguous(), self.grid, expert, self.expert_total, self.records,
+                                         self.input_width)
+        gated = features * prob.to(torch.float16)[:, None]
+        return self.decoder(gated).float()[:, :3]
+
+    def storage_stats(self):
+        grid, router_grid = self.grid.numel(), self.router_grid.numel()
+        heads = self.gate.params.numel() + self.decoder.params.numel()
+        return dict(actual_params=grid + router_grid + heads, grid_params=grid, router_grid_params=router_grid,
+                    head_params=heads, experts=self.experts, fp16_parameter_payload_bytes=2 * (grid + router_grid + heads),
+                    input_width=self.input_width, addressing_version='instant-ngp-spatial-hash')
+
+
 def build_model(config, supports, plane_dims, plane_node_caps, **kwargs):
+    if config['representation'] == 'routed_experts':
+        return RoutedExperts(config)
     if config['representation'] == 'hash_grid':
         return HashGrid(config, supports, plane_dims, plane_node_caps)
     return PackedXYPlanes(config, supports, plane_dims, plane_node_caps, **kwargs)

@@ -52,7 +52,9 @@ class NativeOptimizer:
         # the reference trains on a dedicated stream (odie/train.py:73-75); CUDA graphs need a non-default one
         current = torch.cuda.current_stream()
         self.stream = torch.cuda.Stream() if current == torch.cuda.default_stream() else current
-        self.param_groups = [dict(name='grid', params=planes, lr=config['grid_lr'])]
+        experts = config['representation'] == 'routed_experts'
+        grid_params = planes + [model.router_grid] if experts else planes
+        self.param_groups = [dict(name='grid', params=grid_params, lr=config['grid_lr'])]
         if model.gate is not None:
             self.param_groups.append(dict(name='gate', params=list(model.gate.parameters()), lr=config['gate_lr']))
         self.param_groups.append(dict(name='decoder', params=list(model.decoder.parameters()), lr=config['decoder_lr']))
@@ -67,8 +69,11 @@ class NativeOptimizer:
             settings['gate'] = model.gate.params.data_ptr()
         if head_grad is not None:
             settings['head_grad'] = head_grad.data_ptr()
-        if config['representation'] == 'hash_grid':
+        if config['representation'] in ('hash_grid', 'routed_experts'):
             settings['hash_encoding'] = config['hash_encoding']
+        if experts:
+            settings.update(experts=model.experts, router_encoding=config['router_encoding'], router=0,
+                            router_grid=model.router_grid.data_ptr())
         self.handle = self.lib.odie_create(json.dumps(settings).encode())
         if not self.handle:
             raise RuntimeError(_lib.error())
@@ -79,7 +84,7 @@ class NativeOptimizer:
 
     def current_settings(self):
         rates = {g['name'] + '_lr': float(g['lr']) for g in self.param_groups}
-        if self.config['representation'] == 'hash_grid':
+        if self.config['representation'] in ('hash_grid', 'routed_experts'):
             return dict(active=self.model.active_prefix, **rates)
         return dict(active=self.model.active_prefix,
                     **{k: getattr(self.model, k).data_ptr() for k in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap')},

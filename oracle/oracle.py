@@ -347,3 +347,84 @@ def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, l
     result['head_grad'] = np.concatenate([g.reshape(-1) for g in gate_grad + dec_grad]) if (gate_grad or dec_grad) \
         else np.zeros(0)
     return result
+
+
+# ---------------------------------------------------------------- routed experts
+ROUTER_SHAPES = lambda width: [(32, width), (32, 32), (16, 32)]  # noqa: E731  router W1, W2, W3
+
+
+def expert_query(xy, tables16, expert, expert_stride, records, width):
+    """Per-coordinate expert tables: rows routed to expert e read tables16[e * stride : (e + 1) * stride]."""
+    out = np.zeros((xy.shape[0], width), dtype=np.float16)
+    for e in np.unique(expert):
+        rows = np.nonzero(expert == e)[0]
+        out[rows] = hash_query(xy[rows], tables16[e * expert_stride:(e + 1) * expert_stride], records, width)
+    return out
+
+
+def expert_backward(xy, upstream, expert, expert_stride, records, params):
+    grad = np.zeros(params, dtype=np.float64)
+    for e in np.unique(expert):
+        rows = np.nonzero(expert == e)[0]
+        grad[e * expert_stride:(e + 1) * expert_stride] += hash_backward(xy[rows], upstream[rows], records,
+                                                                         expert_stride)
+    return grad
+
+
+def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, experts, router_table, router_records,
+                           router_params, decoder_params, width=32):
+    """One routed-expert training step on the CPU (the restatement the CUDA path is checked against).
+
+    Routing: router grid features -> router MLP with fp32 fma chains (bit-exact
+    definition, `router`), top-1 expert, probability p.  Decoder input =
+    fp16(expert features x fp16(p)).  Decoder, loss and fp16 rounding points as
+    in `reference_step`.  Backward: v = fp16(dz / 128); expert values =
+    fp16(v x fp16(p)); dp = sum_c v_c f_c; dz_j = dp p (delta_je - p_j) with p_j
+    the softmax of the fp16 logits; da = fp16(fp16(dz_j) x 128); router backward
+    to dR; router values = fp16(dR / 128).  Head gradients (scale 16384) in the
+    order router W1, W2, W3 | decoder W1, W2, W3; grid gradients (scale 128) of
+    the expert tables and of the router grid.
+    """
+    height, img_width = shape
+    xy = coords(ids, img_width, height)
+    target = target_u8(rgb, ids)
+    rin = hash_query(xy, router_table.astype(np.float16), router_records, width)
+    r1, r2, r3 = (_f16(w) for w in head_matrices(router_params, ROUTER_SHAPES(width)))
+    expert, prob, logits = router(rin, r1.reshape(-1), r2.reshape(-1), r3.reshape(-1), 32, experts)
+    feats = expert_query(xy, tables.astype(np.float16), expert, expert_stride, records, width)
+    ph = prob.astype(np.float16)
+    weighted = _f16(feats.astype(np.float64) * ph.astype(np.float64)[:, None])
+    d1, d2, d3 = (_f16(w) for w in head_matrices(decoder_params, head_shapes(width, 64, 2, 16)))
+    h1 = _f16(np.maximum(_mm(weighted, d1.T), 0))
+    h2 = _f16(np.maximum(_mm(h1, d2.T), 0))
+    out = _f16(_mm(h2, d3.T))
+    dy, squares = loss_grad(out, target)
+    dh2 = _f16(np.where(h2 > 0, _mm(dy, d3), 0))
+    dh1 = _f16(np.where(h1 > 0, _mm(dh2, d2), 0))
+    dz = _f16(_mm(dh1, d1))
+    v = _f16(dz.astype(np.float64) / 128)
+    values = _f16(v.astype(np.float64) * ph.astype(np.float64)[:, None])
+    dp = (v.astype(np.float64) * feats.astype(np.float64)).sum(1)
+    z = logits.astype(np.float64)[:, :experts]
+    ez = np.exp(z - z.max(1, keepdims=True))
+    pj = ez / ez.sum(1, keepdims=True)
+    onehot = np.zeros_like(pj)
+    onehot[np.arange(len(expert)), expert] = 1
+    da = np.zeros((len(ids), 16))
+    da[:, :experts] = _f16(dp[:, None] * prob.astype(np.float64)[:, None] * (onehot - pj)).astype(np.float64) * 128
+    da = _f16(da)
+    gh1 = _f16(np.maximum(_mm(rin, r1.T), 0))
+    gh2 = _f16(np.maximum(_mm(gh1, r2.T), 0))
+    dgh2 = _f16(np.where(gh2 > 0, _mm(da, r3), 0))
+    dgh1 = _f16(np.where(gh1 > 0, _mm(dgh2, r2), 0))
+    dr = _f16(_mm(dgh1, r1))
+    router_values = _f16(dr.astype(np.float64) / 128)
+    f64 = lambda a: a.astype(np.float64)  # noqa: E731
+    head = [f64(dgh1).T @ f64(rin), f64(dgh2).T @ f64(gh1), f64(da).T @ f64(gh2),
+            f64(dh1).T @ f64(weighted), f64(dh2).T @ f64(h1), f64(dy).T @ f64(h2)]
+    return dict(xy=xy, target=target, router_features=rin, expert=expert, prob=prob, logits=logits, raw=feats,
+                weighted=weighted, out=out, dy=dy, squares=squares, dz=dz, values=values.astype(np.float32),
+                dp=dp, da=da, router_values=router_values.astype(np.float32),
+                grid_grad=expert_backward(xy, values, expert, expert_stride, records, tables.size),
+                router_grid_grad=hash_backward(xy, router_values, router_records, router_table.size),
+                head_grad=np.concatenate([g.reshape(-1) for g in head]))

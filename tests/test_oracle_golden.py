@@ -212,3 +212,28 @@ def test_oracle_router_argmax_and_softmax():
     assert np.array_equal(expert, z.argmax(1))
     soft = np.exp(z - z.max(1, keepdims=True))
     np.testing.assert_allclose(prob, 1 / soft.sum(1), rtol=1e-5)
+
+
+def test_oracle_routed_expert_step_consistency():
+    """The routed-expert restatement: routing follows its logits, values follow p, scatters land in the chosen tables."""
+    from odie_b200.layout import hash_levels
+    rng = np.random.default_rng(4)
+    enc = dict(n_levels=16, n_features_per_level=2, log2_hashmap_size=8, base_resolution=4, per_level_scale=1.5)
+    renc = dict(n_levels=16, n_features_per_level=2, log2_hashmap_size=6, base_resolution=2, per_level_scale=1.2)
+    records, stride = hash_levels(enc)
+    rrecords, rtotal = hash_levels(renc)
+    experts, shape = 3, (9, 11)
+    tables = (rng.standard_normal(experts * stride) * .05).astype(np.float32)
+    router_table = (rng.standard_normal(rtotal) * .5).astype(np.float32)
+    router_params = (rng.standard_normal(32 * 32 + 32 * 32 + 16 * 32) * .2).astype(np.float32)
+    decoder_params = (rng.standard_normal(32 * 64 + 64 * 64 + 16 * 64) * .1).astype(np.float32)
+    rgb = rng.integers(0, 256, (shape[0] * shape[1], 3), dtype=np.uint8)
+    ids = rng.integers(0, shape[0] * shape[1], 200)
+    ref = oracle.reference_step_experts(rgb, ids, shape, tables, records, stride, experts, router_table, rrecords,
+                                        router_params, decoder_params)
+    z = ref['logits'].astype(np.float32)[:, :experts]
+    assert np.array_equal(ref['expert'], z.argmax(1))
+    assert ref['head_grad'].size == 32 * 32 + 32 * 32 + 16 * 32 + 32 * 64 + 64 * 64 + 16 * 64
+    touched = np.nonzero(ref['grid_grad'])[0] // stride
+    assert set(np.unique(touched)) <= set(np.unique(ref['expert']))
+    assert np.isfinite(ref['router_grid_grad']).all() and np.abs(ref['router_grid_grad']).sum() > 0
