@@ -1,6 +1,11 @@
 """Benchmark of the ODIE hot path on B200: train coords/s (fwd + bwd + Adam) and decode Gpix/s.
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2-planes]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2-experts|c2-planes]
+
+Workloads (odie_b200/workloads.py): c2-experts is BASELINE config 2 (16 routed
+hash-grid experts, top-1 router on a coarse shared grid, shared 64-wide head,
+2040 x 1356 u8 image, 2^20 coords per step); c2-planes is the reference's own
+packed-plane method on the same image and batch.
 
 One JSON line on rank 0.  `value` is whole-job coords/s with inputs resident in
 HBM (device-timed with CUDA events, max over ranks); `e2e` is the same metric
@@ -8,7 +13,7 @@ through the public API with the step's pixel ids copied from pinned host memory
 and the loss read back every step.  Multi-GPU: one process per GPU (torchrun),
 each rank trains the model of its own row band of the image (weak scaling),
 and only the shared head gradients cross GPUs (NCCL all-reduce).  The
-`--impl reference` arm times the CPU restatement of the reference step
+`--impl reference` arm times the CPU restatement of the step
 (oracle/cpu_step.py; the reference has no CPU path of its own).
 """
 import argparse
@@ -37,17 +42,55 @@ def parse():
     p.add_argument('--steps', type=int, default=20)
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
-    p.add_argument('--workload', default='c2-planes')
+    p.add_argument('--workload', default='c2-experts', choices=['c2-experts', 'c2-planes'])
     p.add_argument('--batch', type=int, default=BATCH)
+    p.add_argument('--sampling', default='stratified', choices=['stratified', 'uniform'],
+                   help='stratified: the reference default (odie/config.py:20, odie/data.py:63-80), one pixel per '
+                        'square stratum, strata in raster order; uniform: iid uniform pixel ids')
     p.add_argument('--no-cpu-baseline', action='store_true')
     return p.parse_args()
 
 
 def workload(name, rank, ranks, batch):
+    """Model, target, planes, config and image of this rank's band of a workload."""
     from odie_b200 import workloads
-    if name != 'c2-planes':
-        raise SystemExit(f'unknown workload {name}')
-    return workloads.c2_planes(batch=batch, band=(rank, ranks))
+    if name == 'c2-experts':
+        config, rgb, shape = workloads.c2_experts(batch=batch, band=(rank, ranks))
+        model, target, planes = workloads.build_expert_model(config, rgb)
+        return dict(config=config, rgb=rgb, shape=shape, model=model, target=target, planes=planes)
+    config, supports, dims, caps, rgb, shape = workloads.c2_planes(batch=batch, band=(rank, ranks))
+    model, target, planes = workloads.build_plane_model(config, supports, dims, caps, rgb)
+    return dict(config=config, rgb=rgb, shape=shape, model=model, target=target, planes=planes, supports=supports,
+                dims=dims, caps=caps)
+
+
+def cpu_step_of(name, batch):
+    """The oracle's CPU restatement of one training step of the workload (same layout, seeded weights)."""
+    from oracle.cpu_step import CpuExpertStep, CpuStep, hash_levels_for_cpu, plane_levels_for_cpu
+    from odie_b200 import layout as host_layout
+    from odie_b200 import workloads
+    rng = np.random.default_rng(0)
+    if name == 'c2-experts':
+        config, rgb, shape = workloads.c2_experts(batch=batch)
+        records, stride = host_layout.hash_levels(config['hash_encoding'])
+        router_records, router_total = host_layout.hash_levels(config['router_encoding'])
+        width = 32
+        step = CpuExpertStep(shape, rgb.numpy(), hash_levels_for_cpu(records), stride, config['experts'],
+                             hash_levels_for_cpu(router_records),
+                             ((rng.random(config['experts'] * stride, dtype=np.float32) * 2 - 1) * 1e-4),
+                             ((rng.random(router_total, dtype=np.float32) * 2 - 1) * 0.1),
+                             (rng.standard_normal(32 * width + 32 * 32 + 16 * 32) * .2).astype(np.float32),
+                             (rng.standard_normal(width * 64 + 64 * 64 + 1024) * .1).astype(np.float32), width)
+        return step, shape
+    config, supports, dims, caps, rgb, shape = workloads.c2_planes(batch=batch)
+    lay = host_layout.make_layout(config, supports, dims, caps)
+    levels = plane_levels_for_cpu(lay['descriptors'].numpy(), lay['node_bitmap'].numpy(), lay['node_prefix'].numpy(),
+                                  lay['bitmap'].numpy())
+    width = (lay['input_width'] + 15) // 16 * 16
+    step = CpuStep(shape, rgb.numpy(), levels, (rng.standard_normal(lay['params']) * 1e-3).astype(np.float32),
+                   (rng.standard_normal(width * 32 + 512) * .1).astype(np.float32),
+                   (rng.standard_normal(width * 64 + 64 * 64 + 1024) * .1).astype(np.float32), width)
+    return step, shape
 
 
 class Clocks:
@@ -90,18 +133,70 @@ class Clocks:
                 'reasons': reasons, 'samples': len(self.samples)}
 
 
-def algorithmic(stage, levels, features, n, params, head_flops):
-    """Algorithmic bytes (or FLOPs) of one launch of a stage, per the per-unit figures in DESIGN.md."""
-    L, F = levels, features
+def algorithmic(name, stage, model, n):
+    """(bound, algorithmic bytes or FLOPs of one step's launches of a stage) from the per-unit figures:
+    encode forward 8 + 4 L F 2 + L F 2 B/coord per encoding (fp16 tables and features), encode backward
+    8 + L F 2 + 8 L F 4 B/coord per encoding (an fp32 atomic = read + write), heads 6 x sum(in x out)
+    FLOP/coord, router 64 + 8 B/coord, Adam 30 B/param."""
+    L, F = model.n_levels, 2
+    encodings = 2 if name == 'c2-experts' else 1  # the router grid and the routed expert
+    decoder = 32 * 64 + 64 * 64 + 64 * 16
     if stage == 'encode_forward':
-        return 'hbm', (8 + 4 * L * F * 2 + L * F * 2) * n
+        return 'hbm', encodings * (8 + 4 * L * F * 2 + L * F * 2) * n
     if stage == 'encode_backward':
-        return 'hbm', (8 + L * F * 2 + 8 * L * F * 4) * n
+        return 'hbm', encodings * (8 + L * F * 2 + 8 * L * F * 4) * n
     if stage == 'mlp_train':
-        return 'tensor', head_flops * n
+        gate = 32 * 32 + 32 * 32 + 16 * 32 if name == 'c2-experts' else 32 * 32 + 32 * 16
+        return 'tensor', 6 * (gate + decoder) * n
+    if stage == 'router':
+        return 'hbm', (64 + 8) * n
     if stage == 'adam_grid':
+        params = model.grid.numel() + (model.router_grid.numel() if name == 'c2-experts' else 0)
         return 'hbm', 30 * params
     return 'hbm', None
+
+
+def traffic_of(name, stage):
+    """DRAM bytes per step of a stage from the committed ncu summary (profiles/dram_traffic.json), or None."""
+    path = ROOT / 'profiles' / 'dram_traffic.json'
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(name, {}).get(stage)
+    return entry['bytes_per_step'] if entry else None
+
+
+def l2_probe(lib, table_mib=32, operations=1 << 27):
+    """Measured L2 throughput for random 4/16-byte loads and 4/8-byte fp32 reductions over an L2-resident table
+    (odie_l2_probe): the roofline of the gather and scatter kernels, whose tables all fit in L2."""
+    table = torch.zeros((table_mib << 20) // 4, device='cuda')
+    sink = torch.zeros(1, device='cuda')
+    stream = torch.cuda.current_stream()
+    names = ['load4', 'load16', 'red4', 'red8']
+    out = {'table_mib': table_mib, 'operations': operations, 'gops': {}, 'gbs': {}}
+    for mode, name in enumerate(names):
+        best = float('inf')
+        for _ in range(4):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            rc = lib.odie_l2_probe(table.data_ptr(), table.numel() * 4, mode, operations, sink.data_ptr(),
+                                   stream.cuda_stream)
+            end.record()
+            if rc:
+                raise RuntimeError('odie_l2_probe failed')
+            torch.cuda.synchronize()
+            best = min(best, start.elapsed_time(end) / 1e3)
+        gops = operations / best / 1e9
+        out['gops'][name] = gops
+        out['gbs'][name] = gops * {'load4': 4, 'load16': 16, 'red4': 8, 'red8': 16}[name]  # a reduction reads + writes
+    return out
+
+
+def l2_ops(name, stage, model, n):
+    """Table accesses of one step of a gather/scatter stage: 4 corners x levels per coordinate and encoding."""
+    encodings = 2 if name == 'c2-experts' else 1
+    if stage in ('encode_forward', 'encode_backward'):
+        return encodings * 4 * model.n_levels * n
+    return None
 
 
 def peaks():
@@ -113,21 +208,10 @@ def peaks():
 
 
 def cpu_baseline(args, budget=12.0):
-    """The CPU restatement of the reference step on this host's cores (bounded sample)."""
-    from oracle.cpu_step import CpuStep, plane_levels_for_cpu
-    from odie_b200 import layout as host_layout
-    config, supports, dims, caps, rgb, shape = workload(args.workload, 0, 1, args.batch)
+    """The CPU restatement of the step on this host's cores (bounded sample)."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    lay = host_layout.make_layout(config, supports, dims, caps)
-    levels = plane_levels_for_cpu(lay['descriptors'].numpy(), lay['node_bitmap'].numpy(), lay['node_prefix'].numpy(),
-                                  lay['bitmap'].numpy())
-    rng = np.random.default_rng(0)
-    grid = (rng.standard_normal(lay['params']) * 1e-3).astype(np.float32)
-    width = (lay['input_width'] + 15) // 16 * 16
-    gate = (rng.standard_normal(width * 32 + 32 * 16) * .1).astype(np.float32)
-    decoder = (rng.standard_normal(width * 64 + 64 * 64 + 64 * 16) * .1).astype(np.float32)
-    step = CpuStep(shape, rgb.numpy(), levels, grid, gate, decoder, width)
+    step, shape = cpu_step_of(args.workload, args.batch)
     sample = 1 << 14
     pixels = shape[0] * shape[1]
     g = torch.Generator().manual_seed(1)
@@ -147,19 +231,9 @@ def run_reference(args):
     if rank != 0:
         return
     steps, coords, seconds = 0, 0, 0.0
-    from oracle.cpu_step import CpuStep, plane_levels_for_cpu
-    from odie_b200 import layout as host_layout
-    config, supports, dims, caps, rgb, shape = workload(args.workload, 0, 1, args.batch)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    lay = host_layout.make_layout(config, supports, dims, caps)
-    levels = plane_levels_for_cpu(lay['descriptors'].numpy(), lay['node_bitmap'].numpy(), lay['node_prefix'].numpy(),
-                                  lay['bitmap'].numpy())
-    rng = np.random.default_rng(0)
-    width = (lay['input_width'] + 15) // 16 * 16
-    step = CpuStep(shape, rgb.numpy(), levels, (rng.standard_normal(lay['params']) * 1e-3).astype(np.float32),
-                   (rng.standard_normal(width * 32 + 512) * .1).astype(np.float32),
-                   (rng.standard_normal(width * 64 + 64 * 64 + 1024) * .1).astype(np.float32), width)
+    step, shape = cpu_step_of(args.workload, args.batch)
     sample = 1 << 14
     g = torch.Generator().manual_seed(2)
     pixels = shape[0] * shape[1]
@@ -201,17 +275,23 @@ def main():
     from odie_b200 import workloads
     from odie_b200.native_backend import NativeOptimizer
     lib = _lib.library()
-    config, supports, dims, caps, rgb, shape = workload(args.workload, rank, world, args.batch)
-    model, target, planes = workloads.build_plane_model(config, supports, dims, caps, rgb)
+    w = workload(args.workload, rank, world, args.batch)
+    config, shape, model = w['config'], w['shape'], w['model']
     head_grad = None
     if world > 1:
-        width = (model.input_width + 15) // 16 * 16
-        head_grad = torch.zeros(width * 32 + 512 + width * 64 + 64 * 64 + 1024, device='cuda')
-    opt = NativeOptimizer(model, target, shape, config, planes, batch=args.batch, head_grad=head_grad)
+        # the heads are shared: every rank starts from rank 0's weights and applies the same summed gradient
+        for head in (model.gate, model.decoder):
+            dist.broadcast(head.params.data, 0)
+        head_grad = torch.zeros(model.gate.params.numel() + model.decoder.params.numel(), device='cuda')
+    opt = NativeOptimizer(model, w['target'], shape, config, w['planes'], batch=args.batch, head_grad=head_grad)
     pixels = shape[0] * shape[1]
     gen = torch.Generator(device='cuda').manual_seed(1729 + rank)
     total_steps = args.warmup + args.steps
-    ids = torch.randint(0, pixels, (total_steps, args.batch), device='cuda', generator=gen)
+    if args.sampling == 'stratified':
+        from odie_b200.data import stratified_batches
+        ids = torch.stack(list(stratified_batches(shape, args.batch, gen, steps=total_steps)))
+    else:
+        ids = torch.randint(0, pixels, (total_steps, args.batch), device='cuda', generator=gen)
 
     def step(batch_ids):
         if world == 1:
@@ -234,10 +314,12 @@ def main():
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clocks:
         barrier()
+        launches_before = lib.odie_launch_count()
         start.record()
         for k in range(args.steps):
             step(ids[args.warmup + k])
         end.record()
+        launches = lib.odie_launch_count() - launches_before
         barrier()
     ms = start.elapsed_time(end)
     report = json.loads(lib.odie_profile_report(opt.handle))
@@ -286,23 +368,37 @@ def main():
         dist.all_reduce(d_ms, op=dist.ReduceOp.MAX)
     decode_gpix = world * pixels * repeats / (float(d_ms) / 1e3) / 1e9
 
+    probe = l2_probe(lib) if rank == 0 else None
     if rank == 0:
         hbm, tensor_peak, peak_kind = peaks()
         stages = {k: v for k, v in report.items() if v['launches']}
         dominant = max(stages, key=lambda k: stages[k]['ms'])
         total_ms = sum(v['ms'] for v in stages.values())
-        width = (model.input_width + 15) // 16 * 16
-        head_flops = 6 * (width * 32 + 32 * 16 + width * 64 + 64 * 64 + 64 * 16)
-        bound, work = algorithmic(dominant, model.n_levels, 2, args.batch, model.grid.numel(), head_flops)
-        per_launch_s = stages[dominant]['ms'] / stages[dominant]['launches'] / 1e3
+        bound, work = algorithmic(args.workload, dominant, model, args.batch)
+        step_s = stages[dominant]['ms'] / args.steps / 1e3  # the stage's launches of one step
         if bound == 'tensor':
-            achieved, peak, unit = work / per_launch_s / 1e12, tensor_peak, 'TFLOP/s'
+            achieved, peak, unit = work / step_s / 1e12, tensor_peak, 'TFLOP/s'
         else:
-            achieved, peak, unit = (work / per_launch_s / 1e9 if work else None), hbm, 'GB/s'
+            achieved, peak, unit = (work / step_s / 1e9 if work else None), hbm, 'GB/s'
+        per_stage = {}
+        for k, v in stages.items():
+            b, wk = algorithmic(args.workload, k, model, args.batch)
+            sec = v['ms'] / args.steps / 1e3
+            per_stage[k] = {'ms_per_step': v['ms'] / args.steps, 'launches_per_step': v['launches'] / args.steps,
+                            'achieved': (wk / sec / (1e12 if b == 'tensor' else 1e9)) if wk else None,
+                            'unit': 'TFLOP/s' if b == 'tensor' else 'GB/s'}
+            ops = l2_ops(args.workload, k, model, args.batch)
+            if ops:
+                ref = probe['gops']['load4' if k == 'encode_forward' else 'red8']
+                per_stage[k]['l2'] = {'table_accesses_per_step': ops, 'achieved_gops': ops / sec / 1e9,
+                                      'probe_gops': ref, 'frac': ops / sec / 1e9 / ref,
+                                      'probe': 'load4' if k == 'encode_forward' else 'red8'}
         roofline = {'kernel': dominant, 'bound': bound, 'achieved': achieved, 'peak': peak, 'unit': unit,
-                    'frac': (achieved / peak) if achieved else None, 'traffic': None, 'peak_source': peak_kind,
-                    'share': stages[dominant]['ms'] / total_ms,
-                    'stages_ms_per_step': {k: v['ms'] / args.steps for k, v in stages.items()}}
+                    'frac': (achieved / peak) if achieved else None,
+                    'traffic': traffic_of(args.workload, dominant), 'traffic_unit': 'DRAM bytes per step',
+                    'algorithmic_per_step': work, 'peak_source': peak_kind,
+                    'l2': per_stage[dominant].get('l2'), 'l2_probe': probe,
+                    'share': stages[dominant]['ms'] / total_ms, 'stages': per_stage}
         base = None
         if world == 1 and not args.no_cpu_baseline:
             base = cpu_baseline(args)
@@ -311,10 +407,13 @@ def main():
                 'vs_baseline': None, 'dtype': 'f16 (fp32 masters, fp32 accumulate)', 'data': 'synthetic',
                 'config': {'workload': args.workload, 'image_hw': list(shape), 'global_batch': world * args.batch,
                            'batch_per_gpu': args.batch, 'levels': model.n_levels, 'grid_params': model.grid.numel(),
+                           'experts': getattr(model, 'experts', None),
                            'parallelism': f'dp{world} (row bands, head all-reduce)',
+                           'sampling': args.sampling + (' (reference default, odie/config.py:20)'
+                                                        if args.sampling == 'stratified' else ' (iid)'),
                            'l2': 'per-step inputs/activations (~200 MB) larger than L2; model tables L2-resident'},
                 'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': args.batch * 8, 'd2h_bytes_per_step': 8},
-                'gpu_launches': 8 * args.steps, 'roofline': roofline, 'cpu_baseline': base,
+                'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base,
                 'decode': {'value': decode_gpix, 'unit': 'Gpix/s', 'pixels_per_rank': pixels},
                 'loss_first_last': [float(losses[0]), float(losses[-1])], 'clocks': clocks.summary()}
         print(json.dumps(line), flush=True)

@@ -37,6 +37,10 @@ extern "C" {
  * ------------------------------------------------------------------------ */
 /* Thread-local message of the last failure. runtime.cu:320 */
 ODIE_API const char* odie_error(void);
+/* Kernels this library has launched since it was loaded, all threads and
+ * devices (no reference counterpart; read before and after a region to count
+ * its launches). */
+ODIE_API long long odie_launch_count(void);
 /* Create a runtime for one stream; NULL on failure. runtime.cu:321 */
 ODIE_API void* odie_create(const char* json);
 /* One fwd/bwd(/Adam when update) step over n int64 pixel ids. runtime.cu:322 */
@@ -153,6 +157,16 @@ ODIE_API int odie_expert_hash_forward(const float* coords, int64_t n, const floa
 ODIE_API int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
                    int64_t expert_stride, const int32_t* expert, const odie_hash_level* levels, int level_count,
                    float* gradient, int64_t parameter_count, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * L2 probe (measurement; no reference counterpart): `operations` random
+ * accesses over `table` (table_bytes in 4 KiB..64 MiB, so it stays in L2):
+ * mode 0 = 4-byte loads, 1 = 16-byte loads, 2 = 4-byte fp32 reductions,
+ * 3 = 8-byte fp32x2 reductions (each adds 1e-30).  sink: one float, written
+ * only to keep the loads alive.  Time it with CUDA events on `stream`.
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_l2_probe(float* table, int64_t table_bytes, int mode, int64_t operations, float* sink,
+                   uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * Tile top-k allocation (no reference counterpart).

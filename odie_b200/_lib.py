@@ -21,6 +21,7 @@ class HashLevel(C.Structure):
 
 SIGNATURES = {
     'odie_error': (C.c_char_p, []),
+    'odie_launch_count': (C.c_longlong, []),
     'odie_create': (P, [C.c_char_p]),
     'odie_step': (I32, [P, U64, I32, I32]),
     'odie_step_grads': (I32, [P, U64, I32, I32]),
@@ -46,6 +47,7 @@ SIGNATURES = {
     'selection_chunk': (I32, [P, I32, I32, I32, I32, B, P, P, P, P, P, P, I32, I32, P, P, U64]),
     'odie_tile_topk': (I32, [P, P, I32, I32, I32, I32, P, P, P, P, U64]),
     'odie_router_forward': (I32, [P, I64, I32, P, I32, P, P, P, U64]),
+    'odie_l2_probe': (I32, [P, I64, I32, I64, P, U64]),
     'odie_expert_hash_forward': (I32, [P, I64, P, I64, P, C.POINTER(HashLevel), I32, I32, P, U64]),
     'odie_expert_hash_backward': (I32, [P, I64, P, I32, I64, P, C.POINTER(HashLevel), I32, P, I64, U64]),
     'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),

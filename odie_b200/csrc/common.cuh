@@ -29,6 +29,7 @@ struct CudaError : std::runtime_error {
     } while (0)
 
 void set_error(const std::string& message);  // thread-local, read by odie_error()
+void note_launch(int kernels = 1);          // counts this library's kernel launches (odie_launch_count)
 int sm_count();                              // cached multiprocessor count of the current device
 
 inline unsigned blocks_for(long long n, int threads) { return unsigned((n + threads - 1) / threads); }

@@ -7,8 +7,8 @@
 // are bit-identical because the reference rounds every fp32 corner value to
 // fp16 before the chain).  The backward scatter-adds w_k * g into an fp32
 // gradient (odie/packed_kernels.cu:66-88, odie/native/runtime.cu:111-143) with
-// 8-byte vector reductions for F=2 and warp aggregation of equal addresses on
-// coarse levels.
+// 8-byte vector reductions for F=2, one thread per coordinate in a scrambled
+// visiting order, and shared-memory pre-aggregation of coarse levels.
 #include "encode.cuh"
 
 namespace odie {
@@ -134,78 +134,57 @@ __device__ __forceinline__ float upstream_value(const __half* __restrict__ up, c
     return __half2float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
 }
 
-// Sum the values of lanes that target the same address; the lowest lane issues
-// one reduction for the group (the reference's labeled_partition + reduce,
-// odie/native/runtime.cu:137-139).
-__device__ __forceinline__ void aggregated_red2(float* address, float a, float b) {
-    const unsigned active = __activemask();
-    const unsigned peers = __match_any_sync(active, reinterpret_cast<unsigned long long>(address));
-    float sa = 0.0f, sb = 0.0f;
-    unsigned m = peers;
-    while (m) {
-        const int src = __ffs(m) - 1;
-        m &= m - 1;
-        sa += __shfl_sync(peers, a, src);
-        sb += __shfl_sync(peers, b, src);
-    }
-    if ((threadIdx.x & 31) == __ffs(peers) - 1) red_add_v2(address, sa, sb);
-}
-__device__ __forceinline__ void aggregated_red1(float* address, float a) {
-    const unsigned active = __activemask();
-    const unsigned peers = __match_any_sync(active, reinterpret_cast<unsigned long long>(address));
-    float sa = 0.0f;
-    unsigned m = peers;
-    while (m) {
-        const int src = __ffs(m) - 1;
-        m &= m - 1;
-        sa += __shfl_sync(peers, a, src);
-    }
-    if ((threadIdx.x & 31) == __ffs(peers) - 1) red_add_f32(address, sa);
+// Visiting order of the scatter kernels.  Training batches are often spatially
+// coherent (the reference's default stratified sampler emits neighbouring pixels
+// consecutively), and then threads that run together would reduce into the same
+// table entries and serialise on them.  Thread t therefore takes coordinate
+// (t * PERM_MULT) mod 2^k, 2^k >= n (indices >= n are skipped): a bijection that
+// scatters neighbouring coordinates across the launch.  mask = 2^k - 1, or 0 for
+// the identity order.
+constexpr uint32_t PERM_MULT = 0x9E3779B1u;
+__device__ __forceinline__ long long visit(long long t, uint32_t mask) {
+    return mask ? (long long)((uint32_t(t) * PERM_MULT) & mask) : t;
 }
 
+// Direct scatter: one thread per coordinate over all its levels not in
+// skip_levels (those go through the shared-memory kernel below).
 template <bool FROM_DESC>
 __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
                                                               const __grid_constant__ LevelTable table,
                                                               const __half* __restrict__ upstream,
-                                                              float* __restrict__ grad, int warp_limit,
-                                                              unsigned skip_levels) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const int l = blockIdx.y;
-    if (i >= a.n || l >= a.active || (skip_levels >> l & 1u)) return;
-    const Level d = fetch_level<FROM_DESC>(desc, table, l);
+                                                              float* __restrict__ grad, unsigned skip_levels,
+                                                              uint32_t mask) {
+    const long long i = visit((long long)blockIdx.x * blockDim.x + threadIdx.x, mask);
+    if (i >= a.n) return;
     const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
-    const Corner4 g = geometry(p.x, p.y, d.scale);
-    if (!level_on(d, g, a.bitmap)) return;
-    const bool aggregate = d.res <= warp_limit;
-    float* const level_grad = grad + d.offset + (a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL);
-    if (d.F == 2) {
-        const float v0 = upstream_value(upstream, a, i, d.col);
-        const float v1 = upstream_value(upstream, a, i, d.col + 1);
-        if (v0 == 0.0f && v1 == 0.0f) return;
+    const long long base = a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL;
+    const int levels = a.active < a.levels ? a.active : a.levels;
+#pragma unroll 4
+    for (int l = 0; l < levels; ++l) {
+        if (skip_levels >> l & 1u) continue;
+        const Level d = fetch_level<FROM_DESC>(desc, table, l);
+        const Corner4 g = geometry(p.x, p.y, d.scale);
+        if (!level_on(d, g, a.bitmap)) continue;
+        float* const level_grad = grad + d.offset + base;
         int rows[4];
+        if (d.F == 2) {
+            const float v0 = upstream_value(upstream, a, i, d.col);
+            const float v1 = upstream_value(upstream, a, i, d.col + 1);
+            if (v0 == 0.0f && v1 == 0.0f) continue;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                red_add_v2(level_grad + 2LL * rows[k], __fmul_rn(g.w[k], v0), __fmul_rn(g.w[k], v1));
+            continue;
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+        for (int c = 0; c < d.F; ++c) {
+            const float v = upstream_value(upstream, a, i, d.col + c);
+            if (v == 0.0f) continue;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            float* address = level_grad + 2LL * rows[k];
-            const float x = __fmul_rn(g.w[k], v0), y = __fmul_rn(g.w[k], v1);
-            if (aggregate) aggregated_red2(address, x, y);
-            else red_add_v2(address, x, y);
-        }
-        return;
-    }
-    int rows[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
-    for (int c = 0; c < d.F; ++c) {
-        const float v = upstream_value(upstream, a, i, d.col + c);
-        if (v == 0.0f) continue;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            float* address = level_grad + (long long)rows[k] * d.F + c;
-            const float x = __fmul_rn(g.w[k], v);
-            if (aggregate) aggregated_red1(address, x);
-            else red_add_f32(address, x);
+            for (int k = 0; k < 4; ++k) red_add_f32(level_grad + (long long)rows[k] * d.F + c, __fmul_rn(g.w[k], v));
         }
     }
 }
@@ -214,7 +193,8 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
 // contiguous chunk of coordinates in shared memory, then adds each non-zero
 // entry to global memory once.  This turns the heavy same-address contention
 // of coarse tables (2^20 coordinates into a few hundred nodes) into shared-
-// memory updates plus blocks x table-size global reductions.
+// memory updates plus blocks x table-size global reductions.  With routed
+// experts the block holds the level's table of every expert, expert-major.
 struct CoarseList {
     int level[MAX_LEVELS];
     int blocks[MAX_LEVELS];  // blocks working on each listed level (<= gridDim.x)
@@ -224,36 +204,45 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
                                                                      const __grid_constant__ LevelTable table,
                                                                      const __grid_constant__ CoarseList list,
                                                                      const __half* __restrict__ upstream,
-                                                                     float* __restrict__ grad) {
+                                                                     float* __restrict__ grad, uint32_t mask) {
     extern __shared__ float acc[];
     const int l = list.level[blockIdx.y];
     const int blocks = list.blocks[blockIdx.y];
     if ((int)blockIdx.x >= blocks) return;  // uniform per block
     const Level d = table.level[l];
-    const int count = d.points * d.F;
+    const int per_table = d.points * d.F;
+    const int count = per_table * (a.expert ? a.experts : 1);
     for (int j = threadIdx.x; j < count; j += blockDim.x) acc[j] = 0.0f;
     __syncthreads();
-    const long long chunk = (a.n + blocks - 1) / blocks;
+    const long long domain = mask ? (long long)mask + 1 : a.n;  // visiting positions (see visit())
+    const long long chunk = (domain + blocks - 1) / blocks;
     const long long begin = (long long)blockIdx.x * chunk;
-    const long long end = begin + chunk < a.n ? begin + chunk : a.n;
-    for (long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    const long long end = begin + chunk < domain ? begin + chunk : domain;
+    for (long long t = begin + threadIdx.x; t < end; t += blockDim.x) {
+        const long long i = visit(t, mask);
+        if (i >= a.n) continue;
         const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
         const Corner4 g = geometry(p.x, p.y, d.scale);
         if (!level_on(d, g, a.bitmap)) continue;
         int rows[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+        const int e = a.expert ? __ldg(a.expert + i) : 0;
+        if (e < 0 || e >= a.experts) continue;  // an id outside the tables would land outside shared memory
+        float* const tab = acc + e * per_table;
         for (int c = 0; c < d.F; ++c) {
             const float v = upstream_value(upstream, a, i, d.col + c);
             if (v == 0.0f) continue;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) atomicAdd(acc + rows[k] * d.F + c, __fmul_rn(g.w[k], v));
+            for (int k = 0; k < 4; ++k) atomicAdd(tab + rows[k] * d.F + c, __fmul_rn(g.w[k], v));
         }
     }
     __syncthreads();
     for (int j = threadIdx.x; j < count; j += blockDim.x) {
         const float v = acc[j];
-        if (v != 0.0f) red_add_f32(grad + d.offset + j, v);
+        if (v == 0.0f) continue;
+        const int e = j / per_table;
+        red_add_f32(grad + d.offset + (long long)e * a.expert_stride + (j - e * per_table), v);
     }
 }
 
@@ -273,27 +262,38 @@ void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const fl
         if (table32) encode_forward_kernel<float, false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, table32, out, vis);
         else encode_forward_kernel<__half, false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, table16, out, vis);
     }
+    note_launch();
+}
+
+// Mask of the visiting permutation for n coordinates (0: identity, for n above 2^30).
+static uint32_t visit_mask(long long n) {
+    if (n > (1LL << 30)) return 0u;
+    uint32_t size = 1;
+    while ((long long)size < n) size <<= 1;
+    return size - 1;
 }
 
 void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
-                            int warp_limit, cudaStream_t stream) {
+                            cudaStream_t stream) {
     if (a.n <= 0 || a.levels <= 0) return;
     ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
-    const dim3 grid(blocks_for(a.n, 256), a.levels);
+    const uint32_t mask = visit_mask(a.n);
+    const long long threads = mask ? (long long)mask + 1 : a.n;
     if (src.descriptors) {
-        encode_backward_kernel<true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, upstream, grad, warp_limit, 0u);
+        encode_backward_kernel<true><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table, upstream,
+                                                                                  grad, 0u, mask);
+        note_launch();
         return;
     }
-    // Levels whose table fits in shared memory and whose global reductions the
-    // block-level pre-aggregation cuts by >= 4x take the shared-memory path.
-    // (Routed experts split each level over several tables: direct path only.)
+    // Levels whose tables (of every expert) fit in shared memory and whose global
+    // reductions the block-level pre-aggregation cuts by >= 4x take the shared-memory path.
     CoarseList list{};
     int coarse = 0, max_blocks = 0, max_floats = 0;
     unsigned skip = 0;
     const int cap_blocks = 2 * sm_count();
-    for (int l = 0; l < a.levels && l < a.active && !a.expert; ++l) {
+    for (int l = 0; l < a.levels && l < a.active; ++l) {
         const Level& d = src.table.level[l];
-        const long long floats = (long long)d.points * d.F;
+        const long long floats = (long long)d.points * d.F * (a.expert ? a.experts : 1);
         if (floats > COARSE_SMEM_FLOATS) continue;
         long long blocks = (a.n * d.F) / (floats > 0 ? floats : 1);  // flush <= 1/4 of the direct reductions
         if (blocks < 1) continue;
@@ -315,9 +315,15 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
                                            COARSE_SMEM_FLOATS * 4));
             configured |= 1ull << device;
         }
-        encode_backward_shared_kernel<<<dim3(max_blocks, coarse), 512, bytes, stream>>>(a, src.table, list, upstream, grad);
+        encode_backward_shared_kernel<<<dim3(max_blocks, coarse), 512, bytes, stream>>>(a, src.table, list, upstream, grad,
+                                                                                       mask);
+        note_launch();
     }
-    encode_backward_kernel<false><<<grid, 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, warp_limit, skip);
+    const int active = a.active < a.levels ? a.active : a.levels;
+    if (coarse == active) return;  // every level took the shared-memory path
+    encode_backward_kernel<false><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, skip,
+                                                                               mask);
+    note_launch();
 }
 
 }  // namespace odie

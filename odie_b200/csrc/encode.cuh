@@ -33,14 +33,16 @@ struct EncodeArgs {
     // level offsets (every expert has the same level layout).  Null: one table.
     const int* expert = nullptr;
     long long expert_stride = 0;
+    int experts = 1;  // number of expert tables (expert ids are < experts)
 };
 
 // Forward: table is fp32 (master) or fp16 (mirror); vis may be null.
 void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const float* table32, const __half* table16,
                            __half* out, uint8_t* vis, cudaStream_t stream);
-// Backward: scatter-add w_k * upstream into grad (fp32); levels with
-// resolution <= warp_limit aggregate equal addresses within a warp first.
+// Backward: scatter-add w_k * upstream into grad (fp32).  Coordinates are
+// visited in a fixed scrambled order; small levels accumulate per block in
+// shared memory first.
 void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
-                            int warp_limit, cudaStream_t stream);
+                            cudaStream_t stream);
 
 }  // namespace odie

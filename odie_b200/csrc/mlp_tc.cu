@@ -612,12 +612,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             for (int q = 0; q < KW; ++q) {
                 float v[16];
                 tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
-                if (valid) {
+                uint32_t rv[8];
 #pragma unroll
-                    for (int c = 0; c < 16; c += 2)
-                        reinterpret_cast<uint32_t*>(a.router_gvals)[(long long)(8 * q + c / 2) * a.stride + i] =
-                            pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(v[c])))),
-                                       __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1])))));
+                for (int c = 0; c < 16; c += 2)
+                    rv[c / 2] = pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(v[c])))),
+                                           __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1])))));
+                if (valid) {  // row-major [stride][W]: one 32-byte run per 16 columns
+                    uint4* dst = reinterpret_cast<uint4*>(a.router_gvals + i * W + 16 * q);
+                    dst[0] = make_uint4(rv[0], rv[1], rv[2], rv[3]);
+                    dst[1] = make_uint4(rv[4], rv[5], rv[6], rv[7]);
                 }
             }
             if (!is.wait_dw()) break;  // dWr1 has read R and DGH1
@@ -730,7 +733,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         }
         if (valid) {
 #pragma unroll
-            for (int p = 0; p < PAIRS; ++p) reinterpret_cast<uint32_t*>(a.gvals)[(long long)p * a.stride + i] = gv[p];
+            for (int j = 0; j < PAIRS / 4; ++j)  // row-major [stride][W]: the coordinate's values in 16-byte runs
+                reinterpret_cast<uint4*>(a.gvals + i * W)[j] = make_uint4(gv[4 * j], gv[4 * j + 1], gv[4 * j + 2], gv[4 * j + 3]);
         }
         dw_accumulate = 1;
         fold_vis(next_tile);
@@ -833,6 +837,7 @@ void launch_tc(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t strea
         configured |= 1ull << device;
     }
     mlp_tc_kernel<W, GATE, TRAIN, UNIFORM><<<blocks, TC_THREADS, bytes, stream>>>(a, error_flag);
+    note_launch();
 }
 
 template <bool TRAIN>

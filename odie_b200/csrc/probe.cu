@@ -1,0 +1,61 @@
+// L2 bandwidth probe: the roofline denominator of the gather and scatter kernels.
+//
+// The grid tables of every benchmark configuration fit in the 126 MB L2, so
+// their random 4-corner gathers and reductions are bounded by L2 throughput,
+// not HBM.  This probe measures that bound on the running GPU: random 4-byte
+// and 16-byte loads, and random 4-byte and 8-byte fp32 reductions, over a table
+// of `table_bytes` (kept <= 64 MiB so it stays L2-resident), every thread
+// drawing its indices from a hash of its id (no index traffic).  One launch per
+// mode; the caller times it with CUDA events.
+#include "common.cuh"
+
+namespace odie {
+
+namespace {
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+// mode 0: 4-byte loads, 1: 16-byte loads, 2: red.add.f32, 3: red.add.v2.f32
+__global__ void __launch_bounds__(256) l2_probe_kernel(float* table, uint32_t words, int mode, int per_thread,
+                                                       float* sink) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    float acc = 0.0f;
+    uint32_t state = mix32(t * 0x9e3779b9u + 0x1234567u);
+    for (int j = 0; j < per_thread; ++j) {
+        state = mix32(state + uint32_t(j));
+        if (mode == 0) {
+            acc += __ldcg(table + (state % words));
+        } else if (mode == 1) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(table) + (state % (words / 4)));
+            acc += v.x + v.y + v.z + v.w;
+        } else if (mode == 2) {
+            red_add_f32(table + (state % words), 1e-30f);
+        } else {
+            red_add_v2(table + 2 * (state % (words / 2)), 1e-30f, 1e-30f);
+        }
+    }
+    if (acc == 1234.5f) sink[0] = acc;  // keeps the loads alive
+}
+
+}  // namespace
+
+void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
+                     cudaStream_t stream) {
+    ODIE_REQUIRE(mode >= 0 && mode <= 3, "probe mode must be 0..3");
+    ODIE_REQUIRE(table_bytes >= 4096 && table_bytes <= (64LL << 20), "probe table must be 4 KiB..64 MiB");
+    const int per_thread = 64;
+    const long long threads = (operations + per_thread - 1) / per_thread;
+    ODIE_REQUIRE(threads >= 1 && threads <= (1LL << 31) - 1, "probe operation count out of range");
+    l2_probe_kernel<<<blocks_for(threads, 256), 256, 0, stream>>>(table, uint32_t(table_bytes / 4), mode, per_thread,
+                                                                  sink);
+    note_launch();
+}
+
+}  // namespace odie

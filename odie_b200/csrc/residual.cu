@@ -97,6 +97,7 @@ void launch_score_chunk(const float* prediction, const void* target, long long b
     if (active_cells <= 0) return;
     score_cells_kernel<<<blocks_for(active_cells, 256), 256, 0, stream>>>(prediction, target, begin, end, width, resolution,
                                                                           first_y, active_cells, xb, yb, totals, rgb8);
+    note_launch();
 }
 
 void launch_tile_scores(const float* prediction, const uint8_t* target, int height, int width, int tile, double* row_sums,
@@ -104,11 +105,13 @@ void launch_tile_scores(const float* prediction, const uint8_t* target, int heig
     const int tiles = ((width + tile - 1) / tile) * ((height + tile - 1) / tile);
     tile_rows_kernel<<<tiles, 256, 0, stream>>>(prediction, target, height, width, tile, row_sums);
     tile_sum_kernel<<<blocks_for(tiles, 256), 256, 0, stream>>>(row_sums, tiles, tile, scores);
+    note_launch(2);
 }
 
 void launch_topk(const double* scores, int count, int k, long long* chosen, uint8_t* selected, cudaStream_t stream) {
     if (count <= 0) return;
     topk_rank_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(scores, count, k, chosen, selected);
+    note_launch();
 }
 
 // ---------------------------------------------------------------- allocation-free tile top-k

@@ -14,6 +14,7 @@
 // expert tables are encoded at that expert's offset, and the fused heads train
 // router and decoder together; both grids take the scatter and the Adam step.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -33,6 +34,11 @@ thread_local std::string g_error, g_reply;
 }
 
 void set_error(const std::string& message) { g_error = message; }
+
+namespace {
+std::atomic<long long> g_launches{0};
+}
+void note_launch(int kernels) { g_launches.fetch_add(kernels, std::memory_order_relaxed); }
 
 int sm_count() {
     static int cached[64] = {0};
@@ -133,6 +139,8 @@ struct Runtime {
         image_width = int(j.at("width").as_int());
         image_height = int(j.at("height").as_int());
         mode = int(j.value("mode", 20));
+        // The reference's warp-aggregation threshold; accepted for its JSON contract.  The scatter here
+        // needs no threshold: it spreads equal addresses apart by its visiting order instead.
         warp_limit = int(j.value("warp_limit", 128));
         // coordinate capacity per step, padded to whole 128-row tiles (the feature stride)
         capacity = (j.value("batch", 65536) + 127) / 128 * 128;
@@ -425,6 +433,7 @@ struct Runtime {
         EncodeArgs ea = encode_args(n);
         ea.expert = expert_ids.ptr;
         ea.expert_stride = expert_total;
+        ea.experts = experts;
         slot = stage_begin(S_ENCODE_FWD);
         launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, nullptr, stream);
         stage_end(slot);
@@ -490,6 +499,7 @@ struct Runtime {
             route_and_encode(n);
             ea.expert = expert_ids.ptr;
             ea.expert_stride = expert_total;
+            ea.experts = experts;
         } else {
             slot = stage_begin(S_ENCODE_FWD);
             launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, reinterpret_cast<uint8_t*>(vis.ptr), stream);
@@ -501,11 +511,14 @@ struct Runtime {
         launch_mlp_tc_train(ma, input_width, gate_mode(), uniform, blocks, error_flag.ptr, stream);
         stage_end(slot);
         slot = stage_begin(S_ENCODE_BWD);
-        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, warp_limit, stream);
+        ea.row_major = true;  // the heads write each coordinate's gradient values as one row
+        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
         if (experts) {
             LevelSource rsrc;
             rsrc.table = router_table;
-            launch_encode_backward(router_encode_args(n), rsrc, router_gvals.ptr, router_grad.ptr, warp_limit, stream);
+            EncodeArgs ra = router_encode_args(n);
+            ra.row_major = true;
+            launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, stream);
         }
         stage_end(slot);
         slot = stage_begin(S_REDUCE);
@@ -687,12 +700,19 @@ int launch_selection_chunk(const double* scores, int n, int points, int resoluti
                            int chunk, long long* stats, int* trace, cudaStream_t stream);
 }  // namespace odie
 
+namespace odie {
+void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
+                     cudaStream_t stream);
+}  // namespace odie
+
 using odie::guarded;
 using odie::Runtime;
 
 extern "C" {
 
 const char* odie_error(void) { return odie::g_error.c_str(); }
+
+long long odie_launch_count(void) { return odie::g_launches.load(std::memory_order_relaxed); }
 
 void* odie_create(const char* json) {
     try {
@@ -825,7 +845,7 @@ int odie_query_backward(const float* coords, int64_t n, const uint16_t* upstream
         a.stride = n;
         odie::LevelSource src;
         src.descriptors = descriptors;
-        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, s);
         ODIE_CUDA(cudaGetLastError());
     });
 }
@@ -865,7 +885,7 @@ int odie_hash_backward(const float* coords, int64_t n, const uint16_t* upstream,
         a.stride = n;
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
-        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, s);
         ODIE_CUDA(cudaGetLastError());
     });
 }
@@ -929,9 +949,17 @@ int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* up
         a.stride = n;
         a.expert = expert;
         a.expert_stride = expert_stride;
+        a.experts = int(std::max<int64_t>(1, parameter_count / expert_stride));
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
-        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, 128, s);
+        odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, s);
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_l2_probe(float* table, int64_t table_bytes, int mode, int64_t operations, float* sink, uint64_t stream) {
+    return guarded([&] {
+        odie::launch_l2_probe(table, table_bytes, mode, operations, sink, reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
 }

@@ -211,6 +211,7 @@ int launch_selection_init(const double* scores, int n, int points, int* missing,
         build_level_kernel<<<blocks_for((long long)tasks * FAN, 256), 256, 0, stream>>>(
             scores, n, missing, chosen, tree, host_offsets[l], l ? host_offsets[l - 1] : 0, children, host_sizes[l], l == 0);
     }
+    note_launch(1 + levels);
     return int(cudaGetLastError());
 }
 
@@ -219,6 +220,7 @@ int launch_selection_chunk(const double* scores, int n, int points, int resoluti
                            int chunk, long long* stats, int* trace, cudaStream_t stream) {
     greedy_kernel<<<1, SEL_THREADS, 0, stream>>>(scores, n, points, resolution, cap, normalized, missing, chosen, nodes, tree,
                                                  offsets, sizes, levels, chunk, stats, trace);
+    note_launch();
     return int(cudaGetLastError());
 }
 

@@ -115,15 +115,18 @@ void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, boo
                         float* xy, float* target, cudaStream_t stream) {
     if (n <= 0) return;
     input_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(ids, n, rgb, rgb8, width, height, xy, target);
+    note_launch();
 }
 
 void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream) {
     if (n <= 0) return;
     coords_range_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(begin, n, width, height, xy);
+    note_launch();
 }
 
 void launch_reduce_partials(const float* partials, int blocks, int count, float* out, cudaStream_t stream) {
     reduce_partials_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(partials, blocks, count, out);
+    note_launch();
 }
 
 void launch_adam(float* master, __half* copy, float* m, float* v, uint32_t* steps, float* grad, long long count,
@@ -143,13 +146,18 @@ void launch_adam(float* master, __half* copy, float* m, float* v, uint32_t* step
             master, copy, m, v, steps, grad, count, inv_scale, tables.step_size, tables.bc2_sqrt, tables.size, beta1w,
             beta2, beta2w, eps, skip_zero, error_flag);
     }
+    note_launch();
 }
 
 void launch_zero(float* p, long long count, cudaStream_t stream) {
-    if (count > 0) zero_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(p, count);
+    if (count <= 0) return;
+    zero_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(p, count);
+    note_launch();
 }
 void launch_cast_half(const float* in, __half* out, long long count, cudaStream_t stream) {
-    if (count > 0) cast_half_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(in, out, count);
+    if (count <= 0) return;
+    cast_half_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(in, out, count);
+    note_launch();
 }
 
 }  // namespace odie

@@ -34,7 +34,7 @@ struct MlpArgs {
     int levels, raw_width, k_fixed, softplus;
     float three_real;     // fp32(3 * real) of the loss gradient
     FeatureMap fmap;
-    __half* gvals;        // [W/2][stride] grid-gradient values (training)
+    __half* gvals;        // [stride][W] grid-gradient values, row-major (training)
     float* squares;       // [n] per-sample mean-RGB squared error (training)
     float* partials;      // [gridDim.x][head params] weight-gradient partials (training)
     float* rgb;           // [n][3] fp32 decode output (decode)
@@ -43,7 +43,7 @@ struct MlpArgs {
     const __half* router_in;  // [W/2][stride] half2 router-grid features
     const float* prob;        // [n] router probability of the chosen expert
     const int* expert;        // [n] chosen expert
-    __half* router_gvals;     // [W/2][stride] router-grid gradient values (training)
+    __half* router_gvals;     // [stride][W] router-grid gradient values, row-major (training)
     int experts;              // live experts
 };
 

@@ -8,13 +8,23 @@ class; resolutions 8..1020, 13 full-cover levels, 3 on-demand levels with
 caps 181112/181112/181120, results/div2k_50/0028/odie/metrics.json), with the
 on-demand supports chosen as the top cells of a seeded smooth residual field,
 trimmed to their node caps.
+
+c2-experts: BASELINE config 2 itself -- 16 routed experts, each with its own
+hash grid (L=16, F=2, T=2^16, base resolution 16, per-level scale 1.5, tables
+U(-1e-4, 1e-4)), a top-1 router (W -> 32 -> 32 -> 16) over a coarse shared grid
+(L=16, F=2, T=2^12, base 4, scale 1.2: resolutions 4..62, all dense, tables
+U(-0.1, 0.1) so that the initial routing already splits the image), and the
+shared 64-wide decoder, on the same 2040 x 1356 image with 2^20 coords.
+
+Multi-GPU (both workloads): rank r of N trains the model of row band r of the
+image (its own tables: spatial ownership); the heads are shared.
 """
 import numpy as np
 import torch
 
 from . import layout as host_layout
 from .data import ByteTarget, pink_noise, synthetic_image
-from .model import PackedXYPlanes
+from .model import PackedXYPlanes, RoutedExperts
 
 DIV2K_RESOLUTIONS = [8, 11, 15, 21, 29, 40, 56, 77, 106, 147, 203, 280, 387, 534, 738, 1020]
 DIV2K_SPARSE_CAPS = {13: 181112, 14: 181112, 15: 181120}
@@ -73,3 +83,36 @@ def build_plane_model(config, supports, dims, caps, rgb, device='cuda'):
     planes = [torch.nn.Parameter(model.grid[l['plane_offset']:l['plane_offset'] + l['plane_node_capacity'] *
                                             l['plane_dim']].detach()) for l in model.layout['levels']]
     return model, target, planes
+
+
+EXPERT_ENCODING = dict(otype='HashGrid', n_levels=16, n_features_per_level=2, log2_hashmap_size=16,
+                       base_resolution=16, per_level_scale=1.5)
+ROUTER_ENCODING = dict(otype='HashGrid', n_levels=16, n_features_per_level=2, log2_hashmap_size=12,
+                       base_resolution=4, per_level_scale=1.2)
+
+
+def experts_config(experts=16, seed=1729, batch=1 << 20, encoding=None, router_encoding=None):
+    return dict(representation='routed_experts', experts=experts, seed=seed, grid_init=1e-4, router_init=0.1,
+                hash_encoding=dict(encoding or EXPERT_ENCODING), router_encoding=dict(router_encoding or ROUTER_ENCODING),
+                grid_lr=1e-2, gate_lr=1e-3, decoder_lr=1e-3, batch_size=batch)
+
+
+def band_of(rgb, shape, band):
+    rank, ranks = band
+    height, width = shape
+    if ranks == 1:
+        return rgb, shape
+    rows = np.array_split(np.arange(height), ranks)[rank]
+    return rgb.reshape(height, width, 3)[rows[0]:rows[-1] + 1].reshape(-1, 3).contiguous(), (len(rows), width)
+
+
+def c2_experts(seed=1729, batch=1 << 20, band=(0, 1)):
+    """(config, rgb u8 [H*W, 3] on CPU, shape) of rank band[0] of band[1] (row bands)."""
+    rgb, shape = synthetic_image('c2', seed=seed)
+    rgb, shape = band_of(rgb, shape, band)
+    return experts_config(seed=seed + band[0], batch=batch), rgb, shape
+
+
+def build_expert_model(config, rgb, device='cuda'):
+    model = RoutedExperts(config)
+    return model, ByteTarget(rgb.to(device)), [model.grid]

@@ -1,4 +1,4 @@
-"""PyTorch-CPU restatement of the reference training step -- TEST/BENCH INFRASTRUCTURE ONLY.
+"""PyTorch-CPU restatements of the training steps -- TEST/BENCH INFRASTRUCTURE ONLY.
 
 Used only by bench.py as the CPU baseline and as the `--impl reference` arm:
 the reference has no CPU path (its "reference" backend still needs CUDA and
@@ -6,8 +6,9 @@ TCNN, odie/optimizer.py:54-89), so its native step (odie/native/runtime.cu:
 253-312) is restated here with vectorised torch CPU ops: index_select gathers
 of the fp16-rounded corner values, autograd's index_add scatter, F.linear heads
 with fp16 activations, the L2 loss with the reference's 128 x 128 loss scaling
-and torch.optim.Adam (betas 0.9/0.999, eps 1e-15).  It runs on all the host
-threads torch is given.
+and torch.optim.Adam (betas 0.9/0.999, eps 1e-15).  CpuExpertStep restates the
+routed multi-expert step the same way.  Both run on all the
+host threads torch is given.
 """
 import time
 
@@ -41,40 +42,7 @@ class CpuStep:
         return out
 
     def encode(self, xy):
-        n = xy.shape[0]
-        cols = []
-        vis_all = []
-        for lv in self.levels:
-            p = xy * lv['scale'] + 0.5
-            i = torch.floor(p)
-            f = p - i
-            ix, iy = i[:, 0].long(), i[:, 1].long()
-            fx, fy = f[:, 0], f[:, 1]
-            w = torch.stack(((1 - fx) * (1 - fy), fx * (1 - fy), (1 - fx) * fy, fx * fy), 1)
-            if lv['kind'] == 'plane':
-                cell = ix + iy * lv['res']
-                nodes = torch.stack((cell, cell + 1, cell + lv['res'], cell + lv['res'] + 1), 1) % lv['points']
-                vis = lv['cells'][cell.clamp(0, lv['res'] ** 2 - 1)] if lv['cells'] is not None else torch.ones(n, dtype=torch.bool)
-                rows = lv['row_map'][nodes] if lv['row_map'] is not None else nodes
-            else:
-                cx = torch.stack((ix, ix + 1, ix, ix + 1), 1)
-                cy = torch.stack((iy, iy, iy + 1, iy + 1), 1)
-                if lv['kind'] == 'hashed':
-                    idx = (cx ^ ((cy * 2654435761) & 0xffffffff)) & 0xffffffff
-                else:
-                    idx = cx + cy * lv['res']
-                rows = idx % lv['points']
-                vis = torch.ones(n, dtype=torch.bool)
-            rows = torch.where(vis.unsqueeze(1), rows, torch.zeros_like(rows)).clamp(min=0)  # hidden cells read row 0
-            for c in range(lv['F']):
-                values = self.grid.index_select(0, (lv['offset'] + rows * lv['F'] + c).reshape(-1)).view(n, 4)
-                values = values.half().float() + (values - values.detach())  # fp16-rounded corners, fp32 gradient
-                cols.append((w.half().float() * values).sum(1) * vis)
-            vis_all.append(vis)
-        raw = torch.stack(cols, 1)
-        if raw.shape[1] < self.width:
-            raw = torch.cat((raw, torch.ones((n, self.width - raw.shape[1]))), 1)
-        return raw.half().float() + (raw - raw.detach()), torch.stack(vis_all, 1)
+        return encode_levels(self.grid, self.levels, xy, self.width)
 
     def step(self, ids):
         height, width = self.shape
@@ -105,6 +73,94 @@ class CpuStep:
                 p.grad.div_(128.)
         self.optimizer.step()
         return float(loss.detach())
+
+
+def encode_levels(table, levels, xy, width, base=None):
+    """fp16 features [n, width] (fp32 gradient path) and visibility [n, L] of `levels` over `table`;
+    base (int64 [n] or None) offsets every row's parameters (one table per routed expert)."""
+    n = xy.shape[0]
+    cols = []
+    vis_all = []
+    for lv in levels:
+        p = xy * lv['scale'] + 0.5
+        i = torch.floor(p)
+        f = p - i
+        ix, iy = i[:, 0].long(), i[:, 1].long()
+        fx, fy = f[:, 0], f[:, 1]
+        w = torch.stack(((1 - fx) * (1 - fy), fx * (1 - fy), (1 - fx) * fy, fx * fy), 1)
+        if lv['kind'] == 'plane':
+            cell = ix + iy * lv['res']
+            nodes = torch.stack((cell, cell + 1, cell + lv['res'], cell + lv['res'] + 1), 1) % lv['points']
+            vis = lv['cells'][cell.clamp(0, lv['res'] ** 2 - 1)] if lv['cells'] is not None else torch.ones(n, dtype=torch.bool)
+            rows = lv['row_map'][nodes] if lv['row_map'] is not None else nodes
+        else:
+            cx = torch.stack((ix, ix + 1, ix, ix + 1), 1)
+            cy = torch.stack((iy, iy, iy + 1, iy + 1), 1)
+            if lv['kind'] == 'hashed':
+                idx = (cx ^ ((cy * 2654435761) & 0xffffffff)) & 0xffffffff
+            else:
+                idx = cx + cy * lv['res']
+            rows = idx % lv['points']
+            vis = torch.ones(n, dtype=torch.bool)
+        rows = torch.where(vis.unsqueeze(1), rows, torch.zeros_like(rows)).clamp(min=0)  # hidden cells read row 0
+        for c in range(lv['F']):
+            values = table.index_select(0, ((lv['offset'] if base is None else lv['offset'] + base.unsqueeze(1)) + rows * lv['F'] + c).reshape(-1)).view(n, 4)
+            values = values.half().float() + (values - values.detach())  # fp16-rounded corners, fp32 gradient
+            cols.append((w.half().float() * values).sum(1) * vis)
+        vis_all.append(vis)
+    raw = torch.stack(cols, 1)
+    if raw.shape[1] < width:
+        raw = torch.cat((raw, torch.ones((n, width - raw.shape[1]))), 1)
+    return raw.half().float() + (raw - raw.detach()), torch.stack(vis_all, 1)
+
+
+class CpuExpertStep(CpuStep):
+    """The routed multi-expert step (router grid -> top-1 router -> expert tables -> shared decoder) on the CPU.
+
+    Same arithmetic as the CUDA path's definition: router MLP with fp16
+    activations, top-1 of the fp16 logits, decoder input = fp16(features x
+    fp16(p)); autograd through p (softmax probability) and both grids; Adam on
+    expert tables, router grid, router MLP and decoder."""
+
+    def __init__(self, shape, rgb_u8, levels, expert_stride, experts, router_levels, grid, router_grid, router, decoder,
+                 width, lr=(1e-2, 1e-3, 1e-3)):
+        super().__init__(shape, rgb_u8, levels, grid, router, decoder, width, router=True, lr=lr)
+        self.router_levels, self.stride, self.experts = router_levels, expert_stride, experts
+        self.router_grid = torch.nn.Parameter(torch.from_numpy(router_grid.copy()))
+        self.optimizer.add_param_group({'params': [self.router_grid], 'lr': lr[0]})
+
+    def step(self, ids):
+        height, width = self.shape
+        xy = torch.stack(((ids % width).float() * (1.0 / (width - 1)), (ids // width).float() * (1.0 / (height - 1))), 1)
+        target = self.rgb[ids].float() / 255.
+        self.optimizer.zero_grad(set_to_none=True)
+        W = self.width
+        rin, _ = encode_levels(self.router_grid, self.router_levels, xy, W)
+        r1, r2, r3 = self._mats(self.gate, [(32, W), (32, 32), (16, 32)])
+        h = F.relu(F.linear(rin, r1.half().float())).half().float()
+        h = F.relu(F.linear(h, r2.half().float())).half().float()
+        logits = F.linear(h, r3.half().float()).half().float()[:, :self.experts]
+        expert = logits.detach().argmax(1)
+        prob = torch.softmax(logits, 1).gather(1, expert[:, None])
+        raw, _ = encode_levels(self.grid, self.levels, xy, W, base=expert * self.stride)
+        x = (raw * prob.half().float()).half().float()
+        d1, d2, d3 = self._mats(self.decoder, [(64, W), (64, 64), (16, 64)])
+        h1 = F.relu(F.linear(x, d1.half().float())).half().float()
+        h2 = F.relu(F.linear(h1, d2.half().float())).half().float()
+        out = F.linear(h2, d3.half().float()).half().float()[:, :3]
+        loss = (out - target).square().mean()
+        (loss * 128.).backward()
+        for p in (self.grid, self.router_grid, self.decoder, self.gate):
+            if p.grad is not None:
+                p.grad.div_(128.)
+        self.optimizer.step()
+        return float(loss.detach())
+
+
+def hash_levels_for_cpu(records):
+    """Per-level dicts for CpuStep / CpuExpertStep from hash-grid level records."""
+    return [dict(scale=r['scale'], res=r['resolution'], points=r['capacity'], offset=r['offset'], F=r['features'],
+                 col=r['column'], kind='hashed' if r['hashed'] else 'dense', row_map=None, cells=None) for r in records]
 
 
 def plane_levels_for_cpu(descriptors, node_bitmap, node_prefix, bitmap):

@@ -41,6 +41,11 @@ def setup(experts=4, seed=3, batch=1024):
     return config, model, rgb, opt
 
 
+def read_rows(opt, name, n, width):
+    """A row-major [capacity][width] fp16 buffer (the heads' gradient values)."""
+    return opt.copied(name, (opt.pointers['capacity'], width), torch.float16)[:n].cpu().numpy()
+
+
 def read_pair_major(opt, name, n, width):
     cap = opt.pointers['capacity']
     pairs = opt.copied(name, (width // 2, cap, 2), torch.float16)[:, :n, :]
@@ -119,9 +124,9 @@ def test_experts_step_matches_oracle(cuda, experts):
     raw = read_pair_major(opt, 'raw', n, W)
     assert np.array_equal(raw.view(np.uint16), ref['raw'].view(np.uint16)), 'expert features differ'
     close(opt.copied('squares', (n,), torch.float32).cpu().numpy(), ref['squares'], 2e-3, 2e-3, 'squares')
-    values = read_pair_major(opt, 'gvals', n, W)
+    values = read_rows(opt, 'gvals', n, W)
     close(values.astype(np.float32), ref['values'], 2e-3, 2e-3, 'expert grid values')
-    router_values = read_pair_major(opt, 'router_gvals', n, W)
+    router_values = read_rows(opt, 'router_gvals', n, W)
     close(router_values.astype(np.float32), ref['router_values'], 2e-3, 2e-3, 'router grid values')
     heads = opt.copied('head_grad', (opt.pointers['head_count'],), torch.float32).cpu().numpy()
     split = opt.pointers['gate_count']

@@ -44,6 +44,11 @@ def snapshot(model):
     return (model.grid.detach().cpu().numpy().copy(), gate, model.decoder.params.detach().cpu().numpy().copy())
 
 
+def read_rows(opt, name, n, width):
+    """A row-major [capacity][width] fp16 buffer (the heads' gradient values)."""
+    return opt.copied(name, (opt.pointers['capacity'], width), torch.float16)[:n].cpu().numpy()
+
+
 def read_pair_major(opt, name, n, width):
     cap = opt.pointers['capacity']
     pairs = opt.copied(name, (width // 2, cap, 2), torch.float16)[:, :n, :]
@@ -81,7 +86,7 @@ def test_step_gradients_match_oracle(cuda, router, k, activation):
     # fp16 network quantities
     squares = opt.copied('squares', (n,), torch.float32).cpu().numpy()
     close(squares, ref['squares'], 2e-3, 2e-3, 'squares')
-    values = read_pair_major(opt, 'gvals', n, W)
+    values = read_rows(opt, 'gvals', n, W)
     close(values.astype(np.float32), ref['values'], 2e-3, 2e-3, 'grid-gradient values')
     heads = opt.copied('head_grad', (opt.pointers['head_count'],), torch.float32).cpu().numpy()
     close(heads, ref['head_grad'], 2e-3, 2e-3, 'head gradients')
