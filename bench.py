@@ -271,8 +271,7 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
-    from odie_b200 import _lib
-    from odie_b200 import workloads
+    from odie_b200 import _lib, parallel
     from odie_b200.native_backend import NativeOptimizer
     lib = _lib.library()
     w = workload(args.workload, rank, world, args.batch)
@@ -280,10 +279,10 @@ def main():
     head_grad = None
     if world > 1:
         # the heads are shared: every rank starts from rank 0's weights and applies the same summed gradient
-        for head in (model.gate, model.decoder):
-            dist.broadcast(head.params.data, 0)
-        head_grad = torch.zeros(model.gate.params.numel() + model.decoder.params.numel(), device='cuda')
+        parallel.broadcast_heads(model)
+        head_grad = parallel.head_gradient_buffer(model)
     opt = NativeOptimizer(model, w['target'], shape, config, w['planes'], batch=args.batch, head_grad=head_grad)
+    dp_step = parallel.DataParallelStep(parallel.NativeRuntime(opt), head_grad)
     pixels = shape[0] * shape[1]
     gen = torch.Generator(device='cuda').manual_seed(1729 + rank)
     total_steps = args.warmup + args.steps
@@ -297,9 +296,7 @@ def main():
         if world == 1:
             opt.check(lib.odie_step(opt.handle, batch_ids.data_ptr(), batch_ids.numel(), 1))
         else:
-            opt.check(lib.odie_step_grads(opt.handle, batch_ids.data_ptr(), batch_ids.numel(), 1))
-            dist.all_reduce(head_grad)
-            opt.check(lib.odie_step_heads(opt.handle))
+            dp_step(batch_ids)
 
     def barrier():
         torch.cuda.synchronize()

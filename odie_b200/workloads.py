@@ -25,6 +25,7 @@ import torch
 from . import layout as host_layout
 from .data import ByteTarget, pink_noise, synthetic_image
 from .model import PackedXYPlanes, RoutedExperts
+from .parallel import band_rows
 
 DIV2K_RESOLUTIONS = [8, 11, 15, 21, 29, 40, 56, 77, 106, 147, 203, 280, 387, 534, 738, 1020]
 DIV2K_SPARSE_CAPS = {13: 181112, 14: 181112, 15: 181120}
@@ -56,12 +57,9 @@ def capped_support(resolution, cap, seed):
 
 def c2_planes(seed=1729, batch=1 << 20, band=(0, 1)):
     """(config, supports, dims, caps, rgb u8 [H*W, 3] on CPU, shape) of rank band[0] of band[1] (row bands)."""
-    rgb, (height, width) = synthetic_image('c2', seed=seed)
+    rgb, shape = synthetic_image('c2', seed=seed)
+    rgb, (height, width) = band_of(rgb, shape, band)
     rank, ranks = band
-    if ranks > 1:
-        rows = np.array_split(np.arange(height), ranks)[rank]
-        rgb = rgb.reshape(height, width, 3)[rows[0]:rows[-1] + 1].reshape(-1, 3).contiguous()
-        height = len(rows)
     dims = [2] * 16
     supports, caps = [], []
     for level, r in enumerate(DIV2K_RESOLUTIONS):
@@ -98,12 +96,13 @@ def experts_config(experts=16, seed=1729, batch=1 << 20, encoding=None, router_e
 
 
 def band_of(rgb, shape, band):
+    """The u8 pixels and shape of row band band[0] of band[1] (odie_b200.parallel.band_rows)."""
     rank, ranks = band
     height, width = shape
     if ranks == 1:
         return rgb, shape
-    rows = np.array_split(np.arange(height), ranks)[rank]
-    return rgb.reshape(height, width, 3)[rows[0]:rows[-1] + 1].reshape(-1, 3).contiguous(), (len(rows), width)
+    first, last = band_rows(height, rank, ranks)
+    return rgb.reshape(height, width, 3)[first:last].reshape(-1, 3).contiguous(), (last - first, width)
 
 
 def c2_experts(seed=1729, batch=1 << 20, band=(0, 1)):
