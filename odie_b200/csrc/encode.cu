@@ -189,15 +189,19 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
     }
 }
 
-// Coarse levels: every block accumulates the gradient of one small level for a
-// contiguous chunk of coordinates in shared memory, then adds each non-zero
-// entry to global memory once.  This turns the heavy same-address contention
-// of coarse tables (2^20 coordinates into a few hundred nodes) into shared-
-// memory updates plus blocks x table-size global reductions.  With routed
-// experts the block holds the level's table of every expert, expert-major.
+// Coarse levels: every block accumulates the gradients of all small levels
+// (the listed ones) for its share of the coordinates in shared memory, then
+// adds each non-zero entry to global memory once.  This turns the heavy
+// same-address contention of coarse tables (2^20 coordinates into a few hundred
+// nodes) into shared-memory updates plus blocks x table-size global reductions,
+// and reads each coordinate and its gradient row once for all those levels.
+// With routed experts the block holds each level's table of every expert,
+// expert-major.
 struct CoarseList {
+    int count;                // levels held in shared memory
+    int total;                // floats of shared memory they take
     int level[MAX_LEVELS];
-    int blocks[MAX_LEVELS];  // blocks working on each listed level (<= gridDim.x)
+    int offset[MAX_LEVELS];   // first float of each listed level's tables in shared memory
 };
 
 __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const EncodeArgs a,
@@ -206,49 +210,52 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
                                                                      const __half* __restrict__ upstream,
                                                                      float* __restrict__ grad, uint32_t mask) {
     extern __shared__ float acc[];
-    const int l = list.level[blockIdx.y];
-    const int blocks = list.blocks[blockIdx.y];
-    if ((int)blockIdx.x >= blocks) return;  // uniform per block
-    const Level d = table.level[l];
-    const int per_table = d.points * d.F;
-    const int count = per_table * (a.expert ? a.experts : 1);
-    for (int j = threadIdx.x; j < count; j += blockDim.x) acc[j] = 0.0f;
+    const int experts = a.expert ? a.experts : 1;
+    for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
     __syncthreads();
     const long long domain = mask ? (long long)mask + 1 : a.n;  // visiting positions (see visit())
-    const long long chunk = (domain + blocks - 1) / blocks;
+    const long long chunk = (domain + gridDim.x - 1) / gridDim.x;
     const long long begin = (long long)blockIdx.x * chunk;
     const long long end = begin + chunk < domain ? begin + chunk : domain;
     for (long long t = begin + threadIdx.x; t < end; t += blockDim.x) {
         const long long i = visit(t, mask);
         if (i >= a.n) continue;
-        const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
-        const Corner4 g = geometry(p.x, p.y, d.scale);
-        if (!level_on(d, g, a.bitmap)) continue;
-        int rows[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
         const int e = a.expert ? __ldg(a.expert + i) : 0;
-        if (e < 0 || e >= a.experts) continue;  // an id outside the tables would land outside shared memory
-        float* const tab = acc + e * per_table;
-        for (int c = 0; c < d.F; ++c) {
-            const float v = upstream_value(upstream, a, i, d.col + c);
-            if (v == 0.0f) continue;
+        if (e < 0 || e >= experts) continue;  // an id outside the tables would land outside shared memory
+        const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+        for (int c = 0; c < list.count; ++c) {
+            const Level d = table.level[list.level[c]];
+            const Corner4 g = geometry(p.x, p.y, d.scale);
+            if (!level_on(d, g, a.bitmap)) continue;
+            int rows[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) atomicAdd(tab + rows[k] * d.F + c, __fmul_rn(g.w[k], v));
+            for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+            float* const tab = acc + list.offset[c] + e * d.points * d.F;
+            for (int f = 0; f < d.F; ++f) {
+                const float v = upstream_value(upstream, a, i, d.col + f);
+                if (v == 0.0f) continue;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) atomicAdd(tab + rows[k] * d.F + f, __fmul_rn(g.w[k], v));
+            }
         }
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < count; j += blockDim.x) {
-        const float v = acc[j];
-        if (v == 0.0f) continue;
-        const int e = j / per_table;
-        red_add_f32(grad + d.offset + (long long)e * a.expert_stride + (j - e * per_table), v);
+    for (int c = 0; c < list.count; ++c) {
+        const Level d = table.level[list.level[c]];
+        const int per_table = d.points * d.F;
+        const float* tab = acc + list.offset[c];
+        for (int j = threadIdx.x; j < per_table * experts; j += blockDim.x) {
+            const float v = tab[j];
+            if (v == 0.0f) continue;
+            const int x = j / per_table;
+            red_add_f32(grad + d.offset + (long long)x * a.expert_stride + (j - x * per_table), v);
+        }
     }
 }
 
 }  // namespace
 
-constexpr int COARSE_SMEM_FLOATS = 24576;  // 96 KB of shared memory per block
+constexpr int COARSE_SMEM_FLOATS = 27648;  // 108 KB of shared memory per block: two blocks per SM
 
 void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const float* table32, const __half* table16,
                            __half* out, uint8_t* vis, cudaStream_t stream) {
@@ -285,28 +292,25 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
         note_launch();
         return;
     }
-    // Levels whose tables (of every expert) fit in shared memory and whose global
-    // reductions the block-level pre-aggregation cuts by >= 4x take the shared-memory path.
+    // The smallest levels, coarsest first, while all their tables (of every
+    // expert) fit in shared memory together and each is small against the
+    // coordinates: the blocks' flushes of a level stay below half of the
+    // 4 x F per-coordinate updates they absorb.
     CoarseList list{};
-    int coarse = 0, max_blocks = 0, max_floats = 0;
     unsigned skip = 0;
-    const int cap_blocks = 2 * sm_count();
+    const long long spread = a.n / 1024 > 1 ? a.n / 1024 : 1;
+    const int blocks = int(spread < 2 * sm_count() ? spread : 2 * sm_count());
     for (int l = 0; l < a.levels && l < a.active; ++l) {
         const Level& d = src.table.level[l];
         const long long floats = (long long)d.points * d.F * (a.expert ? a.experts : 1);
-        if (floats > COARSE_SMEM_FLOATS) continue;
-        long long blocks = (a.n * d.F) / (floats > 0 ? floats : 1);  // flush <= 1/4 of the direct reductions
-        if (blocks < 1) continue;
-        if (blocks > cap_blocks) blocks = cap_blocks;
-        list.level[coarse] = l;
-        list.blocks[coarse] = int(blocks);
-        ++coarse;
+        if (list.total + floats > COARSE_SMEM_FLOATS || (long long)blocks * floats > 2 * a.n * d.F) continue;
+        list.level[list.count] = l;
+        list.offset[list.count] = list.total;
+        list.total += int(floats);
+        ++list.count;
         skip |= 1u << l;
-        if (blocks > max_blocks) max_blocks = int(blocks);
-        if (floats > max_floats) max_floats = int(floats);
     }
-    if (coarse) {
-        const int bytes = max_floats * 4;
+    if (list.count) {
         static unsigned long long configured = 0;
         int device = 0;
         ODIE_CUDA(cudaGetDevice(&device));
@@ -315,12 +319,11 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
                                            COARSE_SMEM_FLOATS * 4));
             configured |= 1ull << device;
         }
-        encode_backward_shared_kernel<<<dim3(max_blocks, coarse), 512, bytes, stream>>>(a, src.table, list, upstream, grad,
-                                                                                       mask);
+        encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad, mask);
         note_launch();
     }
     const int active = a.active < a.levels ? a.active : a.levels;
-    if (coarse == active) return;  // every level took the shared-memory path
+    if (list.count == active) return;  // every level took the shared-memory path
     encode_backward_kernel<false><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, skip,
                                                                                mask);
     note_launch();
