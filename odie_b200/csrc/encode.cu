@@ -134,7 +134,7 @@ __device__ __forceinline__ float upstream_value(const __half* __restrict__ up, c
     return __half2float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
 }
 
-// Visiting order of the scatter kernels.  Training batches are often spatially
+// Visiting order of the direct scatter kernel.  Training batches are often spatially
 // coherent (the reference's default stratified sampler emits neighbouring pixels
 // consecutively), and then threads that run together would reduce into the same
 // table entries and serialise on them.  Thread t therefore takes coordinate
@@ -204,33 +204,101 @@ struct CoarseList {
     int offset[MAX_LEVELS];   // first float of each listed level's tables in shared memory
 };
 
+// Shared-memory atomics serialise on equal addresses, and spatially coherent
+// batches (stratified sampling) put a warp's coordinates into the same coarse
+// cell.  On levels with at most RUN_RES cells per axis the warp first combines
+// lanes that share a cell: all 32 lanes in one cell -> a butterfly sum and one
+// updating lane; no two neighbouring lanes in one cell (typical of random
+// order) -> every lane updates; otherwise runs of consecutive lanes with the
+// same cell are summed by a segmented scan and the last lane of each run
+// updates.  Any order is correct; the saving grows with the coherence.
+constexpr int RUN_RES = 64;
+
+__device__ __forceinline__ void run_sums(float (&v)[8], bool head) {
+    const int lane = threadIdx.x & 31;
+    bool f = head;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        float up[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) up[j] = __shfl_up_sync(0xffffffffu, v[j], d);
+        const bool fu = __shfl_up_sync(0xffffffffu, f, d);
+        if (lane >= d && !f) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(up[j], v[j]);
+        }
+        if (lane >= d) f = f || fu;
+    }
+}
+
 __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const EncodeArgs a,
                                                                      const __grid_constant__ LevelTable table,
                                                                      const __grid_constant__ CoarseList list,
                                                                      const __half* __restrict__ upstream,
-                                                                     float* __restrict__ grad, uint32_t mask) {
+                                                                     float* __restrict__ grad) {
     extern __shared__ float acc[];
     const int experts = a.expert ? a.experts : 1;
+    const int lane = threadIdx.x & 31;
     for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
     __syncthreads();
-    const long long domain = mask ? (long long)mask + 1 : a.n;  // visiting positions (see visit())
-    const long long chunk = (domain + gridDim.x - 1) / gridDim.x;
+    const long long chunk = (a.n + gridDim.x - 1) / gridDim.x;
     const long long begin = (long long)blockIdx.x * chunk;
-    const long long end = begin + chunk < domain ? begin + chunk : domain;
-    for (long long t = begin + threadIdx.x; t < end; t += blockDim.x) {
-        const long long i = visit(t, mask);
-        if (i >= a.n) continue;
-        const int e = a.expert ? __ldg(a.expert + i) : 0;
-        if (e < 0 || e >= experts) continue;  // an id outside the tables would land outside shared memory
-        const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+    const long long end = begin + chunk < a.n ? begin + chunk : a.n;
+    // whole warps iterate together (the run sums shuffle across the warp)
+    for (long long base = begin + (threadIdx.x & ~31); base < end; base += blockDim.x) {
+        const long long i = base + lane;
+        int e = 0;
+        bool valid = i < end;
+        float2 p = make_float2(0.0f, 0.0f);
+        if (valid) {
+            e = a.expert ? __ldg(a.expert + i) : 0;
+            valid = e >= 0 && e < experts;  // an id outside the tables would land outside shared memory
+            p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+        }
         for (int c = 0; c < list.count; ++c) {
             const Level d = table.level[list.level[c]];
             const Corner4 g = geometry(p.x, p.y, d.scale);
-            if (!level_on(d, g, a.bitmap)) continue;
+            const bool on = valid && level_on(d, g, a.bitmap);
+            float* const tab = acc + list.offset[c] + e * d.points * d.F;
+            if (d.F == 2 && d.res <= RUN_RES) {  // warp-uniform branch
+                // cell key within this expert's table; lanes without a contribution get distinct negative keys
+                const int key = on ? e * d.res * d.res + level_cell(d, g) : -1 - lane;
+                const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+                const int next = __shfl_down_sync(0xffffffffu, key, 1);
+                const unsigned joined = __ballot_sync(0xffffffffu, lane > 0 && prev == key);
+                float v[8];
+                const float u0 = on ? upstream_value(upstream, a, i, d.col) : 0.0f;
+                const float u1 = on ? upstream_value(upstream, a, i, d.col + 1) : 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    v[2 * k] = __fmul_rn(g.w[k], u0);
+                    v[2 * k + 1] = __fmul_rn(g.w[k], u1);
+                }
+                bool writer = on;
+                if (joined == 0xfffffffeu) {  // one cell for the whole warp
+#pragma unroll
+                    for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], m));
+                    writer = on && lane == 0;
+                } else if (joined) {  // runs of lanes sharing a cell
+                    run_sums(v, lane == 0 || prev != key);
+                    writer = on && (lane == 31 || next != key);
+                }
+                if (writer) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int row = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+                        if (v[2 * k] != 0.0f) atomicAdd(tab + 2 * row, v[2 * k]);
+                        if (v[2 * k + 1] != 0.0f) atomicAdd(tab + 2 * row + 1, v[2 * k + 1]);
+                    }
+                }
+                continue;
+            }
+            if (!on) continue;
             int rows[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
-            float* const tab = acc + list.offset[c] + e * d.points * d.F;
             for (int f = 0; f < d.F; ++f) {
                 const float v = upstream_value(upstream, a, i, d.col + f);
                 if (v == 0.0f) continue;
@@ -319,7 +387,7 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
                                            COARSE_SMEM_FLOATS * 4));
             configured |= 1ull << device;
         }
-        encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad, mask);
+        encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
         note_launch();
     }
     const int active = a.active < a.levels ? a.active : a.levels;

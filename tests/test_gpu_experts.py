@@ -98,11 +98,13 @@ def test_expert_hash_query_bit_exact_and_scatter(cuda):
           'expert scatter')
 
 
-@pytest.mark.parametrize('experts', [4, 16])
-def test_experts_step_matches_oracle(cuda, experts):
+@pytest.mark.parametrize('experts,order', [(4, 'random'), (16, 'random'), (4, 'sorted')])
+def test_experts_step_matches_oracle(cuda, experts, order):
+    """order 'sorted': raster-ordered ids, so neighbouring lanes share cells (long runs in the scatter)."""
     config, model, rgb, opt = setup(experts=experts)
     n = 1000
-    ids = torch.from_numpy(np.random.default_rng(1).integers(0, SHAPE[0] * SHAPE[1], n)).cuda()
+    ids_np = np.random.default_rng(1).integers(0, SHAPE[0] * SHAPE[1], n)
+    ids = torch.from_numpy(np.sort(ids_np) if order == 'sorted' else ids_np).cuda()
     tables = model.grid.detach().cpu().numpy().copy()
     router_table = model.router_grid.detach().cpu().numpy().copy()
     router_params = model.gate.params.detach().cpu().numpy().copy()

@@ -61,12 +61,15 @@ def reference(model, rgb, ids, grid, gate, dec, router=True, k=0, softplus=False
                                  router=router, k_fixed=k, softplus=softplus)
 
 
-@pytest.mark.parametrize('router,k,activation', [(True, 0, 'sigmoid'), (True, 3, 'softplus'), (False, 0, 'sigmoid')])
-def test_step_gradients_match_oracle(cuda, router, k, activation):
+@pytest.mark.parametrize('router,k,activation,order', [(True, 0, 'sigmoid', 'random'), (True, 3, 'softplus', 'random'),
+                                                      (False, 0, 'sigmoid', 'random'), (True, 0, 'sigmoid', 'sorted')])
+def test_step_gradients_match_oracle(cuda, router, k, activation, order):
+    """order 'sorted': raster-ordered ids, so neighbouring lanes share cells (long runs in the scatter)."""
     config, model, rgb, opt = setup(router=router, k=k, activation=activation)
     grid, gate, dec = snapshot(model)
     n = 1000  # not a multiple of the 16-row tiles
-    ids = torch.from_numpy(np.random.default_rng(1).integers(0, SHAPE[0] * SHAPE[1], n)).cuda()
+    ids_np = np.random.default_rng(1).integers(0, SHAPE[0] * SHAPE[1], n)
+    ids = torch.from_numpy(np.sort(ids_np) if order == 'sorted' else ids_np).cuda()
     lib = _lib.library()
     opt.call('step_grads', ids.data_ptr(), n, 2)
     torch.cuda.synchronize()
