@@ -86,6 +86,10 @@ constexpr long long TABLE_STEPS = 1LL << 22;  // Adam bias-correction tables (st
 
 struct Runtime {
     cudaStream_t stream = nullptr;
+    // Routed experts: the router-grid scatter runs on a second stream, concurrently with the
+    // expert-table scatter (fork/join by events, so a captured graph keeps both branches).
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_event = nullptr, join_event = nullptr;
     int device = 0;
     long long total = 0, capacity = 65536;
     int image_width = 0, image_height = 0, mode = 0, warp_limit = 128;
@@ -213,6 +217,9 @@ struct Runtime {
         vis.allocate((long long)levels * capacity / 32);  // bit-packed [levels][capacity / 32]
         error_flag.allocate(1);
         if (experts) {
+            ODIE_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+            ODIE_CUDA(cudaEventCreateWithFlags(&fork_event, cudaEventDisableTiming));
+            ODIE_CUDA(cudaEventCreateWithFlags(&join_event, cudaEventDisableTiming));
             router_half.allocate(router_total);
             router_grad.allocate(router_total);
             router_m.allocate(router_total);
@@ -512,18 +519,25 @@ struct Runtime {
         stage_end(slot);
         slot = stage_begin(S_ENCODE_BWD);
         ea.row_major = true;  // the heads write each coordinate's gradient values as one row
-        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
         if (experts) {
+            ODIE_CUDA(cudaEventRecord(fork_event, stream));
+            ODIE_CUDA(cudaStreamWaitEvent(side, fork_event, 0));
             LevelSource rsrc;
             rsrc.table = router_table;
             EncodeArgs ra = router_encode_args(n);
             ra.row_major = true;
-            launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, stream);
+            launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, side);
+            launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);  // needs only the heads kernel
+            ODIE_CUDA(cudaEventRecord(join_event, side));
         }
+        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
+        if (experts) ODIE_CUDA(cudaStreamWaitEvent(stream, join_event, 0));
         stage_end(slot);
-        slot = stage_begin(S_REDUCE);
-        launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), stream);
-        stage_end(slot);
+        if (!experts) {
+            slot = stage_begin(S_REDUCE);
+            launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), stream);
+            stage_end(slot);
+        }
         if (update == 1) grid_update();
         else if (update == 0) {
             launch_zero(grid_grad.ptr, total, stream);
@@ -566,6 +580,9 @@ struct Runtime {
 
     ~Runtime() {
         for (auto& e : events) cudaEventDestroy(e);
+        if (fork_event) cudaEventDestroy(fork_event);
+        if (join_event) cudaEventDestroy(join_event);
+        if (side) cudaStreamDestroy(side);
     }
 
     void decode(long long begin, long long n, float* out_rgb, uint8_t* out_rgb8) {
