@@ -134,50 +134,121 @@ __device__ __forceinline__ float upstream_value(const __half* __restrict__ up, c
     return __half2float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
 }
 
-// Visiting order of the direct scatter kernel.  Training batches are often spatially
-// coherent (the reference's default stratified sampler emits neighbouring pixels
-// consecutively), and then threads that run together would reduce into the same
-// table entries and serialise on them.  Thread t therefore takes coordinate
-// (t * PERM_MULT) mod 2^k, 2^k >= n (indices >= n are skipped): a bijection that
-// scatters neighbouring coordinates across the launch.  mask = 2^k - 1, or 0 for
-// the identity order.
+// Visiting order of the direct scatter kernel.  Training batches are often
+// spatially coherent (the reference's default stratified sampler emits
+// neighbouring pixels consecutively), and then warps that run together would
+// reduce into the same table entries and serialise on them.  The kernel keeps
+// each warp on 32 consecutive coordinates (so lanes that share a cell can be
+// combined, below) but scrambles the order of these 32-coordinate groups: warp w
+// takes group (w * PERM_MULT) mod 2^k, 2^k >= the number of groups (groups past
+// the end are skipped) -- a bijection that spreads neighbouring groups across
+// the launch.  mask = 2^k - 1.
 constexpr uint32_t PERM_MULT = 0x9E3779B1u;
 __device__ __forceinline__ long long visit(long long t, uint32_t mask) {
     return mask ? (long long)((uint32_t(t) * PERM_MULT) & mask) : t;
 }
 
-// Direct scatter: one thread per coordinate over all its levels not in
-// skip_levels (those go through the shared-memory kernel below).
+// Sum runs of consecutive lanes with equal keys (segmented inclusive scan):
+// afterwards the last lane of each run holds the run's totals.
+__device__ __forceinline__ void run_sums(float (&v)[8], bool head) {
+    const int lane = threadIdx.x & 31;
+    bool f = head;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        float up[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) up[j] = __shfl_up_sync(0xffffffffu, v[j], d);
+        const bool fu = __shfl_up_sync(0xffffffffu, f, d);
+        if (lane >= d && !f) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(up[j], v[j]);
+        }
+        if (lane >= d) f = f || fu;
+    }
+}
+
+// Combine the 8 corner updates (4 corners x 2 features) of lanes that share a
+// cell (key): all lanes in one cell -> butterfly sum, lane 0 writes; no two
+// neighbouring lanes in one cell -> every lane writes; otherwise runs of equal
+// keys are summed and the last lane of each run writes.  Returns whether this
+// lane writes.  Warp-collective.
+__device__ __forceinline__ bool combine_lanes(float (&v)[8], long long key, bool on) {
+    const int lane = threadIdx.x & 31;
+    const long long prev = __shfl_up_sync(0xffffffffu, key, 1);
+    const long long next = __shfl_down_sync(0xffffffffu, key, 1);
+    const unsigned joined = __ballot_sync(0xffffffffu, lane > 0 && prev == key);
+    if (joined == 0xfffffffeu) {  // one cell for the whole warp
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], m));
+        return on && lane == 0;
+    }
+    if (joined) {
+        run_sums(v, lane == 0 || prev != key);
+        return on && (lane == 31 || next != key);
+    }
+    return on;
+}
+
+// Direct scatter: one warp per 32 consecutive coordinates (group order
+// scrambled), each lane one coordinate over all its levels not in skip_levels
+// (those go through the shared-memory kernel below).  F=2 levels combine lanes
+// that share a cell before the 8-byte vector reductions.
 template <bool FROM_DESC>
 __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
                                                               const __grid_constant__ LevelTable table,
                                                               const __half* __restrict__ upstream,
                                                               float* __restrict__ grad, unsigned skip_levels,
                                                               uint32_t mask) {
-    const long long i = visit((long long)blockIdx.x * blockDim.x + threadIdx.x, mask);
-    if (i >= a.n) return;
-    const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
-    const long long base = a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL;
+    const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const long long i = visit(warp_id, mask) * 32 + lane;
+    const bool valid = i < a.n;
+    if (__all_sync(0xffffffffu, !valid)) return;  // a whole group past the end (uniform per warp)
+    float2 p = make_float2(0.0f, 0.0f);
+    long long base = 0;
+    int e = 0;
+    if (valid) {
+        p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+        if (a.expert) {
+            e = __ldg(a.expert + i);
+            base = (long long)e * a.expert_stride;
+        }
+    }
     const int levels = a.active < a.levels ? a.active : a.levels;
-#pragma unroll 4
+#pragma unroll 2
     for (int l = 0; l < levels; ++l) {
-        if (skip_levels >> l & 1u) continue;
+        if (skip_levels >> l & 1u) continue;  // uniform
         const Level d = fetch_level<FROM_DESC>(desc, table, l);
         const Corner4 g = geometry(p.x, p.y, d.scale);
-        if (!level_on(d, g, a.bitmap)) continue;
+        const bool on = valid && level_on(d, g, a.bitmap);
         float* const level_grad = grad + d.offset + base;
-        int rows[4];
-        if (d.F == 2) {
-            const float v0 = upstream_value(upstream, a, i, d.col);
-            const float v1 = upstream_value(upstream, a, i, d.col + 1);
-            if (v0 == 0.0f && v1 == 0.0f) continue;
+        if (d.F == 2) {  // uniform
+            const float u0 = on ? upstream_value(upstream, a, i, d.col) : 0.0f;
+            const float u1 = on ? upstream_value(upstream, a, i, d.col + 1) : 0.0f;
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[2 * k] = __fmul_rn(g.w[k], u0);
+                v[2 * k + 1] = __fmul_rn(g.w[k], u1);
+            }
+            // cell key (expert, cell): equal keys share the 4 corner entries; lanes without a contribution
+            // get distinct negative keys
+            const long long key = on ? ((long long)e << 32) + level_cell(d, g) : -1LL - lane;
+            if (!combine_lanes(v, key, on)) continue;
+            if (v[0] == 0.0f && v[1] == 0.0f && v[2] == 0.0f && v[3] == 0.0f && v[4] == 0.0f && v[5] == 0.0f &&
+                v[6] == 0.0f && v[7] == 0.0f)
+                continue;
+            int rows[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                red_add_v2(level_grad + 2LL * rows[k], __fmul_rn(g.w[k], v0), __fmul_rn(g.w[k], v1));
+            for (int k = 0; k < 4; ++k) red_add_v2(level_grad + 2LL * rows[k], v[2 * k], v[2 * k + 1]);
             continue;
         }
+        if (!on) continue;
+        int rows[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
         for (int c = 0; c < d.F; ++c) {
@@ -204,32 +275,11 @@ struct CoarseList {
     int offset[MAX_LEVELS];   // first float of each listed level's tables in shared memory
 };
 
-// Shared-memory atomics serialise on equal addresses, and spatially coherent
-// batches (stratified sampling) put a warp's coordinates into the same coarse
-// cell.  On levels with at most RUN_RES cells per axis the warp first combines
-// lanes that share a cell: all 32 lanes in one cell -> a butterfly sum and one
-// updating lane; no two neighbouring lanes in one cell (typical of random
-// order) -> every lane updates; otherwise runs of consecutive lanes with the
-// same cell are summed by a segmented scan and the last lane of each run
-// updates.  Any order is correct; the saving grows with the coherence.
+// Shared-memory atomics serialise on equal addresses too: on levels with at most
+// RUN_RES cells per axis the lanes of a warp that share a cell are combined first
+// (combine_lanes); any visiting order is correct, the saving grows with the
+// coherence of the batch.
 constexpr int RUN_RES = 64;
-
-__device__ __forceinline__ void run_sums(float (&v)[8], bool head) {
-    const int lane = threadIdx.x & 31;
-    bool f = head;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        float up[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) up[j] = __shfl_up_sync(0xffffffffu, v[j], d);
-        const bool fu = __shfl_up_sync(0xffffffffu, f, d);
-        if (lane >= d && !f) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(up[j], v[j]);
-        }
-        if (lane >= d) f = f || fu;
-    }
-}
 
 __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const EncodeArgs a,
                                                                      const __grid_constant__ LevelTable table,
@@ -262,10 +312,7 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
             float* const tab = acc + list.offset[c] + e * d.points * d.F;
             if (d.F == 2 && d.res <= RUN_RES) {  // warp-uniform branch
                 // cell key within this expert's table; lanes without a contribution get distinct negative keys
-                const int key = on ? e * d.res * d.res + level_cell(d, g) : -1 - lane;
-                const int prev = __shfl_up_sync(0xffffffffu, key, 1);
-                const int next = __shfl_down_sync(0xffffffffu, key, 1);
-                const unsigned joined = __ballot_sync(0xffffffffu, lane > 0 && prev == key);
+                const long long key = on ? ((long long)e << 32) + level_cell(d, g) : -1LL - lane;
                 float v[8];
                 const float u0 = on ? upstream_value(upstream, a, i, d.col) : 0.0f;
                 const float u1 = on ? upstream_value(upstream, a, i, d.col + 1) : 0.0f;
@@ -274,18 +321,7 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
                     v[2 * k] = __fmul_rn(g.w[k], u0);
                     v[2 * k + 1] = __fmul_rn(g.w[k], u1);
                 }
-                bool writer = on;
-                if (joined == 0xfffffffeu) {  // one cell for the whole warp
-#pragma unroll
-                    for (int m = 16; m > 0; m >>= 1)
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], m));
-                    writer = on && lane == 0;
-                } else if (joined) {  // runs of lanes sharing a cell
-                    run_sums(v, lane == 0 || prev != key);
-                    writer = on && (lane == 31 || next != key);
-                }
-                if (writer) {
+                if (combine_lanes(v, key, on)) {
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const int row = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
@@ -352,8 +388,9 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
                             cudaStream_t stream) {
     if (a.n <= 0 || a.levels <= 0) return;
     ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
-    const uint32_t mask = visit_mask(a.n);
-    const long long threads = mask ? (long long)mask + 1 : a.n;
+    const long long groups = (a.n + 31) / 32;  // the direct scatter scrambles 32-coordinate groups
+    const uint32_t mask = visit_mask(groups);
+    const long long threads = 32 * (mask ? (long long)mask + 1 : groups);
     if (src.descriptors) {
         encode_backward_kernel<true><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table, upstream,
                                                                                   grad, 0u, mask);

@@ -69,7 +69,8 @@ struct TcSmem {
     static constexpr int da = dy + 4096;                // [128 x 16] gate logit gradient
     static constexpr int bar = da + 4096;               // mbarrier: data products of a phase
     static constexpr int bar_dw = bar + 8;              // mbarrier: weight-gradient products of a phase
-    static constexpr int tmem = bar_dw + 8;             // TMEM base address
+    static constexpr int drain = bar_dw + 8;            // mbarrier: every issuing warp's products (error exit)
+    static constexpr int tmem = drain + 8;              // TMEM base address
     static constexpr int x2 = (tmem + 8 + 127) / 128 * 128;  // [128 x W] second router-feature buffer (experts)
     static constexpr int total = tmem + 8;
     static constexpr int total_experts = x2 + XB;
@@ -191,6 +192,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     const int t = threadIdx.x, warp = t >> 5;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
     uint64_t* bar_dw = reinterpret_cast<uint64_t*>(smem + S::bar_dw);
+    uint64_t* drain = reinterpret_cast<uint64_t*>(smem + S::drain);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
     const uint32_t sbase = tc::smem_u32(smem);
 
@@ -210,7 +212,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
     if (t == 0) {
         tc::bar_init(bar, 1);
-        tc::bar_init(bar_dw, 1);
+        tc::bar_init(bar_dw, TC_THREADS / 32);  // one commit per warp: each warp issues part of every weight-gradient product
+        tc::bar_init(drain, TC_THREADS / 32);
         tc::fence_bar_init();
     }
     if (warp == 0) {
@@ -223,12 +226,24 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
+    if (TRAIN) {
+        // The weight-gradient accumulators start at zero and every product accumulates: the warps issue
+        // parts of one product, so no single MMA can be relied on to come first and overwrite.
+        float zero[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) zero[c] = 0.0f;
+        for (uint32_t col = T_DWD2; col < TMEM_COLUMNS; col += 16) tc::tmem_st16(lane_addr + col, zero);
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+    }
 
     const FeatureMap& fm = a.fmap;
     const int L = a.levels;
     const long long vis_words = a.stride >> 5;
     Issuer is{bar, bar_dw};
-    uint32_t dw_accumulate = 0;  // 0 until the first tile's weight-gradient products
+    uint32_t dw_accumulate = 0;  // 1 once a tile has added to the weight gradients
     const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_G2 = tc::idesc(128, 16, 0, 0);
     constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
@@ -369,7 +384,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
         }
         uint32_t gh2_mask = 0;
-        uint32_t zh[ROUTER_OUT / 2];  // fp16 router logits recomputed for the backward (experts, training)
         if (EXPERTS) {
             // ---- decoder input: the routed expert's features x half(p), one rounding per feature
             const __half2 ph = __float2half2_rn(prob);
@@ -405,9 +419,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh2, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
                 if (!is.complete()) break;
                 float z[ROUTER_OUT];
+                uint32_t zs[ROUTER_OUT / 2];
                 tc::tmem_ld16(lane_addr + T_ACC, z);
 #pragma unroll
-                for (int j = 0; j < ROUTER_OUT / 2; ++j) zh[j] = pack_half2(__float2half_rn(z[2 * j]), __float2half_rn(z[2 * j + 1]));
+                for (int j = 0; j < ROUTER_OUT / 2; ++j) zs[j] = pack_half2(__float2half_rn(z[2 * j]), __float2half_rn(z[2 * j + 1]));
+                // kept for the backward in this row of the DA buffer, which nothing reads before then
+                store_chunk(smem, S::da, t, 0, make_uint4(zs[0], zs[1], zs[2], zs[3]));
+                store_chunk(smem, S::da, t, 1, make_uint4(zs[4], zs[5], zs[6], zs[7]));
             }
         }
         // ---- decoder hidden 1, hidden 2, output
@@ -473,9 +491,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0),
                     tc::idesc(128, 64, 0, 1), 0);
             tc::commit(bar);
-            for (int s = 0; s < 8; ++s)
+        }
+        if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                 tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::dy, 128, s),
-                        tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+                        tc::idesc(64, 16, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         uint32_t packed[32];
@@ -493,9 +513,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s),
                         tc::idesc(128, 64, 0, 1), s > 0);
             tc::commit(bar);
-            for (int s = 0; s < 8; ++s)
+        }
+        if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                 tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::h1, 128, s),
-                        tc::idesc(64, 64, 1, 1), dw_accumulate | uint32_t(s > 0));
+                        tc::idesc(64, 64, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
@@ -512,9 +534,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s),
                         tc::idesc(128, W, 0, 1), s > 0);
             tc::commit(bar);
-            for (int s = 0; s < 8; ++s)
+        }
+        if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                 tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + in_buf, 128, s),
-                        tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+                        tc::idesc(64, W, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
@@ -535,10 +559,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 dp = __fmaf_rn(__half2float(v1), __half2float(hi_half(raw[p])), dp);
             }
             // ---- logit gradients: softmax of the recomputed fp16 logits over the live experts
+            uint32_t zh[ROUTER_OUT / 2];
+            {
+                const uint4 lo = *reinterpret_cast<const uint4*>(smem + S::da + tc::blocked(TC_TILE, t, 0));
+                const uint4 hi = *reinterpret_cast<const uint4*>(smem + S::da + tc::blocked(TC_TILE, t, 8));
+                zh[0] = lo.x; zh[1] = lo.y; zh[2] = lo.z; zh[3] = lo.w;
+                zh[4] = hi.x; zh[5] = hi.y; zh[6] = hi.z; zh[7] = hi.w;
+            }
             float z[ROUTER_OUT], zmax = -INFINITY;
 #pragma unroll
             for (int j = 0; j < ROUTER_OUT; ++j) {
-                z[j] = __half2float((j & 1) ? hi_half(zh[j >> 1]) : lo_half(zh[j >> 1]));
+                z[j] = __half2float((j & 1) ? hi_half(zh[j >> 1]) : lo_half(zh[j >> 1]));  // fp16 logits of the forward
                 if (j < a.experts) zmax = fmaxf(zmax, z[j]);
             }
             float sum = 0.0f;
@@ -564,9 +595,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
                         tc::idesc(128, 32, 0, 1), 0);
                 tc::commit(bar);
-                for (int s = 0; s < 8; ++s)
+            }
+            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                     tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh2, 128, s), tc::mnmajor(sbase + S::da, 128, s),
-                            tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+                            tc::idesc(64, 16, 1, 1), 1u);
                 tc::commit(bar_dw);
             }
             is.wait_data();
@@ -583,9 +616,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::r2, 32, s),
                             tc::idesc(128, 32, 0, 1), s > 0);
                 tc::commit(bar);
-                for (int s = 0; s < 8; ++s)
+            }
+            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                     tc::mma(tmem + T_DWR2, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::gh, 128, s),
-                            tc::idesc(64, 32, 1, 1), dw_accumulate | uint32_t(s > 0));
+                            tc::idesc(64, 32, 1, 1), 1u);
                 tc::commit(bar_dw);
             }
             is.wait_data();
@@ -602,9 +637,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
                             tc::idesc(128, W, 0, 1), s > 0);
                 tc::commit(bar);
-                for (int s = 0; s < 8; ++s)
+            }
+            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                     tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + xbuf, 128, s),
-                            tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+                            tc::idesc(64, W, 1, 1), 1u);
                 tc::commit(bar_dw);
             }
             is.wait_data();
@@ -692,9 +729,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
                         tc::idesc(128, 32, 0, 1), 0);
                 tc::commit(bar);
-                for (int s = 0; s < 8; ++s)
+            }
+            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                     tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh, 128, s), tc::mnmajor(sbase + S::da, 128, s),
-                            tc::idesc(64, 16, 1, 1), dw_accumulate | uint32_t(s > 0));
+                            tc::idesc(64, 16, 1, 1), 1u);
                 tc::commit(bar_dw);
             }
             is.wait_data();
@@ -711,9 +750,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
                             tc::idesc(128, W, 0, 1), s > 0);
                 tc::commit(bar);
-                for (int s = 0; s < 8; ++s)
+            }
+            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
                     tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::x, 128, s),
-                            tc::idesc(64, W, 1, 1), dw_accumulate | uint32_t(s > 0));
+                            tc::idesc(64, W, 1, 1), 1u);
                 tc::commit(bar_dw);
             }
             is.wait_data();
@@ -744,9 +785,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 
     if (!is.ok) {
         if (t == 0) atomicExch(error_flag, 2);
-        // give products still in flight a bounded chance to land before TMEM is released
-        if (t == 0) tc::commit(bar);
-        tc::bar_wait(bar, is.phase, WAIT_LIMIT);
+        // give the products every warp may still have in flight a bounded chance to land before TMEM is released
+        if ((t & 31) == 0) tc::commit(drain);
+        tc::bar_wait(drain, 0, WAIT_LIMIT);
     }
     if (TRAIN) {
         // ---- weight gradients: TMEM (M=64 layout: rows 16w..16w+15 in lanes 32w..32w+15) -> partials
