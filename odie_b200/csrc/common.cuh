@@ -88,20 +88,34 @@ __device__ __forceinline__ int packed_row(const Level& d, const uint64_t* __rest
     return __ldg(prefix + word) + __popcll(__ldg(reinterpret_cast<const unsigned long long*>(node_bitmap) + word) & mask);
 }
 
+// idx mod points without a division in the common cases: a power-of-two table
+// (every hashed level) masks; an index below 2 x points (every in-range dense or
+// plane corner: at most (R+1)^2 - 1 < 2 align8(R^2)) subtracts once; anything
+// else (coordinates outside [0, 1]) takes the full remainder, so no index leaves
+// the table.
+__device__ __forceinline__ uint32_t wrap_index(uint32_t idx, uint32_t points) {
+    if ((points & (points - 1)) == 0) return idx & (points - 1);
+    if (idx < points) return idx;
+    return idx - points < points ? idx - points : idx % points;
+}
+
 // Parameter row of corner k (0: x0y0, 1: x1y0, 2: x0y1, 3: x1y1) of a level.
 __device__ __forceinline__ int corner_row(const Level& d, const Corner4& g, int k,
                                           const uint64_t* __restrict__ node_bitmap, const int* __restrict__ prefix) {
     const int dx = k & 1, dy = k >> 1;
     if (d.kind == PLANE) {
         const int cell = g.ix + g.iy * d.res;
-        const int node = (cell + dx + dy * d.res) % d.points;
+        const int raw = cell + dx + dy * d.res;
+        // the reference's (cell + dx + dy R) % points on a non-negative int; level_on() hides cells outside
+        // the grid, so raw >= 0 here for every visible corner
+        const int node = raw >= 0 ? int(wrap_index(uint32_t(raw), uint32_t(d.points))) : raw % d.points;
         return packed_row(d, node_bitmap, prefix, node);
     }
     const uint32_t cx = uint32_t(g.ix + dx), cy = uint32_t(g.iy + dy);
     uint32_t idx;
     if (d.kind == HASH_HASHED) idx = cx ^ (cy * 2654435761u);
     else idx = cx + cy * uint32_t(d.res);
-    return int(idx % uint32_t(d.points));
+    return int(wrap_index(idx, uint32_t(d.points)));
 }
 
 __device__ __forceinline__ int level_cell(const Level& d, const Corner4& g) { return g.ix + g.iy * d.res; }
