@@ -159,6 +159,22 @@ ODIE_API int odie_expert_hash_backward(const float* coords, int64_t n, const uin
                    float* gradient, int64_t parameter_count, uint64_t stream);
 
 /* ------------------------------------------------------------------------
+ * On-device packed-plane index of one level (replaces the host-side
+ * plane_closure / make_node_index / cell bitmap of odie/model.py:36-61,108-110,
+ * rebuilt at every stage boundary).  support: R*R bytes (0/1, a torch bool
+ * tensor), points = align8(R^2).  Writes node_bitmap u64[ceil(points/64)]
+ * (closure presence, bit b of word w = node 64w+b), node_prefix
+ * i32[ceil(points/64)] (exclusive popcount prefix), cell_bitmap u8[points/8]
+ * (LSB-first cell bits), *node_count (closure size, device int64) and, when
+ * nodes is non-NULL, the sorted closure i64[node count] (capacity points).
+ * scratch: i32[odie_plane_index_scratch(R)], caller-owned.  Returns -1 with
+ * odie_error() on invalid sizes.
+ * ------------------------------------------------------------------------ */
+ODIE_API int64_t odie_plane_index_scratch(int resolution);
+ODIE_API int odie_plane_index(const uint8_t* support, int resolution, uint64_t* node_bitmap, int32_t* node_prefix,
+                   uint8_t* cell_bitmap, int64_t* node_count, int64_t* nodes, int32_t* scratch, uint64_t stream);
+
+/* ------------------------------------------------------------------------
  * L2 probe (measurement; no reference counterpart): `operations` random
  * accesses over `table` (table_bytes in 4 KiB..64 MiB, so it stays in L2):
  * mode 0 = 4-byte loads, 1 = 16-byte loads, 2 = 4-byte fp32 reductions,

@@ -718,6 +718,10 @@ int launch_selection_chunk(const double* scores, int n, int points, int resoluti
 }  // namespace odie
 
 namespace odie {
+long long plane_index_scratch(long long points);
+void launch_plane_index(const uint8_t* support, int resolution, unsigned long long* node_words, int* node_prefix,
+                        uint8_t* cell_bitmap, long long* node_count, long long* nodes, int* scratch,
+                        cudaStream_t stream);
 void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
                      cudaStream_t stream);
 }  // namespace odie
@@ -970,6 +974,22 @@ int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* up
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
         odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, s);
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int64_t odie_plane_index_scratch(int resolution) {
+    if (resolution < 1) return -1;
+    const long long cells = (long long)resolution * resolution;
+    return odie::plane_index_scratch((cells + 7) / 8 * 8);
+}
+
+int odie_plane_index(const uint8_t* support, int resolution, uint64_t* node_bitmap, int32_t* node_prefix,
+                     uint8_t* cell_bitmap, int64_t* node_count, int64_t* nodes, int32_t* scratch, uint64_t stream) {
+    return guarded([&] {
+        odie::launch_plane_index(support, resolution, reinterpret_cast<unsigned long long*>(node_bitmap), node_prefix,
+                                 cell_bitmap, reinterpret_cast<long long*>(node_count), reinterpret_cast<long long*>(nodes),
+                                 scratch, reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
 }

@@ -154,3 +154,92 @@ def hash_levels(encoding):
                         column=level * features, hashed=int(r * r > cap)))
         offset += cap * features
     return out, offset
+
+
+def plane_index_device(support, resolution, with_nodes=True, stream=None):
+    """Node presence words, exclusive word prefix, cell bitmap, node count and (optionally) the sorted closure of
+    one level, built on the GPU (odie_plane_index).  support: CUDA bool [R^2].  Returns device tensors and the node
+    count as a device int64 scalar; nothing is synchronised."""
+    from . import _lib
+    if not support.is_cuda or support.dtype != torch.bool or tuple(support.shape) != (resolution * resolution,):
+        raise ValueError('support must be a flat CUDA bool R^2 tensor')
+    device = support.device
+    points = align8(resolution * resolution)
+    words = -(-points // 64)
+    node_bitmap = torch.empty(words, dtype=torch.uint64, device=device)
+    prefix = torch.empty(words, dtype=torch.int32, device=device)
+    bitmap = torch.empty(points // 8, dtype=torch.uint8, device=device)
+    count = torch.empty((), dtype=torch.int64, device=device)
+    nodes = torch.empty(points, dtype=torch.int64, device=device) if with_nodes else None
+    lib = _lib.library()
+    scratch = torch.empty(int(lib.odie_plane_index_scratch(resolution)), dtype=torch.int32, device=device)
+    support = support.contiguous()
+    _lib.check(lib.odie_plane_index(support.data_ptr(), resolution, node_bitmap.data_ptr(), prefix.data_ptr(),
+                                    bitmap.data_ptr(), count.data_ptr(), _lib.ptr(nodes), scratch.data_ptr(),
+                                    _lib.stream_handle(stream)), 'odie_plane_index')
+    return node_bitmap, prefix, bitmap, count, nodes
+
+
+def make_layout_device(config, supports, plane_dims, plane_node_caps):
+    """make_layout with the per-level closure, node index and cell bitmap built on the GPU.
+
+    supports: CUDA bool [R^2] tensors.  Same validation and the same tables as make_layout (device tensors; the
+    'nodes' entries are device int64 tensors); one host synchronisation reads all levels' node counts."""
+    resolutions = [int(r) for r in config['resolutions']]
+    levels = int(config['n_levels'])
+    if not (len(resolutions) == len(supports) == len(plane_dims) == len(plane_node_caps) == levels):
+        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
+    if any(f not in (1, 2, 4) for f in plane_dims):
+        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
+    if config['representation'] != 'xy_planes':
+        raise ValueError('XY-only representation is required')
+    check_gate_k(config)
+    if config['gate_topology'] != 'shared' or config['gate_position'] != 'feature':
+        raise ValueError('Preserve the shared feature gate')
+    initial = int(config['initial_active_prefix'])
+    built = []
+    for level in range(levels):
+        r, support = resolutions[level], supports[level]
+        if not support.is_cuda or support.dtype != torch.bool or tuple(support.shape) != (r * r,):
+            raise ValueError('Support must be a flat CUDA bool R^2 tensor')
+        built.append(plane_index_device(support, r))
+    counts = torch.stack([b[3] for b in built]).cpu().tolist()
+    full = torch.stack([s.all() for s in supports]).cpu().tolist()
+    allowed = torch.stack([s.sum() for s in supports]).cpu().tolist()
+    descriptors, bitmaps, node_words, prefixes, info, clean = [], [], [], [], [], []
+    params = column = word_offset = byte_offset = 0
+    for level in range(levels):
+        r, dim, cap = resolutions[level], int(plane_dims[level]), int(plane_node_caps[level])
+        if level < initial and not full[level]:
+            raise ValueError('Declared initial full-cover supports must remain full')
+        points = align8(r * r)
+        count = int(counts[level])
+        if cap % 8 or not count <= cap <= points:
+            raise ValueError('Aligned node capacity must contain the complete interpolation closure')
+        if points > INT32_MAX or params + cap * dim > INT32_MAX:
+            raise ValueError('Native points and packed offsets must fit int32 addressing')
+        bits, prefix, bitmap, _, nodes = built[level]
+        direct = count == points
+        if direct:
+            word_start, words = -1, 0
+        else:
+            word_start, words = word_offset, bits.numel()
+            node_words.append(bits)
+            prefixes.append(prefix)
+            word_offset += words
+        descriptors.append([r, points, params, word_start, byte_offset, dim, column, int(direct)])
+        info.append({'level': level, 'resolution': r, 'plane_dim': dim, 'allowed_cells': int(allowed[level]),
+                     'plane_retained_nodes': count, 'plane_node_capacity': cap, 'plane_unused_slots': cap - count,
+                     'native_plane_points': points, 'plane_offset': params, 'feature_offset': column,
+                     'nodes': nodes[:count], 'node_index_words': words, 'direct_node_access': direct})
+        bitmaps.append(bitmap)
+        clean.append(supports[level].clone())
+        params += cap * dim
+        column += dim
+        byte_offset += bitmap.numel()
+    device = supports[0].device
+    return {'descriptors': torch.tensor(descriptors, dtype=torch.int32, device=device),
+            'node_bitmap': torch.cat(node_words) if node_words else torch.empty(0, dtype=torch.uint64, device=device),
+            'node_prefix': torch.cat(prefixes) if prefixes else torch.empty(0, dtype=torch.int32, device=device),
+            'bitmap': torch.cat(bitmaps), 'levels': info, 'supports': clean,
+            'params': params, 'input_width': column}
