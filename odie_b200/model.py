@@ -16,7 +16,7 @@ from torch import nn
 
 from . import _lib
 from .layout import (ADDRESSING_VERSION, COORDINATE_VERSION, LAYOUT_VERSION, align8, check_gate_k, hash_levels,
-                     make_layout, make_node_index, plane_closure)
+                     make_layout, make_layout_device, make_node_index, plane_closure, plane_index_device)
 
 __all__ = ['router_weights', 'align8', 'plane_closure', 'make_node_index', 'make_layout', 'PackedQuery',
            'HashQuery', 'ExpertHashQuery', 'route', 'Head', 'PackedXYPlanes', 'HashGrid', 'RoutedExperts',
@@ -261,16 +261,20 @@ class PackedXYPlanes(nn.Module):
         resolution = self.config['resolutions'][level]
         if support.device.type != 'cpu' or support.dtype != torch.bool or tuple(support.shape) != (resolution**2,):
             raise ValueError('New support must be a flat CPU bool R^2 tensor')
-        nodes = plane_closure(support.numpy(), resolution)
-        cap = self.plane_node_caps[level]
-        if not 0 < nodes.numel() <= cap:
+        device = self.grid.device
+        count = int(plane_index_device(support.to(device), resolution, with_nodes=False)[3])
+        if not 0 < count <= self.plane_node_caps[level]:
             raise ValueError('New support requires a nonempty complete closure within its cap')
         storage = self.grid.data_ptr()
         supports = list(self.supports)
         supports[level] = support.clone()
-        layout = make_layout(self.config, supports, self.plane_dims, self.plane_node_caps)
+        # every level's closure, node index and cell bitmap rebuilt on the GPU (odie_plane_index)
+        layout = make_layout_device(self.config, [s.to(device) for s in supports], self.plane_dims,
+                                    self.plane_node_caps)
+        nodes = layout['levels'][level]['nodes']
         for name in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap'):
-            setattr(self, name, layout.pop(name).to(self.grid.device))
+            setattr(self, name, layout.pop(name))
+        layout['supports'] = [s.cpu() for s in layout['supports']]
         self.layout, self.supports = layout, layout['supports']
         self._initialize_plane(level)
         if self.grid.data_ptr() != storage:

@@ -88,3 +88,34 @@ def test_device_index_at_gigapixel_resolution(cuda):
     assert np.array_equal(bits.cpu().numpy(), h_bits) and np.array_equal(prefix.cpu().numpy(), h_prefix)
     assert np.array_equal(bitmap.cpu().numpy(), h_bitmap)
     print(f'R=8192 plane index: device {device_s * 1e3:.2f} ms, host {host_s * 1e3:.0f} ms')
+
+
+def test_activate_support_builds_the_host_layout_on_device(cuda):
+    """Opening a plane (stage boundary) gives the same tables as the host builder and the reference's init."""
+    from odie_b200.model import PackedXYPlanes
+    from tests.cases import plane_case, plane_config
+    resolutions, dims, supports, caps = plane_case(9, dense=10, packed=4, finest=96)
+    level = 14
+    r = resolutions[level]
+    support = torch.from_numpy(np.random.default_rng(4).random(r * r) < 0.05)
+    caps[level] = layout.align8(layout.plane_closure(support.numpy(), r).numel()) + 8  # fixed at construction
+    config = plane_config(resolutions, dims, 10, seed=9)
+    model = PackedXYPlanes(config, supports, dims, caps)
+    model.set_active_prefix(level)
+    with pytest.raises(ValueError, match='within its cap'):
+        model.activate_support(level, torch.ones(r * r, dtype=torch.bool))
+    report = model.activate_support(level, support)
+    new_supports = list(supports)
+    new_supports[level] = support
+    host = layout.make_layout(config, new_supports, dims, caps)
+    for name in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap'):
+        assert torch.equal(getattr(model, name).cpu(), host[name]), name
+    item = host['levels'][level]
+    nodes = item['nodes']
+    assert report['selected_nodes'] == nodes.numel()
+    seed = ((config['seed'] + 1000003 * (level + 1)) % 2**31 + 104729 * 3) % 2**31
+    dense = torch.empty((item['native_plane_points'], max(2, dims[level])), device='cuda')
+    dense.normal_(0., config['feature_init_std'], generator=torch.Generator(device='cuda').manual_seed(seed))
+    expected = dense.index_select(0, nodes.cuda())[:, :dims[level]].reshape(-1)
+    got = model.grid[item['plane_offset']:item['plane_offset'] + expected.numel()]
+    assert torch.equal(got, expected)
