@@ -107,6 +107,8 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
         }
         if (!a.row_major && (d.col & 1) == 0) {
             reinterpret_cast<__half2*>(out)[(long long)(d.col >> 1) * a.stride + i] = acc;
+        } else if (a.row_major && (d.col & 1) == 0 && (a.width & 1) == 0) {
+            reinterpret_cast<__half2*>(out)[(i * a.width + d.col) >> 1] = acc;
         } else {
             store_feature(out, a.row_major, i, d.col, a.width, a.stride, __low2half(acc));
             store_feature(out, a.row_major, i, d.col + 1, a.width, a.stride, __high2half(acc));
@@ -127,6 +129,42 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
         }
         store_feature(out, a.row_major, i, d.col + c, a.width, a.stride, acc);
     }
+}
+
+// Row-major forward for tables whose levels all have F=2 at columns (2l, 2l+1)
+// (a hash-grid layout) and no visibility output: one thread per coordinate over
+// all its levels, its W-half row written as 16-byte stores.  Used for the router
+// grid, whose small tables stay in L1.
+template <int W>
+__global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeArgs a,
+                                                                  const __grid_constant__ LevelTable table,
+                                                                  const __half* __restrict__ params,
+                                                                  __half* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.n) return;
+    const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
+    const long long base = a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL;
+    uint32_t row[W / 2];
+#pragma unroll
+    for (int l = 0; l < W / 2; ++l) {
+        __half2 acc = __float2half2_rn(0.0f);
+        if (l < a.levels && l < a.active) {
+            const Level d = table.level[l];
+            const Corner4 g = geometry(p.x, p.y, d.scale);
+            if (level_on(d, g, a.bitmap)) {
+                __half2 t[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    t[k] = load_pair(params, base + d.offset + 2LL * corner_row(d, g, k, a.node_bitmap, a.node_prefix));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc = __hfma2(__float2half2_rn(g.w[k]), t[k], acc);
+            }
+        }
+        row[l] = pack_half2(__low2half(acc), __high2half(acc));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + i * W);
+#pragma unroll
+    for (int j = 0; j < W / 8; ++j) dst[j] = make_uint4(row[4 * j], row[4 * j + 1], row[4 * j + 2], row[4 * j + 3]);
 }
 
 __device__ __forceinline__ float upstream_value(const __half* __restrict__ up, const EncodeArgs& a, long long i, int col) {
@@ -366,6 +404,15 @@ void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const fl
     if (a.n <= 0 || a.levels <= 0) return;
     ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
     const dim3 grid(blocks_for(a.n, 256), a.levels);
+    bool rows = !src.descriptors && table16 && !vis && a.row_major && (a.width == 16 || a.width == 32) &&
+                2 * a.levels <= a.width;
+    for (int l = 0; rows && l < a.levels; ++l) rows = src.table.level[l].F == 2 && src.table.level[l].col == 2 * l;
+    if (rows) {
+        if (a.width == 32) encode_forward_rows_kernel<32><<<blocks_for(a.n, 256), 256, 0, stream>>>(a, src.table, table16, out);
+        else encode_forward_rows_kernel<16><<<blocks_for(a.n, 256), 256, 0, stream>>>(a, src.table, table16, out);
+        note_launch();
+        return;
+    }
     if (src.descriptors) {
         if (table32) encode_forward_kernel<float, true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, table32, out, vis);
         else encode_forward_kernel<__half, true><<<grid, 256, 0, stream>>>(a, src.descriptors, src.table, table16, out, vis);

@@ -92,9 +92,9 @@ __device__ __forceinline__ void store_chunk(unsigned char* smem, int base, int r
     *reinterpret_cast<uint4*>(smem + base + tc::blocked(TC_TILE, r, 8 * j)) = q;
 }
 
-// 4-byte asynchronous global -> shared copy; src_bytes = 0 writes zeros.
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+// 16-byte asynchronous global -> shared copy (L2 only); src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_older() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
@@ -271,15 +271,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             if (TRAIN) next_expert = valid ? __ldg(a.expert + i) : 0;
         }
     };
-    // Router features of a tile (experts, training): cp.async into shared buffer `buf`.
+    // Router features of a tile (experts, training; row-major [stride][W]): each row's W halves as
+    // W / 8 16-byte cp.async copies into the blocked layout of shared buffer `buf`.
     auto prefetch_router = [&](long long tile, int buf) {
         const long long i = tile * TC_TILE + t;
         const bool valid = tile < tiles && i < a.n;
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.router_in);
+        const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
 #pragma unroll
-        for (int p = 0; p < PAIRS; ++p)
-            cp_async4(sbase + buf + tc::blocked(TC_TILE, t, 2 * p), valid ? src + (long long)p * a.stride + i : src,
-                      valid ? 4u : 0u);
+        for (int j = 0; j < W / 8; ++j)
+            cp_async16(sbase + buf + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
         cp_async_commit();
     };
     // Visibility: lane l (< levels) loads this warp's word of level l; the

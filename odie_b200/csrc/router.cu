@@ -40,12 +40,24 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const Ro
     for (int c = 0; c < C; ++c) {
         row[c] = first + (long long)c * blockDim.x;
         const long long i = row[c] < a.n ? row[c] : first;  // a missing second row repeats the first, unstored
+        if (a.row_major) {  // the coordinate's row as 16-byte loads
 #pragma unroll
-        for (int p = 0; p < W / 2; ++p) {
-            const __half2 v = __ldg(reinterpret_cast<const __half2*>(a.features) +
-                                    (a.row_major ? i * (W / 2) + p : (long long)p * a.stride + i));
-            x[c][2 * p] = __low2float(v);
-            x[c][2 * p + 1] = __high2float(v);
+            for (int j = 0; j < W / 8; ++j) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(a.features) + i * (W / 8) + j);
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    x[c][8 * j + 2 * h] = __half2float(__ushort_as_half(uint16_t(w4[h] & 0xffffu)));
+                    x[c][8 * j + 2 * h + 1] = __half2float(__ushort_as_half(uint16_t(w4[h] >> 16)));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int p = 0; p < W / 2; ++p) {
+                const __half2 v = __ldg(reinterpret_cast<const __half2*>(a.features) + (long long)p * a.stride + i);
+                x[c][2 * p] = __low2float(v);
+                x[c][2 * p + 1] = __high2float(v);
+            }
         }
     }
     float h1[C][ROUTER_HIDDEN], h2[C][ROUTER_HIDDEN], z[C][ROUTER_OUT];

@@ -408,11 +408,14 @@ struct Runtime {
         return m;
     }
 
+    // Router-grid features are row-major [capacity][router_width]: the heads kernel copies a
+    // coordinate's row into shared memory with 16-byte asynchronous copies.
     EncodeArgs router_encode_args(long long n) const {
         EncodeArgs a = encode_args(n);
         a.levels = router_levels;
         a.active = router_levels;
         a.width = router_width;
+        a.row_major = true;
         return a;
     }
 
@@ -426,6 +429,7 @@ struct Runtime {
         stage_end(slot);
         RouterArgs ra;
         ra.features = router_in.ptr;
+        ra.row_major = true;
         ra.stride = capacity;
         ra.n = n;
         ra.weights = head_half.ptr;
@@ -524,8 +528,7 @@ struct Runtime {
             ODIE_CUDA(cudaStreamWaitEvent(side, fork_event, 0));
             LevelSource rsrc;
             rsrc.table = router_table;
-            EncodeArgs ra = router_encode_args(n);
-            ra.row_major = true;
+            EncodeArgs ra = router_encode_args(n);  // row-major gradient values too
             launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, side);
             launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);  // needs only the heads kernel
             ODIE_CUDA(cudaEventRecord(join_event, side));

@@ -40,7 +40,7 @@ struct MlpArgs {
     float* rgb;           // [n][3] fp32 decode output (decode)
     uint8_t* rgb8;        // [n][3] u8 decode output (decode)
     // GATE_EXPERTS: raw holds the routed expert's features; gate_w the router weights
-    const __half* router_in;  // [W/2][stride] half2 router-grid features
+    const __half* router_in;  // [stride][W] row-major router-grid features
     const float* prob;        // [n] router probability of the chosen expert
     const int* expert;        // [n] chosen expert
     __half* router_gvals;     // [stride][W] router-grid gradient values, row-major (training)

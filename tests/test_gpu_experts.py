@@ -117,7 +117,7 @@ def test_experts_step_matches_oracle(cuda, experts, order):
     W = opt.pointers['input_width']
     xy = opt.copied('xy', (opt.pointers['capacity'], 2), torch.float32)[:n].cpu().numpy()
     assert np.array_equal(xy, ref['xy'])
-    rin = read_pair_major(opt, 'router_in', n, W)
+    rin = read_rows(opt, 'router_in', n, W)
     assert np.array_equal(rin.view(np.uint16), ref['router_features'].view(np.uint16)), 'router-grid features differ'
     expert = opt.copied('expert_ids', (n,), torch.int32).cpu().numpy()
     assert np.array_equal(expert, ref['expert']), 'routing decisions differ'
