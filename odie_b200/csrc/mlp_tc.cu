@@ -259,9 +259,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     auto load_inputs = [&](long long tile) {
         const long long i = tile * TC_TILE + t;
         const bool valid = tile < tiles && i < a.n;
+        if (a.raw_rows) {  // the coordinate's row as 16-byte loads
 #pragma unroll
-        for (int p = 0; p < PAIRS; ++p)
-            next_raw[p] = valid ? __ldg(reinterpret_cast<const uint32_t*>(a.raw) + (long long)p * a.stride + i) : 0u;
+            for (int j = 0; j < PAIRS / 4; ++j) {
+                const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.raw) + i * (PAIRS / 4) + j) : make_uint4(0, 0, 0, 0);
+                next_raw[4 * j] = q.x;
+                next_raw[4 * j + 1] = q.y;
+                next_raw[4 * j + 2] = q.z;
+                next_raw[4 * j + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p)
+                next_raw[p] = valid ? __ldg(reinterpret_cast<const uint32_t*>(a.raw) + (long long)p * a.stride + i) : 0u;
+        }
         if (TRAIN) {
 #pragma unroll
             for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;

@@ -405,6 +405,7 @@ struct Runtime {
         m.expert = expert_ids.ptr;
         m.router_gvals = router_gvals.ptr;
         m.experts = experts;
+        m.raw_rows = experts != 0;
         return m;
     }
 
@@ -445,6 +446,7 @@ struct Runtime {
         ea.expert = expert_ids.ptr;
         ea.expert_stride = expert_total;
         ea.experts = experts;
+        ea.row_major = true;  // one row per coordinate: the per-coordinate gather over all levels
         slot = stage_begin(S_ENCODE_FWD);
         launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, nullptr, stream);
         stage_end(slot);

@@ -26,7 +26,8 @@ enum GateMode : int { GATE_NONE = 0, GATE_LEVELS = 1, GATE_EXPERTS = 2 };
 struct MlpArgs {
     long long n;          // coordinates of this launch
     long long stride;     // pair-major stride of raw/gvals and level stride of vis
-    const __half* raw;    // [W/2][stride] half2 features
+    const __half* raw;    // [W/2][stride] half2 features, or [stride][W] rows when raw_rows
+    bool raw_rows;
     const uint32_t* vis;  // bit-packed visibility [levels][stride / 32]
     const float* target;  // [n][3] fp32 (training) or nullptr
     const __half* gate_w;     // fp16 gate weights (may be null without router)

@@ -123,7 +123,7 @@ def test_experts_step_matches_oracle(cuda, experts, order):
     assert np.array_equal(expert, ref['expert']), 'routing decisions differ'
     assert len(np.unique(expert)) > 1, 'the test case should route to several experts'
     close(opt.copied('prob', (n,), torch.float32).cpu().numpy(), ref['prob'], 1e-5, 0.0, 'router probability')
-    raw = read_pair_major(opt, 'raw', n, W)
+    raw = read_rows(opt, 'raw', n, W)
     assert np.array_equal(raw.view(np.uint16), ref['raw'].view(np.uint16)), 'expert features differ'
     close(opt.copied('squares', (n,), torch.float32).cpu().numpy(), ref['squares'], 2e-3, 2e-3, 'squares')
     values = read_rows(opt, 'gvals', n, W)
