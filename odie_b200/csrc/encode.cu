@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
     const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
     const long long base = a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL;
     uint32_t row[W / 2];
-#pragma unroll
+#pragma unroll 4
     for (int l = 0; l < W / 2; ++l) {
         __half2 acc = __float2half2_rn(0.0f);
         if (l < a.levels && l < a.active) {

@@ -526,6 +526,9 @@ struct Runtime {
         slot = stage_begin(S_ENCODE_BWD);
         ea.row_major = true;  // the heads write each coordinate's gradient values as one row
         if (experts) {
+            // Two branches that meet before the heads' update: the router-grid scatter, the head-gradient
+            // reduction and the router grid's Adam on the side stream; the expert-table scatter and the
+            // expert tables' Adam on the runtime's stream.
             ODIE_CUDA(cudaEventRecord(fork_event, stream));
             ODIE_CUDA(cudaStreamWaitEvent(side, fork_event, 0));
             LevelSource rsrc;
@@ -533,18 +536,21 @@ struct Runtime {
             EncodeArgs ra = router_encode_args(n);  // row-major gradient values too
             launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, side);
             launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);  // needs only the heads kernel
+            if (update == 1) adam_router_grid(side);
             ODIE_CUDA(cudaEventRecord(join_event, side));
-        }
-        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
-        if (experts) ODIE_CUDA(cudaStreamWaitEvent(stream, join_event, 0));
-        stage_end(slot);
-        if (!experts) {
+            launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
+            if (update == 1) adam_expert_tables();
+            ODIE_CUDA(cudaStreamWaitEvent(stream, join_event, 0));
+            stage_end(slot);
+        } else {
+            launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
+            stage_end(slot);
             slot = stage_begin(S_REDUCE);
             launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), stream);
             stage_end(slot);
+            if (update == 1) grid_update();
         }
-        if (update == 1) grid_update();
-        else if (update == 0) {
+        if (update == 0) {
             launch_zero(grid_grad.ptr, total, stream);
             if (experts) launch_zero(router_grad.ptr, router_total, stream);
         }
@@ -552,15 +558,23 @@ struct Runtime {
         ODIE_CUDA(cudaGetLastError());
     }
 
-    void grid_update() {
+    // Adam of the grid tables (sparse: zero gradients are skipped), gradients at loss scale 128.
+    void adam_expert_tables() {
         AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
-        const int slot = stage_begin(S_ADAM_GRID);
         launch_adam(grid, grid_half.ptr, grid_m.ptr, grid_v.ptr, grid_steps.ptr, grid_grad.ptr, total, 1.0f / 128.0f, t,
                     float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), true, error_flag.ptr, stream);
-        if (experts)
-            launch_adam(router_grid, router_half.ptr, router_m.ptr, router_v.ptr, router_steps.ptr, router_grad.ptr,
-                        router_total, 1.0f / 128.0f, t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS),
-                        true, error_flag.ptr, stream);
+    }
+    void adam_router_grid(cudaStream_t on) {
+        AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
+        launch_adam(router_grid, router_half.ptr, router_m.ptr, router_v.ptr, router_steps.ptr, router_grad.ptr,
+                    router_total, 1.0f / 128.0f, t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS),
+                    true, error_flag.ptr, on);
+    }
+
+    void grid_update() {
+        const int slot = stage_begin(S_ADAM_GRID);
+        adam_expert_tables();
+        if (experts) adam_router_grid(stream);
         stage_end(slot);
         ODIE_CUDA(cudaGetLastError());
     }
