@@ -114,6 +114,8 @@ typedef struct {
     int32_t features;     /* features per entry */
     int32_t column;       /* first output column */
     int32_t hashed;       /* 1: spatial hash, 0: dense x + y*resolution (both modulo capacity) */
+    int32_t cells;        /* byte offset of the level's cell-visibility bitmap (routed-expert calls that take
+                             a bitmap), -1: every cell visible; odie_hash_forward/backward need -1 */
 } odie_hash_level;
 ODIE_API int odie_hash_forward(const float* coords, int64_t n, const float* table, const odie_hash_level* levels_host,
                       int levels, int width, uint16_t* features, uint64_t stream);
@@ -148,15 +150,18 @@ ODIE_API int selection_chunk(const double* scores, int n, int points, int resolu
  * odie_expert_hash_forward/backward: odie_hash_forward/backward with one table
  * per expert; coordinate i uses the table starting expert[i] * expert_stride
  * parameters into `tables` / `gradient` (same level records for every expert).
+ * bitmap (may be NULL): cell-visibility bytes of the on-demand allocation,
+ * addressed by each level's `cells` offset; a hidden cell gives zero features
+ * and receives no gradient.
  * ------------------------------------------------------------------------ */
 ODIE_API int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
                    int32_t* expert, float* prob, uint16_t* logits, uint64_t stream);
 ODIE_API int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
                    const int32_t* expert, const odie_hash_level* levels, int level_count, int width,
-                   uint16_t* features, uint64_t stream);
+                   const uint8_t* bitmap, uint16_t* features, uint64_t stream);
 ODIE_API int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width,
                    int64_t expert_stride, const int32_t* expert, const odie_hash_level* levels, int level_count,
-                   float* gradient, int64_t parameter_count, uint64_t stream);
+                   const uint8_t* bitmap, float* gradient, int64_t parameter_count, uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * On-device packed-plane index of one level (replaces the host-side
@@ -173,6 +178,18 @@ ODIE_API int odie_expert_hash_backward(const float* coords, int64_t n, const uin
 ODIE_API int64_t odie_plane_index_scratch(int resolution);
 ODIE_API int odie_plane_index(const uint8_t* support, int resolution, uint64_t* node_bitmap, int32_t* node_prefix,
                    uint8_t* cell_bitmap, int64_t* node_count, int64_t* nodes, int32_t* scratch, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * On-demand allocation of routed experts (no reference
+ * counterpart): the cell-visibility bitmap of one hash level (resolution R,
+ * ceil(R^2 / 8) bytes, LSB-first) from an allocated-tile mask tiles
+ * u8[tiles_y][tiles_x] of tile_px x tile_px tiles over a height x width image:
+ * cell (ix, iy) is visible iff the pixel nearest its centre, column
+ * floor(ix (width - 1) / (R - 1) + 1/2) and row likewise, lies in an allocated
+ * tile.
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int tile_px, int height, int width,
+                   int resolution, uint8_t* bitmap, uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * L2 probe (measurement; no reference counterpart): `operations` random

@@ -16,7 +16,8 @@ P, I32, I64, U64, B = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_bool
 class HashLevel(C.Structure):
     """odie_hash_level of include/odie_b200.h."""
     _fields_ = [('scale', C.c_float), ('resolution', C.c_int32), ('capacity', C.c_int32),
-                ('offset', C.c_int32), ('features', C.c_int32), ('column', C.c_int32), ('hashed', C.c_int32)]
+                ('offset', C.c_int32), ('features', C.c_int32), ('column', C.c_int32), ('hashed', C.c_int32),
+                ('cells', C.c_int32)]
 
 
 SIGNATURES = {
@@ -49,9 +50,10 @@ SIGNATURES = {
     'odie_router_forward': (I32, [P, I64, I32, P, I32, P, P, P, U64]),
     'odie_l2_probe': (I32, [P, I64, I32, I64, P, U64]),
     'odie_plane_index_scratch': (I64, [I32]),
+    'odie_allocation_bitmap': (I32, [P, I32, I32, I32, I32, I32, I32, P, U64]),
     'odie_plane_index': (I32, [P, I32, P, P, P, P, P, P, U64]),
-    'odie_expert_hash_forward': (I32, [P, I64, P, I64, P, C.POINTER(HashLevel), I32, I32, P, U64]),
-    'odie_expert_hash_backward': (I32, [P, I64, P, I32, I64, P, C.POINTER(HashLevel), I32, P, I64, U64]),
+    'odie_expert_hash_forward': (I32, [P, I64, P, I64, P, C.POINTER(HashLevel), I32, I32, P, P, U64]),
+    'odie_expert_hash_backward': (I32, [P, I64, P, I32, I64, P, C.POINTER(HashLevel), I32, P, P, I64, U64]),
     'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),
 }
 

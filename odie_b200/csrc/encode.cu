@@ -37,11 +37,13 @@ __device__ __forceinline__ Level fetch_level(const int* desc, const LevelTable& 
     return table.level[l];
 }
 
-// A plane cell outside the R x R grid (coordinates outside [0, 1], which the
-// reference never produces) is treated as hidden instead of reading outside the
-// bitmap.
+// Visibility of a coordinate's cell: plane cells, and hash-level cells when the
+// level has an allocation bitmap (cells >= 0; on-demand allocation of routed
+// experts), are looked up in the cell bitmap.  A cell outside the R x R grid
+// (coordinates outside [0, 1], which the reference never produces) is treated
+// as hidden instead of reading outside the bitmap.
 __device__ __forceinline__ bool level_on(const Level& d, const Corner4& g, const uint8_t* __restrict__ bitmap) {
-    if (d.kind != PLANE) return true;
+    if (d.kind != PLANE && (d.cells < 0 || !bitmap)) return true;
     if (g.ix < 0 || g.iy < 0 || g.ix >= d.res || g.iy >= d.res) return false;
     return cell_visible(d, bitmap, level_cell(d, g));
 }

@@ -131,7 +131,42 @@ __global__ void closure_nodes_kernel(const unsigned long long* __restrict__ word
     nodes[prefix[n >> 6] + __popcll(word & ((1ull << bit) - 1))] = n;
 }
 
+// On-demand allocation of routed experts (no reference
+// counterpart): cell (ix, iy) of a level of resolution res is visible iff the
+// pixel nearest its centre -- column floor(ix (width - 1) / (res - 1) + 1/2),
+// computed exactly in integers, row likewise -- lies in an allocated
+// tile_px x tile_px tile.  One thread per bitmap byte (8 cells, LSB first).
+__global__ void allocation_kernel(const uint8_t* __restrict__ tiles, int tiles_x, int tiles_y, int tile_px, int height,
+                                  int width, int res, uint8_t* __restrict__ bitmap) {
+    const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long cells = (long long)res * res;
+    if (b * 8 >= cells) return;
+    const long long den = res > 1 ? res - 1 : 1;
+    uint32_t bits = 0;
+    for (int j = 0; j < 8; ++j) {
+        const long long c = b * 8 + j;
+        if (c >= cells) break;
+        const long long ix = c % res, iy = c / res;
+        const long long col = (2 * ix * (width - 1) + den) / (2 * den), row = (2 * iy * (height - 1) + den) / (2 * den);
+        const long long tx = col / tile_px < tiles_x ? col / tile_px : tiles_x - 1;
+        const long long ty = row / tile_px < tiles_y ? row / tile_px : tiles_y - 1;
+        bits |= uint32_t(__ldg(tiles + ty * tiles_x + tx) != 0) << j;
+    }
+    bitmap[b] = uint8_t(bits);
+}
+
 }  // namespace
+
+void launch_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int tile_px, int height, int width,
+                              int res, uint8_t* bitmap, cudaStream_t stream) {
+    ODIE_REQUIRE(tiles_x >= 1 && tiles_y >= 1 && tile_px >= 1 && height >= 1 && width >= 1 && res >= 1,
+                 "allocation sizes must be positive");
+    ODIE_REQUIRE((long long)res * res <= (1LL << 34), "resolution too large");
+    const long long bytes = ((long long)res * res + 7) / 8;
+    allocation_kernel<<<blocks_for(bytes, 256), 256, 0, stream>>>(tiles, tiles_x, tiles_y, tile_px, height, width, res,
+                                                                   bitmap);
+    note_launch();
+}
 
 long long plane_index_scratch(long long points) {
     const long long words = (points + 63) / 64;

@@ -343,6 +343,20 @@ struct Runtime {
             ODIE_REQUIRE(input_width <= 32, "the fused heads take at most 32 input features (16 levels x F2)");
             build_feature_map();
         }
+        if (experts && j.contains("allocation")) {
+            // on-demand allocation of the expert tables: {"bitmap": device pointer, "cells": per-level byte offsets,
+            // -1 for a level whose cells are all visible}; every expert shares the levels' visibility
+            const Json& alloc = j.at("allocation");
+            cell_bitmap = pointer_of<const uint8_t>(alloc, "bitmap");
+            const Json& list = alloc.at("cells");
+            ODIE_REQUIRE(list.type == Json::ARRAY, "allocation cells must be a list");
+            const auto& cells = list.items;
+            ODIE_REQUIRE(int(cells.size()) == levels, "allocation needs one cell offset per expert level");
+            for (int l = 0; l < levels; ++l) {
+                table.level[l].cells = int(cells[l].as_int());
+                ODIE_REQUIRE(table.level[l].cells < 0 || cell_bitmap, "allocation offsets need a bitmap");
+            }
+        }
         lr[0] = j.at("grid_lr").as_double();
         if (router || experts) lr[1] = j.at("gate_lr").as_double();
         lr[2] = j.at("decoder_lr").as_double();
@@ -707,7 +721,7 @@ LevelTable hash_levels_table(const odie_hash_level* host, int levels) {
         L.points = host[l].capacity;
         L.offset = host[l].offset;
         L.words = -1;
-        L.cells = -1;
+        L.cells = host[l].cells;
         L.F = host[l].features;
         L.col = host[l].column;
         L.kind = host[l].hashed ? HASH_HASHED : HASH_DENSE;
@@ -738,6 +752,8 @@ int launch_selection_chunk(const double* scores, int n, int points, int resoluti
 
 namespace odie {
 long long plane_index_scratch(long long points);
+void launch_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int tile_px, int height, int width,
+                              int res, uint8_t* bitmap, cudaStream_t stream);
 void launch_plane_index(const uint8_t* support, int resolution, unsigned long long* node_words, int* node_prefix,
                         uint8_t* cell_bitmap, long long* node_count, long long* nodes, int* scratch,
                         cudaStream_t stream);
@@ -951,7 +967,7 @@ int odie_router_forward(const uint16_t* features, int64_t n, int width, const ui
 
 int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
                              const int32_t* expert, const odie_hash_level* levels_host, int levels, int width,
-                             uint16_t* features, uint64_t stream) {
+                             const uint8_t* bitmap, uint16_t* features, uint64_t stream) {
     return guarded([&] {
         ODIE_REQUIRE(n >= 0 && expert_stride > 0, "invalid sizes");
         odie::EncodeArgs a;
@@ -964,6 +980,7 @@ int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables
         a.stride = n;
         a.expert = expert;
         a.expert_stride = expert_stride;
+        a.bitmap = bitmap;
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
         odie::launch_encode_forward(a, src, tables, nullptr, reinterpret_cast<__half*>(features), nullptr,
@@ -973,8 +990,8 @@ int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables
 }
 
 int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* upstream, int width, int64_t expert_stride,
-                              const int32_t* expert, const odie_hash_level* levels_host, int levels, float* gradient,
-                              int64_t parameter_count, uint64_t stream) {
+                              const int32_t* expert, const odie_hash_level* levels_host, int levels,
+                              const uint8_t* bitmap, float* gradient, int64_t parameter_count, uint64_t stream) {
     return guarded([&] {
         ODIE_REQUIRE(n >= 0 && expert_stride > 0 && parameter_count >= 0, "invalid sizes");
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -990,6 +1007,7 @@ int odie_expert_hash_backward(const float* coords, int64_t n, const uint16_t* up
         a.expert = expert;
         a.expert_stride = expert_stride;
         a.experts = int(std::max<int64_t>(1, parameter_count / expert_stride));
+        a.bitmap = bitmap;
         odie::LevelSource src;
         src.table = odie::hash_levels_table(levels_host, levels);
         odie::launch_encode_backward(a, src, reinterpret_cast<const __half*>(upstream), gradient, s);
@@ -1009,6 +1027,15 @@ int odie_plane_index(const uint8_t* support, int resolution, uint64_t* node_bitm
         odie::launch_plane_index(support, resolution, reinterpret_cast<unsigned long long*>(node_bitmap), node_prefix,
                                  cell_bitmap, reinterpret_cast<long long*>(node_count), reinterpret_cast<long long*>(nodes),
                                  scratch, reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int tile_px, int height, int width,
+                           int resolution, uint8_t* bitmap, uint64_t stream) {
+    return guarded([&] {
+        odie::launch_allocation_bitmap(tiles, tiles_x, tiles_y, tile_px, height, width, resolution, bitmap,
+                                       reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
 }

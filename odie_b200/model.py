@@ -77,7 +77,7 @@ def _hash_table(records):
     table = (_lib.HashLevel * len(records))()
     for i, r in enumerate(records):
         table[i] = _lib.HashLevel(r['scale'], r['resolution'], r['capacity'], r['offset'], r['features'],
-                                  r['column'], r['hashed'])
+                                  r['column'], r['hashed'], int(r.get('cells', -1)))
     return table
 
 
@@ -110,14 +110,15 @@ class ExpertHashQuery(torch.autograd.Function):
     """Hashed encoding with one table per expert: row i reads expert[i]'s table (routed experts)."""
 
     @staticmethod
-    def forward(ctx, coordinates, tables, expert, expert_stride, records, width):
+    def forward(ctx, coordinates, tables, expert, expert_stride, records, width, bitmap=None):
+        """bitmap: optional CUDA uint8 cell-visibility bytes addressed by each record's 'cells' offset."""
         n = coordinates.shape[0]
         features = torch.empty((n, width), dtype=torch.float16, device=coordinates.device)
         _lib.check(_lib.library().odie_expert_hash_forward(
             coordinates.data_ptr(), n, tables.data_ptr(), expert_stride, expert.data_ptr(), _hash_table(records),
-            len(records), width, features.data_ptr(), _stream()), 'odie_expert_hash_forward')
+            len(records), width, _lib.ptr(bitmap), features.data_ptr(), _stream()), 'odie_expert_hash_forward')
         ctx.save_for_backward(coordinates, expert)
-        ctx.records, ctx.count, ctx.stride = records, tables.numel(), expert_stride
+        ctx.records, ctx.count, ctx.stride, ctx.bitmap = records, tables.numel(), expert_stride, bitmap
         ctx.mark_non_differentiable(expert)
         return features
 
@@ -128,9 +129,9 @@ class ExpertHashQuery(torch.autograd.Function):
         gradient = torch.empty(ctx.count, dtype=torch.float32, device=coordinates.device)
         _lib.check(_lib.library().odie_expert_hash_backward(
             coordinates.data_ptr(), coordinates.shape[0], upstream.data_ptr(), upstream.shape[1], ctx.stride,
-            expert.data_ptr(), _hash_table(ctx.records), len(ctx.records), gradient.data_ptr(), ctx.count, _stream()),
-            'odie_expert_hash_backward')
-        return None, gradient, None, None, None, None
+            expert.data_ptr(), _hash_table(ctx.records), len(ctx.records), _lib.ptr(ctx.bitmap), gradient.data_ptr(),
+            ctx.count, _stream()), 'odie_expert_hash_backward')
+        return None, gradient, None, None, None, None, None
 
 
 def route(features, router_weights16, experts):
@@ -438,6 +439,42 @@ class RoutedExperts(nn.Module):
         if prefix != self.n_levels:
             raise ValueError('routed experts always train every level')
 
+    @torch.no_grad()
+    def set_allocation(self, tiles, tile_px, shape, dense_resolution=None):
+        """On-demand allocation: restrict the expert levels finer than dense_resolution to the
+        cells whose centre pixel lies in an allocated tile.  tiles: CUDA uint8/bool [tiles_y, tiles_x] (e.g. the top-k
+        of odie_tile_topk); shape: (height, width) of the image.  Default dense_resolution: cells no smaller than
+        half a tile stay dense.  Hidden cells give zero features and receive no gradient."""
+        tiles = tiles.to(device=self.grid.device, dtype=torch.uint8).contiguous()
+        tiles_y, tiles_x = tiles.shape
+        height, width = shape
+        if dense_resolution is None:
+            dense_resolution = 2 * max(tiles_x, tiles_y) + 1
+        cells, offset = [], 0
+        for r in self.records:
+            if r['resolution'] <= dense_resolution:
+                cells.append(-1)
+            else:
+                cells.append(offset)
+                offset += (r['resolution'] ** 2 + 7) // 8
+        bitmap = torch.zeros(max(offset, 1), dtype=torch.uint8, device=self.grid.device)
+        lib = _lib.library()
+        for r, c in zip(self.records, cells):
+            if c >= 0:
+                _lib.check(lib.odie_allocation_bitmap(tiles.data_ptr(), tiles_x, tiles_y, int(tile_px), int(height),
+                                                      int(width), r['resolution'], bitmap[c:].data_ptr(), _stream()),
+                           'odie_allocation_bitmap')
+        for r, c in zip(self.records, cells):
+            r['cells'] = c
+        self.allocation_bitmap, self.allocation_cells = bitmap, cells
+        return bitmap, cells
+
+    def allocation_settings(self):
+        """The runtime's 'allocation' settings, or None before set_allocation."""
+        if getattr(self, 'allocation_bitmap', None) is None:
+            return None
+        return {'bitmap': self.allocation_bitmap.data_ptr(), 'cells': list(self.allocation_cells)}
+
     def route(self, coordinates):
         with torch.no_grad():
             features = HashQuery.apply(coordinates.contiguous(), self.router_grid, self.router_records, self.input_width)
@@ -446,7 +483,7 @@ class RoutedExperts(nn.Module):
     def forward(self, coordinates):
         expert, prob, _ = self.route(coordinates)
         features = ExpertHashQuery.apply(coordinates.contiguous(), self.grid, expert, self.expert_total, self.records,
-                                         self.input_width)
+                                         self.input_width, getattr(self, 'allocation_bitmap', None))
         gated = features * prob.to(torch.float16)[:, None]
         return self.decoder(gated).float()[:, :3]
 

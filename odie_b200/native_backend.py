@@ -85,7 +85,9 @@ class NativeOptimizer:
     def current_settings(self):
         rates = {g['name'] + '_lr': float(g['lr']) for g in self.param_groups}
         if self.config['representation'] in ('hash_grid', 'routed_experts'):
-            return dict(active=self.model.active_prefix, **rates)
+            allocation = getattr(self.model, 'allocation_settings', lambda: None)()
+            extra = {'allocation': allocation} if allocation else {}
+            return dict(active=self.model.active_prefix, **rates, **extra)
         return dict(active=self.model.active_prefix,
                     **{k: getattr(self.model, k).data_ptr() for k in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap')},
                     **rates)

@@ -158,7 +158,16 @@ void oracle_query_backward(const float* xy, int64_t n, const uint16_t* upstream,
  *   hashed levels: index = (cx * 1 XOR cy * 2654435761) mod capacity (uint32).
  * scale_l and res_l follow odie/config.py:83-94 (hash_grid_layout).
  * lv: per level {float scale, int res, int capacity, int offset, int F, int feature_offset, int hashed}. */
-typedef struct { float scale; int res, capacity, offset, F, feature_offset, hashed, pad; } HashLevel;
+typedef struct { float scale; int res, capacity, offset, F, feature_offset, hashed, cells; } HashLevel;
+/* cells: byte offset of the level's cell-visibility bitmap (bit c mod 8 of byte c / 8 for cell
+ * c = ix + iy * res), or -1 for a level whose cells are all visible.  A hidden cell (or one outside the
+ * res x res grid) contributes zero features and receives no gradient, as the packed planes' cells do. */
+static inline int hash_visible(const HashLevel* h, const uint8_t* bitmap, int ix, int iy) {
+    if (h->cells < 0 || !bitmap) return 1;
+    if (ix < 0 || iy < 0 || ix >= h->res || iy >= h->res) return 0;
+    const int64_t c = (int64_t)ix + (int64_t)iy * h->res;
+    return (bitmap[h->cells + (c >> 3)] >> (c & 7)) & 1;
+}
 
 static inline uint32_t hash_index(const HashLevel* h, int cx, int cy) {
     uint32_t idx;
@@ -182,9 +191,9 @@ void oracle_hash_indices(const float* xy, int64_t n, const HashLevel* lv, int le
         }
 }
 
-/* Hash-grid forward with fp16 tables (table bits) and the same fp16 hfma chain as a6. */
+/* Hash-grid forward with fp16 tables (table bits) and the same fp16 hfma chain as a6; bitmap may be NULL. */
 void oracle_hash_query(const float* xy, int64_t n, const uint16_t* table, const HashLevel* lv, int levels,
-                       int width, uint16_t* out) {
+                       int width, const uint8_t* bitmap, uint16_t* out) {
     for (int64_t i = 0; i < n; ++i)
         for (int l = 0; l < levels; ++l) {
             const HashLevel* h = lv + l;
@@ -192,9 +201,10 @@ void oracle_hash_query(const float* xy, int64_t n, const uint16_t* table, const 
             const int ix = (int)floorf(px), iy = (int)floorf(py);
             const float fx = px - (float)ix, fy = py - (float)iy;
             float w[4] = {(1.0f - fx) * (1.0f - fy), fx * (1.0f - fy), (1.0f - fx) * fy, fx * fy};
+            const int on = hash_visible(h, bitmap, ix, iy);
             for (int c = 0; c < h->F; ++c) {
                 half v = h_of(0.0);
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < 4 && on; ++k) {
                     uint32_t idx = hash_index(h, ix + (k & 1), iy + (k >> 1));
                     v = hfma(h_of(w[k]), h_of_bits(table[h->offset + idx * h->F + c]), v);
                 }
@@ -204,12 +214,13 @@ void oracle_hash_query(const float* xy, int64_t n, const uint16_t* table, const 
 }
 
 void oracle_hash_backward(const float* xy, int64_t n, const uint16_t* upstream, int width,
-                          const HashLevel* lv, int levels, double* grad) {
+                          const HashLevel* lv, int levels, const uint8_t* bitmap, double* grad) {
     for (int64_t i = 0; i < n; ++i)
         for (int l = 0; l < levels; ++l) {
             const HashLevel* h = lv + l;
             const float px = fmaf(h->scale, xy[2 * i], 0.5f), py = fmaf(h->scale, xy[2 * i + 1], 0.5f);
             const int ix = (int)floorf(px), iy = (int)floorf(py);
+            if (!hash_visible(h, bitmap, ix, iy)) continue;
             const float fx = px - (float)ix, fy = py - (float)iy;
             float w[4] = {(1.0f - fx) * (1.0f - fy), fx * (1.0f - fy), (1.0f - fx) * fy, fx * fy};
             for (int c = 0; c < h->F; ++c) {
@@ -600,5 +611,25 @@ void oracle_router(const uint16_t* x, int64_t n, int in_width, const uint16_t* w
         for (int e = 0; e < experts; ++e) sum += expf(z[e] - z[best]);
         expert[i] = best;
         prob[i] = 1.0f / sum;
+    }
+}
+
+/* ------------------------------------------------------------------ on-demand allocation */
+/* Per-level cell visibility from a tile mask (no reference counterpart): cell (ix, iy) of a level
+ * of resolution res is visible iff the pixel nearest its centre, column
+ * floor(ix * (width - 1) / (res - 1) + 0.5) (exact in int64), row likewise, lies in an allocated
+ * tile_px x tile_px tile.  Bits LSB-first, res^2 cells padded to whole bytes. */
+void oracle_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int tile_px, int height, int width,
+                              int res, uint8_t* bitmap) {
+    const int64_t cells = (int64_t)res * res;
+    memset(bitmap, 0, (size_t)((cells + 7) / 8));
+    for (int64_t c = 0; c < cells; ++c) {
+        const int64_t ix = c % res, iy = c / res;
+        const int64_t den = res > 1 ? res - 1 : 1;
+        const int64_t col = (2 * ix * (width - 1) + den) / (2 * den), row = (2 * iy * (height - 1) + den) / (2 * den);
+        int64_t tx = col / tile_px, ty = row / tile_px;
+        if (tx >= tiles_x) tx = tiles_x - 1;
+        if (ty >= tiles_y) ty = tiles_y - 1;
+        if (tiles[ty * tiles_x + tx]) bitmap[c >> 3] |= (uint8_t)(1u << (c & 7));
     }
 }

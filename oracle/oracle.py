@@ -49,14 +49,14 @@ def _p(a):
 
 class HashLevelC(C.Structure):
     _fields_ = [('scale', C.c_float), ('res', C.c_int), ('capacity', C.c_int), ('offset', C.c_int),
-                ('F', C.c_int), ('feature_offset', C.c_int), ('hashed', C.c_int), ('pad', C.c_int)]
+                ('F', C.c_int), ('feature_offset', C.c_int), ('hashed', C.c_int), ('cells', C.c_int)]
 
 
 def _hash_levels(records):
     arr = (HashLevelC * len(records))()
     for i, r in enumerate(records):
         arr[i] = HashLevelC(r['scale'], r['resolution'], r['capacity'], r['offset'], r['features'], r['column'],
-                            r['hashed'], 0)
+                            r['hashed'], int(r.get('cells', -1)))
     return arr
 
 
@@ -117,22 +117,37 @@ def hash_indices(xy, records):
     return idx, w
 
 
-def hash_query(xy, table16, records, width):
+def _bitmap(bitmap):
+    return None if bitmap is None else np.ascontiguousarray(bitmap, dtype=np.uint8)
+
+
+def hash_query(xy, table16, records, width, bitmap=None):
+    """bitmap: cell-visibility bytes addressed by each record's 'cells' offset (-1 or absent: all visible)."""
     xy = np.ascontiguousarray(xy, dtype=np.float32)
     table = np.ascontiguousarray(table16, dtype=np.float16).view(np.uint16)
     out = np.zeros((xy.shape[0], width), dtype=np.uint16)
+    bits = _bitmap(bitmap)
     lib().oracle_hash_query(_p(xy), C.c_int64(xy.shape[0]), _p(table), _hash_levels(records), len(records), width,
-                            _p(out))
+                            None if bits is None else _p(bits), _p(out))
     return out.view(np.float16)
 
 
-def hash_backward(xy, upstream, records, params):
+def hash_backward(xy, upstream, records, params, bitmap=None):
     xy = np.ascontiguousarray(xy, dtype=np.float32)
     up = np.ascontiguousarray(upstream, dtype=np.float16).view(np.uint16)
     grad = np.zeros(params, dtype=np.float64)
+    bits = _bitmap(bitmap)
     lib().oracle_hash_backward(_p(xy), C.c_int64(xy.shape[0]), _p(up), up.shape[1], _hash_levels(records),
-                               len(records), _p(grad))
+                               len(records), None if bits is None else _p(bits), _p(grad))
     return grad
+
+
+def allocation_bitmap(tiles, tile_px, height, width, res):
+    """Cell visibility of one level from an allocated-tile mask (oracle_allocation_bitmap)."""
+    t = np.ascontiguousarray(tiles, dtype=np.uint8)
+    out = np.zeros((res * res + 7) // 8, dtype=np.uint8)
+    lib().oracle_allocation_bitmap(_p(t), t.shape[1], t.shape[0], tile_px, height, width, res, _p(out))
+    return out
 
 
 def gate_forward(raw, logits, vis, feature_level, k_fixed=0, softplus=False):
@@ -353,26 +368,26 @@ def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, l
 ROUTER_SHAPES = lambda width: [(32, width), (32, 32), (16, 32)]  # noqa: E731  router W1, W2, W3
 
 
-def expert_query(xy, tables16, expert, expert_stride, records, width):
+def expert_query(xy, tables16, expert, expert_stride, records, width, bitmap=None):
     """Per-coordinate expert tables: rows routed to expert e read tables16[e * stride : (e + 1) * stride]."""
     out = np.zeros((xy.shape[0], width), dtype=np.float16)
     for e in np.unique(expert):
         rows = np.nonzero(expert == e)[0]
-        out[rows] = hash_query(xy[rows], tables16[e * expert_stride:(e + 1) * expert_stride], records, width)
+        out[rows] = hash_query(xy[rows], tables16[e * expert_stride:(e + 1) * expert_stride], records, width, bitmap)
     return out
 
 
-def expert_backward(xy, upstream, expert, expert_stride, records, params):
+def expert_backward(xy, upstream, expert, expert_stride, records, params, bitmap=None):
     grad = np.zeros(params, dtype=np.float64)
     for e in np.unique(expert):
         rows = np.nonzero(expert == e)[0]
         grad[e * expert_stride:(e + 1) * expert_stride] += hash_backward(xy[rows], upstream[rows], records,
-                                                                         expert_stride)
+                                                                         expert_stride, bitmap)
     return grad
 
 
 def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, experts, router_table, router_records,
-                           router_params, decoder_params, width=32):
+                           router_params, decoder_params, width=32, bitmap=None):
     """One routed-expert training step on the CPU (the restatement the CUDA path is checked against).
 
     Routing: router grid features -> router MLP with fp32 fma chains (bit-exact
@@ -391,7 +406,7 @@ def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, expe
     rin = hash_query(xy, router_table.astype(np.float16), router_records, width)
     r1, r2, r3 = (_f16(w) for w in head_matrices(router_params, ROUTER_SHAPES(width)))
     expert, prob, logits = router(rin, r1.reshape(-1), r2.reshape(-1), r3.reshape(-1), 32, experts)
-    feats = expert_query(xy, tables.astype(np.float16), expert, expert_stride, records, width)
+    feats = expert_query(xy, tables.astype(np.float16), expert, expert_stride, records, width, bitmap)
     ph = prob.astype(np.float16)
     weighted = _f16(feats.astype(np.float64) * ph.astype(np.float64)[:, None])
     d1, d2, d3 = (_f16(w) for w in head_matrices(decoder_params, head_shapes(width, 64, 2, 16)))
@@ -425,6 +440,6 @@ def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, expe
     return dict(xy=xy, target=target, router_features=rin, expert=expert, prob=prob, logits=logits, raw=feats,
                 weighted=weighted, out=out, dy=dy, squares=squares, dz=dz, values=values.astype(np.float32),
                 dp=dp, da=da, router_values=router_values.astype(np.float32),
-                grid_grad=expert_backward(xy, values, expert, expert_stride, records, tables.size),
+                grid_grad=expert_backward(xy, values, expert, expert_stride, records, tables.size, bitmap),
                 router_grid_grad=hash_backward(xy, router_values, router_records, router_table.size),
                 head_grad=np.concatenate([g.reshape(-1) for g in head]))

@@ -92,7 +92,7 @@ def test_expert_hash_query_bit_exact_and_scatter(cuda):
     from odie_b200.model import _hash_table, _stream
     _lib.check(_lib.library().odie_expert_hash_backward(xy_d.data_ptr(), n, up_d.data_ptr(), 32, stride,
                                                         expert_d.data_ptr(), _hash_table(records), len(records),
-                                                        grad.data_ptr(), tables.size, _stream()))
+                                                        None, grad.data_ptr(), tables.size, _stream()))
     torch.cuda.synchronize()
     close(grad.cpu().numpy(), oracle.expert_backward(xy, upstream, expert, stride, records, tables.size), 1e-5, 1e-6,
           'expert scatter')

@@ -237,3 +237,12 @@ def test_oracle_routed_expert_step_consistency():
     touched = np.nonzero(ref['grid_grad'])[0] // stride
     assert set(np.unique(touched)) <= set(np.unique(ref['expert']))
     assert np.isfinite(ref['router_grid_grad']).all() and np.abs(ref['router_grid_grad']).sum() > 0
+
+
+def test_oracle_allocation_bitmap_hand_case():
+    """4 x 4 image, 2 x 2 tiles, only the top-left tile allocated; a level of resolution 3 has cell centres at
+    pixel columns/rows 0, 1.5 -> 2 (nearest, halves up) and 3, so only cell (0, 0) lies in the allocated tile."""
+    tiles = np.array([[1, 0], [0, 0]], dtype=np.uint8)
+    assert np.array_equal(oracle.allocation_bitmap(tiles, 2, 4, 4, 3), np.array([1, 0], dtype=np.uint8))
+    assert np.array_equal(oracle.allocation_bitmap(np.ones((2, 2), np.uint8), 2, 4, 4, 3),
+                          np.array([255, 1], dtype=np.uint8))
