@@ -42,8 +42,9 @@ def parse():
     p.add_argument('--steps', type=int, default=20)
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
-    p.add_argument('--workload', default='c2-experts', choices=['c2-experts', 'c2-planes'])
-    p.add_argument('--batch', type=int, default=BATCH)
+    p.add_argument('--workload', default='c2-experts', choices=['c2-experts', 'c2-planes', 'c3-experts'])
+    p.add_argument('--batch', type=int, default=None, help='coordinates per step (default: the workload\'s: '
+                   '2^20 for the C2 workloads, 2^21 for c3-experts)')
     p.add_argument('--sampling', default='stratified', choices=['stratified', 'uniform'],
                    help='stratified: the reference default (odie/config.py:20, odie/data.py:63-80), one pixel per '
                         'square stratum, strata in raster order; uniform: iid uniform pixel ids')
@@ -54,8 +55,11 @@ def parse():
 def workload(name, rank, ranks, batch):
     """Model, target, planes, config and image of this rank's band of a workload."""
     from odie_b200 import workloads
-    if name == 'c2-experts':
-        config, rgb, shape = workloads.c2_experts(batch=batch, band=(rank, ranks))
+    if name in ('c2-experts', 'c3-experts'):
+        if name == 'c2-experts':
+            config, rgb, shape = workloads.c2_experts(batch=batch, band=(rank, ranks))
+        else:
+            config, rgb, shape = workloads.c3_experts(batch=batch, band=(rank, ranks))
         model, target, planes = workloads.build_expert_model(config, rgb)
         return dict(config=config, rgb=rgb, shape=shape, model=model, target=target, planes=planes)
     config, supports, dims, caps, rgb, shape = workloads.c2_planes(batch=batch, band=(rank, ranks))
@@ -70,8 +74,12 @@ def cpu_step_of(name, batch):
     from odie_b200 import layout as host_layout
     from odie_b200 import workloads
     rng = np.random.default_rng(0)
-    if name == 'c2-experts':
-        config, rgb, shape = workloads.c2_experts(batch=batch)
+    if name in ('c2-experts', 'c3-experts'):
+        if name == 'c2-experts':
+            config, rgb, shape = workloads.c2_experts(batch=batch)
+        else:
+            config, rgb, shape = workloads.c3_experts(batch=batch,
+                                                      device='cuda' if torch.cuda.is_available() else 'cpu')
         records, stride = host_layout.hash_levels(config['hash_encoding'])
         router_records, router_total = host_layout.hash_levels(config['router_encoding'])
         width = 32
@@ -139,19 +147,20 @@ def algorithmic(name, stage, model, n):
     8 + L F 2 + 8 L F 4 B/coord per encoding (an fp32 atomic = read + write), heads 6 x sum(in x out)
     FLOP/coord, router 64 + 8 B/coord, Adam 30 B/param."""
     L, F = model.n_levels, 2
-    encodings = 2 if name == 'c2-experts' else 1  # the router grid and the routed expert
+    experts = name.endswith('experts')
+    encodings = 2 if experts else 1  # the router grid and the routed expert
     decoder = 32 * 64 + 64 * 64 + 64 * 16
     if stage == 'encode_forward':
         return 'hbm', encodings * (8 + 4 * L * F * 2 + L * F * 2) * n
     if stage == 'encode_backward':
         return 'hbm', encodings * (8 + L * F * 2 + 8 * L * F * 4) * n
     if stage == 'mlp_train':
-        gate = 32 * 32 + 32 * 32 + 16 * 32 if name == 'c2-experts' else 32 * 32 + 32 * 16
+        gate = 32 * 32 + 32 * 32 + 16 * 32 if experts else 32 * 32 + 32 * 16
         return 'tensor', 6 * (gate + decoder) * n
     if stage == 'router':
         return 'hbm', (64 + 8) * n
     if stage == 'adam_grid':
-        params = model.grid.numel() + (model.router_grid.numel() if name == 'c2-experts' else 0)
+        params = model.grid.numel() + (model.router_grid.numel() if experts else 0)
         return 'hbm', 30 * params
     return 'hbm', None
 
@@ -193,7 +202,7 @@ def l2_probe(lib, table_mib=32, operations=1 << 27):
 
 def l2_ops(name, stage, model, n):
     """Table accesses of one step of a gather/scatter stage: 4 corners x levels per coordinate and encoding."""
-    encodings = 2 if name == 'c2-experts' else 1
+    encodings = 2 if name.endswith('experts') else 1
     if stage in ('encode_forward', 'encode_backward'):
         return encodings * 4 * model.n_levels * n
     return None
@@ -257,8 +266,47 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def allocate(args, lib, opt, model, target, shape):
+    """BASELINE config 3's allocation stage on the current model: decode every pixel, the fp64 residual of every
+    256 x 256 tile, the exact top 30 %, and the expert levels restricted to the chosen tiles' cells.  Timed with CUDA
+    events; returns the tile mask and the timings."""
+    import json as _json
+    from odie_b200 import _lib
+    from odie_b200.workloads import C3_TILE
+    height, width = shape
+    tiles_y, tiles_x = -(-height // C3_TILE), -(-width // C3_TILE)
+    count = tiles_x * tiles_y
+    k = int(round(0.3 * count))
+    stream = torch.cuda.current_stream()
+    prediction = torch.empty((height * width, 3), device='cuda')
+    scores = torch.empty(count, dtype=torch.float64, device='cuda')
+    chosen = torch.empty(k, dtype=torch.int64, device='cuda')
+    selected = torch.empty(count, dtype=torch.uint8, device='cuda')
+    row_sums = torch.empty(count * C3_TILE, dtype=torch.float64, device='cuda')
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    events[0].record()
+    opt.decode(0, height * width, rgb=prediction)
+    events[1].record()
+    _lib.check(lib.odie_tile_topk(prediction.data_ptr(), target.data.data_ptr(), height, width, C3_TILE, k,
+                                  row_sums.data_ptr(), scores.data_ptr(), chosen.data_ptr(), selected.data_ptr(),
+                                  stream.cuda_stream))
+    events[2].record()
+    tiles = selected.reshape(tiles_y, tiles_x)
+    model.set_allocation(tiles, C3_TILE, shape)
+    opt.check(lib.odie_configure(opt.handle, _json.dumps(opt.current_settings()).encode()))
+    events[3].record()
+    torch.cuda.synchronize()
+    return {'tiles': tiles.bool(), 'tiles_allocated': k, 'tiles_total': count, 'tile_px': C3_TILE,
+            'decode_ms': events[0].elapsed_time(events[1]), 'score_select_ms': events[1].elapsed_time(events[2]),
+            'bitmaps_ms': events[2].elapsed_time(events[3]), 'stage_ms': events[0].elapsed_time(events[3]),
+            'sampling': '70 % of coordinates uniform in the allocated tiles, 30 % uniform over the image'}
+
+
 def main():
     args = parse()
+    if args.batch is None:
+        args.batch = 1 << 21 if args.workload == 'c3-experts' else BATCH
     if args.impl == 'reference':
         run_reference(args)
         return
@@ -286,7 +334,13 @@ def main():
     pixels = shape[0] * shape[1]
     gen = torch.Generator(device='cuda').manual_seed(1729 + rank)
     total_steps = args.warmup + args.steps
-    if args.sampling == 'stratified':
+    allocation = None
+    if args.workload == 'c3-experts':
+        allocation = allocate(args, lib, opt, model, w['target'], shape)
+        from odie_b200.workloads import allocated_ids
+        ids = torch.stack([allocated_ids(allocation['tiles'], shape, args.batch, gen) for _ in range(total_steps)])
+        allocation = {k: v for k, v in allocation.items() if k != 'tiles'}
+    elif args.sampling == 'stratified':
         from odie_b200.data import stratified_batches
         ids = torch.stack(list(stratified_batches(shape, args.batch, gen, steps=total_steps)))
     else:
@@ -406,13 +460,16 @@ def main():
                            'batch_per_gpu': args.batch, 'levels': model.n_levels, 'grid_params': model.grid.numel(),
                            'experts': getattr(model, 'experts', None),
                            'parallelism': f'dp{world} (row bands, head all-reduce)',
-                           'sampling': args.sampling + (' (reference default, odie/config.py:20)'
-                                                        if args.sampling == 'stratified' else ' (iid)'),
+                           'sampling': ('70 % in the allocated tiles, 30 % uniform' if args.workload == 'c3-experts'
+                                        else args.sampling + (' (reference default, odie/config.py:20)'
+                                                              if args.sampling == 'stratified' else ' (iid)')),
                            'l2': 'per-step inputs/activations (~200 MB) larger than L2; model tables L2-resident'},
                 'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': args.batch * 8, 'd2h_bytes_per_step': 8},
                 'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base,
                 'decode': {'value': decode_gpix, 'unit': 'Gpix/s', 'pixels_per_rank': pixels},
                 'loss_first_last': [float(losses[0]), float(losses[-1])], 'clocks': clocks.summary()}
+        if allocation:
+            line['allocation'] = allocation
         print(json.dumps(line), flush=True)
     opt.close()
     if dist is not None:

@@ -16,7 +16,13 @@ U(-1e-4, 1e-4)), a top-1 router (W -> 32 -> 32 -> 16) over a coarse shared grid
 U(-0.1, 0.1) so that the initial routing already splits the image), and the
 shared 64-wide decoder, on the same 2040 x 1356 image with 2^20 coords.
 
-Multi-GPU (both workloads): rank r of N trains the model of row band r of the
+c3-experts: BASELINE config 3, the on-demand allocation path -- a 4096 x 4096
+image (1/f^2 noise + 200 sharp polygons), 8 routed experts with T = 2^17, the
+residual of every 256 x 256 tile of the current model's decode, the top 30 %
+tiles allocated (the fine expert levels restricted to their cells), and 2^21
+coordinates per step, 70 % of them drawn from the allocated tiles.
+
+Multi-GPU (all workloads): rank r of N trains the model of row band r of the
 image (its own tables: spatial ownership); the heads are shared.
 """
 import numpy as np
@@ -115,3 +121,32 @@ def c2_experts(seed=1729, batch=1 << 20, band=(0, 1)):
 def build_expert_model(config, rgb, device='cuda'):
     model = RoutedExperts(config)
     return model, ByteTarget(rgb.to(device)), [model.grid]
+
+
+C3_TILE = 256
+
+
+def c3_experts(seed=1729, batch=1 << 21, band=(0, 1), device='cuda'):
+    """(config, rgb u8 [H*W, 3] on CPU, shape) of BASELINE config 3 for rank band[0] of band[1]."""
+    rgb, shape = synthetic_image('c3', seed=seed, device=device)
+    rgb, shape = band_of(rgb.cpu(), shape, band)
+    encoding = dict(EXPERT_ENCODING, log2_hashmap_size=17)
+    return experts_config(experts=8, seed=seed + band[0], batch=batch, encoding=encoding), rgb, shape
+
+
+def allocated_ids(tiles, shape, count, generator, fraction=0.7, tile_px=C3_TILE):
+    """count pixel ids: `fraction` of them uniform inside the allocated tiles (tiles: CUDA bool [ty, tx]), the rest
+    uniform over the image, in random order."""
+    height, width = shape
+    device = tiles.device
+    chosen = torch.nonzero(tiles.reshape(-1)).reshape(-1)
+    inside = int(round(count * fraction)) if chosen.numel() else 0
+    pick = chosen[torch.randint(0, chosen.numel(), (inside,), device=device, generator=generator)] if inside else \
+        torch.zeros(0, dtype=torch.long, device=device)
+    ty, tx = pick // tiles.shape[1], pick % tiles.shape[1]
+    y = ty * tile_px + torch.randint(0, tile_px, (inside,), device=device, generator=generator)
+    x = tx * tile_px + torch.randint(0, tile_px, (inside,), device=device, generator=generator)
+    y, x = y.clamp_(max=height - 1), x.clamp_(max=width - 1)
+    rest = torch.randint(0, height * width, (count - inside,), device=device, generator=generator)
+    ids = torch.cat((y * width + x, rest))
+    return ids[torch.randperm(count, device=device, generator=generator)]
