@@ -102,25 +102,54 @@ def cpu_step_of(name, batch):
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML every 5 ms (read-only queries of the
+    device that runs this rank, found by PCI bus id), else nvidia-smi every 200 ms."""
     QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
              'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
              'clocks_event_reasons.sw_power_cap')
+    REASONS = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
 
     def __init__(self, index):
-        self.index, self.samples, self.stop = index, [], threading.Event()
+        self.index, self.samples, self.stop, self.source = index, [], threading.Event(), 'nvidia-smi'
+        self.nvml = self.handle = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            p = torch.cuda.get_device_properties(index)
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(
+                f'{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0')
+            self.nvml, self.source = pynvml, 'nvml'
+            self.bits = (pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nvml = None
         self.thread = threading.Thread(target=self.run, daemon=True)
+
+    def sample_nvml(self):
+        n = self.nvml
+        sm = float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+        mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        return sm, self.max_mhz, [name for name, bit in zip(self.REASONS, self.bits) if mask & bit]
+
+    def sample_smi(self):
+        out = subprocess.run(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
+                              '--format=csv,noheader,nounits'], capture_output=True, text=True, timeout=5)
+        if out.returncode != 0 or not out.stdout.strip():
+            return None
+        f = [x.strip() for x in out.stdout.strip().split(',')]
+        num = lambda x: float(x) if x.replace('.', '').isdigit() else None
+        return num(f[1]), num(f[2]), [name for i, name in enumerate(self.REASONS) if len(f) > 5 + i and f[5 + i] == 'Active']
 
     def run(self):
         while not self.stop.is_set():
             try:
-                out = subprocess.run(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
-                                      '--format=csv,noheader,nounits'], capture_output=True, text=True, timeout=5)
-                if out.returncode == 0 and out.stdout.strip():
-                    self.samples.append([s.strip() for s in out.stdout.strip().split(',')])
+                s = self.sample_nvml() if self.nvml else self.sample_smi()
+                if s:
+                    self.samples.append(s)
             except Exception:
                 pass
-            self.stop.wait(0.2)
+            self.stop.wait(0.005 if self.nvml else 0.2)
 
     def __enter__(self):
         self.thread.start()
@@ -132,13 +161,12 @@ class Clocks:
 
     def summary(self):
         if not self.samples:
-            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
-        sm = [float(s[1]) for s in self.samples if s[1].replace('.', '').isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace('.', '').isdigit()]
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == 'Active'})
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0, 'source': self.source}
+        sm = [s[0] for s in self.samples if s[0] is not None]
+        mx = [s[1] for s in self.samples if s[1] is not None]
         return {'sm_mhz': float(np.median(sm)) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
-                'reasons': reasons, 'samples': len(self.samples)}
+                'reasons': sorted({r for s in self.samples for r in s[2]}), 'samples': len(self.samples),
+                'source': self.source}
 
 
 def algorithmic(name, stage, model, n):
@@ -231,8 +259,8 @@ def cpu_baseline(args, budget=12.0):
         coords += sample
     seconds = time.perf_counter() - started
     return {'value': coords / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port',
-            'sample': f'{coords // sample} steps of {sample} coords of {args.workload} (same layout, batch scaled '
-                      f'down), torch CPU, {threads} threads, {seconds:.1f} s'}
+            'sample': f'{coords // sample} steps of {sample} uniform coords of {args.workload} (same layout, batch '
+                      f'scaled down), torch CPU, {threads} threads, {seconds:.1f} s'}
 
 
 def run_reference(args):
@@ -283,7 +311,7 @@ def allocate(args, lib, opt, model, target, shape):
     chosen = torch.empty(k, dtype=torch.int64, device='cuda')
     selected = torch.empty(count, dtype=torch.uint8, device='cuda')
     row_sums = torch.empty(count * C3_TILE, dtype=torch.float64, device='cuda')
-    events = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     torch.cuda.synchronize()
     events[0].record()
     opt.decode(0, height * width, rgb=prediction)
@@ -294,13 +322,17 @@ def allocate(args, lib, opt, model, target, shape):
     events[2].record()
     tiles = selected.reshape(tiles_y, tiles_x)
     model.set_allocation(tiles, C3_TILE, shape)
-    opt.check(lib.odie_configure(opt.handle, _json.dumps(opt.current_settings()).encode()))
     events[3].record()
+    opt.check(lib.odie_configure(opt.handle, _json.dumps(opt.current_settings()).encode()))
+    events[4].record()
     torch.cuda.synchronize()
     return {'tiles': tiles.bool(), 'tiles_allocated': k, 'tiles_total': count, 'tile_px': C3_TILE,
             'decode_ms': events[0].elapsed_time(events[1]), 'score_select_ms': events[1].elapsed_time(events[2]),
-            'bitmaps_ms': events[2].elapsed_time(events[3]), 'stage_ms': events[0].elapsed_time(events[3]),
-            'sampling': '70 % of coordinates uniform in the allocated tiles, 30 % uniform over the image'}
+            'bitmaps_ms': events[2].elapsed_time(events[3]), 'configure_ms': events[3].elapsed_time(events[4]),
+            'stage_ms': events[0].elapsed_time(events[4]),
+            'sampling': ('70 % of coordinates on jittered strata spread evenly over the allocated tiles, 30 % on '
+                         'jittered strata over the image, tile by tile' if args.sampling == 'stratified' else
+                         '70 % of coordinates uniform in the allocated tiles, 30 % uniform over the image (iid)')}
 
 
 def main():
@@ -337,8 +369,9 @@ def main():
     allocation = None
     if args.workload == 'c3-experts':
         allocation = allocate(args, lib, opt, model, w['target'], shape)
-        from odie_b200.workloads import allocated_ids
-        ids = torch.stack([allocated_ids(allocation['tiles'], shape, args.batch, gen) for _ in range(total_steps)])
+        from odie_b200.workloads import allocated_ids, allocated_stratified_ids
+        sampler = allocated_stratified_ids if args.sampling == 'stratified' else allocated_ids
+        ids = torch.stack([sampler(allocation['tiles'], shape, args.batch, gen) for _ in range(total_steps)])
         allocation = {k: v for k, v in allocation.items() if k != 'tiles'}
     elif args.sampling == 'stratified':
         from odie_b200.data import stratified_batches
@@ -460,9 +493,9 @@ def main():
                            'batch_per_gpu': args.batch, 'levels': model.n_levels, 'grid_params': model.grid.numel(),
                            'experts': getattr(model, 'experts', None),
                            'parallelism': f'dp{world} (row bands, head all-reduce)',
-                           'sampling': ('70 % in the allocated tiles, 30 % uniform' if args.workload == 'c3-experts'
-                                        else args.sampling + (' (reference default, odie/config.py:20)'
-                                                              if args.sampling == 'stratified' else ' (iid)')),
+                           'sampling': (args.sampling + (' (reference default, odie/config.py:20)'
+                                                         if args.sampling == 'stratified' else ' (iid)')
+                                        + (', 70 % in the allocated tiles' if args.workload == 'c3-experts' else '')),
                            'l2': 'per-step inputs/activations (~200 MB) larger than L2; model tables L2-resident'},
                 'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': args.batch * 8, 'd2h_bytes_per_step': 8},
                 'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base,

@@ -100,10 +100,13 @@ __device__ __forceinline__ uint32_t wrap_index(uint32_t idx, uint32_t points) {
 }
 
 // Parameter row of corner k (0: x0y0, 1: x1y0, 2: x0y1, 3: x1y1) of a level.
+// KIND: the level's kind when the caller knows it at compile time (smaller code), -1 to read d.kind.
+template <int KIND = -1>
 __device__ __forceinline__ int corner_row(const Level& d, const Corner4& g, int k,
                                           const uint64_t* __restrict__ node_bitmap, const int* __restrict__ prefix) {
     const int dx = k & 1, dy = k >> 1;
-    if (d.kind == PLANE) {
+    const int kind = KIND >= 0 ? KIND : d.kind;
+    if (kind == PLANE) {
         const int cell = g.ix + g.iy * d.res;
         const int raw = cell + dx + dy * d.res;
         // the reference's (cell + dx + dy R) % points on a non-negative int; level_on() hides cells outside
@@ -113,7 +116,7 @@ __device__ __forceinline__ int corner_row(const Level& d, const Corner4& g, int 
     }
     const uint32_t cx = uint32_t(g.ix + dx), cy = uint32_t(g.iy + dy);
     uint32_t idx;
-    if (d.kind == HASH_HASHED) idx = cx ^ (cy * 2654435761u);
+    if (kind == HASH_HASHED) idx = cx ^ (cy * 2654435761u);
     else idx = cx + cy * uint32_t(d.res);
     return int(wrap_index(idx, uint32_t(d.points)));
 }

@@ -231,6 +231,30 @@ __device__ __forceinline__ bool combine_lanes(float (&v)[8], long long key, bool
     return on;
 }
 
+// combine_lanes with a two-part key (key, tag): lanes combine when both parts are equal.
+__device__ __forceinline__ bool combine_lanes(float (&v)[8], long long key, int tag, bool on) {
+    const int lane = threadIdx.x & 31;
+    const long long prev = __shfl_up_sync(0xffffffffu, key, 1);
+    const long long next = __shfl_down_sync(0xffffffffu, key, 1);
+    const int prev_tag = __shfl_up_sync(0xffffffffu, tag, 1);
+    const int next_tag = __shfl_down_sync(0xffffffffu, tag, 1);
+    const bool same_prev = lane > 0 && prev == key && prev_tag == tag;
+    const bool same_next = lane < 31 && next == key && next_tag == tag;
+    const unsigned joined = __ballot_sync(0xffffffffu, same_prev);
+    if (joined == 0xfffffffeu) {  // one cell for the whole warp
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], m));
+        return on && lane == 0;
+    }
+    if (joined) {
+        run_sums(v, !same_prev);
+        return on && !same_next;
+    }
+    return on;
+}
+
 // Direct scatter: one warp per 32 consecutive coordinates (group order
 // scrambled), each lane one coordinate over all its levels not in skip_levels
 // (those go through the shared-memory kernel below).  F=2 levels combine lanes
@@ -397,6 +421,137 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
     }
 }
 
+
+// Lane-contiguous runs over the shared-memory levels (all with F = 2): each
+// thread walks its own run of consecutive coordinates and keeps, for each level
+// of a group of RUNS_GROUP levels, the running sums of the 8 corner updates
+// (4 corners x 2 features) of the cell it is in; it adds them to the block's
+// shared tables only when the cell changes and at the end of its run.  On a
+// spatially coherent batch (the reference's stratified sampler) a coarse cell
+// spans many consecutive coordinates, so most updates are register FMAs and the
+// shared-memory atomics -- which serialise on equal addresses -- become rare.
+// VEC: the gradient values are row-major and listed level c has columns
+// (2c, 2c + 1), so one 16-byte load brings a group's 4 value pairs.
+constexpr int RUNS_THREADS = 384;
+constexpr int RUNS_GROUP = 4;
+
+// Adds one cell's 8 corner sums to the block's shared table of expert e and clears them.
+template <int KIND>
+__device__ __forceinline__ void runs_flush(const Level& d, float* tab, int e, int ix, int iy, float (&v)[8],
+                                           const uint64_t* __restrict__ node_bitmap, const int* __restrict__ prefix) {
+    Corner4 g;
+    g.ix = ix;
+    g.iy = iy;
+    float* const t = tab + (long long)e * d.points * 2;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int row = corner_row<KIND>(d, g, k, node_bitmap, prefix);
+        if (v[2 * k] != 0.0f) atomicAdd(t + 2 * row, v[2 * k]);
+        if (v[2 * k + 1] != 0.0f) atomicAdd(t + 2 * row + 1, v[2 * k + 1]);
+        v[2 * k] = 0.0f;
+        v[2 * k + 1] = 0.0f;
+    }
+}
+
+template <bool VEC, int KIND>
+__global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(const EncodeArgs a,
+                                                                              const __grid_constant__ LevelTable table,
+                                                                              const __grid_constant__ CoarseList list,
+                                                                              const __half* __restrict__ upstream,
+                                                                              float* __restrict__ grad) {
+    extern __shared__ float acc[];
+    const int experts = a.expert ? a.experts : 1;
+    for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
+    __syncthreads();
+    const long long chunk = (a.n + gridDim.x - 1) / gridDim.x;
+    const long long begin = (long long)blockIdx.x * chunk;
+    const long long end = begin + chunk < a.n ? begin + chunk : a.n;
+    const long long run = (chunk + blockDim.x - 1) / blockDim.x;
+    const long long first = begin + threadIdx.x * run;
+    const long long last = first + run < end ? first + run : end;
+    const float2* const coords = reinterpret_cast<const float2*>(a.coords);
+    for (int c0 = 0; c0 < list.count; c0 += RUNS_GROUP) {
+        int ce[RUNS_GROUP], cx[RUNS_GROUP], cy[RUNS_GROUP];
+        float v[RUNS_GROUP][8];
+#pragma unroll
+        for (int g = 0; g < RUNS_GROUP; ++g) {
+            ce[g] = -1;
+            cx[g] = cy[g] = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[g][j] = 0.0f;
+        }
+        for (long long i = first; i < last; ++i) {
+            int e = 0;
+            bool valid = true;
+            if (a.expert) {
+                e = __ldg(a.expert + i);
+                valid = e >= 0 && e < experts;  // an id outside the tables would land outside shared memory
+            }
+            const float2 p = __ldg(coords + i);
+            uint32_t pairs[RUNS_GROUP];
+            if (VEC) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(upstream + i * a.width + 2 * c0));
+                pairs[0] = q.x;
+                pairs[1] = q.y;
+                pairs[2] = q.z;
+                pairs[3] = q.w;
+            }
+#pragma unroll
+            for (int g = 0; g < RUNS_GROUP; ++g) {
+                const int c = c0 + g;
+                if (c >= list.count) break;
+                const Level d = table.level[list.level[c]];
+                const Corner4 geo = geometry(p.x, p.y, d.scale);
+                if (!valid || !level_on(d, geo, a.bitmap)) continue;
+                if (geo.ix != cx[g] || geo.iy != cy[g] || e != ce[g]) {
+                    if (ce[g] >= 0)
+                        runs_flush<KIND>(d, acc + list.offset[c], ce[g], cx[g], cy[g], v[g], a.node_bitmap, a.node_prefix);
+                    ce[g] = e;
+                    cx[g] = geo.ix;
+                    cy[g] = geo.iy;
+                }
+                float u0, u1;
+                if (VEC) {
+                    u0 = __half2float(lo_half(pairs[g]));
+                    u1 = __half2float(hi_half(pairs[g]));
+                } else {
+                    u0 = upstream_value(upstream, a, i, d.col);
+                    u1 = upstream_value(upstream, a, i, d.col + 1);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    v[g][2 * k] = __fmaf_rn(geo.w[k], u0, v[g][2 * k]);
+                    v[g][2 * k + 1] = __fmaf_rn(geo.w[k], u1, v[g][2 * k + 1]);
+                }
+            }
+        }
+        // the runs end together: neighbouring lanes often end in one cell, so they are combined first
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int g = 0; g < RUNS_GROUP; ++g) {
+            const int c = c0 + g;
+            if (c >= list.count) break;
+            const bool on = ce[g] >= 0;
+            const long long key = ((long long)cx[g] << 32) | uint32_t(cy[g]);
+            if (combine_lanes(v[g], key, on ? ce[g] : -1 - lane, on))
+                runs_flush<KIND>(table.level[list.level[c]], acc + list.offset[c], ce[g], cx[g], cy[g], v[g],
+                                 a.node_bitmap, a.node_prefix);
+        }
+    }
+    __syncthreads();
+    for (int c = 0; c < list.count; ++c) {
+        const Level d = table.level[list.level[c]];
+        const int per_table = d.points * d.F;
+        const float* tab = acc + list.offset[c];
+        for (int j = threadIdx.x; j < per_table * experts; j += blockDim.x) {
+            const float v = tab[j];
+            if (v == 0.0f) continue;
+            const int x = j / per_table;
+            red_add_f32(grad + d.offset + (long long)x * a.expert_stride + (j - x * per_table), v);
+        }
+    }
+}
+
 }  // namespace
 
 constexpr int COARSE_SMEM_FLOATS = 27648;  // 108 KB of shared memory per block: two blocks per SM
@@ -431,6 +586,34 @@ static uint32_t visit_mask(long long n) {
     uint32_t size = 1;
     while ((long long)size < n) size <<= 1;
     return size - 1;
+}
+
+template <int KIND>
+static void set_runs_smem() {
+    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<true, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   COARSE_SMEM_FLOATS * 4));
+    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<false, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   COARSE_SMEM_FLOATS * 4));
+}
+
+struct RunsLaunch {
+    const EncodeArgs& a;
+    const LevelTable& table;
+    const CoarseList& list;
+    const __half* upstream;
+    float* grad;
+    int blocks, smem;
+    cudaStream_t stream;
+};
+
+template <int KIND>
+static void launch_runs(const RunsLaunch& l, bool vec) {
+    if (vec)
+        encode_backward_runs_kernel<true, KIND><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
+                                                                                            l.upstream, l.grad);
+    else
+        encode_backward_runs_kernel<false, KIND><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
+                                                                                             l.upstream, l.grad);
 }
 
 void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
@@ -471,9 +654,32 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
         if (!(configured >> device & 1ull)) {
             ODIE_CUDA(cudaFuncSetAttribute(encode_backward_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            COARSE_SMEM_FLOATS * 4));
+            set_runs_smem<PLANE>();
+            set_runs_smem<HASH_DENSE>();
+            set_runs_smem<HASH_HASHED>();
+            set_runs_smem<-1>();
             configured |= 1ull << device;
         }
-        encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
+        // runs kernel: every listed level has F = 2; the 16-byte value loads also need row-major values with
+        // listed level c in columns (2c, 2c + 1) and 16-byte aligned rows
+        bool pairs = true, vec = a.row_major && (a.width % 8) == 0 && (reinterpret_cast<uintptr_t>(upstream) & 15) == 0 &&
+                                 2 * ((list.count + RUNS_GROUP - 1) / RUNS_GROUP * RUNS_GROUP) <= a.width;
+        int kind = src.table.level[list.level[0]].kind;
+        for (int c = 0; c < list.count; ++c) {
+            const Level& d = src.table.level[list.level[c]];
+            pairs = pairs && d.F == 2;
+            vec = vec && d.col == 2 * c;
+            if (d.kind != kind) kind = -1;
+        }
+        if (pairs) {
+            const RunsLaunch l{a, src.table, list, upstream, grad, blocks, list.total * 4, stream};
+            if (kind == PLANE) launch_runs<PLANE>(l, vec);
+            else if (kind == HASH_DENSE) launch_runs<HASH_DENSE>(l, vec);
+            else if (kind == HASH_HASHED) launch_runs<HASH_HASHED>(l, vec);
+            else launch_runs<-1>(l, vec);
+        }
+        else
+            encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
         note_launch();
     }
     const int active = a.active < a.levels ? a.active : a.levels;

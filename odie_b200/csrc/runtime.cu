@@ -486,15 +486,17 @@ struct Runtime {
         profiling = enable;
         recorded = 0;
     }
-    int stage_begin(Stage s) {
+    // A stage's events go on the stream its kernels run on (the side stream for the router-grid branch);
+    // stage_end must name the same stream as stage_begin.
+    int stage_begin(Stage s, cudaStream_t on = nullptr) {
         if (!profiling || recorded >= EVENT_PAIRS) return -1;
         const int slot = recorded++;
         event_stage[slot] = s;
-        ODIE_CUDA(cudaEventRecord(events[2 * slot], stream));
+        ODIE_CUDA(cudaEventRecord(events[2 * slot], on ? on : stream));
         return slot;
     }
-    void stage_end(int slot) {
-        if (slot >= 0) ODIE_CUDA(cudaEventRecord(events[2 * slot + 1], stream));
+    void stage_end(int slot, cudaStream_t on = nullptr) {
+        if (slot >= 0) ODIE_CUDA(cudaEventRecord(events[2 * slot + 1], on ? on : stream));
     }
     std::string profile_report() {
         ODIE_CUDA(cudaStreamSynchronize(stream));
@@ -537,26 +539,39 @@ struct Runtime {
         slot = stage_begin(S_MLP);
         launch_mlp_tc_train(ma, input_width, gate_mode(), uniform, blocks, error_flag.ptr, stream);
         stage_end(slot);
-        slot = stage_begin(S_ENCODE_BWD);
         ea.row_major = true;  // the heads write each coordinate's gradient values as one row
         if (experts) {
             // Two branches that meet before the heads' update: the router-grid scatter, the head-gradient
             // reduction and the router grid's Adam on the side stream; the expert-table scatter and the
-            // expert tables' Adam on the runtime's stream.
+            // expert tables' Adam on the runtime's stream.  Stage timers run on each branch's own stream.
             ODIE_CUDA(cudaEventRecord(fork_event, stream));
             ODIE_CUDA(cudaStreamWaitEvent(side, fork_event, 0));
             LevelSource rsrc;
             rsrc.table = router_table;
             EncodeArgs ra = router_encode_args(n);  // row-major gradient values too
+            slot = stage_begin(S_ENCODE_BWD, side);
             launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, side);
+            stage_end(slot, side);
+            slot = stage_begin(S_REDUCE, side);
             launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);  // needs only the heads kernel
-            if (update == 1) adam_router_grid(side);
+            stage_end(slot, side);
+            if (update == 1) {
+                slot = stage_begin(S_ADAM_GRID, side);
+                adam_router_grid(side);
+                stage_end(slot, side);
+            }
             ODIE_CUDA(cudaEventRecord(join_event, side));
+            slot = stage_begin(S_ENCODE_BWD);
             launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
-            if (update == 1) adam_expert_tables();
-            ODIE_CUDA(cudaStreamWaitEvent(stream, join_event, 0));
             stage_end(slot);
+            if (update == 1) {
+                slot = stage_begin(S_ADAM_GRID);
+                adam_expert_tables();
+                stage_end(slot);
+            }
+            ODIE_CUDA(cudaStreamWaitEvent(stream, join_event, 0));
         } else {
+            slot = stage_begin(S_ENCODE_BWD);
             launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, stream);
             stage_end(slot);
             slot = stage_begin(S_REDUCE);

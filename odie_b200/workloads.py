@@ -25,7 +25,10 @@ coordinates per step, 70 % of them drawn from the allocated tiles.
 Multi-GPU (all workloads): rank r of N trains the model of row band r of the
 image (its own tables: spatial ownership); the heads are shared.
 """
+import math
+
 import numpy as np
+
 import torch
 
 from . import layout as host_layout
@@ -150,3 +153,43 @@ def allocated_ids(tiles, shape, count, generator, fraction=0.7, tile_px=C3_TILE)
     rest = torch.randint(0, height * width, (count - inside,), device=device, generator=generator)
     ids = torch.cat((y * width + x, rest))
     return ids[torch.randperm(count, device=device, generator=generator)]
+
+
+def allocated_stratified_ids(tiles, shape, count, generator, fraction=0.7, tile_px=C3_TILE):
+    """count pixel ids with the distribution of allocated_ids, stratified: `fraction` of them spread evenly over the
+    allocated tiles (tile t in row-major tile order takes base + (t < extra) samples), each tile's share on a
+    jittered columns x rows grid (columns = ceil(sqrt(share)), rows = ceil(share / columns)), then the rest on a
+    jittered grid over the whole image; emitted tile by tile, row-major inside each grid, like the reference's
+    stratified sampler (odie/data.py:63-80)."""
+    height, width = shape
+    device = tiles.device
+    chosen = torch.nonzero(tiles.reshape(-1)).reshape(-1)
+    inside = int(round(count * fraction)) if chosen.numel() else 0
+    parts = []
+    if inside:
+        n_tiles = chosen.numel()
+        share = torch.full((n_tiles,), inside // n_tiles, dtype=torch.long, device=device)
+        share[:inside % n_tiles] += 1
+        first = torch.cumsum(share, 0) - share
+        tile = torch.repeat_interleave(torch.arange(n_tiles, device=device), share, output_size=inside)
+        j = torch.arange(inside, device=device) - first[tile]
+        cols = torch.ceil(torch.sqrt(share.double())).long().clamp_(min=1)[tile]
+        rows = ((share[tile] + cols - 1) // cols).clamp_(min=1)
+        t = chosen[tile]
+        x0, y0 = (t % tiles.shape[1]) * tile_px, (t // tiles.shape[1]) * tile_px
+        u = ((j % cols).double() + torch.rand(inside, device=device, generator=generator, dtype=torch.float64)) / cols
+        v = ((j // cols).double() + torch.rand(inside, device=device, generator=generator, dtype=torch.float64)) / rows
+        x = (x0 + (u * tile_px).long()).clamp_(max=width - 1)
+        y = (y0 + (v * tile_px).long()).clamp_(max=height - 1)
+        parts.append(y * width + x)
+    rest = count - inside
+    if rest:
+        cols = max(1, math.ceil(math.sqrt(rest)))
+        rows = -(-rest // cols)
+        j = torch.arange(rest, device=device)
+        u = ((j % cols).double() + torch.rand(rest, device=device, generator=generator, dtype=torch.float64)) / cols
+        v = ((j // cols).double() + torch.rand(rest, device=device, generator=generator, dtype=torch.float64)) / rows
+        x = (u * width).long().clamp_(max=width - 1)
+        y = (v * height).long().clamp_(max=height - 1)
+        parts.append(y * width + x)
+    return torch.cat(parts) if parts else torch.zeros(0, dtype=torch.long, device=device)
