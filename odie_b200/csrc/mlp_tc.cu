@@ -78,13 +78,21 @@ struct TcSmem {
     static_assert(dgh + 16384 <= bar, "DGH read 64 wide stays inside the activation buffers");
 };
 
+// Two floats rounded to fp16 (round to nearest even) in one packed conversion; lo in bits 0..15.
+__device__ __forceinline__ uint32_t cvt_pair(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ __half2 as_half2(uint32_t v) { return *reinterpret_cast<const __half2*>(&v); }
+__device__ __forceinline__ uint32_t as_u32(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+// half(half(x) / 128) for a pair: an fp16 product with 2^-7 rounds the same real value as the fp32
+// quotient does (both exact before the one rounding to fp16), so the pair stays in fp16.
+__device__ __forceinline__ __half2 grid_pair(float x0, float x1) {
+    return __hmul2_rn(as_half2(cvt_pair(x0, x1)), __float2half2_rn(0.0078125f));
+}
+
 __device__ __forceinline__ uint4 pack8(const float* v) {
-    uint4 q;
-    q.x = pack_half2(__float2half_rn(v[0]), __float2half_rn(v[1]));
-    q.y = pack_half2(__float2half_rn(v[2]), __float2half_rn(v[3]));
-    q.z = pack_half2(__float2half_rn(v[4]), __float2half_rn(v[5]));
-    q.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
-    return q;
+    return make_uint4(cvt_pair(v[0], v[1]), cvt_pair(v[2], v[3]), cvt_pair(v[4], v[5]), cvt_pair(v[6], v[7]));
 }
 
 // Row r, columns [8j, 8j+8) of a blocked [128 x cols] matrix.
@@ -110,7 +118,10 @@ struct Issuer {
     uint64_t* bar;
     uint64_t* bar_dw;
     uint32_t phase = 0, phase_dw = 0;
-    bool ok = true, data_ok = true;
+    // ok: CTA-uniform, updated once per tile; fine: this thread's waits all completed.  Each thread
+    // waits on the mbarriers itself, so no CTA barrier is needed after a wait; a wait that gives up
+    // lets the tile run on and ends the loop at the tile's end, for every thread at once.
+    bool ok = true, fine = true;
     // Make every thread's shared-memory writes visible to the tensor cores and
     // every TMEM read complete, then let thread 0 issue.
     __device__ void before_issue() {
@@ -120,28 +131,29 @@ struct Issuer {
         if (threadIdx.x == 0) tc::fence_after_sync();
     }
     // Thread 0 commits; everybody waits (bounded) for the products to land.
-    __device__ bool complete() {
+    __device__ void complete() {
         if (threadIdx.x == 0) tc::commit(bar);
-        const bool done = tc::bar_wait(bar, phase, WAIT_LIMIT);
+        fine = tc::bar_wait(bar, phase, WAIT_LIMIT) && fine;
         phase ^= 1u;
-        ok = __syncthreads_and(done) != 0;
         tc::fence_after_sync();
-        return ok;
     }
     // Backward phases commit the data product (bar) and the weight-gradient
     // products (bar_dw) separately: the epilogue reads the data product while
     // the weight-gradient products still run, and waits for them only before
     // overwriting an operand they read.
     __device__ void wait_data() {
-        data_ok = tc::bar_wait(bar, phase, WAIT_LIMIT);
+        fine = tc::bar_wait(bar, phase, WAIT_LIMIT) && fine;
         phase ^= 1u;
         tc::fence_after_sync();
     }
-    __device__ bool wait_dw() {
-        const bool done = tc::bar_wait(bar_dw, phase_dw, WAIT_LIMIT);
+    __device__ void wait_dw() {
+        fine = tc::bar_wait(bar_dw, phase_dw, WAIT_LIMIT) && fine;
         phase_dw ^= 1u;
-        ok = __syncthreads_and(done && data_ok) != 0;
         tc::fence_after_sync();
+    }
+    // End of a tile (CTA-wide): whether every thread's waits completed.
+    __device__ bool settle() {
+        ok = __syncthreads_and(fine) != 0;
         return ok;
     }
 };
@@ -152,22 +164,23 @@ __device__ __forceinline__ void masked_pack16(uint32_t taddr, uint32_t mask, uin
     tc::tmem_ld16(taddr, v);
 #pragma unroll
     for (int c = 0; c < 16; c += 2)
-        out[c / 2] = pack_half2(__float2half_rn((mask >> c & 1u) ? v[c] : 0.0f),
-                                __float2half_rn((mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f));
+        out[c / 2] = cvt_pair((mask >> c & 1u) ? v[c] : 0.0f, (mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f);
 }
 
 // Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
 __device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
     float v[16];
     tc::tmem_ld16(taddr, v);
-    uint32_t mask = 0;
+    uint32_t mask = 0, h[8];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        v[c] = __half2float(__float2half_rn(v[c] > 0.0f ? v[c] : 0.0f));
-        mask |= uint32_t(v[c] > 0.0f) << c;
+    for (int c = 0; c < 16; c += 2) {
+        // relu then fp16; the mask marks values still positive in fp16 (+0 where relu or rounding gave zero)
+        h[c / 2] = cvt_pair(v[c] > 0.0f ? v[c] : 0.0f, v[c + 1] > 0.0f ? v[c + 1] : 0.0f);
+        mask |= uint32_t((h[c / 2] & 0x7fffu) != 0u) << c;
+        mask |= uint32_t((h[c / 2] & 0x7fff0000u) != 0u) << (c + 1);
     }
-    store_chunk(smem, base, r, j0, pack8(v));
-    store_chunk(smem, base, r, j0 + 1, pack8(v + 8));
+    store_chunk(smem, base, r, j0, make_uint4(h[0], h[1], h[2], h[3]));
+    store_chunk(smem, base, r, j0 + 1, make_uint4(h[4], h[5], h[6], h[7]));
     return mask;
 }
 // x / 128 as an exact multiply: both round the same real value x * 2^-7, underflow included.
@@ -351,7 +364,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             if (t == 0)
                 for (int s = 0; s < KW; ++s)
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
-            if (!is.complete()) break;
+            is.complete();
             gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
             gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
             // ---- logits = GH Wg2^T; gated decoder input raw * half(s_l * vis_l) (runtime.cu:66-75)
@@ -359,7 +372,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             if (t == 0)
                 for (int s = 0; s < 2; ++s)
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
-            if (!is.complete()) break;
+            is.complete();
             float z[16];
             tc::tmem_ld16(lane_addr + T_ACC, z);
             uint32_t wx[PAIRS];
@@ -414,26 +427,26 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 if (t == 0)
                     for (int s = 0; s < KW; ++s)
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
-                if (!is.complete()) break;
+                is.complete();
                 gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
                 gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
                 is.before_issue();
                 if (t == 0)
                     for (int s = 0; s < 2; ++s)
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
-                if (!is.complete()) break;
+                is.complete();
                 gh2_mask = relu_store16(lane_addr + T_ACC, smem, S::gh2, t, 0);
                 gh2_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh2, t, 2) << 16;
                 is.before_issue();
                 if (t == 0)
                     for (int s = 0; s < 2; ++s)
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh2, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
-                if (!is.complete()) break;
+                is.complete();
                 float z[ROUTER_OUT];
                 uint32_t zs[ROUTER_OUT / 2];
                 tc::tmem_ld16(lane_addr + T_ACC, z);
 #pragma unroll
-                for (int j = 0; j < ROUTER_OUT / 2; ++j) zs[j] = pack_half2(__float2half_rn(z[2 * j]), __float2half_rn(z[2 * j + 1]));
+                for (int j = 0; j < ROUTER_OUT / 2; ++j) zs[j] = cvt_pair(z[2 * j], z[2 * j + 1]);
                 // kept for the backward in this row of the DA buffer, which nothing reads before then
                 store_chunk(smem, S::da, t, 0, make_uint4(zs[0], zs[1], zs[2], zs[3]));
                 store_chunk(smem, S::da, t, 1, make_uint4(zs[4], zs[5], zs[6], zs[7]));
@@ -445,21 +458,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         if (t == 0)
             for (int s = 0; s < KW; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + in_buf, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
-        if (!is.complete()) break;
+        is.complete();
 #pragma unroll
         for (int q = 0; q < 4; ++q) h1_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
-        if (!is.complete()) break;
+        is.complete();
 #pragma unroll
         for (int q = 0; q < 4; ++q) h2_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
-        if (!is.complete()) break;
+        is.complete();
         float out[16];
         tc::tmem_ld16(lane_addr + T_ACC, out);
         load_inputs(next_tile);  // prefetch: consumed at the start of the next tile
@@ -513,7 +526,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         is.wait_data();
 #pragma unroll
         for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h2_mask[q], packed + 8 * q);
-        if (!is.wait_dw()) break;  // dW3 has read H2: dh2 may overwrite it
+        is.wait_dw();  // dW3 has read H2: dh2 may overwrite it
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             store_chunk(smem, S::h2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
@@ -534,7 +547,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         is.wait_data();
 #pragma unroll
         for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h1_mask[q], packed + 8 * q);
-        if (!is.wait_dw()) break;  // dWd2 has read H1: dh1 may overwrite it
+        is.wait_dw();  // dWd2 has read H1: dh1 may overwrite it
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             store_chunk(smem, S::h1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
@@ -559,15 +572,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         uint32_t gv[PAIRS];
         if (EXPERTS) {
             // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
-            const __half ph = __float2half_rn(prob);
+            const __half2 ph = __float2half2_rn(prob);
             float dp = 0.0f;
 #pragma unroll
             for (int p = 0; p < PAIRS; ++p) {
-                const __half v0 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p]))));
-                const __half v1 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p + 1]))));
-                gv[p] = pack_half2(__hmul_rn(v0, ph), __hmul_rn(v1, ph));
-                dp = __fmaf_rn(__half2float(v0), __half2float(lo_half(raw[p])), dp);
-                dp = __fmaf_rn(__half2float(v1), __half2float(hi_half(raw[p])), dp);
+                const __half2 v = grid_pair(dzf[2 * p], dzf[2 * p + 1]);
+                gv[p] = as_u32(__hmul2_rn(v, ph));
+                dp = __fmaf_rn(__low2float(v), __half2float(lo_half(raw[p])), dp);
+                dp = __fmaf_rn(__high2float(v), __half2float(hi_half(raw[p])), dp);
             }
             // ---- logit gradients: softmax of the recomputed fp16 logits over the live experts
             uint32_t zh[ROUTER_OUT / 2];
@@ -597,7 +609,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 const float derivative = __fmul_rn(dpp, __fsub_rn(j == expert ? 1.0f : 0.0f, pj));
                 da[j] = j < a.experts ? __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f))) : 0.0f;
             }
-            if (!is.wait_dw()) break;  // dWd1 done before the next products are queued
+            is.wait_dw();  // dWd1 done before the next products are queued
             store_chunk(smem, S::da, t, 0, pack8(da));
             store_chunk(smem, S::da, t, 1, pack8(da + 8));
             // ---- dgh2 = DA Wr3; dWr3^T += GH2^T DA
@@ -616,7 +628,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             is.wait_data();
             masked_pack16(lane_addr + T_ACC, gh2_mask & 0xffffu, packed);
             masked_pack16(lane_addr + T_ACC + 16, gh2_mask >> 16, packed + 8);
-            if (!is.wait_dw()) break;
+            is.wait_dw();
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
@@ -637,7 +649,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             is.wait_data();
             masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
             masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
-            if (!is.wait_dw()) break;  // dWr2 has read DGH2: dgh1 may overwrite it
+            is.wait_dw();  // dWr2 has read DGH2: dgh1 may overwrite it
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
@@ -662,23 +674,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
                 uint32_t rv[8];
 #pragma unroll
-                for (int c = 0; c < 16; c += 2)
-                    rv[c / 2] = pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(v[c])))),
-                                           __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1])))));
+                for (int c = 0; c < 16; c += 2) rv[c / 2] = as_u32(grid_pair(v[c], v[c + 1]));
                 if (valid) {  // row-major [stride][W]: one 32-byte run per 16 columns
                     uint4* dst = reinterpret_cast<uint4*>(a.router_gvals + i * W + 16 * q);
                     dst[0] = make_uint4(rv[0], rv[1], rv[2], rv[3]);
                     dst[1] = make_uint4(rv[4], rv[5], rv[6], rv[7]);
                 }
             }
-            if (!is.wait_dw()) break;  // dWr1 has read R and DGH1
+            is.wait_dw();  // dWr1 has read R and DGH1
         } else if (!ROUTER) {
-            if (!is.wait_dw()) break;  // dWd1 has read X: the next tile may overwrite it
+            is.wait_dw();  // dWd1 has read X: the next tile may overwrite it
             // grid values without router: half(dz / 128) (runtime.cu:123)
 #pragma unroll
-            for (int p = 0; p < PAIRS; ++p)
-                gv[p] = pack_half2(__float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p])))),
-                                   __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * p + 1])))));
+            for (int p = 0; p < PAIRS; ++p) gv[p] = as_u32(grid_pair(dzf[2 * p], dzf[2 * p + 1]));
         } else {
             // ---- gate backward per level (runtime.cu:76-92): direct and logit gradients
             uint32_t direct[PAIRS];
@@ -692,8 +700,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     if (l < L) {
                         const float vis = float((visbits >> l) & 1u);
                         const __half w = __float2half_rn(__fmul_rn(sig[l], vis));
-                        const __half v0 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * l]))));
-                        const __half v1 = __float2half_rn(div128(__half2float(__float2half_rn(dzf[2 * l + 1]))));
+                        const __half2 vv = grid_pair(dzf[2 * l], dzf[2 * l + 1]);
+                        const __half v0 = __low2half(vv), v1 = __high2half(vv);
                         direct[l] = pack_half2(__hmul_rn(v0, w), __hmul_rn(v1, w));
                         __half reduced = __hadd_rn(__float2half_rn(0.0f), __hmul_rn(v0, lo_half(raw[l])));
                         reduced = __hadd_rn(reduced, __hmul_rn(v1, hi_half(raw[l])));
@@ -731,7 +739,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
                 for (int p = 0; p < PAIRS; ++p) direct[p] = pack_half2(directh[2 * p], directh[2 * p + 1]);
             }
-            if (!is.wait_dw()) break;  // dWd1 done before the next products are queued
+            is.wait_dw();  // dWd1 done before the next products are queued
             store_chunk(smem, S::da, t, 0, pack8(da));
             store_chunk(smem, S::da, t, 1, pack8(da + 8));
             // ---- dgh = DA Wg2; dWg2^T += GH^T DA
@@ -750,7 +758,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             is.wait_data();
             masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
             masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
-            if (!is.wait_dw()) break;
+            is.wait_dw();
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
@@ -776,18 +784,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
                 for (int c = 0; c < 16; c += 2) {
                     const int p = 8 * q + c / 2;
-                    const __half r0 = __float2half_rn(div128(__half2float(__float2half_rn(v[c]))));
-                    const __half r1 = __float2half_rn(div128(__half2float(__float2half_rn(v[c + 1]))));
-                    gv[p] = pack_half2(__hadd_rn(lo_half(direct[p]), r0), __hadd_rn(hi_half(direct[p]), r1));
+                    gv[p] = as_u32(__hadd2_rn(as_half2(direct[p]), grid_pair(v[c], v[c + 1])));
                 }
             }
-            if (!is.wait_dw()) break;  // dWg1 has read X and DGH: the next tile may overwrite them
+            is.wait_dw();  // dWg1 has read X and DGH: the next tile may overwrite them
         }
         if (valid) {
 #pragma unroll
             for (int j = 0; j < PAIRS / 4; ++j)  // row-major [stride][W]: the coordinate's values in 16-byte runs
                 reinterpret_cast<uint4*>(a.gvals + i * W)[j] = make_uint4(gv[4 * j], gv[4 * j + 1], gv[4 * j + 2], gv[4 * j + 3]);
         }
+        if (!is.settle()) break;
         dw_accumulate = 1;
         fold_vis(next_tile);
         if (EXPERTS && TRAIN) xbuf = xbuf == S::x ? S::x2 : S::x;
