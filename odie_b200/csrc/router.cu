@@ -3,10 +3,10 @@
 // The router is a small MLP over the coarse shared grid's features: W -> 32
 // (ReLU) -> 32 (ReLU) -> 16 logits, fp16 weights [out][in], no biases.  The
 // routing decision must be reproducible bit for bit, so this forward pass does
-// not use the tensor cores (whose fp32 accumulation order is unspecified): one
-// thread per coordinate evaluates every output as an fp32 fused-multiply-add
-// chain in ascending input order from +0, rounds every layer's output to fp16,
-// and picks the first maximum of the fp16 logits over the live experts.  The
+// not use the tensor cores (whose fp32 accumulation order is unspecified): every
+// output of a coordinate is an fp32 fused-multiply-add chain in ascending input
+// order from +0 on the CUDA cores; every layer's output is rounded to fp16, and
+// the choice is the first maximum of the fp16 logits over the live experts.  The
 // gate probability of the chosen expert is 1 / sum_j exp(z_j - z_max), the sum
 // taken in ascending expert order.  2 560 FMAs per coordinate.
 #include "router.cuh"
@@ -19,12 +19,12 @@ constexpr int ROUTER_THREADS = 128;
 
 __device__ __forceinline__ float half_round(float x) { return __half2float(__float2half_rn(x)); }
 
-// One thread per coordinate.  Every layer runs its outputs in pairs (o, o + 1)
+// Two coordinates per thread.  Every layer runs its outputs in pairs (o, o + 1)
 // as packed fma chains (fma.rn.f32x2: two IEEE fp32 fused multiply-adds, each
 // rounded exactly as __fmaf_rn) over the input broadcast as {x_k, x_k}; the
-// weights sit in shared memory pair-interleaved, {W[o][k], W[o + 1][k]}, so one
-// 8-byte load feeds one packed instruction.
-constexpr int ROUTER_PER_THREAD = 1;
+// weights sit in shared memory pair-interleaved, {W[o][k], W[o + 1][k]}, and each
+// weight load serves both coordinates (the kernel is bound by shared-memory loads).
+constexpr int ROUTER_PER_THREAD = 2;
 
 using f32x2 = unsigned long long;
 __device__ __forceinline__ f32x2 pack2(float a, float b) {
@@ -39,29 +39,47 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
     return d;
 }
 
-// out[o] = act(sum_k W[o][k] in[k]) for OUT outputs over IN inputs; w: pair-interleaved weights.
-// The input stays in registers (broadcast pairs); the output pairs are produced in a
-// loop that is not unrolled (the kernel's code stays small enough for the
-// instruction cache) and written to this thread's column of act[][blockDim].
+// Two coordinates a and b per thread: out[o] = act(sum_k W[o][k] in[k]) for OUT outputs over
+// IN inputs (IN even), for both.  w: pair-interleaved weights {W[o][k], W[o + 1][k]}, 16-byte
+// aligned rows, so one 16-byte shared load (a broadcast) brings pairs k and k + 1 and feeds
+// four packed FMAs.  Each coordinate's outputs are its own fma chains in ascending k from +0,
+// exactly as one coordinate per thread computes them.  The inputs stay in registers
+// (broadcast pairs); the output pairs come from a loop that is not unrolled (the code stays
+// small enough for the instruction cache) and go to the coordinates' columns of act.
 template <int IN, int OUT, bool RELU>
-__device__ __forceinline__ void layer(const f32x2* __restrict__ w, const float* in, float* act) {
-    f32x2 bcast[IN];
+__device__ __forceinline__ void layer(const f32x2* __restrict__ w, const float* in_a, const float* in_b, float* act_a,
+                                      float* act_b) {
+    f32x2 ba[IN], bb[IN];
 #pragma unroll
-    for (int k = 0; k < IN; ++k) bcast[k] = pack2(in[k], in[k]);
+    for (int k = 0; k < IN; ++k) {
+        ba[k] = pack2(in_a[k], in_a[k]);
+        bb[k] = pack2(in_b[k], in_b[k]);
+    }
 #pragma unroll 1
     for (int o = 0; o < OUT; o += 2) {
-        const f32x2* wo = w + (o / 2) * IN;
-        f32x2 acc = 0;  // {+0, +0}
+        const ulonglong2* wo = reinterpret_cast<const ulonglong2*>(w + (o / 2) * IN);
+        f32x2 acc_a = 0, acc_b = 0;  // {+0, +0}
 #pragma unroll
-        for (int k = 0; k < IN; ++k) acc = fma2(wo[k], bcast[k], acc);
-        float a, b;
-        unpack2(acc, a, b);
-        if (RELU) {
-            a = a > 0.0f ? a : 0.0f;
-            b = b > 0.0f ? b : 0.0f;
+        for (int k = 0; k < IN; k += 2) {
+            const ulonglong2 q = wo[k / 2];
+            acc_a = fma2(q.x, ba[k], acc_a);
+            acc_b = fma2(q.x, bb[k], acc_b);
+            acc_a = fma2(q.y, ba[k + 1], acc_a);
+            acc_b = fma2(q.y, bb[k + 1], acc_b);
         }
-        act[o * ROUTER_THREADS + threadIdx.x] = half_round(a);
-        act[(o + 1) * ROUTER_THREADS + threadIdx.x] = half_round(b);
+        float a0, a1, b0, b1;
+        unpack2(acc_a, a0, a1);
+        unpack2(acc_b, b0, b1);
+        if (RELU) {
+            a0 = a0 > 0.0f ? a0 : 0.0f;
+            a1 = a1 > 0.0f ? a1 : 0.0f;
+            b0 = b0 > 0.0f ? b0 : 0.0f;
+            b1 = b1 > 0.0f ? b1 : 0.0f;
+        }
+        act_a[o * ROUTER_THREADS + threadIdx.x] = half_round(a0);
+        act_a[(o + 1) * ROUTER_THREADS + threadIdx.x] = half_round(a1);
+        act_b[o * ROUTER_THREADS + threadIdx.x] = half_round(b0);
+        act_b[(o + 1) * ROUTER_THREADS + threadIdx.x] = half_round(b1);
     }
 }
 
@@ -71,10 +89,14 @@ __device__ __forceinline__ void read_column(const float* act, float* out) {
     for (int k = 0; k < N; ++k) out[k] = act[k * ROUTER_THREADS + threadIdx.x];
 }
 
+// Router-grid features of coordinate i (zeros past the end).
 template <int W>
-__device__ __forceinline__ void route_one(const RouterArgs& a, const f32x2* __restrict__ w, float* act, long long i) {
-    constexpr int P1 = ROUTER_HIDDEN * W, P2 = ROUTER_HIDDEN * ROUTER_HIDDEN;
-    float x[W];
+__device__ __forceinline__ void load_features(const RouterArgs& a, long long i, float* x) {
+    if (i >= a.n) {
+#pragma unroll
+        for (int k = 0; k < W; ++k) x[k] = 0.0f;
+        return;
+    }
     if (a.row_major) {  // the coordinate's row as 16-byte loads
 #pragma unroll
         for (int j = 0; j < W / 8; ++j) {
@@ -94,13 +116,10 @@ __device__ __forceinline__ void route_one(const RouterArgs& a, const f32x2* __re
             x[2 * p + 1] = __high2float(v);
         }
     }
-    float h[ROUTER_HIDDEN], z[ROUTER_OUT];
-    layer<W, ROUTER_HIDDEN, true>(w, x, act);
-    read_column<ROUTER_HIDDEN>(act, h);
-    layer<ROUTER_HIDDEN, ROUTER_HIDDEN, true>(w + P1 / 2, h, act);
-    read_column<ROUTER_HIDDEN>(act, h);
-    layer<ROUTER_HIDDEN, ROUTER_OUT, false>(w + (P1 + P2) / 2, h, act);
-    read_column<ROUTER_OUT>(act, z);
+}
+
+// Top-1 over the live experts (first maximum of the fp16 logits) and its softmax probability.
+__device__ __forceinline__ void choose(const RouterArgs& a, const float* z, long long i) {
     int best = 0;
     float zbest = z[0];
 #pragma unroll
@@ -122,11 +141,36 @@ __device__ __forceinline__ void route_one(const RouterArgs& a, const f32x2* __re
     }
 }
 
+// Coordinates i and j (j may lie past the end: computed on zeros, not stored).
+template <int W>
+__device__ __forceinline__ void route_two(const RouterArgs& a, const f32x2* __restrict__ w, float* act_a, float* act_b,
+                                          long long i, long long j) {
+    constexpr int P1 = ROUTER_HIDDEN * W, P2 = ROUTER_HIDDEN * ROUTER_HIDDEN;
+    float xa[W], xb[W];
+    load_features<W>(a, i, xa);
+    load_features<W>(a, j, xb);
+    float ha[ROUTER_HIDDEN], hb[ROUTER_HIDDEN];
+    layer<W, ROUTER_HIDDEN, true>(w, xa, xb, act_a, act_b);
+    read_column<ROUTER_HIDDEN>(act_a, ha);
+    read_column<ROUTER_HIDDEN>(act_b, hb);
+    layer<ROUTER_HIDDEN, ROUTER_HIDDEN, true>(w + P1 / 2, ha, hb, act_a, act_b);
+    read_column<ROUTER_HIDDEN>(act_a, ha);
+    read_column<ROUTER_HIDDEN>(act_b, hb);
+    layer<ROUTER_HIDDEN, ROUTER_OUT, false>(w + (P1 + P2) / 2, ha, hb, act_a, act_b);
+    float z[ROUTER_OUT];
+    read_column<ROUTER_OUT>(act_a, z);
+    choose(a, z, i);
+    if (j < a.n) {
+        read_column<ROUTER_OUT>(act_b, z);
+        choose(a, z, j);
+    }
+}
+
 template <int W>
 __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const RouterArgs a) {
     constexpr int P1 = ROUTER_HIDDEN * W, P2 = ROUTER_HIDDEN * ROUTER_HIDDEN, P3 = ROUTER_OUT * ROUTER_HIDDEN;
     __shared__ __align__(16) f32x2 w[(P1 + P2 + P3) / 2];
-    __shared__ float act[ROUTER_HIDDEN * ROUTER_THREADS];  // each thread's layer outputs, one column per thread
+    __shared__ float act[2][ROUTER_HIDDEN * ROUTER_THREADS];  // each thread's layer outputs, one column per coordinate
     // pair-interleave each layer's rows: entry (o / 2) * IN + k = {W[o][k], W[o + 1][k]}
     for (int j = threadIdx.x; j < (P1 + P2 + P3) / 2; j += blockDim.x) {
         int base = 0, in = W, e = j;
@@ -136,10 +180,10 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const Ro
         w[j] = pack2(__half2float(a.weights[base + o * in + k]), __half2float(a.weights[base + (o + 1) * in + k]));
     }
     __syncthreads();
-    // persistent blocks: the weights are staged once per block, then the block walks the coordinates
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += (long long)gridDim.x * blockDim.x) {
-        route_one<W>(a, w, act, i);
-    }
+    // persistent blocks: the weights are staged once per block, then the block walks the coordinates,
+    // 2 x blockDim at a time (thread t: base + t and base + blockDim + t)
+    for (long long base = (long long)blockIdx.x * 2 * blockDim.x; base < a.n; base += (long long)gridDim.x * 2 * blockDim.x)
+        route_two<W>(a, w, act[0], act[1], base + threadIdx.x, base + blockDim.x + threadIdx.x);
 }
 
 }  // namespace
@@ -147,11 +191,16 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const Ro
 void launch_router_forward(const RouterArgs& a, int width, cudaStream_t stream) {
     if (a.n <= 0) return;
     ODIE_REQUIRE(a.experts >= 1 && a.experts <= ROUTER_OUT, "the router chooses among 1..16 experts");
+    if (width != 32 && width != 16) throw std::invalid_argument("the router takes 16 or 32 input features");
+    // persistent blocks: as many as fit on the GPU at once
+    int per_sm = 0;
+    if (width == 32) ODIE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, router_forward_kernel<32>, ROUTER_THREADS, 0));
+    else ODIE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, router_forward_kernel<16>, ROUTER_THREADS, 0));
+    const long long resident = (long long)(per_sm > 0 ? per_sm : 1) * sm_count();
     const long long needed = blocks_for(a.n, ROUTER_THREADS * ROUTER_PER_THREAD);
-    const unsigned blocks = unsigned(needed < 8LL * sm_count() ? needed : 8LL * sm_count());
+    const unsigned blocks = unsigned(needed < resident ? needed : resident);
     if (width == 32) router_forward_kernel<32><<<blocks, ROUTER_THREADS, 0, stream>>>(a);
-    else if (width == 16) router_forward_kernel<16><<<blocks, ROUTER_THREADS, 0, stream>>>(a);
-    else throw std::invalid_argument("the router takes 16 or 32 input features");
+    else router_forward_kernel<16><<<blocks, ROUTER_THREADS, 0, stream>>>(a);
     note_launch();
 }
 
