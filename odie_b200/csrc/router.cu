@@ -17,14 +17,12 @@ namespace {
 
 constexpr int ROUTER_THREADS = 128;
 
-__device__ __forceinline__ float half_round(float x) { return __half2float(__float2half_rn(x)); }
-
-// Two coordinates per thread.  Every layer runs its outputs in pairs (o, o + 1)
+// ROUTER_PER_THREAD coordinates per thread.  Every layer runs its outputs in pairs (o, o + 1)
 // as packed fma chains (fma.rn.f32x2: two IEEE fp32 fused multiply-adds, each
 // rounded exactly as __fmaf_rn) over the input broadcast as {x_k, x_k}; the
 // weights sit in shared memory pair-interleaved, {W[o][k], W[o + 1][k]}, and each
-// weight load serves both coordinates (the kernel is bound by shared-memory loads).
-constexpr int ROUTER_PER_THREAD = 2;
+// weight load serves all of the thread's coordinates (the kernel is bound by shared-memory loads).
+constexpr int ROUTER_PER_THREAD = 4;
 
 using f32x2 = unsigned long long;
 __device__ __forceinline__ f32x2 pack2(float a, float b) {
@@ -39,54 +37,57 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
     return d;
 }
 
-// Two coordinates a and b per thread: out[o] = act(sum_k W[o][k] in[k]) for OUT outputs over
-// IN inputs (IN even), for both.  w: pair-interleaved weights {W[o][k], W[o + 1][k]}, 16-byte
+// C coordinates per thread: out[o] = act(sum_k W[o][k] in[k]) for OUT outputs over IN
+// inputs (IN even), for each.  w: pair-interleaved weights {W[o][k], W[o + 1][k]}, 16-byte
 // aligned rows, so one 16-byte shared load (a broadcast) brings pairs k and k + 1 and feeds
-// four packed FMAs.  Each coordinate's outputs are its own fma chains in ascending k from +0,
-// exactly as one coordinate per thread computes them.  The inputs stay in registers
-// (broadcast pairs); the output pairs come from a loop that is not unrolled (the code stays
-// small enough for the instruction cache) and go to the coordinates' columns of act.
-template <int IN, int OUT, bool RELU>
-__device__ __forceinline__ void layer(const f32x2* __restrict__ w, const float* in_a, const float* in_b, float* act_a,
-                                      float* act_b) {
-    f32x2 ba[IN], bb[IN];
+// 2 C packed FMAs.  Each coordinate's outputs are its own fma chains in ascending k from +0,
+// exactly as one coordinate per thread computes them.  The output pairs come from a loop that
+// is not unrolled (the code stays small enough for the instruction cache) and land as fp16
+// pairs in the coordinates' columns of act.
+template <int C, int IN, int OUT, bool RELU>
+__device__ __forceinline__ void layer(const f32x2* __restrict__ w, const float (&in)[C][IN], __half2* act) {
+    f32x2 bc[C][IN];
 #pragma unroll
-    for (int k = 0; k < IN; ++k) {
-        ba[k] = pack2(in_a[k], in_a[k]);
-        bb[k] = pack2(in_b[k], in_b[k]);
-    }
+    for (int c = 0; c < C; ++c)
+#pragma unroll
+        for (int k = 0; k < IN; ++k) bc[c][k] = pack2(in[c][k], in[c][k]);
 #pragma unroll 1
     for (int o = 0; o < OUT; o += 2) {
         const ulonglong2* wo = reinterpret_cast<const ulonglong2*>(w + (o / 2) * IN);
-        f32x2 acc_a = 0, acc_b = 0;  // {+0, +0}
+        f32x2 acc[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) acc[c] = 0;  // {+0, +0}
 #pragma unroll
         for (int k = 0; k < IN; k += 2) {
             const ulonglong2 q = wo[k / 2];
-            acc_a = fma2(q.x, ba[k], acc_a);
-            acc_b = fma2(q.x, bb[k], acc_b);
-            acc_a = fma2(q.y, ba[k + 1], acc_a);
-            acc_b = fma2(q.y, bb[k + 1], acc_b);
+#pragma unroll
+            for (int c = 0; c < C; ++c) acc[c] = fma2(q.x, bc[c][k], acc[c]);
+#pragma unroll
+            for (int c = 0; c < C; ++c) acc[c] = fma2(q.y, bc[c][k + 1], acc[c]);
         }
-        float a0, a1, b0, b1;
-        unpack2(acc_a, a0, a1);
-        unpack2(acc_b, b0, b1);
-        if (RELU) {
-            a0 = a0 > 0.0f ? a0 : 0.0f;
-            a1 = a1 > 0.0f ? a1 : 0.0f;
-            b0 = b0 > 0.0f ? b0 : 0.0f;
-            b1 = b1 > 0.0f ? b1 : 0.0f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            float v0, v1;
+            unpack2(acc[c], v0, v1);
+            if (RELU) {
+                v0 = v0 > 0.0f ? v0 : 0.0f;
+                v1 = v1 > 0.0f ? v1 : 0.0f;
+            }
+            // the pair rounded to fp16, as one 4-byte store
+            act[(c * ROUTER_HIDDEN / 2 + o / 2) * ROUTER_THREADS + threadIdx.x] = __floats2half2_rn(v0, v1);
         }
-        act_a[o * ROUTER_THREADS + threadIdx.x] = half_round(a0);
-        act_a[(o + 1) * ROUTER_THREADS + threadIdx.x] = half_round(a1);
-        act_b[o * ROUTER_THREADS + threadIdx.x] = half_round(b0);
-        act_b[(o + 1) * ROUTER_THREADS + threadIdx.x] = half_round(b1);
     }
 }
 
+// The N fp16 outputs of coordinate c of this thread (pairs stored as half2).
 template <int N>
-__device__ __forceinline__ void read_column(const float* act, float* out) {
+__device__ __forceinline__ void read_column(const __half2* act, int c, float* out) {
 #pragma unroll
-    for (int k = 0; k < N; ++k) out[k] = act[k * ROUTER_THREADS + threadIdx.x];
+    for (int p = 0; p < N / 2; ++p) {
+        const __half2 v = act[(c * ROUTER_HIDDEN / 2 + p) * ROUTER_THREADS + threadIdx.x];
+        out[2 * p] = __low2float(v);
+        out[2 * p + 1] = __high2float(v);
+    }
 }
 
 // Router-grid features of coordinate i (zeros past the end).
@@ -141,36 +142,39 @@ __device__ __forceinline__ void choose(const RouterArgs& a, const float* z, long
     }
 }
 
-// Coordinates i and j (j may lie past the end: computed on zeros, not stored).
-template <int W>
-__device__ __forceinline__ void route_two(const RouterArgs& a, const f32x2* __restrict__ w, float* act_a, float* act_b,
-                                          long long i, long long j) {
+// Coordinates first + c * blockDim for c < C (those past the end: computed on zeros, not stored).
+template <int C, int W>
+__device__ __forceinline__ void route_group(const RouterArgs& a, const f32x2* __restrict__ w, __half2* act,
+                                            long long first) {
     constexpr int P1 = ROUTER_HIDDEN * W, P2 = ROUTER_HIDDEN * ROUTER_HIDDEN;
-    float xa[W], xb[W];
-    load_features<W>(a, i, xa);
-    load_features<W>(a, j, xb);
-    float ha[ROUTER_HIDDEN], hb[ROUTER_HIDDEN];
-    layer<W, ROUTER_HIDDEN, true>(w, xa, xb, act_a, act_b);
-    read_column<ROUTER_HIDDEN>(act_a, ha);
-    read_column<ROUTER_HIDDEN>(act_b, hb);
-    layer<ROUTER_HIDDEN, ROUTER_HIDDEN, true>(w + P1 / 2, ha, hb, act_a, act_b);
-    read_column<ROUTER_HIDDEN>(act_a, ha);
-    read_column<ROUTER_HIDDEN>(act_b, hb);
-    layer<ROUTER_HIDDEN, ROUTER_OUT, false>(w + (P1 + P2) / 2, ha, hb, act_a, act_b);
-    float z[ROUTER_OUT];
-    read_column<ROUTER_OUT>(act_a, z);
-    choose(a, z, i);
-    if (j < a.n) {
-        read_column<ROUTER_OUT>(act_b, z);
-        choose(a, z, j);
+    float x[C][W];
+#pragma unroll
+    for (int c = 0; c < C; ++c) load_features<W>(a, first + (long long)c * blockDim.x, x[c]);
+    float h[C][ROUTER_HIDDEN];
+    layer<C, W, ROUTER_HIDDEN, true>(w, x, act);
+#pragma unroll
+    for (int c = 0; c < C; ++c) read_column<ROUTER_HIDDEN>(act, c, h[c]);
+    layer<C, ROUTER_HIDDEN, ROUTER_HIDDEN, true>(w + P1 / 2, h, act);
+#pragma unroll
+    for (int c = 0; c < C; ++c) read_column<ROUTER_HIDDEN>(act, c, h[c]);
+    layer<C, ROUTER_HIDDEN, ROUTER_OUT, false>(w + (P1 + P2) / 2, h, act);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const long long i = first + (long long)c * blockDim.x;
+        if (i < a.n) {
+            float z[ROUTER_OUT];
+            read_column<ROUTER_OUT>(act, c, z);
+            choose(a, z, i);
+        }
     }
 }
 
 template <int W>
 __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const RouterArgs a) {
     constexpr int P1 = ROUTER_HIDDEN * W, P2 = ROUTER_HIDDEN * ROUTER_HIDDEN, P3 = ROUTER_OUT * ROUTER_HIDDEN;
+    constexpr int C = ROUTER_PER_THREAD;
     __shared__ __align__(16) f32x2 w[(P1 + P2 + P3) / 2];
-    __shared__ float act[2][ROUTER_HIDDEN * ROUTER_THREADS];  // each thread's layer outputs, one column per coordinate
+    __shared__ __half2 act[C * ROUTER_HIDDEN / 2 * ROUTER_THREADS];  // each coordinate's layer outputs (fp16 pairs)
     // pair-interleave each layer's rows: entry (o / 2) * IN + k = {W[o][k], W[o + 1][k]}
     for (int j = threadIdx.x; j < (P1 + P2 + P3) / 2; j += blockDim.x) {
         int base = 0, in = W, e = j;
@@ -181,9 +185,9 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const Ro
     }
     __syncthreads();
     // persistent blocks: the weights are staged once per block, then the block walks the coordinates,
-    // 2 x blockDim at a time (thread t: base + t and base + blockDim + t)
-    for (long long base = (long long)blockIdx.x * 2 * blockDim.x; base < a.n; base += (long long)gridDim.x * 2 * blockDim.x)
-        route_two<W>(a, w, act[0], act[1], base + threadIdx.x, base + blockDim.x + threadIdx.x);
+    // C x blockDim at a time (thread t: base + t, base + blockDim + t, ...)
+    for (long long base = (long long)blockIdx.x * C * blockDim.x; base < a.n; base += (long long)gridDim.x * C * blockDim.x)
+        route_group<C, W>(a, w, act, base + threadIdx.x);
 }
 
 }  // namespace
