@@ -10,7 +10,8 @@ packed-plane method on the same image and batch.
 One JSON line on rank 0.  `value` is whole-job coords/s with inputs resident in
 HBM (device-timed with CUDA events, max over ranks); `e2e` is the same metric
 through the public API with the step's pixel ids copied from pinned host memory
-and the loss read back every step.  Multi-GPU: one process per GPU (torchrun),
+and the loss read back every step (the next step's ids upload on a copy stream
+while a step runs, as a training loop's loader prefetches).  Multi-GPU: one process per GPU (torchrun),
 each rank trains the model of its own row band of the image (weak scaling),
 and only the shared head gradients cross GPUs (NCCL all-reduce).  The
 `--impl reference` arm times the CPU restatement of the step
@@ -414,19 +415,43 @@ def main():
     ms = float(ms_t)
     value = world * args.batch * args.steps / (ms / 1e3)
 
-    # end to end through the public API: pinned host ids in, loss out, every step
+    # end to end through the public API: pinned host ids in, loss out, every step.  As a training
+    # loop's data loader does, step k + 1's ids upload on a copy stream (double buffer) while
+    # step k runs; every copy is inside the timed region.
     host_ids = ids[args.warmup:].cpu().pin_memory()
-    device_ids = torch.empty(args.batch, dtype=torch.int64, device='cuda')
+    device_ids = [torch.empty(args.batch, dtype=torch.int64, device='cuda') for _ in range(2)]
     loss_host = torch.empty(args.steps, dtype=torch.float64).pin_memory()
     squares = torch.empty(args.batch, device='cuda')
+    main_stream, copy_stream = torch.cuda.current_stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    released = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(k):
+        buf = k % 2
+        with torch.cuda.stream(copy_stream):
+            if k >= 2:
+                copy_stream.wait_event(released[buf])  # step k - 2 has consumed this buffer
+            device_ids[buf].copy_(host_ids[k], non_blocking=True)
+            uploaded[buf].record(copy_stream)
+
+    # warm-up of the loop's own operations (the loss read's torch kernels load lazily on first use)
+    opt.check(lib.odie_copy(squares.data_ptr(), opt.pointers['squares'], args.batch * 4, main_stream.cuda_stream))
+    loss_host[:1].copy_(squares.double().mean().reshape(1), non_blocking=True)
+    upload(0)
     barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
+    copy_stream.wait_event(e_start)
+    upload(0)
     for k in range(args.steps):
-        device_ids.copy_(host_ids[k], non_blocking=True)
-        step(device_ids)
+        buf = k % 2
+        if k + 1 < args.steps:
+            upload(k + 1)
+        main_stream.wait_event(uploaded[buf])
+        step(device_ids[buf])
+        released[buf].record(main_stream)
         opt.check(lib.odie_copy(squares.data_ptr(), opt.pointers['squares'], args.batch * 4,
-                                torch.cuda.current_stream().cuda_stream))
+                                main_stream.cuda_stream))
         loss_host[k:k + 1].copy_(squares.double().mean().reshape(1), non_blocking=True)
     e_end.record()
     barrier()

@@ -124,6 +124,12 @@ __device__ __forceinline__ int corner_row(const Level& d, const Corner4& g, int 
 __device__ __forceinline__ int level_cell(const Level& d, const Corner4& g) { return g.ix + g.iy * d.res; }
 
 // ---------------------------------------------------------------- fp16 bits
+// {half(x), half(x)}: one packed conversion (round to nearest even, as __float2half_rn).
+__device__ __forceinline__ __half2 half2_dup(float x) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(r) : "f"(x));
+    return *reinterpret_cast<const __half2*>(&r);
+}
 __device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
     return uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
 }

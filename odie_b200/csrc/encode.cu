@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
             for (int k = 0; k < 4; ++k) t[k] = load_pair(params, base + 2LL * rows[k]);
             // __hfma2 rounds each lane once, exactly as the reference's per-channel __hfma chain.
 #pragma unroll
-            for (int k = 0; k < 4; ++k) acc = __hfma2(__float2half2_rn(g.w[k]), t[k], acc);
+            for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
         }
         if (!a.row_major && (d.col & 1) == 0) {
             reinterpret_cast<__half2*>(out)[(long long)(d.col >> 1) * a.stride + i] = acc;
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
                 for (int k = 0; k < 4; ++k)
                     t[k] = load_pair(params, base + d.offset + 2LL * corner_row(d, g, k, a.node_bitmap, a.node_prefix));
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc = __hfma2(__float2half2_rn(g.w[k]), t[k], acc);
+                for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
             }
         }
         row[l] = pack_half2(__low2half(acc), __high2half(acc));
