@@ -602,12 +602,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 sum = __fadd_rn(sum, z[j]);
             }
             const float dpp = __fmul_rn(dp, prob);
+            const float inv = __frcp_rn(sum);  // p_j = z_j / sum within an ulp; feeds only the fp16 logit gradients
             float da[ROUTER_OUT];
 #pragma unroll
-            for (int j = 0; j < ROUTER_OUT; ++j) {
-                const float pj = __fdiv_rn(z[j], sum);
-                const float derivative = __fmul_rn(dpp, __fsub_rn(j == expert ? 1.0f : 0.0f, pj));
-                da[j] = j < a.experts ? __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f))) : 0.0f;
+            for (int j = 0; j < ROUTER_OUT; j += 2) {
+                const float d0 = __fmul_rn(dpp, __fsub_rn(j == expert ? 1.0f : 0.0f, __fmul_rn(z[j], inv)));
+                const float d1 = __fmul_rn(dpp, __fsub_rn(j + 1 == expert ? 1.0f : 0.0f, __fmul_rn(z[j + 1], inv)));
+                // fp16(fp16(derivative) x 128): the scaling by 2^7 is exact unless it overflows, as in fp16 arithmetic
+                const __half2 h = __hmul2_rn(as_half2(cvt_pair(d0, d1)), __float2half2_rn(128.0f));
+                da[j] = j < a.experts ? __low2float(h) : 0.0f;
+                da[j + 1] = j + 1 < a.experts ? __high2float(h) : 0.0f;
             }
             is.wait_dw();  // dWd1 done before the next products are queued
             store_chunk(smem, S::da, t, 0, pack8(da));
