@@ -158,29 +158,30 @@ struct Issuer {
     }
 };
 
-// Load 16 TMEM columns, keep those whose forward activation was positive, pack to fp16 pairs.
-__device__ __forceinline__ void masked_pack16(uint32_t taddr, uint32_t mask, uint32_t* out) {
-    float v[16];
-    tc::tmem_ld16(taddr, v);
+// Load 32 TMEM columns, keep those whose forward activation was positive (bit c of mask: column c),
+// pack to 16 fp16 pairs.
+__device__ __forceinline__ void masked_pack32(uint32_t taddr, uint32_t mask, uint32_t* out) {
+    float v[32];
+    tc::tmem_ld32(taddr, v);
 #pragma unroll
-    for (int c = 0; c < 16; c += 2)
+    for (int c = 0; c < 32; c += 2)
         out[c / 2] = cvt_pair((mask >> c & 1u) ? v[c] : 0.0f, (mask >> (c + 1) & 1u) ? v[c + 1] : 0.0f);
 }
-
-// Load 16 TMEM columns, apply ReLU, round to fp16; returns the positive mask; stores two chunks.
-__device__ __forceinline__ uint32_t relu_store16(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
-    float v[16];
-    tc::tmem_ld16(taddr, v);
-    uint32_t mask = 0, h[8];
+// Load 32 TMEM columns, apply ReLU, round to fp16, store four chunks from j0; returns the 32-bit
+// mask of the values still positive in fp16.
+__device__ __forceinline__ uint32_t relu_store32(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
+    float v[32];
+    tc::tmem_ld32(taddr, v);
+    uint32_t mask = 0, h[16];
 #pragma unroll
-    for (int c = 0; c < 16; c += 2) {
-        // relu then fp16; the mask marks values still positive in fp16 (+0 where relu or rounding gave zero)
+    for (int c = 0; c < 32; c += 2) {
         h[c / 2] = cvt_pair(v[c] > 0.0f ? v[c] : 0.0f, v[c + 1] > 0.0f ? v[c + 1] : 0.0f);
         mask |= uint32_t((h[c / 2] & 0x7fffu) != 0u) << c;
         mask |= uint32_t((h[c / 2] & 0x7fff0000u) != 0u) << (c + 1);
     }
-    store_chunk(smem, base, r, j0, make_uint4(h[0], h[1], h[2], h[3]));
-    store_chunk(smem, base, r, j0 + 1, make_uint4(h[4], h[5], h[6], h[7]));
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        store_chunk(smem, base, r, j0 + q, make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]));
     return mask;
 }
 // x / 128 as an exact multiply: both round the same real value x * 2^-7, underflow included.
@@ -365,8 +366,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 for (int s = 0; s < KW; ++s)
                     tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
             is.complete();
-            gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
-            gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
+            gh_mask = relu_store32(lane_addr + T_ACC, smem, S::gh, t, 0);
             // ---- logits = GH Wg2^T; gated decoder input raw * half(s_l * vis_l) (runtime.cu:66-75)
             is.before_issue();
             if (t == 0)
@@ -428,15 +428,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     for (int s = 0; s < KW; ++s)
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
                 is.complete();
-                gh_mask = relu_store16(lane_addr + T_ACC, smem, S::gh, t, 0);
-                gh_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh, t, 2) << 16;
+                gh_mask = relu_store32(lane_addr + T_ACC, smem, S::gh, t, 0);
                 is.before_issue();
                 if (t == 0)
                     for (int s = 0; s < 2; ++s)
                         tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
                 is.complete();
-                gh2_mask = relu_store16(lane_addr + T_ACC, smem, S::gh2, t, 0);
-                gh2_mask |= relu_store16(lane_addr + T_ACC + 16, smem, S::gh2, t, 2) << 16;
+                gh2_mask = relu_store32(lane_addr + T_ACC, smem, S::gh2, t, 0);
                 is.before_issue();
                 if (t == 0)
                     for (int s = 0; s < 2; ++s)
@@ -460,14 +458,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + in_buf, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) h1_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
+        for (int q = 0; q < 4; q += 2) {
+            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
+            h1_mask[q] = m & 0xffffu;
+            h1_mask[q + 1] = m >> 16;
+        }
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) h2_mask[q] = relu_store16(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
+        for (int q = 0; q < 4; q += 2) {
+            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
+            h2_mask[q] = m & 0xffffu;
+            h2_mask[q + 1] = m >> 16;
+        }
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
@@ -525,7 +531,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         uint32_t packed[32];
         is.wait_data();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h2_mask[q], packed + 8 * q);
+        for (int q = 0; q < 4; q += 2)
+            masked_pack32(lane_addr + T_ACC + 16 * q, h2_mask[q] | (h2_mask[q + 1] << 16), packed + 8 * q);
         is.wait_dw();  // dW3 has read H2: dh2 may overwrite it
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -546,7 +553,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         }
         is.wait_data();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) masked_pack16(lane_addr + T_ACC + 16 * q, h1_mask[q], packed + 8 * q);
+        for (int q = 0; q < 4; q += 2)
+            masked_pack32(lane_addr + T_ACC + 16 * q, h1_mask[q] | (h1_mask[q + 1] << 16), packed + 8 * q);
         is.wait_dw();  // dWd2 has read H1: dh1 may overwrite it
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -567,8 +575,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         }
         is.wait_data();
         float dzf[W];
+        if (W == 32) {
+            tc::tmem_ld32(lane_addr + T_ACC, dzf);
+        } else {
 #pragma unroll
-        for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
+            for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
+        }
         uint32_t gv[PAIRS];
         if (EXPERTS) {
             // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
@@ -630,8 +642,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::commit(bar_dw);
             }
             is.wait_data();
-            masked_pack16(lane_addr + T_ACC, gh2_mask & 0xffffu, packed);
-            masked_pack16(lane_addr + T_ACC + 16, gh2_mask >> 16, packed + 8);
+            masked_pack32(lane_addr + T_ACC, gh2_mask, packed);
             is.wait_dw();
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -651,8 +662,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::commit(bar_dw);
             }
             is.wait_data();
-            masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
-            masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
+            masked_pack32(lane_addr + T_ACC, gh_mask, packed);
             is.wait_dw();  // dWr2 has read DGH2: dgh1 may overwrite it
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -760,8 +770,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                 tc::commit(bar_dw);
             }
             is.wait_data();
-            masked_pack16(lane_addr + T_ACC, gh_mask & 0xffffu, packed);
-            masked_pack16(lane_addr + T_ACC + 16, gh_mask >> 16, packed + 8);
+            masked_pack32(lane_addr + T_ACC, gh_mask, packed);
             is.wait_dw();
 #pragma unroll
             for (int j = 0; j < 4; ++j)

@@ -103,6 +103,7 @@ struct Runtime {
     LevelTable router_table{};
     float* router_grid = nullptr;  // caller-owned fp32 master of the router grid
     double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
+    double uploaded_lr[3] = {-1.0, -1.0, -1.0};  // the rates the device step tables hold (-1: none yet)
     // caller-owned
     float* grid = nullptr;
     const uint8_t* rgb = nullptr;
@@ -364,12 +365,16 @@ struct Runtime {
         if (grid_half.count) sync_weights();
     }
 
+    // The per-step learning-rate tables (16 MB each); rebuilt only for a group whose rate changed, so a
+    // reconfiguration that changes the layout or the allocation costs no table upload.
     void upload_step_tables() {
-        std::vector<float> host(TABLE_STEPS);
+        std::vector<float> host;
         for (int g = 0; g < 3; ++g) {
-            if (!table_step[g].ptr) continue;
+            if (!table_step[g].ptr || uploaded_lr[g] == lr[g]) continue;
+            host.resize(TABLE_STEPS);
             for (long long s = 0; s < TABLE_STEPS; ++s) host[s] = float(lr[g] / host_bc1[s]);
             ODIE_CUDA(cudaMemcpy(table_step[g].ptr, host.data(), TABLE_STEPS * sizeof(float), cudaMemcpyHostToDevice));
+            uploaded_lr[g] = lr[g];
         }
     }
 
