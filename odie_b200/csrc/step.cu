@@ -34,12 +34,29 @@ __global__ void coords_range_kernel(long long begin, long long n, int width, int
                                                    __fmul_rn(float(id / uint32_t(width)), ry));
 }
 
-__global__ void reduce_partials_kernel(const float* __restrict__ partials, int blocks, int count, float* __restrict__ out) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= count) return;
+// Sum of the per-CTA partials of every head parameter, in a fixed order (deterministic): a block
+// takes 32 parameters; slice k of its 8 threads per parameter sums partials k, k + 8, k + 16, ...
+// in ascending order, then the 8 slice sums are added in slice order.
+constexpr int RP_PARAMS = 32, RP_SLICES = 8;
+__global__ void __launch_bounds__(RP_PARAMS * RP_SLICES) reduce_partials_kernel(const float* __restrict__ partials,
+                                                                              int blocks, int count,
+                                                                              float* __restrict__ out) {
+    __shared__ float part[RP_SLICES][RP_PARAMS + 1];
+    const int lane = threadIdx.x % RP_PARAMS, slice = threadIdx.x / RP_PARAMS;
+    const int j = blockIdx.x * RP_PARAMS + lane;
     float s = 0.0f;
-    for (int b = 0; b < blocks; ++b) s = __fadd_rn(s, partials[(long long)b * count + j]);
-    out[j] = s;
+    if (j < count) {
+#pragma unroll 4
+        for (int b = slice; b < blocks; b += RP_SLICES) s = __fadd_rn(s, partials[(long long)b * count + j]);
+    }
+    part[slice][lane] = s;
+    __syncthreads();
+    if (slice == 0 && j < count) {
+        float t = part[0][lane];
+#pragma unroll
+        for (int k = 1; k < RP_SLICES; ++k) t = __fadd_rn(t, part[k][lane]);
+        out[j] = t;
+    }
 }
 
 // One Adam update (fp32): m = fma(w1, g - m, m); v = fma(w2 * g, g, v * b2);
@@ -125,7 +142,9 @@ void launch_coords_range(long long begin, long long n, int width, int height, fl
 }
 
 void launch_reduce_partials(const float* partials, int blocks, int count, float* out, cudaStream_t stream) {
-    reduce_partials_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(partials, blocks, count, out);
+    if (count <= 0) return;
+    reduce_partials_kernel<<<blocks_for(count, RP_PARAMS), RP_PARAMS * RP_SLICES, 0, stream>>>(partials, blocks, count,
+                                                                                                out);
     note_launch();
 }
 
