@@ -446,8 +446,9 @@ __device__ __forceinline__ void runs_flush(const Level& d, float* tab, int e, in
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int row = corner_row<KIND>(d, g, k, node_bitmap, prefix);
-        if (v[2 * k] != 0.0f) atomicAdd(t + 2 * row, v[2 * k]);
-        if (v[2 * k + 1] != 0.0f) atomicAdd(t + 2 * row + 1, v[2 * k + 1]);
+        // straight-line adds: adding an exact zero leaves an entry as it is
+        atomicAdd(t + 2 * row, v[2 * k]);
+        atomicAdd(t + 2 * row + 1, v[2 * k + 1]);
         v[2 * k] = 0.0f;
         v[2 * k + 1] = 0.0f;
     }

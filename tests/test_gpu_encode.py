@@ -97,8 +97,17 @@ def test_query_backward_vs_oracle_and_reference(cuda):
         ref = reference_query_module()
     except pytest.skip.Exception:
         return
-    ref_grad = ref.backward(coords, torch.from_numpy(upstream).cuda(), desc, nb, pf, bm, grid.size)
-    close(g.grad.cpu().numpy(), ref_grad.cpu().numpy(), 1e-5, 1e-6, 'query backward vs reference kernel')
+    ref_grad = ref.backward(coords, torch.from_numpy(upstream).cuda(), desc, nb, pf, bm, grid.size).cpu().numpy()
+    # Both kernels sum thousands of fp32 atomics per coarse entry in an order that changes from run to run, so
+    # neither is exact: ours must stay within the tolerance of the reference kernel plus that kernel's own
+    # deviation from the fp64 sum (ours is held to the plain tolerance against the fp64 sum above).
+    ours = g.grad.cpu().numpy().astype(np.float64)
+    ref64 = ref_grad.astype(np.float64)
+    own_error = np.abs(ref64 - expected)
+    allowed = 1e-5 * np.abs(ref64) + 1e-6 * np.abs(ref64).max() + own_error
+    bad = np.abs(ours - ref64) > allowed
+    assert not bad.any(), f'query backward vs reference kernel: {bad.sum()} of {bad.size} outside tolerance'
+    assert own_error.max() <= 1e-4 * np.abs(expected).max(), 'the reference kernel itself drifted from the fp64 sum'
 
 
 def test_query_empty_and_tiny_batches(cuda):
