@@ -377,12 +377,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             tc::tmem_ld16(lane_addr + T_ACC, z);
             uint32_t wx[PAIRS];
             if (UNIFORM) {
+                float zh[16];  // the fp16-rounded logits, converted in pairs
+#pragma unroll
+                for (int l = 0; l < 16; l += 2) {
+                    const __half2 h = as_half2(cvt_pair(z[l], z[l + 1]));
+                    zh[l] = __low2float(h);
+                    zh[l + 1] = __high2float(h);
+                }
 #pragma unroll
                 for (int l = 0; l < PAIRS; ++l) {
-                    sig[l] = gate_value(__half2float(__float2half_rn(z[l])), l, a.k_fixed, a.softplus);
+                    sig[l] = gate_value(zh[l], l, a.k_fixed, a.softplus);
                     if (l < L) {
-                        const __half w = __float2half_rn(__fmul_rn(sig[l], float((visbits >> l) & 1u)));
-                        wx[l] = pack_half2(__hmul_rn(lo_half(raw[l]), w), __hmul_rn(hi_half(raw[l]), w));
+                        // both features times half(s_l vis_l), each product rounded once as by __hmul_rn
+                        const __half2 w = half2_dup(__fmul_rn(sig[l], float((visbits >> l) & 1u)));
+                        wx[l] = as_u32(__hmul2_rn(as_half2(raw[l]), w));
                     } else {
                         wx[l] = raw[l];
                     }
@@ -708,21 +716,32 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int l = 0; l < 16; ++l) da[l] = 0.0f;
             if (UNIFORM) {
+                float derivative[16];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) derivative[l] = 0.0f;
 #pragma unroll
                 for (int l = 0; l < PAIRS; ++l) {
                     direct[l] = 0u;
                     if (l < L) {
                         const float vis = float((visbits >> l) & 1u);
-                        const __half w = __float2half_rn(__fmul_rn(sig[l], vis));
                         const __half2 vv = grid_pair(dzf[2 * l], dzf[2 * l + 1]);
-                        const __half v0 = __low2half(vv), v1 = __high2half(vv);
-                        direct[l] = pack_half2(__hmul_rn(v0, w), __hmul_rn(v1, w));
-                        __half reduced = __hadd_rn(__float2half_rn(0.0f), __hmul_rn(v0, lo_half(raw[l])));
-                        reduced = __hadd_rn(reduced, __hmul_rn(v1, hi_half(raw[l])));
-                        const float derivative =
+                        // elementwise fp16 products, each rounded once as by __hmul_rn
+                        direct[l] = as_u32(__hmul2_rn(vv, half2_dup(__fmul_rn(sig[l], vis))));
+                        const __half2 pr = __hmul2_rn(vv, as_half2(raw[l]));
+                        __half reduced = __hadd_rn(__float2half_rn(0.0f), __low2half(pr));
+                        reduced = __hadd_rn(reduced, __high2half(pr));
+                        derivative[l] =
                             gate_derivative(__fmul_rn(__half2float(reduced), vis), sig[l], l, a.k_fixed, a.softplus);
-                        da[l] = __half2float(__hmul_rn(__float2half_rn(derivative), __float2half_rn(128.0f)));
                     }
+                }
+                // da = fp16(fp16(derivative) x 128), two levels per packed conversion
+#pragma unroll
+                for (int l = 0; l < 16; l += 2) {
+                    if (l >= L) break;
+                    const __half2 h = __hmul2_rn(as_half2(cvt_pair(derivative[l], derivative[l + 1])),
+                                                 __float2half2_rn(128.0f));
+                    da[l] = __low2float(h);
+                    if (l + 1 < L) da[l + 1] = __high2float(h);
                 }
             } else {
                 __half directh[W];
