@@ -137,7 +137,8 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
 // (a hash-grid layout) and no visibility output: one thread per coordinate over
 // all its levels, its W-half row written as 16-byte stores.  Used for the router
 // grid, whose small tables stay in L1.
-template <int W>
+// KIND: every level's kind when they all share one (compiled out of the corner addressing), else -1.
+template <int W, int KIND>
 __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeArgs a,
                                                                   const __grid_constant__ LevelTable table,
                                                                   const __half* __restrict__ params,
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
                 __half2 t[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    t[k] = load_pair(params, base + d.offset + 2LL * corner_row(d, g, k, a.node_bitmap, a.node_prefix));
+                    t[k] = load_pair(params, base + d.offset + 2LL * corner_row<KIND>(d, g, k, a.node_bitmap, a.node_prefix));
 #pragma unroll
                 for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
             }
@@ -566,8 +567,19 @@ void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const fl
                 2 * a.levels <= a.width;
     for (int l = 0; rows && l < a.levels; ++l) rows = src.table.level[l].F == 2 && src.table.level[l].col == 2 * l;
     if (rows) {
-        if (a.width == 32) encode_forward_rows_kernel<32><<<blocks_for(a.n, 256), 256, 0, stream>>>(a, src.table, table16, out);
-        else encode_forward_rows_kernel<16><<<blocks_for(a.n, 256), 256, 0, stream>>>(a, src.table, table16, out);
+        int kind = src.table.level[0].kind;
+        for (int l = 1; l < a.levels; ++l)
+            if (src.table.level[l].kind != kind) kind = -1;
+        const unsigned blocks = blocks_for(a.n, 256);
+        if (a.width == 32) {
+            if (kind == HASH_DENSE) encode_forward_rows_kernel<32, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            else if (kind == HASH_HASHED) encode_forward_rows_kernel<32, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            else encode_forward_rows_kernel<32, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+        } else {
+            if (kind == HASH_DENSE) encode_forward_rows_kernel<16, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            else if (kind == HASH_HASHED) encode_forward_rows_kernel<16, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            else encode_forward_rows_kernel<16, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+        }
         note_launch();
         return;
     }
