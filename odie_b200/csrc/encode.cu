@@ -137,12 +137,24 @@ __global__ void __launch_bounds__(256) encode_forward_kernel(const EncodeArgs a,
 // (a hash-grid layout) and no visibility output: one thread per coordinate over
 // all its levels, its W-half row written as 16-byte stores.  Used for the router
 // grid, whose small tables stay in L1.
-// KIND: every level's kind when they all share one (compiled out of the corner addressing), else -1.
+// The 4 corner pairs of one level of the row gather, corner addressing compiled for KIND.
+template <int KIND>
+__device__ __forceinline__ void corner_pairs(const EncodeArgs& a, const Level& d, const Corner4& g, long long base,
+                                             const __half* __restrict__ params, __half2 (&t)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        t[k] = load_pair(params, base + d.offset + 2LL * corner_row<KIND>(d, g, k, a.node_bitmap, a.node_prefix));
+}
+
+// KIND: every level's kind when they all share one (compiled out of the corner addressing).
+// KIND = -1 with split >= 0: levels [0, split) are dense and [split, levels) hashed (a hash
+// grid's usual order), each range addressed with its own compiled kind; split < 0: any kinds,
+// read per level.
 template <int W, int KIND>
 __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeArgs a,
                                                                   const __grid_constant__ LevelTable table,
                                                                   const __half* __restrict__ params,
-                                                                  __half* __restrict__ out) {
+                                                                  __half* __restrict__ out, int split) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.n) return;
     const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
@@ -156,9 +168,9 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
             const Corner4 g = geometry(p.x, p.y, d.scale);
             if (level_on(d, g, a.bitmap)) {
                 __half2 t[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    t[k] = load_pair(params, base + d.offset + 2LL * corner_row<KIND>(d, g, k, a.node_bitmap, a.node_prefix));
+                if (KIND >= 0 || split < 0) corner_pairs<KIND>(a, d, g, base, params, t);
+                else if (l < split) corner_pairs<HASH_DENSE>(a, d, g, base, params, t);
+                else corner_pairs<HASH_HASHED>(a, d, g, base, params, t);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
             }
@@ -570,15 +582,20 @@ void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const fl
         int kind = src.table.level[0].kind;
         for (int l = 1; l < a.levels; ++l)
             if (src.table.level[l].kind != kind) kind = -1;
+        // mixed kinds: dense levels first, then hashed ones (split = the first hashed level), else -1
+        int split = 0;
+        while (split < a.levels && src.table.level[split].kind == HASH_DENSE) ++split;
+        for (int l = split; l < a.levels; ++l)
+            if (src.table.level[l].kind != HASH_HASHED) split = -1;
         const unsigned blocks = blocks_for(a.n, 256);
         if (a.width == 32) {
-            if (kind == HASH_DENSE) encode_forward_rows_kernel<32, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
-            else if (kind == HASH_HASHED) encode_forward_rows_kernel<32, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
-            else encode_forward_rows_kernel<32, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            if (kind == HASH_DENSE) encode_forward_rows_kernel<32, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, 0);
+            else if (kind == HASH_HASHED) encode_forward_rows_kernel<32, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, 0);
+            else encode_forward_rows_kernel<32, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, split);
         } else {
-            if (kind == HASH_DENSE) encode_forward_rows_kernel<16, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
-            else if (kind == HASH_HASHED) encode_forward_rows_kernel<16, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
-            else encode_forward_rows_kernel<16, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out);
+            if (kind == HASH_DENSE) encode_forward_rows_kernel<16, HASH_DENSE><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, 0);
+            else if (kind == HASH_HASHED) encode_forward_rows_kernel<16, HASH_HASHED><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, 0);
+            else encode_forward_rows_kernel<16, -1><<<blocks, 256, 0, stream>>>(a, src.table, table16, out, split);
         }
         note_launch();
         return;
