@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
                                                               const __grid_constant__ LevelTable table,
                                                               const __half* __restrict__ upstream,
                                                               float* __restrict__ grad, unsigned skip_levels,
-                                                              uint32_t mask) {
+                                                              uint32_t mask, int split) {
     const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const long long i = visit(warp_id, mask) * 32 + lane;
@@ -317,9 +317,19 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
             if (v[0] == 0.0f && v[1] == 0.0f && v[2] == 0.0f && v[3] == 0.0f && v[4] == 0.0f && v[5] == 0.0f &&
                 v[6] == 0.0f && v[7] == 0.0f)
                 continue;
+            // corner addressing compiled per kind where the level's kind is known: planes (descriptors), or a
+            // hash grid's dense levels [0, split) and hashed levels [split, levels)
             int rows[4];
+            if (FROM_DESC || split < 0) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+                for (int k = 0; k < 4; ++k) rows[k] = corner_row(d, g, k, a.node_bitmap, a.node_prefix);
+            } else if (l < split) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) rows[k] = corner_row<HASH_DENSE>(d, g, k, a.node_bitmap, a.node_prefix);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) rows[k] = corner_row<HASH_HASHED>(d, g, k, a.node_bitmap, a.node_prefix);
+            }
 #pragma unroll
             for (int k = 0; k < 4; ++k) red_add_v2(level_grad + 2LL * rows[k], v[2 * k], v[2 * k + 1]);
             continue;
@@ -655,7 +665,7 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     const long long threads = 32 * (mask ? (long long)mask + 1 : groups);
     if (src.descriptors) {
         encode_backward_kernel<true><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table, upstream,
-                                                                                  grad, 0u, mask);
+                                                                                  grad, 0u, mask, -1);
         note_launch();
         return;
     }
@@ -714,8 +724,13 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     }
     const int active = a.active < a.levels ? a.active : a.levels;
     if (list.count == active) return;  // every level took the shared-memory path
+    // a hash grid's dense levels come first, then its hashed ones: split = the first hashed level, else -1
+    int split = 0;
+    while (split < a.levels && src.table.level[split].kind == HASH_DENSE) ++split;
+    for (int l = split; l < a.levels; ++l)
+        if (src.table.level[l].kind != HASH_HASHED) split = -1;
     encode_backward_kernel<false><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, skip,
-                                                                               mask);
+                                                                               mask, split);
     note_launch();
 }
 
