@@ -461,6 +461,35 @@ def main():
     e2e = world * args.batch * args.steps / (float(e_ms) / 1e3)
     losses = loss_host.numpy()
 
+    # the sampler of a training loop, per step: the reference's stratified_batches (torch RNG and
+    # arithmetic kernels) against the device sampler, and the step with the sampler fused in
+    sampler = None
+    if world == 1 and args.workload != 'c3-experts' and args.sampling == 'stratified':
+        from odie_b200.data import device_stratified_ids, stratified_batches
+        reps = 10
+        s_events = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        batches = stratified_batches(shape, args.batch, torch.Generator(device='cuda').manual_seed(7), steps=2 * reps)
+        next(batches)
+        device_stratified_ids(shape, args.batch, 7, 0)
+        barrier()
+        s_events[0].record()
+        for _ in range(reps):
+            next(batches)
+        s_events[1].record()
+        for k in range(reps):
+            device_stratified_ids(shape, args.batch, 7, k)
+        s_events[2].record()
+        for k in range(args.steps):
+            opt.check(lib.odie_step_stratified(opt.handle, 7, k, args.batch, 1))
+        s_events[3].record()
+        barrier()
+        sampler = {'torch_stratified_ms': s_events[0].elapsed_time(s_events[1]) / reps,
+                   'device_stratified_ms': s_events[1].elapsed_time(s_events[2]) / reps,
+                   'fused_step_ms': s_events[2].elapsed_time(s_events[3]) / args.steps,
+                   'step_ms': ms / args.steps,
+                   'note': 'stratified_batches (odie/data.py:63-80) as the reference runs it each step, vs '
+                           'odie_stratified_ids; odie_step_stratified = odie_step with the sampler fused in'}
+
     # decode of this rank's band (all pixels), Gpix/s
     rgb8 = torch.empty((pixels, 3), dtype=torch.uint8, device='cuda')
     opt.decode(0, pixels, rgb8=rgb8)
@@ -528,6 +557,8 @@ def main():
                 'loss_first_last': [float(losses[0]), float(losses[-1])], 'clocks': clocks.summary()}
         if allocation:
             line['allocation'] = allocation
+        if sampler:
+            line['sampler'] = sampler
         print(json.dumps(line), flush=True)
     opt.close()
     if dist is not None:

@@ -74,6 +74,20 @@ ODIE_API int odie_step_grads(void* handle, uint64_t ids, int n, int update);
 ODIE_API int odie_step_heads(void* handle);
 ODIE_API int odie_grid_update(void* handle);
 
+/* Stratified batches on the device (replaces the reference's per-step sampler,
+ * odie/data.py:63-80, stratified_batches, which draws torch.rand and then
+ * gathers targets in separate kernels): slot j of step `step` takes stratum
+ * (j mod side, j / side), side = sqrt(n), and offsets r = (word >> 8) 2^-24
+ * from a Philox4x32-10 stream (key = seed, counter = (j, step));
+ * uv = r / side + stratum / side in fp32; pixel = trunc(uv (W, H)) clamped;
+ * id = y W + x.  n must be a square power of two, as in the reference.
+ * odie_stratified_ids writes the n int64 ids; odie_step_stratified is
+ * odie_step on the batch of (seed, step), with the sampler fused into the
+ * step's input kernel (ids -> coordinates and targets). */
+ODIE_API int odie_stratified_ids(uint64_t seed, uint64_t step, int width, int height, int64_t n, int64_t* ids,
+                   uint64_t stream);
+ODIE_API int odie_step_stratified(void* handle, uint64_t seed, uint64_t step, int n, int update);
+
 /* Stage timers (no reference counterpart): enable/disable CUDA-event timing of
  * every stage launch on the runtime's stream (resets the record), and a JSON
  * report {stage: {"launches": k, "ms": total}} of what was recorded. */

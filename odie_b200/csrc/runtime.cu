@@ -521,10 +521,18 @@ struct Runtime {
         return o.str();
     }
 
-    void step_grads(const int64_t* ids, int n, int update) {
+    // sampled: the batch is the stratified sampler's (seed, step) instead of the caller's ids
+    struct Sampled {
+        uint64_t seed, step;
+    };
+    void step_grads(const int64_t* ids, int n, int update, const Sampled* sampled = nullptr) {
         ODIE_REQUIRE(n > 0 && n <= capacity, "invalid batch size for this runtime");
         int slot = stage_begin(S_INPUT);
-        launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, xy.ptr, target.ptr, stream);
+        if (sampled)
+            launch_stratified_batch(sampled->seed, sampled->step, n, rgb, rgb8, image_width, image_height, xy.ptr,
+                                    target.ptr, stream);
+        else
+            launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, xy.ptr, target.ptr, stream);
         stage_end(slot);
         LevelSource src;
         src.table = table;
@@ -804,6 +812,22 @@ int odie_step(void* handle, uint64_t ids, int n, int update) {
         auto* r = static_cast<Runtime*>(handle);
         r->step_grads(reinterpret_cast<const int64_t*>(ids), n, update != 0 ? 1 : 0);
         r->step_heads(update != 0);
+    });
+}
+
+int odie_step_stratified(void* handle, uint64_t seed, uint64_t step, int n, int update) {
+    return guarded([&] {
+        auto* r = static_cast<Runtime*>(handle);
+        const odie::Runtime::Sampled sampled{seed, step};
+        r->step_grads(nullptr, n, update != 0 ? 1 : 0, &sampled);
+        r->step_heads(update != 0);
+    });
+}
+
+int odie_stratified_ids(uint64_t seed, uint64_t step, int width, int height, int64_t n, int64_t* ids, uint64_t stream) {
+    return guarded([&] {
+        odie::launch_stratified_ids(seed, step, width, height, n, ids, reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
     });
 }
 

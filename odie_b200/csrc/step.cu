@@ -5,11 +5,9 @@ namespace odie {
 
 namespace {
 
-__global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n, const uint8_t* __restrict__ rgb,
-                                   bool rgb8, int width, int height, float* __restrict__ xy, float* __restrict__ target) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    uint32_t id = uint32_t(ids[i]);
+// Coordinates and target of pixel id for batch slot i.
+__device__ __forceinline__ void input_of(long long i, uint32_t id, const uint8_t* __restrict__ rgb, bool rgb8, int width,
+                                         int height, float* __restrict__ xy, float* __restrict__ target) {
     // an id outside the image (never produced by the samplers) reads pixel 0
     // instead of memory outside the target
     if ((unsigned long long)id >= (unsigned long long)width * (unsigned long long)height) id = 0;
@@ -23,6 +21,64 @@ __global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n,
             target[3 * i + c] = rgb8 ? __fmul_rn(float(rgb[3ull * id + c]), 1.0f / 255.0f)
                                      : reinterpret_cast<const float*>(rgb)[3ull * id + c];
     }
+}
+
+__global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n, const uint8_t* __restrict__ rgb,
+                                   bool rgb8, int width, int height, float* __restrict__ xy, float* __restrict__ target) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    input_of(i, uint32_t(ids[i]), rgb, rgb8, width, height, xy, target);
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011):
+// a counter-based generator, so slot j of step s has its own stream with no state to carry.
+struct Philox4 {
+    uint32_t v[4];
+};
+__device__ __forceinline__ Philox4 philox4x32_10(Philox4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        if (r > 0) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint32_t lo0 = 0xD2511F53u * c.v[0], hi0 = __umulhi(0xD2511F53u, c.v[0]);
+        const uint32_t lo1 = 0xCD9E8D57u * c.v[2], hi1 = __umulhi(0xCD9E8D57u, c.v[2]);
+        c = Philox4{{hi1 ^ c.v[1] ^ k0, lo1, hi0 ^ c.v[3] ^ k1, lo0}};
+    }
+    return c;
+}
+
+// Stratified pixel id of slot j (the reference's sampler, odie/data.py:63-80, with this generator):
+// stratum (j mod side, j / side); uv = r / side + stratum / side in fp32 (side a power of two, so the
+// quotients are exact), r = (philox word >> 8) 2^-24 in [0, 1); pixel = trunc(uv (W, H)) clamped.
+__device__ __forceinline__ uint32_t stratified_id(uint64_t seed, uint64_t step, long long j, int side_log2, int width,
+                                                  int height) {
+    const Philox4 r = philox4x32_10(Philox4{{uint32_t(j), uint32_t(uint64_t(j) >> 32), uint32_t(step),
+                                             uint32_t(step >> 32)}},
+                                    uint32_t(seed), uint32_t(seed >> 32));
+    const float inv = __uint_as_float(uint32_t(127 - side_log2) << 23);  // 2^-side_log2, exact
+    const long long sx = j & ((1LL << side_log2) - 1), sy = j >> side_log2;
+    const float ux = __fadd_rn(__fmul_rn(float(r.v[0] >> 8) * 0x1p-24f, inv), __fmul_rn(float(sx), inv));
+    const float uy = __fadd_rn(__fmul_rn(float(r.v[1] >> 8) * 0x1p-24f, inv), __fmul_rn(float(sy), inv));
+    int x = int(__fmul_rn(ux, float(width))), y = int(__fmul_rn(uy, float(height)));
+    x = x < width - 1 ? x : width - 1;
+    y = y < height - 1 ? y : height - 1;
+    return uint32_t(y) * uint32_t(width) + uint32_t(x);
+}
+
+__global__ void stratified_ids_kernel(uint64_t seed, uint64_t step, int side_log2, int width, int height, long long n,
+                                      int64_t* __restrict__ ids) {
+    const long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) ids[j] = stratified_id(seed, step, j, side_log2, width, height);
+}
+
+// The step's input stage with the sampler fused in: stratified id -> coordinates and target.
+__global__ void stratified_batch_kernel(uint64_t seed, uint64_t step, int side_log2, long long n,
+                                        const uint8_t* __restrict__ rgb, bool rgb8, int width, int height,
+                                        float* __restrict__ xy, float* __restrict__ target) {
+    const long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) input_of(j, stratified_id(seed, step, j, side_log2, width, height), rgb, rgb8, width, height, xy, target);
 }
 
 __global__ void coords_range_kernel(long long begin, long long n, int width, int height, float* __restrict__ xy) {
@@ -132,6 +188,32 @@ void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, boo
                         float* xy, float* target, cudaStream_t stream) {
     if (n <= 0) return;
     input_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(ids, n, rgb, rgb8, width, height, xy, target);
+    note_launch();
+}
+
+// side_log2 of a stratified batch: n must be a square power of two (as the reference's sampler requires).
+static int stratified_side_log2(long long n) {
+    ODIE_REQUIRE(n >= 1 && n <= (1LL << 30) && (n & (n - 1)) == 0,
+                 "stratified sampling requires a square power-of-two batch size");
+    int log2n = 0;
+    while ((1LL << log2n) < n) ++log2n;
+    ODIE_REQUIRE(log2n % 2 == 0, "stratified sampling requires a square power-of-two batch size");
+    return log2n / 2;
+}
+
+void launch_stratified_ids(uint64_t seed, uint64_t step, int width, int height, long long n, int64_t* ids,
+                           cudaStream_t stream) {
+    const int side_log2 = stratified_side_log2(n);
+    ODIE_REQUIRE(width >= 2 && height >= 2, "the image needs at least 2 x 2 pixels");
+    stratified_ids_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(seed, step, side_log2, width, height, n, ids);
+    note_launch();
+}
+
+void launch_stratified_batch(uint64_t seed, uint64_t step, long long n, const uint8_t* rgb, bool rgb8, int width,
+                             int height, float* xy, float* target, cudaStream_t stream) {
+    const int side_log2 = stratified_side_log2(n);
+    stratified_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(seed, step, side_log2, n, rgb, rgb8, width, height,
+                                                                    xy, target);
     note_launch();
 }
 

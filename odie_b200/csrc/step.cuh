@@ -61,6 +61,12 @@ void launch_mlp_tc_decode(const MlpArgs& args, int width, GateMode gate, bool un
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
                         float* xy, float* target, cudaStream_t stream);
 void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream);
+// Stratified pixel ids (the reference's sampler, odie/data.py:63-80, on a Philox4x32-10 stream keyed by
+// seed, counter (slot, step)); n a square power of two.  The batch variant fuses the step's input stage.
+void launch_stratified_ids(uint64_t seed, uint64_t step, int width, int height, long long n, int64_t* ids,
+                           cudaStream_t stream);
+void launch_stratified_batch(uint64_t seed, uint64_t step, long long n, const uint8_t* rgb, bool rgb8, int width,
+                             int height, float* xy, float* target, cudaStream_t stream);
 
 // Sum of the per-block weight-gradient partials in block order (deterministic).
 void launch_reduce_partials(const float* partials, int blocks, int count, float* out, cudaStream_t stream);

@@ -50,6 +50,18 @@ def stratified_batches(shape, batch, generator, device='cuda', steps=None):
         yield xy[:, 1].clamp_(0, height - 1) * width + xy[:, 0].clamp_(0, width - 1)
 
 
+def device_stratified_ids(shape, batch, seed, step, stream=None):
+    """The stratified batch of (seed, step) drawn on the GPU (odie_stratified_ids): the strata of
+    stratified_batches with a Philox4x32-10 stream instead of torch's generator; int64 CUDA tensor."""
+    from . import _lib
+    height, width = shape
+    ids = torch.empty(batch, dtype=torch.int64, device='cuda')
+    stream = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(_lib.library().odie_stratified_ids(int(seed), int(step), width, height, batch, ids.data_ptr(),
+                                                   stream.cuda_stream), 'odie_stratified_ids')
+    return ids
+
+
 def uniform_ids(shape, batch, generator, device='cuda'):
     """Uniform pixel ids in [0, H*W) (the benchmark configs' uniform coordinates)."""
     return torch.randint(0, shape[0] * shape[1], (batch,), device=device, generator=generator)

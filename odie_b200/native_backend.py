@@ -112,6 +112,12 @@ class NativeOptimizer:
         with self.on_stream():
             self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), int(update)))
 
+    def step_stratified(self, seed, step, n, update=True):
+        """One step on the stratified batch (seed, step) drawn on the device (odie_step_stratified): the
+        reference's stratified_batches (odie/data.py:63-80) fused into the step's input kernel."""
+        with self.on_stream():
+            self.check(self.lib.odie_step_stratified(self.handle, int(seed), int(step), int(n), int(update)))
+
     def copied(self, name, shape, dtype):
         with self.on_stream():
             result = torch.empty(shape, device='cuda', dtype=dtype)

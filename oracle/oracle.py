@@ -443,3 +443,43 @@ def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, expe
                 grid_grad=expert_backward(xy, values, expert, expert_stride, records, tables.size, bitmap),
                 router_grid_grad=hash_backward(xy, router_values, router_records, router_table.size),
                 head_grad=np.concatenate([g.reshape(-1) for g in head]))
+
+
+# ---------------------------------------------------------------- stratified sampler (device variant)
+def philox4x32_10(counter, key):
+    """Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC 2011) on uint32 arrays: counter [4][...], key [2][...]."""
+    c = [np.asarray(x, dtype=np.uint64) & 0xFFFFFFFF for x in counter]
+    k0, k1 = (np.asarray(x, dtype=np.uint64) & 0xFFFFFFFF for x in key)
+    mask = np.uint64(0xFFFFFFFF)
+    for r in range(10):
+        if r:
+            k0 = (k0 + np.uint64(0x9E3779B9)) & mask
+            k1 = (k1 + np.uint64(0xBB67AE85)) & mask
+        p0 = c[0] * np.uint64(0xD2511F53)
+        p1 = c[2] * np.uint64(0xCD9E8D57)
+        hi0, lo0 = p0 >> np.uint64(32), p0 & mask
+        hi1, lo1 = p1 >> np.uint64(32), p1 & mask
+        c = [hi1 ^ c[1] ^ k0, lo1, hi0 ^ c[3] ^ k1, lo0]
+    return [x.astype(np.uint32) for x in c]
+
+
+def stratified_ids(seed, step, width, height, n):
+    """The device stratified sampler (odie_stratified_ids) restated: slot j takes stratum (j mod side, j / side),
+    r = (philox word >> 8) 2^-24 with key = seed, counter = (j, step); uv = r / side + stratum / side in fp32;
+    pixel = trunc(uv (W, H)) clamped -- the form of the reference's stratified_batches (odie/data.py:63-80)."""
+    side = int(round(n ** 0.5))
+    assert side * side == n and n & (n - 1) == 0
+    j = np.arange(n, dtype=np.uint64)
+    words = philox4x32_10([j & 0xFFFFFFFF, j >> np.uint64(32), np.full(n, step & 0xFFFFFFFF, np.uint64),
+                           np.full(n, step >> 32, np.uint64)],
+                          [np.full(n, seed & 0xFFFFFFFF, np.uint64), np.full(n, seed >> 32, np.uint64)])
+    inv = np.float32(1.0 / side)  # a power of two: exact
+    r0 = (words[0] >> np.uint32(8)).astype(np.float32) * np.float32(2.0 ** -24)
+    r1 = (words[1] >> np.uint32(8)).astype(np.float32) * np.float32(2.0 ** -24)
+    sx = (j % np.uint64(side)).astype(np.float32)
+    sy = (j // np.uint64(side)).astype(np.float32)
+    ux = r0 * inv + sx * inv
+    uy = r1 * inv + sy * inv
+    x = np.minimum((ux * np.float32(width)).astype(np.int64), width - 1)
+    y = np.minimum((uy * np.float32(height)).astype(np.int64), height - 1)
+    return y * width + x

@@ -246,3 +246,19 @@ def test_oracle_allocation_bitmap_hand_case():
     assert np.array_equal(oracle.allocation_bitmap(tiles, 2, 4, 4, 3), np.array([1, 0], dtype=np.uint8))
     assert np.array_equal(oracle.allocation_bitmap(np.ones((2, 2), np.uint8), 2, 4, 4, 3),
                           np.array([255, 1], dtype=np.uint8))
+
+
+def test_stratified_sampler_restatement_properties():
+    """The device sampler's restatement: ids inside the image, one per stratum, offsets spread over the strata."""
+    shape, n = (1356, 2040), 1 << 14
+    side = 128
+    ids = oracle.stratified_ids(5, 9, shape[1], shape[0], n)
+    assert ids.min() >= 0 and ids.max() < shape[0] * shape[1]
+    j = np.arange(n)
+    x, y = ids % shape[1], ids // shape[1]
+    fx = (x + 0.5) * side / shape[1] - j % side
+    fy = (y + 0.5) * side / shape[0] - j // side
+    assert np.all((fx > -0.1) & (fx < 1.1)) and np.all((fy > -0.1) & (fy < 1.1))
+    assert abs(fx.mean() - 0.5) < 0.02 and abs(fy.mean() - 0.5) < 0.02
+    assert np.array_equal(ids, oracle.stratified_ids(5, 9, shape[1], shape[0], n))
+    assert not np.array_equal(ids, oracle.stratified_ids(5, 10, shape[1], shape[0], n))
