@@ -626,15 +626,12 @@ struct Runtime {
         const int slot = stage_begin(S_ADAM_HEADS);
         // head gradients carry the 128 x 128 loss scale (odie/native/runtime.cu:59,300-309)
         const float inv = 1.0f / 16384.0f;
-        if (gate_count) {
-            AdamTables t{table_step[1].ptr, table_bc2.ptr, TABLE_STEPS};
-            launch_adam(gate_master, head_half.ptr, head_m.ptr, head_v.ptr, head_steps.ptr, head_grad(), gate_count, inv,
-                        t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
-        }
-        AdamTables t{table_step[2].ptr, table_bc2.ptr, TABLE_STEPS};
-        launch_adam(decoder_master, head_half.ptr + gate_count, head_m.ptr + gate_count, head_v.ptr + gate_count,
-                    head_steps.ptr + gate_count, head_grad() + gate_count, decoder_count, inv, t, float(1.0 - BETA1),
-                    float(BETA2), float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
+        // gate (or router) and decoder in one launch, each with its own master array and learning rate
+        const AdamTables gate_t{table_step[1].ptr, table_bc2.ptr, TABLE_STEPS};
+        const AdamTables decoder_t{table_step[2].ptr, table_bc2.ptr, TABLE_STEPS};
+        launch_adam2(gate_master, decoder_master, head_half.ptr, head_m.ptr, head_v.ptr, head_steps.ptr, head_grad(),
+                     gate_count, decoder_count, inv, gate_t, decoder_t, float(1.0 - BETA1), float(BETA2),
+                     float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
         stage_end(slot);
         ODIE_CUDA(cudaGetLastError());
     }

@@ -125,22 +125,31 @@ __device__ __forceinline__ void adam_update(float& p, float& m, float& v, float 
     p = __fadd_rn(p, __fdiv_rn(__fmul_rn(-step_size, m), denom));
 }
 
-// Four parameters per thread (16-byte vectors) when every array is 16-byte
-// aligned; one per thread otherwise.
+// One Adam segment: parameters, fp16 copy, moments, per-parameter steps, gradient, learning-rate table.
+struct AdamSegment {
+    float* master;
+    __half* copy;
+    float* m;
+    float* v;
+    uint32_t* steps;
+    float* grad;
+    long long count;
+    const float* step_size;
+};
+
+// Quad q (VEC: parameters 4q..4q+3) or parameter q of a segment.
 template <bool VEC>
-__global__ void adam_kernel(float* __restrict__ master, __half* __restrict__ copy, float* __restrict__ m,
-                            float* __restrict__ v, uint32_t* __restrict__ steps, float* __restrict__ grad,
-                            long long count, float inv_scale, const float* __restrict__ step_size,
-                            const float* __restrict__ bc2_sqrt, long long table, float beta1w, float beta2,
-                            float beta2w, float eps, bool skip_zero, int* error_flag) {
-    const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void adam_at(const AdamSegment& a, long long q, float inv_scale, const float* __restrict__ bc2_sqrt,
+                                        long long table, float beta1w, float beta2, float beta2w, float eps,
+                                        bool skip_zero, int* error_flag) {
+    const long long count = a.count;
     if (VEC && (q + 1) * 4 <= count) {
-        float4 g4 = reinterpret_cast<float4*>(grad)[q];
+        float4 g4 = reinterpret_cast<float4*>(a.grad)[q];
         if (skip_zero && g4.x == 0.0f && g4.y == 0.0f && g4.z == 0.0f && g4.w == 0.0f) return;
-        float4 p4 = reinterpret_cast<float4*>(master)[q];
-        float4 m4 = reinterpret_cast<float4*>(m)[q];
-        float4 v4 = reinterpret_cast<float4*>(v)[q];
-        uint4 s4 = reinterpret_cast<uint4*>(steps)[q];
+        float4 p4 = reinterpret_cast<float4*>(a.master)[q];
+        float4 m4 = reinterpret_cast<float4*>(a.m)[q];
+        float4 v4 = reinterpret_cast<float4*>(a.v)[q];
+        uint4 s4 = reinterpret_cast<uint4*>(a.steps)[q];
         float* gp = &g4.x; float* pp = &p4.x; float* mp = &m4.x; float* vp = &v4.x; uint32_t* sp = &s4.x;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -148,29 +157,41 @@ __global__ void adam_kernel(float* __restrict__ master, __half* __restrict__ cop
             if (skip_zero && gj == 0.0f) continue;
             const uint32_t s = ++sp[j];
             if ((long long)s > table) { atomicExch(error_flag, 1); continue; }
-            adam_update(pp[j], mp[j], vp[j], gj, step_size[s - 1], bc2_sqrt[s - 1], beta1w, beta2, beta2w, eps);
+            adam_update(pp[j], mp[j], vp[j], gj, a.step_size[s - 1], bc2_sqrt[s - 1], beta1w, beta2, beta2w, eps);
         }
-        reinterpret_cast<float4*>(master)[q] = p4;
-        reinterpret_cast<float4*>(m)[q] = m4;
-        reinterpret_cast<float4*>(v)[q] = v4;
-        reinterpret_cast<uint4*>(steps)[q] = s4;
-        reinterpret_cast<float4*>(grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-        __half2* ch = reinterpret_cast<__half2*>(copy + 4 * q);
+        reinterpret_cast<float4*>(a.master)[q] = p4;
+        reinterpret_cast<float4*>(a.m)[q] = m4;
+        reinterpret_cast<float4*>(a.v)[q] = v4;
+        reinterpret_cast<uint4*>(a.steps)[q] = s4;
+        reinterpret_cast<float4*>(a.grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        __half2* ch = reinterpret_cast<__half2*>(a.copy + 4 * q);
         ch[0] = __floats2half2_rn(p4.x, p4.y);
         ch[1] = __floats2half2_rn(p4.z, p4.w);
         return;
     }
     const long long first = VEC ? 4 * q : q, last = VEC ? (4 * q + 4 < count ? 4 * q + 4 : count) : (q < count ? q + 1 : q);
     for (long long i = first; i < last; ++i) {
-        const float gj = __fmul_rn(grad[i], inv_scale);
+        const float gj = __fmul_rn(a.grad[i], inv_scale);
         if (skip_zero && gj == 0.0f) continue;
-        const uint32_t s = ++steps[i];
+        const uint32_t s = ++a.steps[i];
         if ((long long)s > table) { atomicExch(error_flag, 1); continue; }
-        float p = master[i], mi = m[i], vi = v[i];
-        adam_update(p, mi, vi, gj, step_size[s - 1], bc2_sqrt[s - 1], beta1w, beta2, beta2w, eps);
-        master[i] = p; m[i] = mi; v[i] = vi; grad[i] = 0.0f;
-        copy[i] = __float2half_rn(p);
+        float p = a.master[i], mi = a.m[i], vi = a.v[i];
+        adam_update(p, mi, vi, gj, a.step_size[s - 1], bc2_sqrt[s - 1], beta1w, beta2, beta2w, eps);
+        a.master[i] = p; a.m[i] = mi; a.v[i] = vi; a.grad[i] = 0.0f;
+        a.copy[i] = __float2half_rn(p);
     }
+}
+
+// Four parameters per thread (16-byte vectors) when every array is 16-byte
+// aligned; one per thread otherwise.  Blocks [0, blocks0) update segment s0, the rest s1
+// (s1.count == 0: one segment).
+template <bool VEC>
+__global__ void adam_kernel(const AdamSegment s0, const AdamSegment s1, long long blocks0, float inv_scale,
+                            const float* __restrict__ bc2_sqrt, long long table, float beta1w, float beta2,
+                            float beta2w, float eps, bool skip_zero, int* error_flag) {
+    const bool second = blockIdx.x >= blocks0;
+    const long long q = (long long)(blockIdx.x - (second ? blocks0 : 0)) * blockDim.x + threadIdx.x;
+    adam_at<VEC>(second ? s1 : s0, q, inv_scale, bc2_sqrt, table, beta1w, beta2, beta2w, eps, skip_zero, error_flag);
 }
 
 __global__ void zero_kernel(float* p, long long count) {
@@ -230,24 +251,54 @@ void launch_reduce_partials(const float* partials, int blocks, int count, float*
     note_launch();
 }
 
+static bool adam_vec(const AdamSegment& a) {
+    auto aligned = [](const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; };
+    return aligned(a.master, 16) && aligned(a.m, 16) && aligned(a.v, 16) && aligned(a.steps, 16) && aligned(a.grad, 16) &&
+           aligned(a.copy, 8);
+}
+
+static void launch_adam_segments(const AdamSegment& s0, const AdamSegment& s1, float inv_scale, const float* bc2_sqrt,
+                                 long long table, float beta1w, float beta2, float beta2w, float eps, bool skip_zero,
+                                 int* error_flag, cudaStream_t stream) {
+    const bool vec = adam_vec(s0) && (s1.count == 0 || adam_vec(s1));
+    const long long per = vec ? 4 : 1;
+    const long long b0 = blocks_for((s0.count + per - 1) / per, 256), b1 = blocks_for((s1.count + per - 1) / per, 256);
+    if (b0 + b1 == 0) return;
+    if (vec)
+        adam_kernel<true><<<unsigned(b0 + b1), 256, 0, stream>>>(s0, s1, b0, inv_scale, bc2_sqrt, table, beta1w, beta2,
+                                                                 beta2w, eps, skip_zero, error_flag);
+    else
+        adam_kernel<false><<<unsigned(b0 + b1), 256, 0, stream>>>(s0, s1, b0, inv_scale, bc2_sqrt, table, beta1w, beta2,
+                                                                  beta2w, eps, skip_zero, error_flag);
+    note_launch();
+}
+
 void launch_adam(float* master, __half* copy, float* m, float* v, uint32_t* steps, float* grad, long long count,
                  float inv_scale, AdamTables tables, float beta1w, float beta2, float beta2w, float eps, bool skip_zero,
                  int* error_flag, cudaStream_t stream) {
     if (count <= 0) return;
-    auto aligned = [](const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; };
-    const bool vec = aligned(master, 16) && aligned(m, 16) && aligned(v, 16) && aligned(steps, 16) &&
-                     aligned(grad, 16) && aligned(copy, 8);
-    if (vec) {
-        const long long quads = (count + 3) / 4;
-        adam_kernel<true><<<blocks_for(quads, 256), 256, 0, stream>>>(
-            master, copy, m, v, steps, grad, count, inv_scale, tables.step_size, tables.bc2_sqrt, tables.size, beta1w,
-            beta2, beta2w, eps, skip_zero, error_flag);
-    } else {
-        adam_kernel<false><<<blocks_for(count, 256), 256, 0, stream>>>(
-            master, copy, m, v, steps, grad, count, inv_scale, tables.step_size, tables.bc2_sqrt, tables.size, beta1w,
-            beta2, beta2w, eps, skip_zero, error_flag);
+    const AdamSegment s0{master, copy, m, v, steps, grad, count, tables.step_size};
+    const AdamSegment none{master, copy, m, v, steps, grad, 0, tables.step_size};
+    launch_adam_segments(s0, none, inv_scale, tables.bc2_sqrt, tables.size, beta1w, beta2, beta2w, eps, skip_zero,
+                         error_flag, stream);
+}
+
+void launch_adam2(float* master0, float* master1, __half* copy, float* m, float* v, uint32_t* steps, float* grad,
+                  long long count0, long long count1, float inv_scale, AdamTables tables0, AdamTables tables1,
+                  float beta1w, float beta2, float beta2w, float eps, bool skip_zero, int* error_flag,
+                  cudaStream_t stream) {
+    ODIE_REQUIRE(tables0.bc2_sqrt == tables1.bc2_sqrt && tables0.size == tables1.size,
+                 "the two segments share their bias-correction table");
+    const AdamSegment s0{master0, copy, m, v, steps, grad, count0, tables0.step_size};
+    const AdamSegment s1{master1, copy + count0, m + count0, v + count0, steps + count0, grad + count0, count1,
+                         tables1.step_size};
+    if (count0 <= 0) {
+        launch_adam_segments(s1, AdamSegment{master1, copy, m, v, steps, grad, 0, tables1.step_size}, inv_scale,
+                             tables1.bc2_sqrt, tables1.size, beta1w, beta2, beta2w, eps, skip_zero, error_flag, stream);
+        return;
     }
-    note_launch();
+    launch_adam_segments(s0, s1, inv_scale, tables0.bc2_sqrt, tables0.size, beta1w, beta2, beta2w, eps, skip_zero,
+                         error_flag, stream);
 }
 
 void launch_zero(float* p, long long count, cudaStream_t stream) {

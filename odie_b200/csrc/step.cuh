@@ -85,6 +85,12 @@ struct AdamTables {
 void launch_adam(float* master, __half* copy, float* m, float* v, uint32_t* steps, float* grad, long long count,
                  float inv_scale, AdamTables tables, float beta1w, float beta2, float beta2w, float eps, bool skip_zero,
                  int* error_flag, cudaStream_t stream);
+// Two parameter groups with their own masters and learning-rate tables, one launch: group 1's copy,
+// moments, steps and gradient follow group 0's in the same arrays (the heads: gate, then decoder).
+void launch_adam2(float* master0, float* master1, __half* copy, float* m, float* v, uint32_t* steps, float* grad,
+                  long long count0, long long count1, float inv_scale, AdamTables tables0, AdamTables tables1,
+                  float beta1w, float beta2, float beta2w, float eps, bool skip_zero, int* error_flag,
+                  cudaStream_t stream);
 void launch_zero(float* p, long long count, cudaStream_t stream);
 void launch_cast_half(const float* in, __half* out, long long count, cudaStream_t stream);
 
