@@ -45,10 +45,17 @@ def test_ids_reject_non_square_batches(cuda):
             device_stratified_ids((64, 64), n, 1, 1)
 
 
-def test_fused_step_input_matches_step_on_the_same_ids(cuda):
-    config, model, rgb, opt = setup(experts=4, batch=1024)
+@pytest.mark.parametrize('model_kind', ['experts', 'planes'])
+def test_fused_step_input_matches_step_on_the_same_ids(cuda, model_kind):
+    if model_kind == 'experts':
+        config, model, rgb, opt = setup(experts=4, batch=1024)
+        shape = SHAPE
+    else:
+        from tests import test_gpu_step
+        config, model, rgb, opt = test_gpu_step.setup(batch=1024)[:4]
+        shape = test_gpu_step.SHAPE
     n = 1024
-    ids = device_stratified_ids(SHAPE, n, 99, 5)
+    ids = device_stratified_ids(shape, n, 99, 5)
     opt.check(opt.lib.odie_step(opt.handle, ids.data_ptr(), n, 0))  # update 0: weights stay as they are
     torch.cuda.synchronize()
     plain = [opt.copied(name, shape, torch.float32).cpu().numpy() for name, shape in
