@@ -437,11 +437,26 @@ def main():
     host_ids = ids[args.warmup:].cpu().pin_memory()
     device_ids = [torch.empty(args.batch, dtype=torch.int64, device='cuda') for _ in range(2)]
     loss_host = torch.empty(args.steps, dtype=torch.float64).pin_memory()
-    # the runtime's per-sample squared errors, viewed in place (no copy): the loss is their fp64 mean
+    # the runtime's per-sample squared errors, viewed in place: the loss is their fp64 mean.  Each step's
+    # errors are copied (4 MB, device to device) on a loss stream, and the next step waits only for that
+    # copy; the reduction and the 8-byte read to the host run beside the next step.
     squares = torch.as_tensor(DeviceArray(opt.pointers['squares'], args.batch, '<f4'), device='cuda')
-    main_stream, copy_stream = torch.cuda.current_stream(), torch.cuda.Stream()
+    main_stream, copy_stream, loss_stream = torch.cuda.current_stream(), torch.cuda.Stream(), torch.cuda.Stream()
     uploaded = [torch.cuda.Event() for _ in range(2)]
     released = [torch.cuda.Event() for _ in range(2)]
+    stepped = [torch.cuda.Event() for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    snapshots = [torch.empty(args.batch, device='cuda') for _ in range(2)]
+
+    def read_loss(k):
+        buf = k % 2
+        stepped[buf].record(main_stream)
+        with torch.cuda.stream(loss_stream):
+            loss_stream.wait_event(stepped[buf])
+            snapshots[buf].copy_(squares)
+            copied[buf].record(loss_stream)
+            loss_host[k:k + 1].copy_((snapshots[buf].sum(dtype=torch.float64) / args.batch).reshape(1),
+                                     non_blocking=True)
 
     def upload(k):
         buf = k % 2
@@ -452,7 +467,7 @@ def main():
             uploaded[buf].record(copy_stream)
 
     # warm-up of the loop's own operations (the loss read's torch kernels load lazily on first use)
-    loss_host[:1].copy_((squares.sum(dtype=torch.float64) / args.batch).reshape(1), non_blocking=True)
+    read_loss(0)
     upload(0)
     barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -464,9 +479,12 @@ def main():
         if k + 1 < args.steps:
             upload(k + 1)
         main_stream.wait_event(uploaded[buf])
+        if k >= 1:
+            main_stream.wait_event(copied[(k - 1) % 2])  # step k - 1's errors are copied out
         step(device_ids[buf])
         released[buf].record(main_stream)
-        loss_host[k:k + 1].copy_((squares.sum(dtype=torch.float64) / args.batch).reshape(1), non_blocking=True)
+        read_loss(k)
+    main_stream.wait_stream(loss_stream)  # the last loss has reached the host buffer
     e_end.record()
     barrier()
     e_ms = torch.tensor([e_start.elapsed_time(e_end)], device='cuda')
