@@ -2,7 +2,7 @@
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2-experts|c2-planes]
 
-Workloads (odie_b200/workloads.py): c2-experts is BASELINE config 2 (16 routed
+Workloads (odie_b200/workloads.py): c2-experts is the routed-expert benchmark (16 routed
 hash-grid experts, top-1 router on a coarse shared grid, shared 64-wide head,
 2040 x 1356 u8 image, 2^20 coords per step); c2-planes is the reference's own
 packed-plane method on the same image and batch.
@@ -305,7 +305,7 @@ def run_reference(args):
 
 
 def allocate(args, lib, opt, model, target, shape):
-    """BASELINE config 3's allocation stage on the current model: decode every pixel, the fp64 residual of every
+    """The on-demand allocation stage on the current model: decode every pixel, the fp64 residual of every
     256 x 256 tile, the exact top 30 %, and the expert levels restricted to the chosen tiles' cells.  Timed with CUDA
     events; returns the tile mask and the timings."""
     import json as _json

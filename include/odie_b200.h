@@ -155,7 +155,7 @@ ODIE_API int selection_chunk(const double* scores, int n, int points, int resolu
                     int chunk, int64_t* stats, int* trace, uint64_t stream);
 
 /* ------------------------------------------------------------------------
- * Routed multi-expert encoding (no reference counterpart).
+ * Routed multi-expert encoding (16 routed experts in the benchmark; no reference counterpart).
  * odie_router_forward: features f16[n][width] (width 16 or 32, row-major),
  * weights f16 [32*width | 32*32 | 16*32] (router W1, W2, W3, row-major
  * [out][in]); writes expert i32[n] (first maximum of the fp16 logits over
@@ -194,7 +194,7 @@ ODIE_API int odie_plane_index(const uint8_t* support, int resolution, uint64_t* 
                    uint8_t* cell_bitmap, int64_t* node_count, int64_t* nodes, int32_t* scratch, uint64_t stream);
 
 /* ------------------------------------------------------------------------
- * On-demand allocation of routed experts (no reference
+ * On-demand allocation of routed experts (the allocation benchmark; no reference
  * counterpart): the cell-visibility bitmap of one hash level (resolution R,
  * ceil(R^2 / 8) bytes, LSB-first) from an allocated-tile mask tiles
  * u8[tiles_y][tiles_x] of tile_px x tile_px tiles over a height x width image:
@@ -216,7 +216,7 @@ ODIE_API int odie_l2_probe(float* table, int64_t table_bytes, int mode, int64_t 
                    uint64_t stream);
 
 /* ------------------------------------------------------------------------
- * Tile top-k allocation (no reference counterpart).
+ * Tile top-k allocation (the allocation benchmark; no reference counterpart).
  * prediction f32[H*W][3], target u8[H*W][3]; row_sums f64[tiles*tile] scratch;
  * scores f64[tiles]; chosen i64[k] (tile ids by rank); selected u8[tiles].
  * ------------------------------------------------------------------------ */

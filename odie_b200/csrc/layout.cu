@@ -131,7 +131,7 @@ __global__ void closure_nodes_kernel(const unsigned long long* __restrict__ word
     nodes[prefix[n >> 6] + __popcll(word & ((1ull << bit) - 1))] = n;
 }
 
-// On-demand allocation of routed experts (no reference
+// On-demand allocation of routed experts (the allocation benchmark; no reference
 // counterpart): cell (ix, iy) of a level of resolution res is visible iff the
 // pixel nearest its centre -- column floor(ix (width - 1) / (res - 1) + 1/2),
 // computed exactly in integers, row likewise -- lies in an allocated

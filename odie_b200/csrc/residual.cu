@@ -8,7 +8,7 @@
 // and a fixed order make the totals bit-identical to the CPU reference
 // (odie/selection.py:58-73).
 //
-// Tile scores (no reference counterpart): per tile of
+// Tile scores (the allocation benchmark, no reference counterpart): per tile of
 // tile x tile pixels, fp64 row sums in raster order, then the fp64 sum of the
 // row sums in row order; then an exact top-k by (score desc, tile id asc).
 #include <mutex>

@@ -399,7 +399,7 @@ class HashGrid(nn.Module):
 
 
 class RoutedExperts(nn.Module):
-    """Routed multi-expert hash-grid encoding with a shared decoder (no reference counterpart).
+    """Routed multi-expert hash-grid encoding with a shared decoder (16 routed experts in the benchmark; no reference counterpart).
 
     A coarse shared hash grid (``router_encoding``) feeds the router MLP
     (W -> 32 -> 32 -> 16 logits, top-1 over ``experts``); coordinate i is then
@@ -441,7 +441,7 @@ class RoutedExperts(nn.Module):
 
     @torch.no_grad()
     def set_allocation(self, tiles, tile_px, shape, dense_resolution=None):
-        """On-demand allocation: restrict the expert levels finer than dense_resolution to the
+        """On-demand allocation (the allocation benchmark): restrict the expert levels finer than dense_resolution to the
         cells whose centre pixel lies in an allocated tile.  tiles: CUDA uint8/bool [tiles_y, tiles_x] (e.g. the top-k
         of odie_tile_topk); shape: (height, width) of the image.  Default dense_resolution: cells no smaller than
         half a tile stay dense.  Hidden cells give zero features and receive no gradient."""

@@ -1,7 +1,7 @@
 """Benchmark workloads: seeded synthetic images plus the model layouts they train.
 
 c2-planes: the reference's own method (packed multiresolution planes with a
-per-level sigmoid router, odie/model.py) at BASELINE config 2's image shape
+per-level sigmoid router, odie/model.py) at the routed-expert benchmark's image shape
 (2040 x 1356 u8, blobs + gratings + 1/f^2 noise) and batch (2^20 coords).  The
 layout is the reference's DIV2K plan (odie/config.py:resolve at this image
 class; resolutions 8..1020, 13 full-cover levels, 3 on-demand levels with
@@ -9,14 +9,14 @@ caps 181112/181112/181120, results/div2k_50/0028/odie/metrics.json), with the
 on-demand supports chosen as the top cells of a seeded smooth residual field,
 trimmed to their node caps.
 
-c2-experts: BASELINE config 2 itself -- 16 routed experts, each with its own
+c2-experts: the routed-expert benchmark itself -- 16 routed experts, each with its own
 hash grid (L=16, F=2, T=2^16, base resolution 16, per-level scale 1.5, tables
 U(-1e-4, 1e-4)), a top-1 router (W -> 32 -> 32 -> 16) over a coarse shared grid
 (L=16, F=2, T=2^12, base 4, scale 1.2: resolutions 4..62, all dense, tables
 U(-0.1, 0.1) so that the initial routing already splits the image), and the
 shared 64-wide decoder, on the same 2040 x 1356 image with 2^20 coords.
 
-c3-experts: BASELINE config 3, the on-demand allocation path -- a 4096 x 4096
+c3-experts: the on-demand allocation benchmark -- a 4096 x 4096
 image (1/f^2 noise + 200 sharp polygons), 8 routed experts with T = 2^17, the
 residual of every 256 x 256 tile of the current model's decode, the top 30 %
 tiles allocated (the fine expert levels restricted to their cells), and 2^21
@@ -130,7 +130,7 @@ C3_TILE = 256
 
 
 def c3_experts(seed=1729, batch=1 << 21, band=(0, 1), device='cuda'):
-    """(config, rgb u8 [H*W, 3] on CPU, shape) of BASELINE config 3 for rank band[0] of band[1]."""
+    """(config, rgb u8 [H*W, 3] on CPU, shape) of the allocation benchmark for rank band[0] of band[1]."""
     rgb, shape = synthetic_image('c3', seed=seed, device=device)
     rgb, shape = band_of(rgb.cpu(), shape, band)
     encoding = dict(EXPERT_ENCODING, log2_hashmap_size=17)

@@ -7,7 +7,7 @@ TCNN, odie/optimizer.py:54-89), so its native step (odie/native/runtime.cu:
 of the fp16-rounded corner values, autograd's index_add scatter, F.linear heads
 with fp16 activations, the L2 loss with the reference's 128 x 128 loss scaling
 and torch.optim.Adam (betas 0.9/0.999, eps 1e-15).  CpuExpertStep restates the
-routed multi-expert step (BASELINE config 2) the same way.  Both run on all the
+routed multi-expert step the same way.  Both run on all the
 host threads torch is given.
 """
 import time

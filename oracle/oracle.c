@@ -536,7 +536,7 @@ int64_t oracle_select_mean_rank(const double* scores, int resolution, int64_t ca
 }
 
 /* ------------------------------------------------------------------ tiles */
-/* Tile top-k selection (no reference counterpart).
+/* Tile top-k selection (the allocation benchmark; no reference counterpart).
  * Per-tile residual: per tile row, the fp64 sum in raster order of the
  * per-pixel (fp64(d0^2)+fp64(d1^2))+fp64(d2^2))/3 with fp32 d = pred - u8/255
  * (the a17 pixel rule); then the fp64 sum of the row sums in row order (rows
@@ -576,7 +576,7 @@ void oracle_topk(const double* scores, int64_t count, int64_t k, int64_t* chosen
 }
 
 /* ------------------------------------------------------------------ router */
-/* Top-1 expert router (no reference counterpart).
+/* Top-1 expert router (16 routed experts in the benchmark; no reference counterpart).
  * Input fp16 features [n x in_width]; weights fp16 row-major [out][in];
  * each layer: fp32 accumulation in ascending input order with fmaf, ReLU on
  * hidden layers, fp16 rounding of every layer's output.  Expert = argmax of the
@@ -614,7 +614,7 @@ void oracle_router(const uint16_t* x, int64_t n, int in_width, const uint16_t* w
     }
 }
 
-/* ------------------------------------------------------------------ on-demand allocation */
+/* ------------------------------------------------------------------ on-demand allocation (the allocation benchmark) */
 /* Per-level cell visibility from a tile mask (no reference counterpart): cell (ix, iy) of a level
  * of resolution res is visible iff the pixel nearest its centre, column
  * floor(ix * (width - 1) / (res - 1) + 0.5) (exact in int64), row likewise, lies in an allocated

@@ -364,7 +364,7 @@ def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, l
     return result
 
 
-# ---------------------------------------------------------------- routed experts (BASELINE config 2)
+# ---------------------------------------------------------------- routed experts
 ROUTER_SHAPES = lambda width: [(32, width), (32, 32), (16, 32)]  # noqa: E731  router W1, W2, W3
 
 

@@ -1,4 +1,4 @@
-"""GPU parity of the on-demand allocation of routed experts.
+"""GPU parity of the on-demand allocation of routed experts (the allocation benchmark).
 
 Tile residuals and the top-k tile selection are bit-exact (tests/test_gpu_selection.py);
 here: the per-level cell-visibility bitmaps built from the allocated tiles, the

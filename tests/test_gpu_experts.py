@@ -1,4 +1,4 @@
-"""GPU parity of the routed multi-expert path (BASELINE config 2) through the C-ABI.
+"""GPU parity of the routed multi-expert path through the C-ABI.
 
 Routing decisions, hash indices and encoded features are bit-exact against the
 CPU oracle; the router probability within 1e-5 (fp32: CUDA's expf may differ
