@@ -215,6 +215,13 @@ ODIE_API int odie_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles
 ODIE_API int odie_l2_probe(float* table, int64_t table_bytes, int mode, int64_t operations, float* sink,
                    uint64_t stream);
 
+/* Failure-detection check (no reference counterpart): one block waits on an
+ * mbarrier that nothing completes, with the bounded wait the fused heads
+ * kernel uses, giving up after `limit` polls (1..2^20).  *status (device
+ * int32) = 2 when the wait ran out -- the code the heads kernel leaves in
+ * its error flag -- and 0 if it completed.  The context stays usable. */
+ODIE_API int odie_wait_probe(uint32_t limit, int32_t* status, uint64_t stream);
+
 /* ------------------------------------------------------------------------
  * Tile top-k allocation (the allocation benchmark; no reference counterpart).
  * prediction f32[H*W][3], target u8[H*W][3]; row_sums f64[tiles*tile] scratch;

@@ -28,6 +28,7 @@ SIGNATURES = {
     'odie_step_grads': (I32, [P, U64, I32, I32]),
     'odie_step_stratified': (I32, [P, U64, U64, I32, I32]),
     'odie_stratified_ids': (I32, [U64, U64, I32, I32, I64, P, U64]),
+    'odie_wait_probe': (I32, [C.c_uint32, P, U64]),
     'odie_step_heads': (I32, [P]),
     'odie_grid_update': (I32, [P]),
     'odie_profile': (I32, [P, I32]),

@@ -8,6 +8,7 @@
 // drawing its indices from a hash of its id (no index traffic).  One launch per
 // mode; the caller times it with CUDA events.
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace odie {
 
@@ -44,7 +45,28 @@ __global__ void __launch_bounds__(256) l2_probe_kernel(float* table, uint32_t wo
     if (acc == 1234.5f) sink[0] = acc;  // keeps the loads alive
 }
 
+// The bounded mbarrier wait of the heads kernel, made to run out: one block waits on a barrier
+// that expects one arrival which nothing makes.  tc::bar_wait gives up after `limit` polls and
+// the block reports 2 (the heads kernel's "a wait ran out" code) instead of hanging.
+__global__ void wait_probe_kernel(uint32_t limit, int* __restrict__ status) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        tc::bar_init(&bar, 1);
+        tc::fence_bar_init();
+    }
+    __syncthreads();
+    const bool done = tc::bar_wait(&bar, 0, limit);
+    const int ok = __syncthreads_and(done);
+    if (threadIdx.x == 0) *status = ok ? 0 : 2;
+}
+
 }  // namespace
+
+void launch_wait_probe(uint32_t limit, int* status, cudaStream_t stream) {
+    ODIE_REQUIRE(limit >= 1 && limit <= (1u << 20), "wait probe limit must be 1..2^20 polls");
+    wait_probe_kernel<<<1, 128, 0, stream>>>(limit, status);
+    note_launch();
+}
 
 void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
                      cudaStream_t stream) {

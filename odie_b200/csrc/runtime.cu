@@ -784,6 +784,7 @@ void launch_plane_index(const uint8_t* support, int resolution, unsigned long lo
                         cudaStream_t stream);
 void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
                      cudaStream_t stream);
+void launch_wait_probe(uint32_t limit, int* status, cudaStream_t stream);
 }  // namespace odie
 
 using odie::guarded;
@@ -1077,6 +1078,13 @@ int odie_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int t
     return guarded([&] {
         odie::launch_allocation_bitmap(tiles, tiles_x, tiles_y, tile_px, height, width, resolution, bitmap,
                                        reinterpret_cast<cudaStream_t>(stream));
+        ODIE_CUDA(cudaGetLastError());
+    });
+}
+
+int odie_wait_probe(uint32_t limit, int32_t* status, uint64_t stream) {
+    return guarded([&] {
+        odie::launch_wait_probe(limit, status, reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
 }
