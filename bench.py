@@ -1,21 +1,28 @@
 """Benchmark of the ODIE hot path on B200: train coords/s (fwd + bwd + Adam) and decode Gpix/s.
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2-experts|c2-planes]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c4-experts|...]
 
-Workloads (odie_b200/workloads.py): c2-experts is the routed-expert benchmark (16 routed
-hash-grid experts, top-1 router on a coarse shared grid, shared 64-wide head,
-2040 x 1356 u8 image, 2^20 coords per step); c2-planes is the reference's own
-packed-plane method on the same image and batch.
+Workloads (odie_b200/workloads.py):
+  c4-experts (default): the gigapixel benchmark -- a 32768 x 32768 procedural u8 image, 64 routed
+    hash-grid experts under a 50 MiB fp16 budget (T = 2^14), owned spatially by 8 row bands of 8
+    experts, a top-1 router (64 logits) on a coarse shared grid, the shared 64-wide decoder, 20 % of
+    the 256 x 256 tiles allocated (exact top-k of the decoded residual), 2^22 coordinates per step and
+    GPU, 70 % of them in the allocated tiles.  The decode line is the gigapixel reconstruction: every
+    pixel of the image in launches of 2^24 pixels, u8 RGB out.
+  c2-experts: 16 routed experts (T = 2^16) on a 2040 x 1356 image, 2^20 coords per step.
+  c2-planes: the reference's own packed-plane method on the same image and batch.
+  c3-experts: 8 routed experts (T = 2^17) on a 4096 x 4096 image with 30 % tile allocation, 2^21.
 
-One JSON line on rank 0.  `value` is whole-job coords/s with inputs resident in
-HBM (device-timed with CUDA events, max over ranks); `e2e` is the same metric
-through the public API with the step's pixel ids copied from pinned host memory
-and the loss read back every step (the next step's ids upload on a copy stream
-while a step runs, as a training loop's loader prefetches).  Multi-GPU: one process per GPU (torchrun),
-each rank trains the model of its own row band of the image (weak scaling),
-and only the shared head gradients cross GPUs (NCCL all-reduce).  The
-`--impl reference` arm times the CPU restatement of the step
-(oracle/cpu_step.py; the reference has no CPU path of its own).
+One JSON line on rank 0.  `value` is whole-job coords/s with inputs resident in HBM (device-timed
+with CUDA events, max over ranks); `e2e` is the same metric through the public API with the step's
+pixel ids copied from pinned host memory and the loss read back every step (the next step's ids
+upload on a copy stream while a step runs, as a training loop's loader prefetches).  Multi-GPU: one
+process per GPU (torchrun).  c4: rank r of N holds 8/N bands of the one fixed model (their rows and
+experts) and trains 2^22 coordinates of them per step (weak scaling); the router MLP, decoder and
+router grid are shared, their gradients summed by one NCCL all-reduce per step that overlaps the
+rank's expert-table scatter and update.  c2/c3: each rank trains the model of its own row band.
+The `--impl reference` arm times the CPU restatement of the step (oracle/cpu_step.py; the reference
+has no CPU path of its own) on the host's cores.
 """
 import argparse
 import json
@@ -34,7 +41,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = 'train coords/s (fwd+bwd+Adam) & decode Gpix/s at 1/2/4/8 B200'
 UNIT = 'coords/s'
-BATCH = 1 << 20
+WORKLOADS = ('c4-experts', 'c2-experts', 'c2-planes', 'c3-experts')
+BATCHES = {'c4-experts': 1 << 22, 'c3-experts': 1 << 21, 'c2-experts': 1 << 20, 'c2-planes': 1 << 20}
+DECODE_LAUNCH = 1 << 24  # pixels per decode launch of the gigapixel reconstruction
+CPU_WINDOW_ROWS = 1024   # rows of the gigapixel image the CPU legs sample from (their cost does not depend on it)
 
 
 def parse():
@@ -43,24 +53,30 @@ def parse():
     p.add_argument('--steps', type=int, default=20)
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
-    p.add_argument('--workload', default='c2-experts', choices=['c2-experts', 'c2-planes', 'c3-experts'])
-    p.add_argument('--batch', type=int, default=None, help='coordinates per step (default: the workload\'s: '
-                   '2^20 for the C2 workloads, 2^21 for c3-experts)')
+    p.add_argument('--workload', default='c4-experts', choices=WORKLOADS)
+    p.add_argument('--batch', type=int, default=None, help='coordinates per step and GPU (default: the workload\'s: '
+                   '2^22 for c4, 2^21 for c3, 2^20 for the c2 workloads)')
     p.add_argument('--sampling', default='stratified', choices=['stratified', 'uniform'],
                    help='stratified: the reference default (odie/config.py:20, odie/data.py:63-80), one pixel per '
-                        'square stratum, strata in raster order; uniform: iid uniform pixel ids')
+                        'stratum, strata in raster order; uniform: iid uniform pixel ids')
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--shape', type=int, nargs=2, default=None, metavar=('H', 'W'),
+                   help='c4 only: a smaller image of the same model and kernels (H a multiple of 2048), for profiling')
+    p.add_argument('--decode-launch', type=int, default=DECODE_LAUNCH, help='c4: pixels per decode launch')
     return p.parse_args()
 
 
-def workload(name, rank, ranks, batch):
-    """Model, target, planes, config and image of this rank's band of a workload."""
+def workload(name, rank, ranks, batch, shape=None):
+    """Model, target, planes, config and image of this rank's part of a workload."""
     from odie_b200 import workloads
-    if name in ('c2-experts', 'c3-experts'):
+    if name in ('c2-experts', 'c3-experts', 'c4-experts'):
         if name == 'c2-experts':
             config, rgb, shape = workloads.c2_experts(batch=batch, band=(rank, ranks))
-        else:
+        elif name == 'c3-experts':
             config, rgb, shape = workloads.c3_experts(batch=batch, band=(rank, ranks))
+        else:
+            config, rgb, shape = workloads.c4_experts(batch=batch, band=(rank, ranks),
+                                                      shape=tuple(shape) if shape else workloads.C4_SHAPE)
         model, target, planes = workloads.build_expert_model(config, rgb)
         return dict(config=config, rgb=rgb, shape=shape, model=model, target=target, planes=planes)
     config, supports, dims, caps, rgb, shape = workloads.c2_planes(batch=batch, band=(rank, ranks))
@@ -69,27 +85,48 @@ def workload(name, rank, ranks, batch):
                 dims=dims, caps=caps)
 
 
-def cpu_step_of(name, batch):
-    """The oracle's CPU restatement of one training step of the workload (same layout, seeded weights)."""
+def c4_window(procedural=True):
+    """The CPU legs' sample window of the gigapixel image: its first CPU_WINDOW_ROWS rows as u8 [rows * W, 3] on the
+    host, drawn by this library's generator on the GPU (input data, not timed) when `procedural` and a GPU is
+    there, else seeded random bytes of the same shape (the CPU step's cost does not depend on the pixel values)."""
+    from odie_b200.workloads import C4_SHAPE
+    if procedural and torch.cuda.is_available():
+        from odie_b200.data import procedural_image
+        return procedural_image(C4_SHAPE, 1729, 0, CPU_WINDOW_ROWS).cpu()
+    g = torch.Generator().manual_seed(1729)
+    return torch.randint(0, 256, (CPU_WINDOW_ROWS * C4_SHAPE[1], 3), dtype=torch.uint8, generator=g)
+
+
+def cpu_step_of(name, batch, procedural=True):
+    """The oracle's CPU restatement of one training step of the workload (same layout, seeded weights), and the
+    (height, width) of the image window its coordinates are sampled from."""
     from oracle.cpu_step import CpuExpertStep, CpuStep, hash_levels_for_cpu, plane_levels_for_cpu
     from odie_b200 import layout as host_layout
     from odie_b200 import workloads
     rng = np.random.default_rng(0)
-    if name in ('c2-experts', 'c3-experts'):
+    if name in ('c2-experts', 'c3-experts', 'c4-experts'):
+        banding = None
         if name == 'c2-experts':
             config, rgb, shape = workloads.c2_experts(batch=batch)
-        else:
+        elif name == 'c3-experts':
             config, rgb, shape = workloads.c3_experts(batch=batch,
                                                       device='cuda' if torch.cuda.is_available() else 'cpu')
+        else:
+            config = workloads.experts_config(experts=64, batch=batch, encoding=workloads.C4_ENCODING)
+            rgb, shape = c4_window(procedural), (CPU_WINDOW_ROWS, workloads.C4_SHAPE[1])
+            banding = dict(bands=workloads.C4_BANDS, first_band=0, per_band=workloads.C4_PER_BAND,
+                           rows=workloads.C4_SHAPE[0], row_offset=0)
         records, stride = host_layout.hash_levels(config['hash_encoding'])
         router_records, router_total = host_layout.hash_levels(config['router_encoding'])
-        width = 32
-        step = CpuExpertStep(shape, rgb.numpy(), hash_levels_for_cpu(records), stride, config['experts'],
+        width, experts = 32, config['experts']
+        router_rows = 16 if experts <= 16 else 64
+        step = CpuExpertStep(shape, rgb.cpu().numpy(), hash_levels_for_cpu(records), stride, experts,
                              hash_levels_for_cpu(router_records),
-                             ((rng.random(config['experts'] * stride, dtype=np.float32) * 2 - 1) * 1e-4),
+                             ((rng.random(experts * stride, dtype=np.float32) * 2 - 1) * 1e-4),
                              ((rng.random(router_total, dtype=np.float32) * 2 - 1) * 0.1),
-                             (rng.standard_normal(32 * width + 32 * 32 + 16 * 32) * .2).astype(np.float32),
-                             (rng.standard_normal(width * 64 + 64 * 64 + 1024) * .1).astype(np.float32), width)
+                             (rng.standard_normal(32 * width + 32 * 32 + router_rows * 32) * .2).astype(np.float32),
+                             (rng.standard_normal(width * 64 + 64 * 64 + 1024) * .1).astype(np.float32), width,
+                             banding=banding)
         return step, shape
     config, supports, dims, caps, rgb, shape = workloads.c2_planes(batch=batch)
     lay = host_layout.make_layout(config, supports, dims, caps)
@@ -179,28 +216,44 @@ class Clocks:
                 'source': self.source}
 
 
-def algorithmic(name, stage, model, n):
-    """(bound, algorithmic bytes or FLOPs of one step's launches of a stage) from the per-unit figures:
-    encode forward 8 + 4 L F 2 + L F 2 B/coord per encoding (fp16 tables and features), encode backward
-    8 + L F 2 + 8 L F 4 B/coord per encoding (an fp32 atomic = read + write), heads 6 x sum(in x out)
-    FLOP/coord, router 64 + 8 B/coord, Adam 30 B/param."""
+def per_coordinate(name, model):
+    """Algorithmic work per coordinate of a training step's stages (the figures the roofline divides):
+    encode forward 8 + 4 L F 2 + L F 2 B per encoding (fp16 tables, fp16 features), encode backward
+    8 + L F 2 + 8 L F 4 B per encoding (an fp32 atomic = read + write), router 64 + 8 B (+ 2 live B per
+    logit stored), heads 6 x sum(in x out) FLOP (forward, data and weight gradients)."""
     L, F = model.n_levels, 2
     experts = name.endswith('experts')
     encodings = 2 if experts else 1  # the router grid and the routed expert
     decoder = 32 * 64 + 64 * 64 + 64 * 16
-    if stage == 'encode_forward':
-        return 'hbm', encodings * (8 + 4 * L * F * 2 + L * F * 2) * n
-    if stage == 'encode_backward':
-        return 'hbm', encodings * (8 + L * F * 2 + 8 * L * F * 4) * n
-    if stage == 'mlp_train':
-        gate = 32 * 32 + 32 * 32 + 16 * 32 if experts else 32 * 32 + 32 * 16
-        return 'tensor', 6 * (gate + decoder) * n
-    if stage == 'router':
-        return 'hbm', (64 + 8) * n
-    if stage == 'adam_grid':
-        params = model.grid.numel() + (model.router_grid.numel() if experts else 0)
-        return 'hbm', 30 * params
-    return 'hbm', None
+    if experts:
+        live = 8 if model.per_band <= 8 else 16
+        router_rows = 16 if model.experts <= 16 else 64
+        # the heads recompute the router's hidden layers; the logit layer's products run 64 (or 16) wide
+        gate = 32 * 32 + 32 * 32 + router_rows * 32
+    else:
+        live, gate = 0, 32 * 32 + 32 * 16
+    return {'encode_forward': ('hbm', encodings * (8 + 4 * L * F * 2 + L * F * 2)),
+            'encode_backward': ('hbm', encodings * (8 + L * F * 2 + 8 * L * F * 4)),
+            'router': ('hbm', 64 + 8 + 2 * live) if experts else ('hbm', None),
+            'mlp_train': ('tensor', 6 * (gate + decoder))}
+
+
+def adam_bytes(total_params, touched):
+    """Algorithmic bytes of the zero-skipping Adam sweep: every parameter's gradient read (4 B); for each touched
+    one p, m, v read and written (24 B), its step counter read and written (8 B), the fp16 copy (2 B) and the
+    gradient cleared (4 B)."""
+    return 4 * total_params + 38 * touched
+
+
+def decode_per_pixel(name, model):
+    """(algorithmic bytes, FLOP) per decoded pixel: the fp16 corner reads of every encoding (4 L F 2 B each) plus the
+    u8 RGB written; router (live logits only) and decoder products."""
+    L, F = model.n_levels, 2
+    experts = name.endswith('experts')
+    encodings = 2 if experts else 1
+    decoder = 32 * 64 + 64 * 64 + 64 * 16
+    gate = (32 * 32 + 32 * 32 + model.per_band * 32) if experts else (32 * 32 + 32 * 16)
+    return encodings * 4 * L * F * 2 + 3, 2 * (gate + decoder)
 
 
 def traffic_of(name, stage):
@@ -214,12 +267,12 @@ def traffic_of(name, stage):
 
 def l2_probe(lib, table_mib=32, operations=1 << 27):
     """Measured L2 throughput for random 4/16-byte loads and 4/8-byte fp32 reductions over an L2-resident table
-    (odie_l2_probe): the roofline of the gather and scatter kernels, whose tables all fit in L2."""
+    (odie_l2_probe): context for the gather and scatter kernels, whose tables all fit in L2."""
     table = torch.zeros((table_mib << 20) // 4, device='cuda')
     sink = torch.zeros(1, device='cuda')
     stream = torch.cuda.current_stream()
     names = ['load4', 'load16', 'red4', 'red8']
-    out = {'table_mib': table_mib, 'operations': operations, 'gops': {}, 'gbs': {}}
+    out = {'table_mib': table_mib, 'operations': operations, 'gops': {}}
     for mode, name in enumerate(names):
         best = float('inf')
         for _ in range(4):
@@ -232,55 +285,54 @@ def l2_probe(lib, table_mib=32, operations=1 << 27):
                 raise RuntimeError('odie_l2_probe failed')
             torch.cuda.synchronize()
             best = min(best, start.elapsed_time(end) / 1e3)
-        gops = operations / best / 1e9
-        out['gops'][name] = gops
-        out['gbs'][name] = gops * {'load4': 4, 'load16': 16, 'red4': 8, 'red8': 16}[name]  # a reduction reads + writes
+        out['gops'][name] = operations / best / 1e9
     return out
-
-
-def l2_ops(name, stage, model, n):
-    """Table accesses of one step of a gather/scatter stage: 4 corners x levels per coordinate and encoding."""
-    encodings = 2 if name.endswith('experts') else 1
-    if stage in ('encode_forward', 'encode_backward'):
-        return encodings * 4 * model.n_levels * n
-    return None
 
 
 def peaks():
     path = ROOT / 'MEASURED_PEAKS.json'
     if path.exists():
         data = json.loads(path.read_text())
-        return data['hbm_gbs'], data['bf16_tflops'], 'measured'
-    return 6650.0, 1590.0, 'fallback'
+        return data['hbm_gbs'], data['bf16_tflops'], data.get('bf16_tflops_sustained', data['bf16_tflops']), 'measured'
+    return 6650.0, 1590.0, 1400.0, 'fallback'
 
 
-def cpu_baseline(args, budget=12.0):
-    """The CPU restatement of the step on this host's cores (bounded sample)."""
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+def cpu_legs(args, budget=10.0, threads_list=None):
+    """The CPU restatement of the step on this host's cores (bounded samples of 2^14 uniform coordinates per step):
+    once with every host thread, once with one (the reference pins one thread, odie/train.py:72)."""
+    all_threads = os.cpu_count() or 1
+    threads_list = threads_list or [all_threads, 1]
     step, shape = cpu_step_of(args.workload, args.batch)
     sample = 1 << 14
     pixels = shape[0] * shape[1]
     g = torch.Generator().manual_seed(1)
-    step.step(torch.randint(0, pixels, (sample,), generator=g))  # warm-up
-    started, coords = time.perf_counter(), 0
-    while time.perf_counter() - started < budget:
-        step.step(torch.randint(0, pixels, (sample,), generator=g))
-        coords += sample
-    seconds = time.perf_counter() - started
-    return {'value': coords / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port',
-            'sample': f'{coords // sample} steps of {sample} uniform coords of {args.workload} (same layout, batch '
-                      f'scaled down), torch CPU, {threads} threads, {seconds:.1f} s'}
+    legs = []
+    for threads in threads_list:
+        torch.set_num_threads(threads)
+        step.step(torch.randint(0, pixels, (sample,), generator=g))  # warm-up
+        started, coords, steps = time.perf_counter(), 0, 0
+        while time.perf_counter() - started < budget or steps < 2:
+            step.step(torch.randint(0, pixels, (sample,), generator=g))
+            coords += sample
+            steps += 1
+        seconds = time.perf_counter() - started
+        legs.append({'value': coords / seconds, 'unit': UNIT, 'cores': threads, 'kind': 'port',
+                     'sample': f'{steps} steps of {sample} uniform coords of {args.workload} (full model and '
+                               f'layout, coordinates from a {shape[0]} x {shape[1]} window), torch CPU, {threads} '
+                               f'thread(s), {seconds:.1f} s'})
+    torch.set_num_threads(all_threads)
+    return legs
 
 
 def run_reference(args):
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
-    steps, coords, seconds = 0, 0, 0.0
+    steps, coords = 0, 0
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    step, shape = cpu_step_of(args.workload, args.batch)
+    # this arm runs none of this library's kernels: the gigapixel window is seeded random bytes
+    step, shape = cpu_step_of(args.workload, args.batch, procedural=False)
     sample = 1 << 14
     g = torch.Generator().manual_seed(2)
     pixels = shape[0] * shape[1]
@@ -297,7 +349,7 @@ def run_reference(args):
             'warmup': args.warmup, 'ms_per_step': seconds / steps * 1e3, 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'f32/f16', 'data': 'synthetic', 'impl': 'reference',
             'config': {'workload': args.workload, 'batch_per_step': sample, 'full_batch': args.batch,
-                       'note': 'bounded sample of the workload per step'},
+                       'note': 'bounded sample of the workload per step (full model and layout)'},
             'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port',
                              'sample': f'{steps} steps x {sample} coords, torch CPU restatement, {threads} threads'},
             'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
@@ -305,10 +357,9 @@ def run_reference(args):
 
 
 def allocate(args, lib, opt, model, target, shape):
-    """The on-demand allocation stage on the current model: decode every pixel, the fp64 residual of every
+    """c3: the on-demand allocation stage on the current model: decode every pixel, the fp64 residual of every
     256 x 256 tile, the exact top 30 %, and the expert levels restricted to the chosen tiles' cells.  Timed with CUDA
     events; returns the tile mask and the timings."""
-    import json as _json
     from odie_b200 import _lib
     from odie_b200.workloads import C3_TILE
     height, width = shape
@@ -333,7 +384,7 @@ def allocate(args, lib, opt, model, target, shape):
     tiles = selected.reshape(tiles_y, tiles_x)
     model.set_allocation(tiles, C3_TILE, shape)
     events[3].record()
-    opt.check(lib.odie_configure(opt.handle, _json.dumps(opt.current_settings()).encode()))
+    opt.check(lib.odie_configure(opt.handle, json.dumps(opt.current_settings()).encode()))
     events[4].record()
     torch.cuda.synchronize()
     return {'tiles': tiles.bool(), 'tiles_allocated': k, 'tiles_total': count, 'tile_px': C3_TILE,
@@ -345,10 +396,67 @@ def allocate(args, lib, opt, model, target, shape):
                          '70 % of coordinates uniform in the allocated tiles, 30 % uniform over the image (iid)')}
 
 
+def allocate_global(args, lib, opt, model, target, shape, dist):
+    """c4: the allocation stage over the whole gigapixel image, split across ranks.  Each rank decodes its own rows
+    one row of 256 x 256 tiles at a time and scores those tiles (fp64 residual, odie_tile_topk with k = 0); the
+    ranks' scores are gathered in row order, every rank takes the same exact top 20 % of all tiles (odie_topk) and
+    restricts the expert levels to the chosen tiles' cells with the full image's geometry, so the model is the same
+    at every GPU count.  Returns the rank's own rows of the tile mask and the timings."""
+    from odie_b200 import _lib
+    from odie_b200.workloads import C4_ALLOCATED, C4_TILE
+    tile = C4_TILE
+    rows, width = shape
+    row0 = int(opt.config.get('row_offset', 0))
+    full_rows = model.image_rows
+    if row0 % tile or rows % tile or full_rows % tile:
+        raise ValueError('the rank rows must be whole rows of tiles')
+    tiles_x, local_ty, full_ty = -(-width // tile), rows // tile, full_rows // tile
+    stream = torch.cuda.current_stream()
+    prediction = torch.empty((tile * width, 3), device='cuda')
+    row_sums = torch.empty(tiles_x * tile, dtype=torch.float64, device='cuda')
+    local = torch.empty(local_ty * tiles_x, dtype=torch.float64, device='cuda')
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    torch.cuda.synchronize()
+    events[0].record()
+    for ty in range(local_ty):
+        opt.decode(ty * tile * width, tile * width, rgb=prediction)
+        _lib.check(lib.odie_tile_topk(prediction.data_ptr(), target.data.data_ptr() + ty * tile * width * 3, tile,
+                                      width, tile, 0, row_sums.data_ptr(), local[ty * tiles_x:].data_ptr(), None, None,
+                                      stream.cuda_stream))
+    events[1].record()
+    if dist is not None:
+        gathered = [torch.empty_like(local) for _ in range(dist.get_world_size())]
+        dist.all_gather(gathered, local)
+        scores = torch.cat(gathered)
+    else:
+        scores = local
+    count = full_ty * tiles_x
+    k = int(round(C4_ALLOCATED * count))
+    chosen = torch.empty(k, dtype=torch.int64, device='cuda')
+    selected = torch.empty(count, dtype=torch.uint8, device='cuda')
+    _lib.check(lib.odie_topk(scores.data_ptr(), count, k, chosen.data_ptr(), selected.data_ptr(), stream.cuda_stream))
+    events[2].record()
+    tiles = selected.reshape(full_ty, tiles_x)
+    model.set_allocation(tiles, tile, (full_rows, width))
+    events[3].record()
+    opt.check(lib.odie_configure(opt.handle, json.dumps(opt.current_settings()).encode()))
+    events[4].record()
+    torch.cuda.synchronize()
+    first = row0 // tile
+    return {'tiles': tiles[first:first + local_ty].bool(), 'tiles_allocated': k, 'tiles_total': count, 'tile_px': tile,
+            'decode_and_score_ms': events[0].elapsed_time(events[1]), 'select_ms': events[1].elapsed_time(events[2]),
+            'bitmaps_ms': events[2].elapsed_time(events[3]), 'configure_ms': events[3].elapsed_time(events[4]),
+            'stage_ms': events[0].elapsed_time(events[4]),
+            'bitmap_bytes': int(model.allocation_bitmap.numel()),
+            'sampling': ('70 % of coordinates on jittered strata spread evenly over the allocated tiles of the rank, '
+                         '30 % on jittered strata over the rank\'s rows, tile by tile' if args.sampling == 'stratified'
+                         else '70 % uniform in the rank\'s allocated tiles, 30 % uniform over its rows (iid)')}
+
+
 def main():
     args = parse()
     if args.batch is None:
-        args.batch = 1 << 21 if args.workload == 'c3-experts' else BATCH
+        args.batch = BATCHES[args.workload]
     if args.impl == 'reference':
         run_reference(args)
         return
@@ -363,25 +471,39 @@ def main():
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
     from odie_b200 import _lib, parallel
     from odie_b200.native_backend import NativeOptimizer
+    from odie_b200.workloads import C4_TILE, allocated_ids, allocated_stratified_ids, fp16_payload_bytes
     lib = _lib.library()
-    w = workload(args.workload, rank, world, args.batch)
+    c4 = args.workload == 'c4-experts'
+    experts = args.workload.endswith('experts')
+    w = workload(args.workload, rank, world, args.batch, args.shape if c4 else None)
     config, shape, model = w['config'], w['shape'], w['model']
-    head_grad = None
+    shared = head_grad = router_grad = None
     if world > 1:
-        # the heads are shared: every rank starts from rank 0's weights and applies the same summed gradient
+        # the shared parameters: every rank starts from rank 0's and applies the same summed gradient
         parallel.broadcast_heads(model)
-        head_grad = parallel.head_gradient_buffer(model)
-    opt = NativeOptimizer(model, w['target'], shape, config, w['planes'], batch=args.batch, head_grad=head_grad)
-    dp_step = parallel.DataParallelStep(parallel.NativeRuntime(opt), head_grad)
+        if c4:
+            dist.broadcast(model.router_grid.data, 0)
+        shared, head_grad, router_grad = parallel.head_gradient_buffer(model, router_grid=c4)
+    # c4 decodes in launches of 2^24 pixels: the runtime's buffers hold that many coordinates
+    capacity = max(args.batch, args.decode_launch) if c4 else args.batch
+    opt = NativeOptimizer(model, w['target'], shape, config, w['planes'], batch=capacity, head_grad=head_grad,
+                          router_grad=router_grad)
+    runtime = parallel.NativeRuntime(opt)
+    overlap = runtime.side_stream() if world > 1 else None
+    dp_step = parallel.DataParallelStep(runtime, shared, overlap_stream=overlap)
     pixels = shape[0] * shape[1]
     gen = torch.Generator(device='cuda').manual_seed(1729 + rank)
     total_steps = args.warmup + args.steps
     allocation = None
-    if args.workload == 'c3-experts':
-        allocation = allocate(args, lib, opt, model, w['target'], shape)
-        from odie_b200.workloads import allocated_ids, allocated_stratified_ids
+    if args.workload in ('c3-experts', 'c4-experts'):
+        if c4:
+            allocation = allocate_global(args, lib, opt, model, w['target'], shape, dist)
+        else:
+            allocation = allocate(args, lib, opt, model, w['target'], shape)
         sampler = allocated_stratified_ids if args.sampling == 'stratified' else allocated_ids
-        ids = torch.stack([sampler(allocation['tiles'], shape, args.batch, gen) for _ in range(total_steps)])
+        tile_px = allocation['tile_px']
+        ids = torch.stack([sampler(allocation['tiles'], shape, args.batch, gen, tile_px=tile_px)
+                           for _ in range(total_steps)])
         allocation = {k: v for k, v in allocation.items() if k != 'tiles'}
     elif args.sampling == 'stratified':
         from odie_b200.data import stratified_batches
@@ -401,8 +523,22 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    for w in range(args.warmup):
-        step(ids[w])
+    def view(name, count, typestr='<f4'):
+        return torch.as_tensor(DeviceArray(opt.pointers[name], count, typestr), device='cuda')
+
+    # warm-up; its first step keeps the grid gradients long enough to count the parameters a step touches
+    # (the zero-skipping Adam reads p, m, v only for those)
+    grid_params = model.grid.numel() + (model.router_grid.numel() if experts else 0)
+    opt.check(lib.odie_step_grads(opt.handle, ids[0].data_ptr(), args.batch, 2))
+    touched = int(torch.count_nonzero(view('grid_grad', model.grid.numel())))
+    if experts:
+        touched += int(torch.count_nonzero(view('router_grad', model.router_grid.numel())))
+    opt.check(lib.odie_grid_update(opt.handle))
+    if dist is not None:
+        dist.all_reduce(shared)
+    opt.check(lib.odie_step_heads(opt.handle))
+    for k in range(1, args.warmup):
+        step(ids[k])
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clocks:
@@ -415,16 +551,18 @@ def main():
         launches = lib.odie_launch_count() - launches_before
         barrier()
     ms = start.elapsed_time(end)
-    # Stage timers (the roofline's kernel durations): a second timed pass of the same K steps with CUDA
-    # events recorded between the stages on their own streams.  The events cost a few per cent of a
-    # step, so the pass that gives `value` runs without them.
-    opt.check(lib.odie_profile(opt.handle, 1))
+    # Stage timers (the roofline's kernel durations): a second pass of the same K steps with CUDA events between
+    # the stages and the step's two branches serialised on one stream, so that each stage's time is its own
+    # kernels' (concurrent branches would charge each other's waits).  Not part of `value`.
+    dp_step.overlap_stream = None
+    opt.check(lib.odie_profile(opt.handle, 2))
     barrier()
     for k in range(args.steps):
         step(ids[args.warmup + k])
     barrier()
     report = json.loads(lib.odie_profile_report(opt.handle))
     opt.check(lib.odie_profile(opt.handle, 0))
+    dp_step.overlap_stream = overlap
     ms_t = torch.tensor([ms], device='cuda')
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -438,9 +576,9 @@ def main():
     device_ids = [torch.empty(args.batch, dtype=torch.int64, device='cuda') for _ in range(2)]
     loss_host = torch.empty(args.steps, dtype=torch.float64).pin_memory()
     # the runtime's per-sample squared errors, viewed in place: the loss is their fp64 mean.  Each step's
-    # errors are copied (4 MB, device to device) on a loss stream, and the next step waits only for that
-    # copy; the reduction and the 8-byte read to the host run beside the next step.
-    squares = torch.as_tensor(DeviceArray(opt.pointers['squares'], args.batch, '<f4'), device='cuda')
+    # errors are copied (device to device) on a loss stream, and the next step waits only for that copy;
+    # the reduction and the 8-byte read to the host run beside the next step.
+    squares = view('squares', args.batch)
     main_stream, copy_stream, loss_stream = torch.cuda.current_stream(), torch.cuda.Stream(), torch.cuda.Stream()
     uploaded = [torch.cuda.Event() for _ in range(2)]
     released = [torch.cuda.Event() for _ in range(2)]
@@ -496,7 +634,7 @@ def main():
     # the sampler of a training loop, per step: the reference's stratified_batches (torch RNG and
     # arithmetic kernels) against the device sampler, and the step with the sampler fused in
     sampler = None
-    if world == 1 and args.workload != 'c3-experts' and args.sampling == 'stratified':
+    if world == 1 and args.workload in ('c2-experts', 'c2-planes') and args.sampling == 'stratified':
         from odie_b200.data import device_stratified_ids, stratified_batches
         reps = 10
         s_events = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
@@ -522,12 +660,12 @@ def main():
                    'note': 'stratified_batches (odie/data.py:63-80) as the reference runs it each step, vs '
                            'odie_stratified_ids; odie_step_stratified = odie_step with the sampler fused in'}
 
-    # decode of this rank's band (all pixels), Gpix/s
+    # decode of this rank's rows, every pixel (c4: the gigapixel reconstruction in launches of 2^24 pixels)
     rgb8 = torch.empty((pixels, 3), dtype=torch.uint8, device='cuda')
     opt.decode(0, pixels, rgb8=rgb8)
     barrier()
     d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    repeats = 5
+    repeats = 2 if c4 else 5
     d_start.record()
     for _ in range(repeats):
         opt.decode(0, pixels, rgb8=rgb8)
@@ -536,56 +674,79 @@ def main():
     d_ms = torch.tensor([d_start.elapsed_time(d_end)], device='cuda')
     if dist is not None:
         dist.all_reduce(d_ms, op=dist.ReduceOp.MAX)
-    decode_gpix = world * pixels * repeats / (float(d_ms) / 1e3) / 1e9
+    d_seconds = float(d_ms) / 1e3
+    decode_gpix = world * pixels * repeats / d_seconds / 1e9
+    del rgb8
 
     probe = l2_probe(lib) if rank == 0 else None
     if rank == 0:
-        hbm, tensor_peak, peak_kind = peaks()
+        hbm, tensor_burst, tensor_sustained, peak_kind = peaks()
+        units = per_coordinate(args.workload, model)
         stages = {k: v for k, v in report.items() if v['launches']}
-        dominant = max(stages, key=lambda k: stages[k]['ms'])
-        total_ms = sum(v['ms'] for v in stages.values())
-        bound, work = algorithmic(args.workload, dominant, model, args.batch)
-        step_s = stages[dominant]['ms'] / args.steps / 1e3  # the stage's launches of one step
-        if bound == 'tensor':
-            achieved, peak, unit = work / step_s / 1e12, tensor_peak, 'TFLOP/s'
-        else:
-            achieved, peak, unit = (work / step_s / 1e9 if work else None), hbm, 'GB/s'
         per_stage = {}
         for k, v in stages.items():
-            b, wk = algorithmic(args.workload, k, model, args.batch)
-            sec = v['ms'] / args.steps / 1e3
+            seconds = v['ms'] / args.steps / 1e3
+            bound, work = units.get(k, ('hbm', None))
+            if work is not None:
+                work = work * args.batch
+            if k == 'adam_grid':
+                work = adam_bytes(grid_params, touched)
+            if k == 'input_batch':
+                work = (8 + 3 + 8 + 12) * args.batch  # id, u8 target in; xy, fp32 target out
+            achieved = (work / seconds / (1e12 if bound == 'tensor' else 1e9)) if work else None
+            peak = tensor_sustained if bound == 'tensor' else hbm
             per_stage[k] = {'ms_per_step': v['ms'] / args.steps, 'launches_per_step': v['launches'] / args.steps,
-                            'achieved': (wk / sec / (1e12 if b == 'tensor' else 1e9)) if wk else None,
-                            'unit': 'TFLOP/s' if b == 'tensor' else 'GB/s'}
-            ops = l2_ops(args.workload, k, model, args.batch)
-            if ops:
-                ref = probe['gops']['load4' if k == 'encode_forward' else 'red8']
-                per_stage[k]['l2'] = {'table_accesses_per_step': ops, 'achieved_gops': ops / sec / 1e9,
-                                      'probe_gops': ref, 'frac': ops / sec / 1e9 / ref,
-                                      'probe': 'load4' if k == 'encode_forward' else 'red8'}
-        roofline = {'kernel': dominant, 'bound': bound, 'achieved': achieved, 'peak': peak, 'unit': unit,
-                    'frac': (achieved / peak) if achieved else None,
-                    'traffic': traffic_of(args.workload, dominant), 'traffic_unit': 'DRAM bytes per step',
-                    'algorithmic_per_step': work, 'peak_source': peak_kind,
-                    'l2': per_stage[dominant].get('l2'), 'l2_probe': probe,
-                    'share': stages[dominant]['ms'] / total_ms, 'stages': per_stage}
+                            'bound': bound, 'algorithmic_per_step': work, 'achieved': achieved,
+                            'unit': 'TFLOP/s' if bound == 'tensor' else 'GB/s',
+                            'frac': (achieved / peak) if achieved else None}
+        dominant = max(stages, key=lambda k: stages[k]['ms'])
+        d = per_stage[dominant]
+        peak = tensor_sustained if d['bound'] == 'tensor' else hbm
+        roofline = {'kernel': dominant, 'bound': d['bound'], 'achieved': d['achieved'], 'peak': peak,
+                    'unit': d['unit'], 'frac': d['frac'], 'traffic': traffic_of(args.workload, dominant),
+                    'traffic_unit': 'DRAM bytes per step (ncu, profiles/dram_traffic.json)',
+                    'algorithmic_per_step': d['algorithmic_per_step'],
+                    'peak_source': f'{peak_kind} ({"sustained dense bf16" if d["bound"] == "tensor" else "HBM copy"})',
+                    'timing': 'stage events with the step branches serialised (kernel time)',
+                    'share': stages[dominant]['ms'] / sum(v['ms'] for v in stages.values()),
+                    'touched_params_per_step': touched, 'grid_params': grid_params,
+                    'stages': per_stage, 'l2_probe_gops': probe['gops']}
+        dec_bytes, dec_flop = decode_per_pixel(args.workload, model)
+        dec_rate = pixels * repeats / d_seconds
+        decode = {'value': decode_gpix, 'unit': 'Gpix/s', 'pixels_per_rank': pixels,
+                  'launch_pixels': min(capacity, pixels), 'launches_per_pass': -(-pixels // capacity),
+                  'roofline': {'bound': 'hbm', 'algorithmic_bytes_per_pixel': dec_bytes,
+                               'achieved': dec_rate * dec_bytes / 1e9, 'peak': hbm, 'unit': 'GB/s',
+                               'frac': dec_rate * dec_bytes / 1e9 / hbm, 'flop_per_pixel': dec_flop,
+                               'tflops': dec_rate * dec_flop / 1e12,
+                               'note': 'table corner reads of both encodings + u8 out; the tables are L2-resident'}}
         base = None
         if world == 1 and not args.no_cpu_baseline:
-            base = cpu_baseline(args)
+            legs = cpu_legs(args)
+            base = dict(legs[0], one_thread=legs[1])
+        payload = fp16_payload_bytes(model) if experts else 2 * (model.grid.numel() + model.decoder.params.numel())
         line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
                 'vs_baseline': None, 'dtype': 'f16 (fp32 masters, fp32 accumulate)', 'data': 'synthetic',
-                'config': {'workload': args.workload, 'image_hw': list(shape), 'global_batch': world * args.batch,
-                           'batch_per_gpu': args.batch, 'levels': model.n_levels, 'grid_params': model.grid.numel(),
+                'config': {'workload': args.workload,
+                           'image_hw': [model.image_rows, shape[1]] if c4 else list(shape),
+                           'rows_per_rank': shape[0], 'global_batch': world * args.batch,
+                           'batch_per_gpu': args.batch, 'levels': model.n_levels,
+                           'grid_params_per_rank': model.grid.numel(),
                            'experts': getattr(model, 'experts', None),
-                           'parallelism': f'dp{world} (row bands, head all-reduce)',
+                           'experts_per_rank': getattr(model, 'experts_held', None),
+                           'bands': getattr(model, 'bands', None),
+                           'fp16_payload_mib': payload / 2 ** 20,
+                           'parallelism': (f'dp{world} (one model: 8 row bands of 8 experts split over ranks; '
+                                           'all-reduce of router MLP + decoder + router grid)' if c4 else
+                                           f'dp{world} (row bands, head all-reduce)'),
                            'sampling': (args.sampling + (' (reference default, odie/config.py:20)'
                                                          if args.sampling == 'stratified' else ' (iid)')
-                                        + (', 70 % in the allocated tiles' if args.workload == 'c3-experts' else '')),
-                           'l2': 'per-step inputs/activations (~200 MB) larger than L2; model tables L2-resident'},
+                                        + (', 70 % in the allocated tiles' if allocation else '')),
+                           'l2': 'per-step inputs and activations (c4: > 1 GB) larger than L2; model tables '
+                                 'L2-resident'},
                 'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': args.batch * 8, 'd2h_bytes_per_step': 8},
-                'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base,
-                'decode': {'value': decode_gpix, 'unit': 'Gpix/s', 'pixels_per_rank': pixels},
+                'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base, 'decode': decode,
                 'loss_first_last': [float(losses[0]), float(losses[-1])], 'clocks': clocks.summary()}
         if allocation:
             line['allocation'] = allocation

@@ -30,10 +30,21 @@ extern "C" {
  * bakes in at compile time (odie/build.py:26-30): "levels", "raw_width",
  * "router", "gate_k", "softplus", "rgb8", and "batch" (maximum coordinates per
  * step; the reference fixes 65536).
- * Routed experts (no reference counterpart): "experts" (1..16) with
- * "hash_encoding" (one expert's grid; "grid" holds experts x its parameters,
- * expert-major), "router_encoding" (the coarse shared grid; fp32 master in
- * "router_grid") and "gate" (router MLP W1 | W2 | W3, fp32 master, "gate_lr").
+ * Routed experts (no reference counterpart): "experts" (1..64 tables held)
+ * with "hash_encoding" (one expert's grid; "grid" holds experts x its
+ * parameters, expert-major), "router_encoding" (the coarse shared grid; fp32
+ * master in "router_grid") and "gate" (router MLP W1 | W2 | W3 with
+ * router_out = 16 (up to 16 model experts) or 64 logit rows, fp32 master,
+ * "gate_lr").  Spatial expert ownership: "bands" (rows of the full image cut
+ * into this many equal bands, default 1), "experts_per_band" (8 or 16 when
+ * bands > 1; default: experts), "first_band" (the first band held here,
+ * default 0): band b owns the model's experts [b * per, (b + 1) * per) and a
+ * coordinate chooses among its band's experts only.  "full_height" and
+ * "row_offset" (defaults: height, 0) place this image's rows in the full
+ * image, whose rows the coordinates use.  "router_grad" (optional, device
+ * f32[router grid params], zeroed here): a caller-owned router-grid gradient
+ * (a router grid shared across ranks); its update then runs in
+ * odie_step_heads, after the caller has summed it.
  * ------------------------------------------------------------------------ */
 /* Thread-local message of the last failure. runtime.cu:320 */
 ODIE_API const char* odie_error(void);
@@ -88,9 +99,11 @@ ODIE_API int odie_stratified_ids(uint64_t seed, uint64_t step, int width, int he
                    uint64_t stream);
 ODIE_API int odie_step_stratified(void* handle, uint64_t seed, uint64_t step, int n, int update);
 
-/* Stage timers (no reference counterpart): enable/disable CUDA-event timing of
- * every stage launch on the runtime's stream (resets the record), and a JSON
- * report {stage: {"launches": k, "ms": total}} of what was recorded. */
+/* Stage timers (no reference counterpart): enable (1) / disable (0) CUDA-event
+ * timing of every stage launch on the stream it runs on (resets the record), or
+ * enable with the step's concurrent branches run one after the other on the
+ * runtime's stream (2), so that each stage's time is its kernels' own; and a
+ * JSON report {stage: {"launches": k, "ms": total}} of what was recorded. */
 ODIE_API int odie_profile(void* handle, int enable);
 ODIE_API const char* odie_profile_report(void* handle);
 
@@ -155,12 +168,18 @@ ODIE_API int selection_chunk(const double* scores, int n, int points, int resolu
                     int chunk, int64_t* stats, int* trace, uint64_t stream);
 
 /* ------------------------------------------------------------------------
- * Routed multi-expert encoding (16 routed experts in the benchmark; no reference counterpart).
- * odie_router_forward: features f16[n][width] (width 16 or 32, row-major),
- * weights f16 [32*width | 32*32 | 16*32] (router W1, W2, W3, row-major
- * [out][in]); writes expert i32[n] (first maximum of the fp16 logits over
- * experts 1..16), prob f32[n] (softmax probability of that expert) and, when
- * logits is non-NULL, f16[n][16].  Bit-exact: fp32 fma chains in input order.
+ * Routed multi-expert encoding (no reference counterpart).
+ * odie_router_forward_banded: features f16[n][width] (width 16 or 32,
+ * row-major), xy f32[n][2] (read when bands > 1: the band of a coordinate is
+ * floor(row * bands / rows) with row = rint(y * (rows - 1))), weights
+ * f16 [32*width | 32*32 | OUT*32] (router W1, W2, W3, row-major [out][in];
+ * OUT = 16 for up to 16 model experts (bands x experts_per_band), else 64).
+ * Writes expert i32[n] (local number: (band - first_band) * experts_per_band
+ * + the first maximum of the fp16 logits of the band's experts), prob f32[n]
+ * (softmax probability of that expert over its band's) and, when logits is
+ * non-NULL, f16[n][live] (the band's logits; live 8 or 16, >= experts_per_band,
+ * zero padded).  Bit-exact: fp32 fma chains in input order.
+ * odie_router_forward: the unbanded form (experts 1..16, logits f16[n][16]).
  * odie_expert_hash_forward/backward: odie_hash_forward/backward with one table
  * per expert; coordinate i uses the table starting expert[i] * expert_stride
  * parameters into `tables` / `gradient` (same level records for every expert).
@@ -170,6 +189,9 @@ ODIE_API int selection_chunk(const double* scores, int n, int points, int resolu
  * ------------------------------------------------------------------------ */
 ODIE_API int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
                    int32_t* expert, float* prob, uint16_t* logits, uint64_t stream);
+ODIE_API int odie_router_forward_banded(const uint16_t* features, const float* xy, int64_t n, int width,
+                   const uint16_t* weights, int experts, int bands, int first_band, int experts_per_band, int rows,
+                   int32_t* expert, float* prob, uint16_t* logits, int live, uint64_t stream);
 ODIE_API int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
                    const int32_t* expert, const odie_hash_level* levels, int level_count, int width,
                    const uint8_t* bitmap, uint16_t* features, uint64_t stream);
@@ -229,6 +251,22 @@ ODIE_API int odie_wait_probe(uint32_t limit, int32_t* status, uint64_t stream);
  * ------------------------------------------------------------------------ */
 ODIE_API int odie_tile_topk(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
                    double* row_sums, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream);
+/* The exact top-k alone: chosen i64[k] = the k highest of scores f64[count] by
+ * (score descending, index ascending), selected u8[count] (1 for those).  For
+ * tile scores gathered from several ranks before one global choice.  Requires
+ * 0 <= k <= count (else cudaErrorInvalidValue with a message). */
+ODIE_API int odie_topk(const double* scores, int count, int k, int64_t* chosen, uint8_t* selected, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Procedural gigapixel test image (benchmark input; no reference counterpart).
+ * Writes rows [row0, row0 + rows) of a height x width u8 RGB image into
+ * rgb u8[rows][width][3]: seeded fractal value noise with a 1/f^2 spectrum,
+ * Voronoi regions with sharp borders and a 64 x 64-cell atlas of patterns.
+ * Each pixel depends only on (seed, column, row, width, height), so ranks that
+ * draw their own bands draw one image.  -1 with odie_error() on bad rows.
+ * ------------------------------------------------------------------------ */
+ODIE_API int odie_procedural_image(uint64_t seed, int width, int height, int row0, int rows, uint8_t* rgb,
+                   uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * Allocation-free tile top-k (no counterpart in the reference).
@@ -240,7 +278,10 @@ ODIE_API int odie_tile_topk(const float* prediction, const uint8_t* target, int 
  * device or is forbidden.  tiles * tile above 262144 returns
  * cudaErrorInvalidValue with a message in odie_error().  The first call on each
  * device looks up the array's device address (cudaGetSymbolAddress); make that
- * first call before any stream capture.  All calls on one device share the
+ * first call before any stream capture.  The address is kept for the
+ * process: after a cudaDeviceReset of that device, do not call this entry
+ * point there.  tile must not exceed max(height, width).  All calls on one
+ * device share the
  * array: calls that can overlap on the GPU (different streams, or several host
  * threads) race and must be serialised by the caller.
  * ------------------------------------------------------------------------ */

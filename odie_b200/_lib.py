@@ -51,6 +51,7 @@ SIGNATURES = {
     'selection_chunk': (I32, [P, I32, I32, I32, I32, B, P, P, P, P, P, P, I32, I32, P, P, U64]),
     'odie_tile_topk': (I32, [P, P, I32, I32, I32, I32, P, P, P, P, U64]),
     'odie_router_forward': (I32, [P, I64, I32, P, I32, P, P, P, U64]),
+    'odie_router_forward_banded': (I32, [P, P, I64, I32, P, I32, I32, I32, I32, I32, P, P, P, I32, U64]),
     'odie_l2_probe': (I32, [P, I64, I32, I64, P, U64]),
     'odie_plane_index_scratch': (I64, [I32]),
     'odie_allocation_bitmap': (I32, [P, I32, I32, I32, I32, I32, I32, P, U64]),
@@ -58,6 +59,8 @@ SIGNATURES = {
     'odie_expert_hash_forward': (I32, [P, I64, P, I64, P, C.POINTER(HashLevel), I32, I32, P, P, U64]),
     'odie_expert_hash_backward': (I32, [P, I64, P, I32, I64, P, C.POINTER(HashLevel), I32, P, P, I64, U64]),
     'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),
+    'odie_topk': (I32, [P, I32, I32, P, P, U64]),
+    'odie_procedural_image': (I32, [U64, I32, I32, I32, I32, P, U64]),
 }
 
 

@@ -28,6 +28,8 @@
 // router backward down to the router-grid gradient values.  The router
 // features of the next tile stream into a second shared-memory buffer with
 // cp.async while the current tile runs.
+#include <atomic>
+
 #include "router.cuh"
 #include "step.cuh"
 #include "tc.cuh"
@@ -52,17 +54,15 @@ constexpr uint32_t T_ACC = 0, T_DWD2 = 64, T_DWD1 = 128, T_DW3T = 160, T_DWG2T =
 template <int W>
 struct TcSmem {
     static constexpr int XB = 128 * W * 2;              // one [128 x W] buffer
-    static constexpr int g1 = 0;                        // [32 x W] gate / router W1
-    static constexpr int g2 = g1 + 32 * W * 2;          // [16 x 32] gate W2 / router W3
-    static constexpr int r2 = g2 + 16 * 32 * 2;         // [32 x 32] router W2
-    static constexpr int d1 = r2 + 32 * 32 * 2;         // [64 x W]
+    static constexpr int g1 = 0;                        // [32 x W] gate W1
+    static constexpr int g2 = g1 + 32 * W * 2;          // [16 x 32] gate W2
+    static constexpr int d1 = g2 + 16 * 32 * 2;         // [64 x W]
     static constexpr int d2 = d1 + 64 * W * 2;          // [64 x 64]
     static constexpr int d3 = d2 + 64 * 64 * 2;         // [16 x 64]
     static constexpr int x = d3 + 16 * 64 * 2;          // [128 x W] raw features
     static constexpr int wx = x + XB;                   // [128 x W] gated decoder input
-    static constexpr int gh = wx + XB;                  // [128 x 32] gate / router hidden 1
-    static constexpr int gh2 = gh + 8192;               // [128 x 32] router hidden 2
-    static constexpr int h1 = gh2 + 8192;               // [128 x 64] decoder hidden 1, then dh1
+    static constexpr int gh = wx + XB;                  // [128 x 32] gate hidden
+    static constexpr int h1 = gh + 8192;                // [128 x 64] decoder hidden 1, then dh1
     static constexpr int h2 = h1 + 16384;               // [128 x 64] decoder hidden 2, then dh2
     static constexpr int dgh = h2 + 16384;              // [128 x 32] gate hidden gradient
     static constexpr int dy = dgh + 8192;               // [128 x 16] output gradient
@@ -71,9 +71,7 @@ struct TcSmem {
     static constexpr int bar_dw = bar + 8;              // mbarrier: weight-gradient products of a phase
     static constexpr int drain = bar_dw + 8;            // mbarrier: every issuing warp's products (error exit)
     static constexpr int tmem = drain + 8;              // TMEM base address
-    static constexpr int x2 = (tmem + 8 + 127) / 128 * 128;  // [128 x W] second router-feature buffer (experts)
     static constexpr int total = tmem + 8;
-    static constexpr int total_experts = x2 + XB;
     static_assert(gh + 16384 <= dgh, "GH read 64 wide stays inside the activation buffers");
     static_assert(dgh + 16384 <= bar, "DGH read 64 wide stays inside the activation buffers");
 };
@@ -216,11 +214,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, S::g1);
         stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, S::g2);
     }
-    if (EXPERTS && TRAIN) {
-        stage_blocked(a.gate_w, ROUTER_HIDDEN, W, smem, S::g1);
-        stage_blocked(a.gate_w + ROUTER_HIDDEN * W, ROUTER_HIDDEN, ROUTER_HIDDEN, smem, S::r2);
-        stage_blocked(a.gate_w + ROUTER_HIDDEN * W + ROUTER_HIDDEN * ROUTER_HIDDEN, ROUTER_OUT, ROUTER_HIDDEN, smem, S::g2);
-    }
+    static_assert(!(EXPERTS && TRAIN), "routed-expert training runs in experts_train_kernel");
     stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
@@ -269,7 +263,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     uint32_t next_raw[PAIRS], next_vis = 0;
     float next_target[3] = {0.0f, 0.0f, 0.0f};
     float next_prob = 0.0f;
-    int next_expert = 0;
     auto load_inputs = [&](long long tile) {
         const long long i = tile * TC_TILE + t;
         const bool valid = tile < tiles && i < a.n;
@@ -291,21 +284,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
         }
-        if (EXPERTS) {
-            next_prob = valid ? __ldg(a.prob + i) : 0.0f;
-            if (TRAIN) next_expert = valid ? __ldg(a.expert + i) : 0;
-        }
-    };
-    // Router features of a tile (experts, training; row-major [stride][W]): each row's W halves as
-    // W / 8 16-byte cp.async copies into the blocked layout of shared buffer `buf`.
-    auto prefetch_router = [&](long long tile, int buf) {
-        const long long i = tile * TC_TILE + t;
-        const bool valid = tile < tiles && i < a.n;
-        const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
-#pragma unroll
-        for (int j = 0; j < W / 8; ++j)
-            cp_async16(sbase + buf + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
-        cp_async_commit();
+        if (EXPERTS) next_prob = valid ? __ldg(a.prob + i) : 0.0f;
     };
     // Visibility: lane l (< levels) loads this warp's word of level l; the
     // words are broadcast with shuffles when the bits are folded per row.
@@ -325,19 +304,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     load_inputs(blockIdx.x);
     issue_vis(blockIdx.x);
     fold_vis(blockIdx.x);
-    int xbuf = S::x;  // router features of the current tile (experts: alternates with S::x2)
-    if (EXPERTS && TRAIN) prefetch_router(blockIdx.x, S::x);
 
     for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
         const long long i = tile * TC_TILE + t;
         const bool valid = i < a.n;
-        if (EXPERTS && TRAIN) {
-            // the other buffer was last read by the previous tile's router weight-gradient product, which has completed
-            prefetch_router(tile + gridDim.x, xbuf == S::x ? S::x2 : S::x);
-            cp_async_wait_older();  // this tile's features have landed
-        }
         const float prob = next_prob;
-        const int expert = next_expert;
         // ---- inputs: raw features (pad columns 1.0), visibility bits, target
         uint32_t raw[PAIRS];
         const __half one = __float2half_rn(1.0f);
@@ -415,7 +386,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             for (int j = 0; j < W / 8; ++j)
                 store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
         }
-        uint32_t gh2_mask = 0;
         if (EXPERTS) {
             // ---- decoder input: the routed expert's features x half(p), one rounding per feature
             const __half2 ph = __float2half2_rn(prob);
@@ -429,34 +399,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
                 store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
-            if (TRAIN) {
-                // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T), Z = GH2 Wr3^T
-                is.before_issue();
-                if (t == 0)
-                    for (int s = 0; s < KW; ++s)
-                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
-                is.complete();
-                gh_mask = relu_store32(lane_addr + T_ACC, smem, S::gh, t, 0);
-                is.before_issue();
-                if (t == 0)
-                    for (int s = 0; s < 2; ++s)
-                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
-                is.complete();
-                gh2_mask = relu_store32(lane_addr + T_ACC, smem, S::gh2, t, 0);
-                is.before_issue();
-                if (t == 0)
-                    for (int s = 0; s < 2; ++s)
-                        tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh2, 128, s), tc::kmajor(sbase + S::g2, 16, s), ID_G2, s > 0);
-                is.complete();
-                float z[ROUTER_OUT];
-                uint32_t zs[ROUTER_OUT / 2];
-                tc::tmem_ld16(lane_addr + T_ACC, z);
-#pragma unroll
-                for (int j = 0; j < ROUTER_OUT / 2; ++j) zs[j] = cvt_pair(z[2 * j], z[2 * j + 1]);
-                // kept for the backward in this row of the DA buffer, which nothing reads before then
-                store_chunk(smem, S::da, t, 0, make_uint4(zs[0], zs[1], zs[2], zs[3]));
-                store_chunk(smem, S::da, t, 1, make_uint4(zs[4], zs[5], zs[6], zs[7]));
-            }
         }
         // ---- decoder hidden 1, hidden 2, output
         uint32_t h1_mask[4], h2_mask[4];
@@ -590,121 +532,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
             for (int q = 0; q < KW; ++q) tc::tmem_ld16(lane_addr + T_ACC + 16 * q, dzf + 16 * q);
         }
         uint32_t gv[PAIRS];
-        if (EXPERTS) {
-            // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
-            const __half2 ph = __float2half2_rn(prob);
-            float dp = 0.0f;
-#pragma unroll
-            for (int p = 0; p < PAIRS; ++p) {
-                const __half2 v = grid_pair(dzf[2 * p], dzf[2 * p + 1]);
-                gv[p] = as_u32(__hmul2_rn(v, ph));
-                dp = __fmaf_rn(__low2float(v), __half2float(lo_half(raw[p])), dp);
-                dp = __fmaf_rn(__high2float(v), __half2float(hi_half(raw[p])), dp);
-            }
-            // ---- logit gradients: softmax of the recomputed fp16 logits over the live experts
-            uint32_t zh[ROUTER_OUT / 2];
-            {
-                const uint4 lo = *reinterpret_cast<const uint4*>(smem + S::da + tc::blocked(TC_TILE, t, 0));
-                const uint4 hi = *reinterpret_cast<const uint4*>(smem + S::da + tc::blocked(TC_TILE, t, 8));
-                zh[0] = lo.x; zh[1] = lo.y; zh[2] = lo.z; zh[3] = lo.w;
-                zh[4] = hi.x; zh[5] = hi.y; zh[6] = hi.z; zh[7] = hi.w;
-            }
-            float z[ROUTER_OUT], zmax = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < ROUTER_OUT; ++j) {
-                z[j] = __half2float((j & 1) ? hi_half(zh[j >> 1]) : lo_half(zh[j >> 1]));  // fp16 logits of the forward
-                if (j < a.experts) zmax = fmaxf(zmax, z[j]);
-            }
-            float sum = 0.0f;
-#pragma unroll
-            for (int j = 0; j < ROUTER_OUT; ++j) {
-                z[j] = j < a.experts ? expf(__fsub_rn(z[j], zmax)) : 0.0f;
-                sum = __fadd_rn(sum, z[j]);
-            }
-            const float dpp = __fmul_rn(dp, prob);
-            const float inv = __frcp_rn(sum);  // p_j = z_j / sum within an ulp; feeds only the fp16 logit gradients
-            float da[ROUTER_OUT];
-#pragma unroll
-            for (int j = 0; j < ROUTER_OUT; j += 2) {
-                const float d0 = __fmul_rn(dpp, __fsub_rn(j == expert ? 1.0f : 0.0f, __fmul_rn(z[j], inv)));
-                const float d1 = __fmul_rn(dpp, __fsub_rn(j + 1 == expert ? 1.0f : 0.0f, __fmul_rn(z[j + 1], inv)));
-                // fp16(fp16(derivative) x 128): the scaling by 2^7 is exact unless it overflows, as in fp16 arithmetic
-                const __half2 h = __hmul2_rn(as_half2(cvt_pair(d0, d1)), __float2half2_rn(128.0f));
-                da[j] = j < a.experts ? __low2float(h) : 0.0f;
-                da[j + 1] = j + 1 < a.experts ? __high2float(h) : 0.0f;
-            }
-            is.wait_dw();  // dWd1 done before the next products are queued
-            store_chunk(smem, S::da, t, 0, pack8(da));
-            store_chunk(smem, S::da, t, 1, pack8(da + 8));
-            // ---- dgh2 = DA Wr3; dWr3^T += GH2^T DA
-            is.before_issue();
-            if (t == 0) {
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, 0), tc::mnmajor(sbase + S::g2, 16, 0),
-                        tc::idesc(128, 32, 0, 1), 0);
-                tc::commit(bar);
-            }
-            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
-                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                    tc::mma(tmem + T_DWG2T, tc::mnmajor(sbase + S::gh2, 128, s), tc::mnmajor(sbase + S::da, 128, s),
-                            tc::idesc(64, 16, 1, 1), 1u);
-                tc::commit(bar_dw);
-            }
-            is.wait_data();
-            masked_pack32(lane_addr + T_ACC, gh2_mask, packed);
-            is.wait_dw();
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
-            // ---- dgh1 = DGH2 Wr2; dWr2 += DGH2^T GH1
-            is.before_issue();
-            if (t == 0) {
-                for (int s = 0; s < 2; ++s)
-                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::r2, 32, s),
-                            tc::idesc(128, 32, 0, 1), s > 0);
-                tc::commit(bar);
-            }
-            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
-                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                    tc::mma(tmem + T_DWR2, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::gh, 128, s),
-                            tc::idesc(64, 32, 1, 1), 1u);
-                tc::commit(bar_dw);
-            }
-            is.wait_data();
-            masked_pack32(lane_addr + T_ACC, gh_mask, packed);
-            is.wait_dw();  // dWr2 has read DGH2: dgh1 may overwrite it
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                store_chunk(smem, S::dgh, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
-            // ---- dR = DGH1 Wr1; dWr1 += DGH1^T R; router grid values half(dR / 128)
-            is.before_issue();
-            if (t == 0) {
-                for (int s = 0; s < 2; ++s)
-                    tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
-                            tc::idesc(128, W, 0, 1), s > 0);
-                tc::commit(bar);
-            }
-            if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
-                for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                    tc::mma(tmem + T_DWG1, tc::mnmajor(sbase + S::dgh, 128, s), tc::mnmajor(sbase + xbuf, 128, s),
-                            tc::idesc(64, W, 1, 1), 1u);
-                tc::commit(bar_dw);
-            }
-            is.wait_data();
-#pragma unroll
-            for (int q = 0; q < KW; ++q) {
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
-                uint32_t rv[8];
-#pragma unroll
-                for (int c = 0; c < 16; c += 2) rv[c / 2] = as_u32(grid_pair(v[c], v[c + 1]));
-                if (valid) {  // row-major [stride][W]: one 32-byte run per 16 columns
-                    uint4* dst = reinterpret_cast<uint4*>(a.router_gvals + i * W + 16 * q);
-                    dst[0] = make_uint4(rv[0], rv[1], rv[2], rv[3]);
-                    dst[1] = make_uint4(rv[4], rv[5], rv[6], rv[7]);
-                }
-            }
-            is.wait_dw();  // dWr1 has read R and DGH1
-        } else if (!ROUTER) {
+        if (!ROUTER) {
             is.wait_dw();  // dWd1 has read X: the next tile may overwrite it
             // grid values without router: half(dz / 128) (runtime.cu:123)
 #pragma unroll
@@ -829,10 +657,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         if (!is.settle()) break;
         dw_accumulate = 1;
         fold_vis(next_tile);
-        if (EXPERTS && TRAIN) xbuf = xbuf == S::x ? S::x2 : S::x;
     }
-    if (EXPERTS && TRAIN) asm volatile("cp.async.wait_all;\n" ::: "memory");  // no copy outlives the block
-
     if (!is.ok) {
         if (t == 0) atomicExch(error_flag, 2);
         // give the products every warp may still have in flight a bounded chance to land before TMEM is released
@@ -841,7 +666,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     }
     if (TRAIN) {
         // ---- weight gradients: TMEM (M=64 layout: rows 16w..16w+15 in lanes 32w..32w+15) -> partials
-        constexpr int GP = ROUTER ? gate_params(W) : EXPERTS ? router_params(W) : 0;
+        constexpr int GP = ROUTER ? gate_params(W) : 0;
         constexpr int P = GP + decoder_params(W);
         float* part = a.partials + (long long)blockIdx.x * P;
         float* dec = part + GP;
@@ -887,46 +712,523 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     for (int c = 0; c < 16; ++c) part[row * W + 16 * q + c] = any ? v[c] : 0.0f;
             }
         }
-        if (EXPERTS) {
-            constexpr int R2 = ROUTER_HIDDEN * W, R3 = R2 + ROUTER_HIDDEN * ROUTER_HIDDEN;
-#pragma unroll
-            for (int q = 0; q < KW; ++q) {  // dWr1 [32][W] from [64 (32 valid)][W]
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_DWG1 + 16 * q, v);
-                if (holds && row < ROUTER_HIDDEN)
-                    for (int c = 0; c < 16; ++c) part[row * W + 16 * q + c] = any ? v[c] : 0.0f;
-            }
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {  // dWr2 [32][32] from [64 (32 valid)][32]
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_DWR2 + 16 * q, v);
-                if (holds && row < ROUTER_HIDDEN)
-                    for (int c = 0; c < 16; ++c) part[R2 + row * ROUTER_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
-            }
-            {  // dWr3 [16][32] from its transpose [64 (32 valid) in][16 out]
-                float v[16];
-                tc::tmem_ld16(lane_addr + T_DWG2T, v);
-                if (holds && row < ROUTER_HIDDEN)
-                    for (int c = 0; c < 16; ++c) part[R3 + c * ROUTER_HIDDEN + row] = any ? v[c] : 0.0f;
-            }
-        }
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
 }
 
-template <int W, int GATE, bool TRAIN, bool UNIFORM>
-void launch_tc(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
-    static unsigned long long configured = 0;
-    constexpr int bytes = (GATE == GATE_EXPERTS && TRAIN) ? TcSmem<W>::total_experts : TcSmem<W>::total;
+// ---------------------------------------------------------------- routed-expert training
+// TMEM columns of routed-expert training: T_ACC, T_DWD2, T_DWD1 and T_DW3T as above, then dWr3
+// [ROUT out][32 in] (M = 64 rows, N = 32) and one M = 64 accumulator holding dWr1 in rows 0-31 and
+// dWr2 in rows 32-63: 240 of the 256 columns, so two CTAs still share an SM.
+constexpr uint32_t T_DWR3 = 176, T_DWR12 = 208;
+static_assert(T_DWR12 + 32 <= TMEM_COLUMNS, "routed-expert accumulators fit the allocation");
+
+// Shared memory (bytes) of routed-expert training, decoder input width 32.  The router backward reuses the
+// decoder's buffers once the decoder's weight-gradient products have read them: dgh1 | zero | dgh2 is one
+// contiguous 96-column stretch, so the 64-column MN-major views [dgh1 | zero] and [zero | dgh2] feed dWr1
+// and dWr2 into the two halves of one M = 64 accumulator (the zero columns add exact zeros to the other half).
+struct ExpertSmem {
+    static constexpr int W = 32, XB = 128 * W * 2;
+    static constexpr int g1 = 0;                    // [32 x 32] router W1
+    static constexpr int r2 = g1 + 32 * W * 2;      // [32 x 32] router W2
+    static constexpr int g2 = r2 + 32 * 32 * 2;     // [64 x 32] router W3 (ROUT rows, blocked for ROUT rows)
+    static constexpr int d1 = g2 + 64 * 32 * 2;     // [64 x 32] decoder W1
+    static constexpr int d2 = d1 + 64 * W * 2;      // [64 x 64]
+    static constexpr int d3 = d2 + 64 * 64 * 2;     // [16 x 64]
+    static constexpr int x = d3 + 16 * 64 * 2;      // [128 x 32] router features, buffer 0
+    static constexpr int x2 = x + XB;               // [128 x 32] router features, buffer 1
+    static constexpr int gh = x2 + XB;              // [128 x 32] router hidden 1
+    static constexpr int gh2 = gh + 8192;           // [128 x 32] router hidden 2
+    static constexpr int h1 = gh2 + 8192;           // [128 x 64] decoder hidden 1, then dh1
+    static constexpr int wx = h1 + 16384;           // [128 x 32] decoder input
+    static constexpr int dy = wx + XB;              // [128 x 16] output gradient
+    static constexpr int h2 = dy + 4096;            // [128 x 64] decoder hidden 2, then dh2
+    static constexpr int dgh1 = h1;                 // [128 x 32] router hidden-1 gradient (router backward)
+    static constexpr int zero = h1 + 8192;          // [128 x 32] zeros (router backward)
+    static constexpr int dgh2 = h1 + 16384;         // [128 x 32] router hidden-2 gradient (router backward)
+    static constexpr int da = h2;                   // [128 x 64] logit gradients, ROUT columns (router backward)
+    static constexpr int bar = h2 + 16384;          // mbarrier: data products of a phase
+    static constexpr int bar_dw = bar + 8;          // mbarrier: weight-gradient products of a phase
+    static constexpr int drain = bar_dw + 8;        // mbarrier: every issuing warp's products (error exit)
+    static constexpr int tmem = drain + 8;          // TMEM base address
+    static constexpr int total = tmem + 8;
+    static_assert(dgh2 == wx && dgh2 + 8192 == dy, "dgh1 | zero | dgh2 is one contiguous stretch ending at dy");
+};
+
+// Routed-expert training step of the heads (no reference counterpart), one CTA per 128-coordinate tile at a
+// time, persistent.  Per tile: router recompute on the tensor cores (GH1 = relu(R Wr1^T), GH2 = relu(GH1
+// Wr2^T); the logits come from router.cu, which chose the expert on the CUDA cores), decoder forward on the
+// gated input fp16(f x fp16(p)), loss gradient, decoder backward, expert values v x fp16(p) with
+// v = fp16(dz / 128) and dp = sum_c v_c f_c, logit gradients dz_j = dp p (delta_je - p_j) over the
+// coordinate's live experts, da = fp16(fp16(dz_j) x 128), router backward down to the router-grid values
+// fp16(dR / 128).  ROUT: router logit rows (16 or 64); LIVE: logits per coordinate as router.cu stores them.
+template <int ROUT, int LIVE>
+__global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpArgs a, int* error_flag) {
+    using S = ExpertSmem;
+    constexpr int W = 32, PAIRS = W / 2, KW = W / 16;
+    static_assert(ROUT == 16 || ROUT == 64, "the router has 16 or 64 logit rows");
+    static_assert(LIVE == 8 || LIVE == 16, "8 or 16 live logits per coordinate");
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int t = threadIdx.x, warp = t >> 5;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
+    uint64_t* bar_dw = reinterpret_cast<uint64_t*>(smem + S::bar_dw);
+    uint64_t* drain = reinterpret_cast<uint64_t*>(smem + S::drain);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
+    const uint32_t sbase = tc::smem_u32(smem);
+
+    stage_blocked(a.gate_w, ROUTER_HIDDEN, W, smem, S::g1);
+    stage_blocked(a.gate_w + ROUTER_HIDDEN * W, ROUTER_HIDDEN, ROUTER_HIDDEN, smem, S::r2);
+    stage_blocked(a.gate_w + ROUTER_HIDDEN * W + ROUTER_HIDDEN * ROUTER_HIDDEN, ROUT, ROUTER_HIDDEN, smem, S::g2);
+    stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
+    if (t == 0) {
+        tc::bar_init(bar, 1);
+        tc::bar_init(bar_dw, TC_THREADS / 32);  // one commit per warp: each warp issues part of every weight-gradient product
+        tc::bar_init(drain, TC_THREADS / 32);
+        tc::fence_bar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, TMEM_COLUMNS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
+    {
+        // the weight-gradient accumulators start at zero; every product accumulates
+        float zero[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) zero[c] = 0.0f;
+        for (uint32_t col = T_DWD2; col < TMEM_COLUMNS; col += 16) tc::tmem_st16(lane_addr + col, zero);
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+    }
+
+    Issuer is{bar, bar_dw};
+    uint32_t dw_accumulate = 0;  // 1 once a tile has added to the weight gradients
+    const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
+    constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
+    const int per = a.per_band;
+
+    // Inputs of a tile (loaded while the previous tile runs its backward products): the routed expert's
+    // feature row, target, probability, expert and the live logits.
+    uint32_t next_raw[PAIRS], next_lg[LIVE / 2];
+    float next_target[3] = {0.0f, 0.0f, 0.0f}, next_prob = 0.0f;
+    int next_expert = 0;
+    auto load_inputs = [&](long long tile) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = tile < tiles && i < a.n;
+#pragma unroll
+        for (int j = 0; j < PAIRS / 4; ++j) {
+            const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.raw) + i * (PAIRS / 4) + j) : make_uint4(0, 0, 0, 0);
+            next_raw[4 * j] = q.x;
+            next_raw[4 * j + 1] = q.y;
+            next_raw[4 * j + 2] = q.z;
+            next_raw[4 * j + 3] = q.w;
+        }
+#pragma unroll
+        for (int j = 0; j < LIVE / 8; ++j) {
+            const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.logits) + i * (LIVE / 8) + j) : make_uint4(0, 0, 0, 0);
+            next_lg[4 * j] = q.x;
+            next_lg[4 * j + 1] = q.y;
+            next_lg[4 * j + 2] = q.z;
+            next_lg[4 * j + 3] = q.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
+        next_prob = valid ? __ldg(a.prob + i) : 0.0f;
+        next_expert = valid ? __ldg(a.expert + i) : 0;
+    };
+    // Router features of a tile (row-major [stride][W]): each row's W halves as W / 8 16-byte cp.async copies
+    // into the blocked layout of shared buffer `buf`.
+    auto prefetch_router = [&](long long tile, int buf) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = tile < tiles && i < a.n;
+        const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
+#pragma unroll
+        for (int j = 0; j < W / 8; ++j)
+            cp_async16(sbase + buf + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
+        cp_async_commit();
+    };
+    load_inputs(blockIdx.x);
+    int xbuf = S::x;  // router features of the current tile (alternates with S::x2)
+    prefetch_router(blockIdx.x, S::x);
+
+    for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = i < a.n;
+        // the other buffer was last read by the previous tile's router weight-gradient product, which has completed
+        prefetch_router(tile + gridDim.x, xbuf == S::x ? S::x2 : S::x);
+        cp_async_wait_older();  // this tile's features have landed
+        uint32_t raw[PAIRS], lg[LIVE / 2];
+#pragma unroll
+        for (int p = 0; p < PAIRS; ++p) raw[p] = next_raw[p];
+#pragma unroll
+        for (int p = 0; p < LIVE / 2; ++p) lg[p] = next_lg[p];
+        const float prob = next_prob, target[3] = {next_target[0], next_target[1], next_target[2]};
+        const int expert = next_expert;
+        const long long next_tile = tile + gridDim.x;
+
+        // ---- decoder input: the routed expert's features x half(p), one rounding per feature
+        {
+            const __half2 ph = __float2half2_rn(prob);
+            uint32_t wx[PAIRS];
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p) wx[p] = as_u32(__hmul2(as_half2(raw[p]), ph));
+#pragma unroll
+            for (int j = 0; j < W / 8; ++j)
+                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+        }
+        // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T)
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
+        is.complete();
+        const uint32_t gh_mask = relu_store32(lane_addr + T_ACC, smem, S::gh, t, 0);
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < 2; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
+        is.complete();
+        const uint32_t gh2_mask = relu_store32(lane_addr + T_ACC, smem, S::gh2, t, 0);
+        // ---- decoder hidden 1, hidden 2, output
+        uint32_t h1_mask[4], h2_mask[4];
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
+        is.complete();
+#pragma unroll
+        for (int q = 0; q < 4; q += 2) {
+            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
+            h1_mask[q] = m & 0xffffu;
+            h1_mask[q + 1] = m >> 16;
+        }
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
+        is.complete();
+#pragma unroll
+        for (int q = 0; q < 4; q += 2) {
+            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
+            h2_mask[q] = m & 0xffffu;
+            h2_mask[q + 1] = m >> 16;
+        }
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
+        is.complete();
+        float out[16];
+        tc::tmem_ld16(lane_addr + T_ACC, out);
+        load_inputs(next_tile);  // prefetch: consumed at the start of the next tile
+        // ---- loss gradient (odie/native/runtime.cu:53-63)
+        {
+            float dy[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) dy[c] = 0.0f;
+            if (valid) {
+                float s = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    const float d = __fsub_rn(__half2float(__float2half_rn(out[c])), target[c]);
+                    s = __fadd_rn(s, __fmul_rn(d, d));
+                    const float scaled = __fmul_rn(__fdiv_rn(__fmul_rn(2.0f, d), a.three_real), 128.0f);
+                    dy[c] = __half2float(__hmul_rn(__float2half_rn(scaled), __float2half_rn(128.0f)));
+                }
+                a.squares[i] = __fdiv_rn(s, 3.0f);
+            }
+            store_chunk(smem, S::dy, t, 0, pack8(dy));
+            store_chunk(smem, S::dy, t, 1, pack8(dy + 8));
+        }
+        uint32_t packed[32];
+        // ---- dh2 = DY Wd3 (B: Wd3 as MN-major); dW3^T += H2^T DY
+        is.before_issue();
+        if (t == 0) {
+            tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0),
+                    tc::idesc(128, 64, 0, 1), 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::dy, 128, s),
+                        tc::idesc(64, 16, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+#pragma unroll
+        for (int q = 0; q < 4; q += 2)
+            masked_pack32(lane_addr + T_ACC + 16 * q, h2_mask[q] | (h2_mask[q + 1] << 16), packed + 8 * q);
+        is.wait_dw();  // dW3 has read H2: dh2 may overwrite it
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            store_chunk(smem, S::h2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        // ---- dh1 = DH2 Wd2; dWd2 += DH2^T H1
+        is.before_issue();
+        if (t == 0) {
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s),
+                        tc::idesc(128, 64, 0, 1), s > 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::h1, 128, s),
+                        tc::idesc(64, 64, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+#pragma unroll
+        for (int q = 0; q < 4; q += 2)
+            masked_pack32(lane_addr + T_ACC + 16 * q, h1_mask[q] | (h1_mask[q + 1] << 16), packed + 8 * q);
+        is.wait_dw();  // dWd2 has read H1: dh1 may overwrite it
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            store_chunk(smem, S::h1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        // ---- dz = DH1 Wd1; dWd1 += DH1^T WX
+        is.before_issue();
+        if (t == 0) {
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s),
+                        tc::idesc(128, W, 0, 1), s > 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::wx, 128, s),
+                        tc::idesc(64, W, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+        float dzf[W];
+        tc::tmem_ld32(lane_addr + T_ACC, dzf);
+        // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
+        uint32_t gv[PAIRS];
+        float dp = 0.0f;
+        {
+            const __half2 ph = __float2half2_rn(prob);
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p) {
+                const __half2 v = grid_pair(dzf[2 * p], dzf[2 * p + 1]);
+                gv[p] = as_u32(__hmul2_rn(v, ph));
+                dp = __fmaf_rn(__low2float(v), __half2float(lo_half(raw[p])), dp);
+                dp = __fmaf_rn(__high2float(v), __half2float(hi_half(raw[p])), dp);
+            }
+        }
+        // ---- logit gradients: softmax of the router's fp16 logits over the coordinate's live experts
+        const int choice = expert % per;          // the chosen expert within its band
+        const int lo = (a.first_band + expert / per) * per;  // the band's first logit column
+        float da[LIVE];
+        {
+            float z[LIVE], zmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < LIVE; ++j) {
+                z[j] = __half2float((j & 1) ? hi_half(lg[j >> 1]) : lo_half(lg[j >> 1]));
+                if (j < per) zmax = fmaxf(zmax, z[j]);
+            }
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < LIVE; ++j) {
+                z[j] = j < per ? expf(__fsub_rn(z[j], zmax)) : 0.0f;
+                sum = __fadd_rn(sum, z[j]);
+            }
+            const float dpp = __fmul_rn(dp, prob);
+            const float inv = __frcp_rn(sum);  // p_j = z_j / sum within an ulp; feeds only the fp16 logit gradients
+#pragma unroll
+            for (int j = 0; j < LIVE; j += 2) {
+                const float d0 = __fmul_rn(dpp, __fsub_rn(j == choice ? 1.0f : 0.0f, __fmul_rn(z[j], inv)));
+                const float d1 = __fmul_rn(dpp, __fsub_rn(j + 1 == choice ? 1.0f : 0.0f, __fmul_rn(z[j + 1], inv)));
+                // fp16(fp16(derivative) x 128): the scaling by 2^7 is exact unless it overflows, as in fp16 arithmetic
+                const __half2 h = __hmul2_rn(as_half2(cvt_pair(d0, d1)), __float2half2_rn(128.0f));
+                da[j] = j < per ? __low2float(h) : 0.0f;
+                da[j + 1] = j + 1 < per ? __high2float(h) : 0.0f;
+            }
+        }
+        is.wait_dw();  // dWd1 has read WX and DH1: h1, wx, dy and h2 are free for the router backward
+        // DA row: the live gradients at the band's columns, zeros elsewhere; and this row of the zero block
+        {
+            const uint4 zero4 = make_uint4(0, 0, 0, 0);
+            const uint4 first = pack8(da), second = LIVE == 16 ? pack8(da + 8) : zero4;
+#pragma unroll
+            for (int c = 0; c < ROUT / 8; ++c)
+                store_chunk(smem, S::da, t, c, 8 * c == lo ? first : (LIVE == 16 && 8 * c == lo + 8) ? second : zero4);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) store_chunk(smem, S::zero, t, c, zero4);
+        }
+        // ---- dgh2 = DA Wr3; dWr3 += DA^T GH2 (M = 64: rows past ROUT are never read)
+        is.before_issue();
+        if (t == 0) {
+            for (int s = 0; s < ROUT / 16; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, s), tc::mnmajor(sbase + S::g2, ROUT, s),
+                        tc::idesc(128, 32, 0, 1), s > 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DWR3, tc::mnmajor(sbase + S::da, 128, s), tc::mnmajor(sbase + S::gh2, 128, s),
+                        tc::idesc(64, 32, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+        masked_pack32(lane_addr + T_ACC, gh2_mask, packed);
+        is.wait_dw();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            store_chunk(smem, S::dgh2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        // ---- dgh1 = DGH2 Wr2; dWr2 (accumulator rows 32-63) += DGH2^T GH1 through the [zero | dgh2] view
+        is.before_issue();
+        if (t == 0) {
+            for (int s = 0; s < 2; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh2, 128, s), tc::mnmajor(sbase + S::r2, 32, s),
+                        tc::idesc(128, 32, 0, 1), s > 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DWR12, tc::mnmajor(sbase + S::zero, 128, s), tc::mnmajor(sbase + S::gh, 128, s),
+                        tc::idesc(64, 32, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+        masked_pack32(lane_addr + T_ACC, gh_mask, packed);
+        is.wait_dw();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            store_chunk(smem, S::dgh1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        // ---- dR = DGH1 Wr1; dWr1 (accumulator rows 0-31) += DGH1^T R through the [dgh1 | zero] view;
+        //      router grid values half(dR / 128)
+        is.before_issue();
+        if (t == 0) {
+            for (int s = 0; s < 2; ++s)
+                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh1, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
+                        tc::idesc(128, W, 0, 1), s > 0);
+            tc::commit(bar);
+        }
+        if ((t & 31) == 0) {
+            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
+                tc::mma(tmem + T_DWR12, tc::mnmajor(sbase + S::dgh1, 128, s), tc::mnmajor(sbase + xbuf, 128, s),
+                        tc::idesc(64, W, 1, 1), 1u);
+            tc::commit(bar_dw);
+        }
+        is.wait_data();
+#pragma unroll
+        for (int q = 0; q < KW; ++q) {
+            float v[16];
+            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
+            uint32_t rv[8];
+#pragma unroll
+            for (int c = 0; c < 16; c += 2) rv[c / 2] = as_u32(grid_pair(v[c], v[c + 1]));
+            if (valid) {  // row-major [stride][W]: one 32-byte run per 16 columns
+                uint4* dst = reinterpret_cast<uint4*>(a.router_gvals + i * W + 16 * q);
+                dst[0] = make_uint4(rv[0], rv[1], rv[2], rv[3]);
+                dst[1] = make_uint4(rv[4], rv[5], rv[6], rv[7]);
+            }
+        }
+        is.wait_dw();  // dWr1 has read R and DGH1
+        if (valid) {
+#pragma unroll
+            for (int j = 0; j < PAIRS / 4; ++j)  // row-major [stride][W]: the coordinate's values in 16-byte runs
+                reinterpret_cast<uint4*>(a.gvals + i * W)[j] = make_uint4(gv[4 * j], gv[4 * j + 1], gv[4 * j + 2], gv[4 * j + 3]);
+        }
+        if (!is.settle()) break;
+        dw_accumulate = 1;
+        xbuf = xbuf == S::x ? S::x2 : S::x;
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");  // no copy outlives the block
+
+    if (!is.ok) {
+        if (t == 0) atomicExch(error_flag, 2);
+        // give the products every warp may still have in flight a bounded chance to land before TMEM is released
+        if ((t & 31) == 0) tc::commit(drain);
+        tc::bar_wait(drain, 0, WAIT_LIMIT);
+    }
+    // ---- weight gradients: TMEM (M=64 layout: rows 16w..16w+15 in lanes 32w..32w+15) -> partials
+    constexpr int GP = router_params(W, ROUT), R2 = ROUTER_HIDDEN * W, R3 = R2 + ROUTER_HIDDEN * ROUTER_HIDDEN;
+    constexpr int P = GP + decoder_params(W);
+    float* part = a.partials + (long long)blockIdx.x * P;
+    float* dec = part + GP;
+    const int row = 16 * warp + (t & 31);
+    const bool holds = (t & 31) < 16;
+    const bool any = dw_accumulate && is.ok;
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // dWd2 [64][64]
+        float v[16];
+        tc::tmem_ld16(lane_addr + T_DWD2 + 16 * q, v);
+        if (holds)
+            for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + row * DEC_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < KW; ++q) {  // dWd1 [64][W]
+        float v[16];
+        tc::tmem_ld16(lane_addr + T_DWD1 + 16 * q, v);
+        if (holds)
+            for (int c = 0; c < 16; ++c) dec[row * W + 16 * q + c] = any ? v[c] : 0.0f;
+    }
+    {  // dW3 [16][64] from its transpose [64 in][16 out]
+        float v[16];
+        tc::tmem_ld16(lane_addr + T_DW3T, v);
+        if (holds)
+            for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN + c * DEC_HIDDEN + row] = any ? v[c] : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // dWr1 [32][W] (rows 0-31) and dWr2 [32][32] (rows 32-63)
+        float v[16];
+        tc::tmem_ld16(lane_addr + T_DWR12 + 16 * q, v);
+        if (holds) {
+            float* dst = row < ROUTER_HIDDEN ? part + row * W : part + R2 + (row - ROUTER_HIDDEN) * ROUTER_HIDDEN;
+            for (int c = 0; c < 16; ++c) dst[16 * q + c] = any ? v[c] : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // dWr3 [ROUT][32]
+        float v[16];
+        tc::tmem_ld16(lane_addr + T_DWR3 + 16 * q, v);
+        if (holds && row < ROUT)
+            for (int c = 0; c < 16; ++c) part[R3 + row * ROUTER_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
+}
+
+// cudaFuncSetAttribute once per kernel and device (devices 0..63).
+template <typename Kernel>
+void set_smem(Kernel kernel, int bytes, std::atomic<unsigned long long>& configured) {
     int device = 0;
     ODIE_CUDA(cudaGetDevice(&device));
-    if (!(configured >> device & 1ull)) {
-        ODIE_CUDA(cudaFuncSetAttribute(mlp_tc_kernel<W, GATE, TRAIN, UNIFORM>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-        configured |= 1ull << device;
+    ODIE_REQUIRE(device >= 0 && device < 64, "the fused heads support devices 0..63");
+    if (!(configured.load(std::memory_order_acquire) >> device & 1ull)) {
+        ODIE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        configured.fetch_or(1ull << device, std::memory_order_acq_rel);
     }
+}
+
+template <int ROUT, int LIVE>
+void launch_experts(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
+    static std::atomic<unsigned long long> configured{0};
+    set_smem(experts_train_kernel<ROUT, LIVE>, ExpertSmem::total, configured);
+    experts_train_kernel<ROUT, LIVE><<<blocks, TC_THREADS, ExpertSmem::total, stream>>>(a, error_flag);
+    note_launch();
+}
+
+template <int W, int GATE, bool TRAIN, bool UNIFORM>
+void launch_tc(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
+    static std::atomic<unsigned long long> configured{0};
+    constexpr int bytes = TcSmem<W>::total;
+    set_smem(mlp_tc_kernel<W, GATE, TRAIN, UNIFORM>, bytes, configured);
     mlp_tc_kernel<W, GATE, TRAIN, UNIFORM><<<blocks, TC_THREADS, bytes, stream>>>(a, error_flag);
     note_launch();
 }
@@ -937,10 +1239,20 @@ void dispatch(const MlpArgs& a, int width, GateMode gate, bool uniform, int bloc
     if (width == WV && gate == G && uniform == U) return launch_tc<WV, G, TRAIN, U>(a, blocks, error_flag, stream);
     ODIE_TC(32, GATE_LEVELS, true) ODIE_TC(32, GATE_LEVELS, false) ODIE_TC(32, GATE_NONE, true) ODIE_TC(32, GATE_NONE, false)
     ODIE_TC(16, GATE_LEVELS, true) ODIE_TC(16, GATE_LEVELS, false) ODIE_TC(16, GATE_NONE, true) ODIE_TC(16, GATE_NONE, false)
-    // routed experts: no per-level epilogue, so the column layout does not matter
-    if (gate == GATE_EXPERTS && width == 32) return launch_tc<32, GATE_EXPERTS, TRAIN, true>(a, blocks, error_flag, stream);
-    if (gate == GATE_EXPERTS && width == 16) return launch_tc<16, GATE_EXPERTS, TRAIN, true>(a, blocks, error_flag, stream);
 #undef ODIE_TC
+    if (gate == GATE_EXPERTS) {
+        ODIE_REQUIRE(width == 32, "routed experts take 32 input features");
+        if (!TRAIN) return launch_tc<32, GATE_EXPERTS, false, true>(a, blocks, error_flag, stream);
+        const Banding b{a.model_experts / a.per_band, a.first_band, a.per_band, 2};
+        check_banding(b, a.experts);
+        ODIE_REQUIRE(a.logits && (a.live == 8 || a.live == 16) && a.live >= a.per_band,
+                     "routed-expert training needs the router's logits rows (8 or 16 halves, at least per band)");
+        const bool wide = router_out(a.model_experts) == ROUTER_MAX_OUT;
+        if (wide && a.live == 8) return launch_experts<64, 8>(a, blocks, error_flag, stream);
+        if (wide) return launch_experts<64, 16>(a, blocks, error_flag, stream);
+        if (a.live == 8) return launch_experts<16, 8>(a, blocks, error_flag, stream);
+        return launch_experts<16, 16>(a, blocks, error_flag, stream);
+    }
     throw std::invalid_argument("the fused heads take 16 or 32 input features");
 }
 

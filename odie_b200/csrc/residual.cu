@@ -102,8 +102,8 @@ void launch_score_chunk(const float* prediction, const void* target, long long b
 
 void launch_tile_scores(const float* prediction, const uint8_t* target, int height, int width, int tile, double* row_sums,
                         double* scores, cudaStream_t stream) {
-    const int tiles = ((width + tile - 1) / tile) * ((height + tile - 1) / tile);
-    tile_rows_kernel<<<tiles, 256, 0, stream>>>(prediction, target, height, width, tile, row_sums);
+    const long long tiles = (((long long)width + tile - 1) / tile) * (((long long)height + tile - 1) / tile);
+    tile_rows_kernel<<<unsigned(tiles), 256, 0, stream>>>(prediction, target, height, width, tile, row_sums);
     tile_sum_kernel<<<blocks_for(tiles, 256), 256, 0, stream>>>(row_sums, tiles, tile, scores);
     note_launch(2);
 }
@@ -125,14 +125,20 @@ static __device__ __align__(256) double g_noalloc_row_sums[NOALLOC_TILE_ROWS];
 long long noalloc_tile_rows_max() { return NOALLOC_TILE_ROWS; }
 
 // Device address of the scratch for the current device, resolved once per device
-// (host code must not pass the symbol itself: it is a host-side stand-in).
+// (host code must not pass the symbol itself: it is a host-side stand-in).  The
+// cached address belongs to the device's current context: it does not survive a
+// cudaDeviceReset of that device, after which this library must not be called on it.
 double* noalloc_row_sums(std::string& error) {
     static std::mutex lock;
     static double* address[64] = {nullptr};
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
-    if (status != cudaSuccess || device < 0 || device >= 64) {
+    if (status != cudaSuccess) {
         error = std::string("cudaGetDevice: ") + cudaGetErrorString(status);
+        return nullptr;
+    }
+    if (device < 0 || device >= 64) {
+        error = "device " + std::to_string(device) + " is beyond the 64 devices this entry point serves";
         return nullptr;
     }
     std::lock_guard<std::mutex> guard(lock);

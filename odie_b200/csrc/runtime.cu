@@ -102,6 +102,12 @@ struct Runtime {
     int router_levels = 0, router_width = 0;
     LevelTable router_table{};
     float* router_grid = nullptr;  // caller-owned fp32 master of the router grid
+    Banding banding;               // spatial expert ownership (router.cuh)
+    int live = 16;                 // router logits kept per coordinate for the heads' backward
+    RowFrame frame;                // this image's rows within the full image (coordinates are the full image's)
+    // Caller-owned router-grid gradient (data-parallel training: the router grid is shared, its gradient is
+    // summed across ranks before its update, which then runs in step_heads); null: library-owned.
+    float* external_router_grad = nullptr;
     double lr[3] = {1e-2, 1e-3, 1e-3};  // grid, gate, decoder
     double uploaded_lr[3] = {-1.0, -1.0, -1.0};  // the rates the device step tables hold (-1: none yet)
     // caller-owned
@@ -131,10 +137,12 @@ struct Runtime {
     DeviceArray<float> router_grad, router_m, router_v, prob;
     DeviceArray<uint32_t> router_steps;
     DeviceArray<int> expert_ids;
+    DeviceArray<__half> logits;
     std::vector<double> host_bc1, host_bc2;
     int partial_blocks = 0;
 
     float* head_grad() { return external_head_grad ? external_head_grad : head_grad_own.ptr; }
+    float* router_gradient() { return external_router_grad ? external_router_grad : router_grad.ptr; }
     GateMode gate_mode() const { return experts ? GATE_EXPERTS : router ? GATE_LEVELS : GATE_NONE; }
 
     explicit Runtime(const Json& j) {
@@ -153,6 +161,11 @@ struct Runtime {
         gate_k = int(j.value("gate_k", 0));
         softplus = j.value("softplus", 0) != 0;
         rgb8 = j.value("rgb8", 1) != 0;
+        // the full image's rows (coordinates y = (row_offset + row) / (full_height - 1)); default: this image
+        frame.row0 = int(j.value("row_offset", 0));
+        frame.rows = int(j.value("full_height", image_height));
+        ODIE_REQUIRE(frame.row0 >= 0 && frame.rows >= 2 && (long long)frame.row0 + image_height <= frame.rows,
+                     "row_offset + height must not exceed full_height");
         ODIE_REQUIRE(total > 0 && total <= 0x7fffffffLL, "total must fit int32 addressing");
         ODIE_REQUIRE(image_width >= 2 && image_height >= 2, "image axes must be >= 2");
         ODIE_REQUIRE(capacity >= 1 && capacity <= (1LL << 26), "batch capacity must be in [1, 2^26]");
@@ -164,8 +177,15 @@ struct Runtime {
         hash_mode = j.contains("hash_encoding");
         experts = int(j.value("experts", 0));
         if (experts) {
-            ODIE_REQUIRE(experts >= 1 && experts <= ROUTER_OUT, "experts must be within 1..16");
+            ODIE_REQUIRE(experts >= 1 && experts <= ROUTER_MAX_OUT, "experts must be within 1..64");
             ODIE_REQUIRE(hash_mode && j.contains("router_encoding"), "routed experts need hash_encoding and router_encoding");
+            banding.bands = int(j.value("bands", 1));
+            banding.first_band = int(j.value("first_band", 0));
+            banding.per_band = int(j.value("experts_per_band", experts));
+            banding.rows = frame.rows;
+            check_banding(banding, experts);
+            live = banding.per_band <= 8 ? 8 : 16;
+            if (j.contains("router_grad")) external_router_grad = pointer_of<float>(j, "router_grad");
             router = false;
             gate_master = pointer_of<float>(j, "gate");
             router_grid = pointer_of<float>(j, "router_grid");
@@ -175,7 +195,8 @@ struct Runtime {
         }
         if (hash_mode) build_hash_table(j.at("hash_encoding"));
         else levels = int(j.value("levels", 16));
-        if (experts) ODIE_REQUIRE(router_width == input_width, "router and expert encodings must have the same width");
+        if (experts) ODIE_REQUIRE(router_width == input_width && input_width == 32,
+                                  "router and expert encodings must both give 32 features");
         ODIE_REQUIRE(levels >= 2 && levels <= 16, "the fused heads support 2..16 levels");
         ODIE_REQUIRE(gate_k >= 0 && gate_k <= levels, "gate_k outside [0, levels]");
         active = levels;
@@ -194,7 +215,8 @@ struct Runtime {
             ODIE_CUDA(cudaMemcpy(table_bc2.ptr, bc2.data(), TABLE_STEPS * sizeof(float), cudaMemcpyHostToDevice));
         }
         configure(j);
-        gate_count = router ? gate_params(input_width) : experts ? router_params(input_width) : 0;
+        gate_count = router ? gate_params(input_width)
+                            : experts ? router_params(input_width, router_out(banding.model_experts())) : 0;
         decoder_count = decoder_params(input_width);
         head_count = gate_count + decoder_count;
         // library-owned buffers
@@ -230,6 +252,10 @@ struct Runtime {
             router_gvals.allocate((long long)router_width * capacity);
             prob.allocate(capacity);
             expert_ids.allocate(capacity);
+            logits.allocate((long long)live * capacity);
+            logits.zero(stream);
+            if (external_router_grad)
+                ODIE_CUDA(cudaMemsetAsync(external_router_grad, 0, size_t(router_total) * sizeof(float), stream));
             for (auto* a : {&router_grad, &router_m, &router_v, &prob}) a->zero(stream);
             router_steps.zero(stream);
             router_in.zero(stream);
@@ -425,6 +451,11 @@ struct Runtime {
         m.router_gvals = router_gvals.ptr;
         m.experts = experts;
         m.raw_rows = experts != 0;
+        m.logits = logits.ptr;
+        m.live = live;
+        m.per_band = banding.per_band;
+        m.first_band = banding.first_band;
+        m.model_experts = banding.model_experts();
         return m;
     }
 
@@ -454,8 +485,12 @@ struct Runtime {
         ra.n = n;
         ra.weights = head_half.ptr;
         ra.experts = experts;
+        ra.banding = banding;
+        ra.xy = xy.ptr;
         ra.expert = expert_ids.ptr;
         ra.prob = prob.ptr;
+        ra.logits = logits.ptr;
+        ra.live = live;
         slot = stage_begin(S_ROUTER);
         launch_router_forward(ra, router_width, stream);
         stage_end(slot);
@@ -477,11 +512,14 @@ struct Runtime {
                                                          "encode_backward", "reduce_partials", "adam_grid", "adam_heads"};
     static constexpr int EVENT_PAIRS = 4096;
     bool profiling = false;
+    bool serial = false;  // profiling with both branches of the step on one stream: stage times are kernel times
     std::vector<cudaEvent_t> events;            // 2 per recorded stage launch
     std::vector<int> event_stage;
     int recorded = 0;
 
-    void profile(bool enable) {
+    void profile(int mode) {
+        const bool enable = mode != 0;
+        serial = mode == 2;
         ODIE_CUDA(cudaStreamSynchronize(stream));
         if (enable && events.empty()) {
             events.resize(2 * EVENT_PAIRS);
@@ -529,10 +567,10 @@ struct Runtime {
         ODIE_REQUIRE(n > 0 && n <= capacity, "invalid batch size for this runtime");
         int slot = stage_begin(S_INPUT);
         if (sampled)
-            launch_stratified_batch(sampled->seed, sampled->step, n, rgb, rgb8, image_width, image_height, xy.ptr,
+            launch_stratified_batch(sampled->seed, sampled->step, n, rgb, rgb8, image_width, image_height, frame, xy.ptr,
                                     target.ptr, stream);
         else
-            launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, xy.ptr, target.ptr, stream);
+            launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, frame, xy.ptr, target.ptr, stream);
         stage_end(slot);
         LevelSource src;
         src.table = table;
@@ -557,18 +595,21 @@ struct Runtime {
             // Two branches that meet before the heads' update: the router-grid scatter, the head-gradient
             // reduction and the router grid's Adam on the side stream; the expert-table scatter and the
             // expert tables' Adam on the runtime's stream.  Stage timers run on each branch's own stream.
+            // the side branch runs on the main stream when profiling serially
+            cudaStream_t side = (profiling && serial) ? stream : this->side;
             ODIE_CUDA(cudaEventRecord(fork_event, stream));
             ODIE_CUDA(cudaStreamWaitEvent(side, fork_event, 0));
             LevelSource rsrc;
             rsrc.table = router_table;
             EncodeArgs ra = router_encode_args(n);  // row-major gradient values too
             slot = stage_begin(S_ENCODE_BWD, side);
-            launch_encode_backward(ra, rsrc, router_gvals.ptr, router_grad.ptr, side);
+            launch_encode_backward(ra, rsrc, router_gvals.ptr, router_gradient(), side);
             stage_end(slot, side);
             slot = stage_begin(S_REDUCE, side);
             launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);  // needs only the heads kernel
             stage_end(slot, side);
-            if (update == 1) {
+            // a shared router grid (caller-owned gradient) is updated in step_heads, after its gradient is summed
+            if (update == 1 && !external_router_grad) {
                 slot = stage_begin(S_ADAM_GRID, side);
                 adam_router_grid(side);
                 stage_end(slot, side);
@@ -594,7 +635,7 @@ struct Runtime {
         }
         if (update == 0) {
             launch_zero(grid_grad.ptr, total, stream);
-            if (experts) launch_zero(router_grad.ptr, router_total, stream);
+            if (experts) launch_zero(router_gradient(), router_total, stream);
         }
         // update == 2 keeps the grid gradient for inspection; grid_update() consumes it
         ODIE_CUDA(cudaGetLastError());
@@ -608,7 +649,7 @@ struct Runtime {
     }
     void adam_router_grid(cudaStream_t on) {
         AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
-        launch_adam(router_grid, router_half.ptr, router_m.ptr, router_v.ptr, router_steps.ptr, router_grad.ptr,
+        launch_adam(router_grid, router_half.ptr, router_m.ptr, router_v.ptr, router_steps.ptr, router_gradient(),
                     router_total, 1.0f / 128.0f, t, float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS),
                     true, error_flag.ptr, on);
     }
@@ -616,13 +657,19 @@ struct Runtime {
     void grid_update() {
         const int slot = stage_begin(S_ADAM_GRID);
         adam_expert_tables();
-        if (experts) adam_router_grid(stream);
+        if (experts && !external_router_grad) adam_router_grid(stream);  // a shared router grid: in step_heads
         stage_end(slot);
         ODIE_CUDA(cudaGetLastError());
     }
 
     void step_heads(bool update) {
         if (!update) return;
+        if (experts && external_router_grad) {
+            // the shared router grid: its summed gradient is ready once the caller's reduction has run
+            const int grid_slot = stage_begin(S_ADAM_GRID);
+            adam_router_grid(stream);
+            stage_end(grid_slot);
+        }
         const int slot = stage_begin(S_ADAM_HEADS);
         // head gradients carry the 128 x 128 loss scale (odie/native/runtime.cu:59,300-309)
         const float inv = 1.0f / 16384.0f;
@@ -648,7 +695,7 @@ struct Runtime {
         src.table = table;
         for (long long done = 0; done < n; done += capacity) {
             const long long count = std::min(capacity, n - done);
-            launch_coords_range(begin + done, count, image_width, image_height, xy.ptr, stream);
+            launch_coords_range(begin + done, count, image_width, image_height, frame, xy.ptr, stream);
             if (experts) {
                 route_and_encode(count);
             } else {
@@ -680,7 +727,8 @@ struct Runtime {
           << ",\"head_v\":" << (unsigned long long)head_v.ptr << ",\"head_steps\":" << (unsigned long long)head_steps.ptr
           << ",\"experts\":" << experts << ",\"expert_total\":" << expert_total << ",\"router_total\":" << router_total
           << ",\"router_width\":" << router_width << ",\"router_half\":" << (unsigned long long)router_half.ptr
-          << ",\"router_grad\":" << (unsigned long long)router_grad.ptr << ",\"router_in\":" << (unsigned long long)router_in.ptr
+          << ",\"router_grad\":" << (unsigned long long)router_gradient() << ",\"logits\":" << (unsigned long long)logits.ptr
+          << ",\"live\":" << live << ",\"side_stream\":" << (unsigned long long)side << ",\"router_in\":" << (unsigned long long)router_in.ptr
           << ",\"router_gvals\":" << (unsigned long long)router_gvals.ptr << ",\"prob\":" << (unsigned long long)prob.ptr
           << ",\"expert_ids\":" << (unsigned long long)expert_ids.ptr << ",\"router_m\":" << (unsigned long long)router_m.ptr
           << ",\"router_v\":" << (unsigned long long)router_v.ptr << ",\"router_steps\":" << (unsigned long long)router_steps.ptr
@@ -842,7 +890,10 @@ int odie_grid_update(void* handle) {
 }
 
 int odie_profile(void* handle, int enable) {
-    return guarded([&] { static_cast<Runtime*>(handle)->profile(enable != 0); });
+    return guarded([&] {
+        ODIE_REQUIRE(enable >= 0 && enable <= 2, "odie_profile: 0 off, 1 on, 2 on with the step's branches serialised");
+        static_cast<Runtime*>(handle)->profile(enable);
+    });
 }
 
 const char* odie_profile_report(void* handle) {
@@ -988,8 +1039,9 @@ int odie_hash_backward(const float* coords, int64_t n, const uint16_t* upstream,
     });
 }
 
-int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
-                        int32_t* expert, float* prob, uint16_t* logits, uint64_t stream) {
+int odie_router_forward_banded(const uint16_t* features, const float* xy, int64_t n, int width, const uint16_t* weights,
+                               int experts, int bands, int first_band, int experts_per_band, int rows, int32_t* expert,
+                               float* prob, uint16_t* logits, int live, uint64_t stream) {
     return guarded([&] {
         ODIE_REQUIRE(n >= 0, "negative coordinate count");
         odie::RouterArgs a;
@@ -999,12 +1051,25 @@ int odie_router_forward(const uint16_t* features, int64_t n, int width, const ui
         a.n = n;
         a.weights = reinterpret_cast<const __half*>(weights);
         a.experts = experts;
+        a.banding = odie::Banding{bands, first_band, experts_per_band, rows};
+        a.xy = xy;
         a.expert = expert;
         a.prob = prob;
         a.logits = reinterpret_cast<__half*>(logits);
+        a.live = live;
         odie::launch_router_forward(a, width, reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
+}
+
+int odie_router_forward(const uint16_t* features, int64_t n, int width, const uint16_t* weights, int experts,
+                        int32_t* expert, float* prob, uint16_t* logits, uint64_t stream) {
+    if (experts < 1 || experts > 16) {
+        odie::set_error("odie_router_forward: experts must be within 1..16 (odie_router_forward_banded takes up to 64)");
+        return -1;
+    }
+    return odie_router_forward_banded(features, nullptr, n, width, weights, experts, 1, 0, experts, 2, expert, prob,
+                                      logits, 16, stream);
 }
 
 int odie_expert_hash_forward(const float* coords, int64_t n, const float* tables, int64_t expert_stride,
@@ -1117,13 +1182,49 @@ int selection_chunk(const double* scores, int n, int points, int resolution, int
                                         reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// Tiles of a height x width image cut into tile x tile squares (edge tiles partial), or -1 with a message
+// when the arguments are invalid.  Widened to 64 bits before any sum, so no tile size overflows.
+long long tile_count(const char* who, int height, int width, int tile, int k) {
+    if (height < 1 || width < 1 || tile < 1 || k < 0) {
+        odie::set_error(std::string(who) + ": height, width and tile must be >= 1 and k >= 0");
+        return -1;
+    }
+    if (tile > std::max(height, width)) {
+        odie::set_error(std::string(who) + ": tile must not exceed the image's larger side");
+        return -1;
+    }
+    const long long tiles = (((long long)width + tile - 1) / tile) * (((long long)height + tile - 1) / tile);
+    if (tiles > 0x7fffffffLL || (long long)tile * tiles > (1LL << 40)) {
+        odie::set_error(std::string(who) + ": too many tiles");
+        return -1;
+    }
+    if (k > tiles) {
+        odie::set_error(std::string(who) + ": k = " + std::to_string(k) + " exceeds the " + std::to_string(tiles) +
+                        " tiles");
+        return -1;
+    }
+    return tiles;
+}
+}  // namespace
+
 int odie_tile_topk(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
                    double* row_sums, double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (height < 1 || width < 1 || tile < 1 || k < 0) return int(cudaErrorInvalidValue);
+    const long long tiles = tile_count("odie_tile_topk", height, width, tile, k);
+    if (tiles < 0) return int(cudaErrorInvalidValue);
     odie::launch_tile_scores(prediction, target, height, width, tile, row_sums, scores, s);
-    const int tiles = ((width + tile - 1) / tile) * ((height + tile - 1) / tile);
-    odie::launch_topk(scores, tiles, k, reinterpret_cast<long long*>(chosen), selected, s);
+    odie::launch_topk(scores, int(tiles), k, reinterpret_cast<long long*>(chosen), selected, s);
+    return int(cudaGetLastError());
+}
+
+int odie_topk(const double* scores, int count, int k, int64_t* chosen, uint8_t* selected, uint64_t stream) {
+    if (count < 0 || k < 0 || k > count) {
+        odie::set_error("odie_topk: need 0 <= k <= count");
+        return int(cudaErrorInvalidValue);
+    }
+    odie::launch_topk(scores, count, k, reinterpret_cast<long long*>(chosen), selected,
+                      reinterpret_cast<cudaStream_t>(stream));
     return int(cudaGetLastError());
 }
 
@@ -1134,11 +1235,8 @@ int odie_tile_topk(const float* prediction, const uint8_t* target, int height, i
 // array instead (size limit checked here, before anything is launched).
 int odie_tile_topk_noalloc(const float* prediction, const uint8_t* target, int height, int width, int tile, int k,
                            double* scores, int64_t* chosen, uint8_t* selected, uint64_t stream) {
-    if (height < 1 || width < 1 || tile < 1 || k < 0) {
-        odie::set_error("odie_tile_topk_noalloc: height, width and tile must be >= 1 and k >= 0");
-        return int(cudaErrorInvalidValue);
-    }
-    const long long tiles = (long long)((width + tile - 1) / tile) * ((height + tile - 1) / tile);
+    const long long tiles = tile_count("odie_tile_topk_noalloc", height, width, tile, k);
+    if (tiles < 0) return int(cudaErrorInvalidValue);
     if (tiles * tile > odie::noalloc_tile_rows_max()) {
         odie::set_error("odie_tile_topk_noalloc: tiles x tile = " + std::to_string(tiles * tile) +
                         " row sums exceed the fixed scratch of " + std::to_string(odie::noalloc_tile_rows_max()));

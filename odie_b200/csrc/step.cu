@@ -5,17 +5,21 @@ namespace odie {
 
 namespace {
 
+// Coordinates of local pixel id: fp32(column) * fp32(1 / (W - 1)), the reciprocal in double rounded to
+// fp32 (odie/native/runtime.cu:34-36); the row is the full image's, row0 + id / W, over its rows.
+__device__ __forceinline__ float2 coords_of(uint32_t id, int width, RowFrame frame) {
+    const float rx = float(1.0 / double(width - 1)), ry = float(1.0 / double(frame.rows - 1));
+    return make_float2(__fmul_rn(float(id % uint32_t(width)), rx),
+                       __fmul_rn(float(uint32_t(frame.row0) + id / uint32_t(width)), ry));
+}
+
 // Coordinates and target of pixel id for batch slot i.
 __device__ __forceinline__ void input_of(long long i, uint32_t id, const uint8_t* __restrict__ rgb, bool rgb8, int width,
-                                         int height, float* __restrict__ xy, float* __restrict__ target) {
+                                         int height, RowFrame frame, float* __restrict__ xy, float* __restrict__ target) {
     // an id outside the image (never produced by the samplers) reads pixel 0
     // instead of memory outside the target
     if ((unsigned long long)id >= (unsigned long long)width * (unsigned long long)height) id = 0;
-    // fp32(id % W) * fp32(1 / (W - 1)): the reciprocal in double rounded to fp32
-    // (odie/native/runtime.cu:34-36).
-    const float rx = float(1.0 / double(width - 1)), ry = float(1.0 / double(height - 1));
-    reinterpret_cast<float2*>(xy)[i] = make_float2(__fmul_rn(float(id % uint32_t(width)), rx),
-                                                   __fmul_rn(float(id / uint32_t(width)), ry));
+    reinterpret_cast<float2*>(xy)[i] = coords_of(id, width, frame);
     if (target) {
         for (int c = 0; c < 3; ++c)
             target[3 * i + c] = rgb8 ? __fmul_rn(float(rgb[3ull * id + c]), 1.0f / 255.0f)
@@ -24,10 +28,13 @@ __device__ __forceinline__ void input_of(long long i, uint32_t id, const uint8_t
 }
 
 __global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n, const uint8_t* __restrict__ rgb,
-                                   bool rgb8, int width, int height, float* __restrict__ xy, float* __restrict__ target) {
+                                   bool rgb8, int width, int height, RowFrame frame, float* __restrict__ xy,
+                                   float* __restrict__ target) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    input_of(i, uint32_t(ids[i]), rgb, rgb8, width, height, xy, target);
+    const int64_t id = ids[i];
+    // ids outside [0, 2^32) become an out-of-image id (pixel 0) instead of wrapping
+    input_of(i, (id < 0 || id > 0xffffffffLL) ? 0xffffffffu : uint32_t(id), rgb, rgb8, width, height, frame, xy, target);
 }
 
 // Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011):
@@ -76,18 +83,16 @@ __global__ void stratified_ids_kernel(uint64_t seed, uint64_t step, int side_log
 // The step's input stage with the sampler fused in: stratified id -> coordinates and target.
 __global__ void stratified_batch_kernel(uint64_t seed, uint64_t step, int side_log2, long long n,
                                         const uint8_t* __restrict__ rgb, bool rgb8, int width, int height,
-                                        float* __restrict__ xy, float* __restrict__ target) {
+                                        RowFrame frame, float* __restrict__ xy, float* __restrict__ target) {
     const long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (j < n) input_of(j, stratified_id(seed, step, j, side_log2, width, height), rgb, rgb8, width, height, xy, target);
+    if (j < n)
+        input_of(j, stratified_id(seed, step, j, side_log2, width, height), rgb, rgb8, width, height, frame, xy, target);
 }
 
-__global__ void coords_range_kernel(long long begin, long long n, int width, int height, float* __restrict__ xy) {
+__global__ void coords_range_kernel(long long begin, long long n, int width, RowFrame frame, float* __restrict__ xy) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const uint32_t id = uint32_t(begin + i);
-    const float rx = float(1.0 / double(width - 1)), ry = float(1.0 / double(height - 1));
-    reinterpret_cast<float2*>(xy)[i] = make_float2(__fmul_rn(float(id % uint32_t(width)), rx),
-                                                   __fmul_rn(float(id / uint32_t(width)), ry));
+    reinterpret_cast<float2*>(xy)[i] = coords_of(uint32_t(begin + i), width, frame);
 }
 
 // Sum of the per-CTA partials of every head parameter, in a fixed order (deterministic): a block
@@ -205,10 +210,18 @@ __global__ void cast_half_kernel(const float* __restrict__ in, __half* __restric
 
 }  // namespace
 
+static RowFrame frame_of(RowFrame frame, int height) {
+    if (frame.rows <= 0) frame = RowFrame{0, height};
+    ODIE_REQUIRE(frame.row0 >= 0 && frame.rows >= 2 && (long long)frame.row0 + height <= frame.rows,
+                 "the local rows must lie within the full image");
+    return frame;
+}
+
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
-                        float* xy, float* target, cudaStream_t stream) {
+                        RowFrame frame, float* xy, float* target, cudaStream_t stream) {
     if (n <= 0) return;
-    input_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(ids, n, rgb, rgb8, width, height, xy, target);
+    frame = frame_of(frame, height);
+    input_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(ids, n, rgb, rgb8, width, height, frame, xy, target);
     note_launch();
 }
 
@@ -231,16 +244,19 @@ void launch_stratified_ids(uint64_t seed, uint64_t step, int width, int height, 
 }
 
 void launch_stratified_batch(uint64_t seed, uint64_t step, long long n, const uint8_t* rgb, bool rgb8, int width,
-                             int height, float* xy, float* target, cudaStream_t stream) {
+                             int height, RowFrame frame, float* xy, float* target, cudaStream_t stream) {
     const int side_log2 = stratified_side_log2(n);
+    frame = frame_of(frame, height);
     stratified_batch_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(seed, step, side_log2, n, rgb, rgb8, width, height,
-                                                                    xy, target);
+                                                                    frame, xy, target);
     note_launch();
 }
 
-void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream) {
+void launch_coords_range(long long begin, long long n, int width, int height, RowFrame frame, float* xy,
+                         cudaStream_t stream) {
     if (n <= 0) return;
-    coords_range_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(begin, n, width, height, xy);
+    frame = frame_of(frame, height);
+    coords_range_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(begin, n, width, frame, xy);
     note_launch();
 }
 

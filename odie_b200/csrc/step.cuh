@@ -45,7 +45,13 @@ struct MlpArgs {
     const float* prob;        // [n] router probability of the chosen expert
     const int* expert;        // [n] chosen expert
     __half* router_gvals;     // [stride][W] router-grid gradient values, row-major (training)
-    int experts;              // live experts
+    int experts;              // expert tables held here
+    const __half* logits;     // [stride][live] fp16 logits of each coordinate's live experts (training)
+    int live;                 // logits row width: 8 or 16
+    // spatial expert ownership (router.cuh Banding): a coordinate's live logit columns are
+    // [band * per_band, (band + 1) * per_band) with band = first_band + expert / per_band
+    int per_band, first_band;
+    int model_experts;        // experts of the whole model (the router's logit rows before padding)
 };
 
 // tcgen05/TMEM fused heads (mlp_tc.cu), decoder input width 16 or 32.  uniform:
@@ -58,15 +64,21 @@ void launch_mlp_tc_train(const MlpArgs& args, int width, GateMode gate, bool uni
 void launch_mlp_tc_decode(const MlpArgs& args, int width, GateMode gate, bool uniform, int* error_flag,
                           cudaStream_t stream);
 
+// Image rows seen by the coordinates: the local image (height rows) is rows [row0, row0 + height) of a full
+// image of `rows` rows, and y = (row0 + local row) / (rows - 1) (row0 = 0, rows = height: the whole image).
+struct RowFrame {
+    int row0 = 0, rows = 0;
+};
 void launch_input_batch(const int64_t* ids, long long n, const uint8_t* rgb, bool rgb8, int width, int height,
-                        float* xy, float* target, cudaStream_t stream);
-void launch_coords_range(long long begin, long long n, int width, int height, float* xy, cudaStream_t stream);
+                        RowFrame frame, float* xy, float* target, cudaStream_t stream);
+void launch_coords_range(long long begin, long long n, int width, int height, RowFrame frame, float* xy,
+                         cudaStream_t stream);
 // Stratified pixel ids (the reference's sampler, odie/data.py:63-80, on a Philox4x32-10 stream keyed by
 // seed, counter (slot, step)); n a square power of two.  The batch variant fuses the step's input stage.
 void launch_stratified_ids(uint64_t seed, uint64_t step, int width, int height, long long n, int64_t* ids,
                            cudaStream_t stream);
 void launch_stratified_batch(uint64_t seed, uint64_t step, long long n, const uint8_t* rgb, bool rgb8, int width,
-                             int height, float* xy, float* target, cudaStream_t stream);
+                             int height, RowFrame frame, float* xy, float* target, cudaStream_t stream);
 
 // Sum of the per-block weight-gradient partials in block order (deterministic).
 void launch_reduce_partials(const float* partials, int blocks, int count, float* out, cudaStream_t stream);

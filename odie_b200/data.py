@@ -156,3 +156,18 @@ def synthetic_image(config, seed=1729, device='cpu'):
     else:
         raise ValueError('unknown synthetic config ' + str(config))
     return to_u8(image).reshape(-1, 3), (h, w)
+
+
+def procedural_image(shape, seed=1729, row0=0, rows=None, device='cuda'):
+    """Rows [row0, row0 + rows) of the seeded procedural image of `shape` (odie_procedural_image: fractal
+    1/f^2 noise, sharp-edged Voronoi regions, a 64 x 64-cell texture atlas) as a CUDA u8 [rows * W, 3]
+    tensor.  The gigapixel benchmark's stand-in: every pixel depends only on (seed, column, row, shape), so
+    each rank draws exactly its own band of one image."""
+    from . import _lib
+    height, width = shape
+    rows = height - row0 if rows is None else rows
+    out = torch.empty((rows * width, 3), dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream()
+    _lib.check(_lib.library().odie_procedural_image(int(seed), width, height, row0, rows, out.data_ptr(),
+                                                     stream.cuda_stream), 'odie_procedural_image')
+    return out

@@ -57,68 +57,97 @@ def cell_bitmap(support, resolution):
 
 
 def check_gate_k(config):
+    """The number of leading levels the gate leaves at weight 1 (must equal coarse_levels)."""
     k = int(config.get('gate_coarse_levels_K', config['coarse_levels']))
-    if not 0 <= k <= int(config['n_levels']) or int(config['coarse_levels']) != k:
-        raise ValueError('Gate K must agree with coarse_levels and remain within declared level count')
+    if int(config['coarse_levels']) != k or not 0 <= k <= int(config['n_levels']):
+        raise ValueError(f'gate K = {k} must equal coarse_levels and lie within 0..n_levels')
     return k
 
 
-def make_layout(config, supports, plane_dims, plane_node_caps):
-    """Descriptors and index tables of all planes (odie/model.py:64-118)."""
-    resolutions = [int(r) for r in config['resolutions']]
+def _check_plan(config, supports, plane_dims, plane_node_caps):
+    """The planes configuration this layout can express: one support, feature count and node cap per level."""
     levels = int(config['n_levels'])
-    if not (len(resolutions) == len(supports) == len(plane_dims) == len(plane_node_caps) == levels):
-        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
-    if any(f not in (1, 2, 4) for f in plane_dims):
-        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
+    lengths = {len(config['resolutions']), len(supports), len(plane_dims), len(plane_node_caps)}
+    if lengths != {levels}:
+        raise ValueError(f'resolutions, supports, feature counts and node caps must each list {levels} levels')
+    if any(int(f) not in (1, 2, 4) for f in plane_dims):
+        raise ValueError('every level holds 1, 2 or 4 features per node')
     if config['representation'] != 'xy_planes':
-        raise ValueError('XY-only representation is required')
-    check_gate_k(config)
+        raise ValueError('a packed-plane layout needs the xy_planes representation')
     if config['gate_topology'] != 'shared' or config['gate_position'] != 'feature':
-        raise ValueError('Preserve the shared feature gate')
-    initial = int(config['initial_active_prefix'])
-    descriptors, bitmaps, node_words, prefixes, info, clean = [], [], [], [], [], []
-    params = column = word_offset = byte_offset = 0
-    for level in range(levels):
-        r, dim, cap, support = resolutions[level], int(plane_dims[level]), int(plane_node_caps[level]), supports[level]
-        if support.device.type != 'cpu' or support.dtype != torch.bool or tuple(support.shape) != (r * r,):
-            raise ValueError('Support must be a flat CPU bool R^2 tensor')
-        if level < initial and not bool(support.all()):
-            raise ValueError('Declared initial full-cover supports must remain full')
+        raise ValueError('the gate is one shared MLP applied to the features')
+    check_gate_k(config)
+
+
+class _Packer:
+    """Running offsets of the packed layout: parameters, feature columns, node-index words, cell-bitmap bytes."""
+
+    def __init__(self):
+        self.params = self.column = self.words = self.cell_bytes = 0
+        self.rows, self.node_words, self.prefixes, self.cell_maps, self.levels, self.supports = [], [], [], [], [], []
+
+    def add(self, level, resolution, dim, cap, support, must_be_full):
+        """A level whose support is a CPU bool tensor: closure, node index and cell bitmap built on the host."""
+        if support.device.type != 'cpu' or support.dtype != torch.bool or tuple(support.shape) != (resolution ** 2,):
+            raise ValueError(f'level {level}: a support is a flat CPU bool tensor of R^2 = {resolution ** 2} cells')
+        if must_be_full and not bool(support.all()):
+            raise ValueError(f'level {level} is one of the initial levels and must cover every cell')
         support = support.clone()
-        points = align8(r * r)
-        nodes = plane_closure(support.numpy(), r)
-        if cap % 8 or not nodes.numel() <= cap <= points:
-            raise ValueError('Aligned node capacity must contain the complete interpolation closure')
-        if points > INT32_MAX or params + cap * dim > INT32_MAX:
-            raise ValueError('Native points and packed offsets must fit int32 addressing')
-        direct = nodes.numel() == points
-        if direct:
-            word_start = -1
-            words = 0
-        else:
-            bits, prefix = make_node_index(nodes, points)
-            word_start, words = word_offset, bits.numel()
-            node_words.append(bits)
-            prefixes.append(prefix)
-            word_offset += words
-        bitmap = cell_bitmap(support.numpy(), r)
-        descriptors.append([r, points, params, word_start, byte_offset, dim, column, int(direct)])
-        info.append({'level': level, 'resolution': r, 'plane_dim': dim, 'allowed_cells': int(support.sum()),
-                     'plane_retained_nodes': nodes.numel(), 'plane_node_capacity': cap,
-                     'plane_unused_slots': cap - nodes.numel(), 'native_plane_points': points,
-                     'plane_offset': params, 'feature_offset': column, 'nodes': nodes,
-                     'node_index_words': words, 'direct_node_access': direct})
-        bitmaps.append(bitmap)
-        clean.append(support)
-        params += cap * dim
-        column += dim
-        byte_offset += bitmap.numel()
-    return {'descriptors': torch.tensor(descriptors, dtype=torch.int32),
-            'node_bitmap': torch.cat(node_words) if node_words else torch.empty(0, dtype=torch.uint64),
-            'node_prefix': torch.cat(prefixes) if prefixes else torch.empty(0, dtype=torch.int32),
-            'bitmap': torch.cat(bitmaps), 'levels': info, 'supports': clean,
-            'params': params, 'input_width': column}
+        points = align8(resolution * resolution)
+        nodes = plane_closure(support.numpy(), resolution)
+        index = make_node_index(nodes, points) if nodes.numel() != points else None
+        self.place(level, resolution, dim, cap, support, nodes, nodes.numel(), int(support.sum()), index,
+                   cell_bitmap(support.numpy(), resolution))
+
+    def place(self, level, resolution, dim, cap, support, nodes, count, allowed, index, cells):
+        """Append one level: its descriptor row, node index (None for a full plane) and cell bitmap."""
+        points = align8(resolution * resolution)
+        if cap % 8 or not count <= cap <= points:
+            raise ValueError(f'level {level}: node cap {cap} must be a multiple of 8 between the closure '
+                             f'({count} nodes) and the plane ({points})')
+        if points > INT32_MAX or self.params + cap * dim > INT32_MAX:
+            raise ValueError(f'level {level}: the layout outgrows int32 offsets')
+        direct = count == points  # a full plane needs no node index
+        word_start, words = -1, 0
+        if not direct:
+            bits, prefix = index
+            word_start, words = self.words, bits.numel()
+            self.node_words.append(bits)
+            self.prefixes.append(prefix)
+            self.words += words
+        self.rows.append([resolution, points, self.params, word_start, self.cell_bytes, dim, self.column, int(direct)])
+        self.levels.append({'level': level, 'resolution': resolution, 'plane_dim': dim, 'allowed_cells': allowed,
+                            'plane_retained_nodes': count, 'plane_node_capacity': cap,
+                            'plane_unused_slots': cap - count, 'native_plane_points': points,
+                            'plane_offset': self.params, 'feature_offset': self.column, 'nodes': nodes,
+                            'node_index_words': words, 'direct_node_access': direct})
+        self.cell_maps.append(cells)
+        self.supports.append(support)
+        self.params += cap * dim
+        self.column += dim
+        self.cell_bytes += cells.numel()
+
+    def tables(self):
+        def joined(parts, dtype):
+            return torch.cat(parts) if parts else torch.empty(0, dtype=dtype)
+        device = self.cell_maps[0].device if self.cell_maps else 'cpu'
+        return {'descriptors': torch.tensor(self.rows, dtype=torch.int32, device=device),
+                'node_bitmap': joined(self.node_words, torch.uint64), 'node_prefix': joined(self.prefixes, torch.int32),
+                'bitmap': torch.cat(self.cell_maps), 'levels': self.levels, 'supports': self.supports,
+                'params': self.params, 'input_width': self.column}
+
+
+def make_layout(config, supports, plane_dims, plane_node_caps):
+    """Descriptor rows and index tables of every plane, built on the host (the contract of odie/model.py:64-118):
+    levels packed in order, each holding cap x F parameters, its features at the next columns, its node index
+    words and cell-bitmap bytes appended after the previous level's."""
+    _check_plan(config, supports, plane_dims, plane_node_caps)
+    initial = int(config['initial_active_prefix'])
+    packer = _Packer()
+    for level, (resolution, dim, cap, support) in enumerate(zip(config['resolutions'], plane_dims, plane_node_caps,
+                                                                 supports)):
+        packer.add(level, int(resolution), int(dim), int(cap), support, level < initial)
+    return packer.tables()
 
 
 def float32(value):
@@ -181,65 +210,24 @@ def plane_index_device(support, resolution, with_nodes=True, stream=None):
 
 
 def make_layout_device(config, supports, plane_dims, plane_node_caps):
-    """make_layout with the per-level closure, node index and cell bitmap built on the GPU.
+    """make_layout with every level's closure, node index and cell bitmap built on the GPU (odie_plane_index).
 
-    supports: CUDA bool [R^2] tensors.  Same validation and the same tables as make_layout (device tensors; the
-    'nodes' entries are device int64 tensors); one host synchronisation reads all levels' node counts."""
+    supports: CUDA bool [R^2] tensors.  Same checks and the same tables as make_layout, as device tensors (the
+    'nodes' entries are device int64 tensors); one host synchronisation reads every level's node count."""
+    _check_plan(config, supports, plane_dims, plane_node_caps)
     resolutions = [int(r) for r in config['resolutions']]
-    levels = int(config['n_levels'])
-    if not (len(resolutions) == len(supports) == len(plane_dims) == len(plane_node_caps) == levels):
-        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
-    if any(f not in (1, 2, 4) for f in plane_dims):
-        raise ValueError('Require aligned level descriptors and F1/F2/F4 features')
-    if config['representation'] != 'xy_planes':
-        raise ValueError('XY-only representation is required')
-    check_gate_k(config)
-    if config['gate_topology'] != 'shared' or config['gate_position'] != 'feature':
-        raise ValueError('Preserve the shared feature gate')
-    initial = int(config['initial_active_prefix'])
     built = []
-    for level in range(levels):
-        r, support = resolutions[level], supports[level]
+    for level, (r, support) in enumerate(zip(resolutions, supports)):
         if not support.is_cuda or support.dtype != torch.bool or tuple(support.shape) != (r * r,):
-            raise ValueError('Support must be a flat CUDA bool R^2 tensor')
+            raise ValueError(f'level {level}: a support is a flat CUDA bool tensor of R^2 = {r * r} cells')
         built.append(plane_index_device(support, r))
-    counts = torch.stack([b[3] for b in built]).cpu().tolist()
-    full = torch.stack([s.all() for s in supports]).cpu().tolist()
-    allowed = torch.stack([s.sum() for s in supports]).cpu().tolist()
-    descriptors, bitmaps, node_words, prefixes, info, clean = [], [], [], [], [], []
-    params = column = word_offset = byte_offset = 0
-    for level in range(levels):
-        r, dim, cap = resolutions[level], int(plane_dims[level]), int(plane_node_caps[level])
-        if level < initial and not full[level]:
-            raise ValueError('Declared initial full-cover supports must remain full')
-        points = align8(r * r)
-        count = int(counts[level])
-        if cap % 8 or not count <= cap <= points:
-            raise ValueError('Aligned node capacity must contain the complete interpolation closure')
-        if points > INT32_MAX or params + cap * dim > INT32_MAX:
-            raise ValueError('Native points and packed offsets must fit int32 addressing')
-        bits, prefix, bitmap, _, nodes = built[level]
-        direct = count == points
-        if direct:
-            word_start, words = -1, 0
-        else:
-            word_start, words = word_offset, bits.numel()
-            node_words.append(bits)
-            prefixes.append(prefix)
-            word_offset += words
-        descriptors.append([r, points, params, word_start, byte_offset, dim, column, int(direct)])
-        info.append({'level': level, 'resolution': r, 'plane_dim': dim, 'allowed_cells': int(allowed[level]),
-                     'plane_retained_nodes': count, 'plane_node_capacity': cap, 'plane_unused_slots': cap - count,
-                     'native_plane_points': points, 'plane_offset': params, 'feature_offset': column,
-                     'nodes': nodes[:count], 'node_index_words': words, 'direct_node_access': direct})
-        bitmaps.append(bitmap)
-        clean.append(supports[level].clone())
-        params += cap * dim
-        column += dim
-        byte_offset += bitmap.numel()
-    device = supports[0].device
-    return {'descriptors': torch.tensor(descriptors, dtype=torch.int32, device=device),
-            'node_bitmap': torch.cat(node_words) if node_words else torch.empty(0, dtype=torch.uint64, device=device),
-            'node_prefix': torch.cat(prefixes) if prefixes else torch.empty(0, dtype=torch.int32, device=device),
-            'bitmap': torch.cat(bitmaps), 'levels': info, 'supports': clean,
-            'params': params, 'input_width': column}
+    summary = torch.stack([torch.stack((b[3], s.sum(), s.all().long())) for b, s in zip(built, supports)]).cpu().tolist()
+    initial = int(config['initial_active_prefix'])
+    packer = _Packer()
+    for level, (r, dim, cap, support, (bits, prefix, cells, _, nodes), (count, allowed, full)) in enumerate(
+            zip(resolutions, plane_dims, plane_node_caps, supports, built, summary)):
+        if level < initial and not full:
+            raise ValueError(f'level {level} is one of the initial levels and must cover every cell')
+        packer.place(level, r, int(dim), int(cap), support.clone(), nodes[:count], int(count), int(allowed),
+                     (bits, prefix), cells)
+    return packer.tables()

@@ -11,6 +11,7 @@ decoder: W1, W2, W3), the layout the fused training kernel reads.
 from copy import deepcopy
 import math
 
+import numpy as np
 import torch
 from torch import nn
 
@@ -134,17 +135,34 @@ class ExpertHashQuery(torch.autograd.Function):
         return None, gradient, None, None, None, None, None
 
 
-def route(features, router_weights16, experts):
-    """Top-1 routing: (expert int32 [N], probability fp32 [N], fp16 logits [N, 16]), bit-exact (router.cu)."""
+def router_out(model_experts):
+    """Logit rows of the router MLP: 16 for up to 16 experts, 64 for up to 64."""
+    if not 1 <= model_experts <= 64:
+        raise ValueError('the router takes 1..64 experts')
+    return 16 if model_experts <= 16 else 64
+
+
+def route(features, router_weights16, experts, xy=None, banding=None):
+    """Top-1 routing, bit-exact (router.cu): (expert int32 [N], probability fp32 [N], fp16 live logits [N, live]).
+
+    Without banding every coordinate chooses among `experts`.  banding (dict: bands, first_band, per_band,
+    rows): spatial expert ownership -- the coordinate (xy, CUDA fp32 [N, 2]) of global row y chooses among the
+    experts of band floor(y * bands / rows); `experts` is then the number held (local numbering)."""
     features = features.to(torch.float16).contiguous()
     n, width = features.shape
+    b = banding or dict(bands=1, first_band=0, per_band=int(experts), rows=2)
+    live = 8 if b['per_band'] <= 8 else 16
     expert = torch.empty(n, dtype=torch.int32, device=features.device)
     prob = torch.empty(n, dtype=torch.float32, device=features.device)
-    logits = torch.empty((n, 16), dtype=torch.float16, device=features.device)
+    logits = torch.empty((n, live), dtype=torch.float16, device=features.device)
     weights = router_weights16.to(torch.float16).contiguous()
-    _lib.check(_lib.library().odie_router_forward(features.data_ptr(), n, width, weights.data_ptr(), int(experts),
-                                                  expert.data_ptr(), prob.data_ptr(), logits.data_ptr(), _stream()),
-               'odie_router_forward')
+    xy = None if xy is None else xy.to(torch.float32).contiguous()
+    if b['bands'] > 1 and xy is None:
+        raise ValueError('banded routing needs the coordinates')
+    _lib.check(_lib.library().odie_router_forward_banded(
+        features.data_ptr(), _lib.ptr(xy), n, width, weights.data_ptr(), int(experts), int(b['bands']),
+        int(b['first_band']), int(b['per_band']), int(b['rows']), expert.data_ptr(), prob.data_ptr(),
+        logits.data_ptr(), live, _stream()), 'odie_router_forward_banded')
     return expert, prob, logits
 
 
@@ -187,166 +205,193 @@ class Head(nn.Module):
         return h
 
 
+def plane_seed(seed, level):
+    """Seed of level `level`'s first-opening draw: the reference's per-level seed for its F = 2 branch
+    ((seed + 1000003 (level + 1)) + 104729 * 3 mod 2^31, odie/model.py:208-224); a seeding contract, so that
+    a plane opened here starts from the same values."""
+    return ((seed + 1000003 * (level + 1)) % 2**31 + 104729 * 3) % 2**31
+
+
 class PackedXYPlanes(nn.Module):
-    """Packed multiresolution planes with a shared per-level gate and decoder (odie/model.py:154-314)."""
+    """Packed multiresolution planes behind a shared per-level gate and decoder: the module the reference's
+    training loop drives (odie/model.py:154-314).
+
+    Storage: one flat fp32 `grid`, level after level, each level holding the rows of its closure nodes
+    (all nodes of a full level).  Index buffers (descriptors, node bitmap words, prefixes, cell bitmap) live on
+    the device and are rebuilt there when a level opens (make_layout_device).  The heads are the fully fused
+    MLP shapes (Head).  forward(coordinates) is the evaluation path; training runs in the native runtime."""
+
+    BUFFERS = ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap')
 
     def __init__(self, config, supports, plane_dims, plane_node_caps, axis_mode='none', kernel_a=0.,
                  kernel_omega=1.5 * math.pi):
         super().__init__()
         if axis_mode != 'none' or kernel_a != 0.:
-            raise ValueError('No axis branches or non-linear interpolation kernel in this ablation')
+            raise ValueError('only the plain planes (no axis branches, bilinear kernel) are built here')
         self.config = deepcopy(config)
+        self.n_levels = int(config['n_levels'])
         self.router_enabled = config.get('router_enabled', True)
         self.gate_coarse_levels_K = check_gate_k(config)
-        self.layout = make_layout(config, supports, plane_dims, plane_node_caps)
-        self.supports = self.layout['supports']
         self.plane_dims, self.plane_node_caps = list(plane_dims), list(plane_node_caps)
-        self.input_width = self.layout['input_width']
-        self.n_levels = int(config['n_levels'])
+        layout = make_layout(config, supports, plane_dims, plane_node_caps)
+        self.input_width = layout['input_width']
         device = torch.device('cuda')
-        seed = int(config['seed'])
-        self.grid = nn.Parameter(torch.zeros(self.layout['params'], dtype=torch.float32, device=device))
+        self.grid = nn.Parameter(torch.zeros(layout['params'], dtype=torch.float32, device=device))
         self.initialized_planes = [False] * self.n_levels
+        self._install(layout, device)
         with torch.no_grad():
-            for level, item in enumerate(self.layout['levels']):
-                if item['nodes'].numel():
+            for level, entry in enumerate(self.layout['levels']):
+                if entry['nodes'].numel():
                     self._initialize_plane(level)
-        for name in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap'):
-            self.register_buffer(name, self.layout[name].to(device), persistent=False)
-        for name in ('node_bitmap', 'node_prefix', 'bitmap'):
-            self.layout.pop(name)
-        feature_levels = [level for level, dim in enumerate(plane_dims) for _ in range(dim)]
-        self.register_buffer('feature_levels', torch.tensor(feature_levels, dtype=torch.int64, device=device),
+        column_level = torch.tensor([l for l, dim in enumerate(plane_dims) for _ in range(dim)], dtype=torch.int64)
+        self.register_buffer('feature_levels', column_level.to(device), persistent=False)
+        self.register_buffer('level_active', torch.ones(self.n_levels, dtype=torch.bool, device=device),
                              persistent=False)
-        self.register_buffer('level_active', torch.ones(self.n_levels, dtype=torch.bool, device=device), persistent=False)
         self.register_buffer('feature_active', torch.ones(self.input_width, dtype=torch.float16, device=device),
                              persistent=False)
         self.active_prefix = self.n_levels
-        self.gate = (Head(self.input_width, self.n_levels, 32, 1, (seed + 2000003) % 2**31)
-                     if self.router_enabled else None)
+        seed = int(config['seed'])
+        self.gate = Head(self.input_width, self.n_levels, 32, 1, (seed + 2000003) % 2**31) if self.router_enabled else None
         self.decoder = Head(self.input_width, 3, 64, 2, (seed + 4000037) % 2**31)
-        gate_count = self.gate.params.numel() if self.gate is not None else 0
-        if gate_count != config['gate_parameters'] or self.decoder.params.numel() != config['decoder_parameters']:
-            raise RuntimeError('Unexpected head allocation for the configured input width')
+        counts = (self.gate.params.numel() if self.gate is not None else 0, self.decoder.params.numel())
+        if counts != (config['gate_parameters'], config['decoder_parameters']):
+            raise RuntimeError(f'head parameters {counts} differ from the configured '
+                               f'{(config["gate_parameters"], config["decoder_parameters"])}')
+
+    def _install(self, layout, device):
+        """Adopt a layout: its index tensors become device buffers, the rest stays in self.layout."""
+        for name in self.BUFFERS:
+            tensor = layout.pop(name).to(device)
+            if name in self._buffers:
+                setattr(self, name, tensor)
+            else:
+                self.register_buffer(name, tensor, persistent=False)
+        layout['supports'] = [support.cpu() for support in layout['supports']]
+        self.layout, self.supports = layout, layout['supports']
 
     def query_features(self, coordinates):
-        if coordinates.dtype != torch.float32 or coordinates.ndim != 2 or coordinates.shape[1] != 2 or \
-                coordinates.requires_grad:
-            raise ValueError('Coordinates must be FP32 Nx2, without coordinate gradients')
+        """fp16 features [N, input_width] and visibility [N, L] of fp32 coordinates [N, 2] (PackedQuery)."""
+        if coordinates.dtype != torch.float32 or coordinates.ndim != 2 or coordinates.shape[1] != 2:
+            raise ValueError(f'coordinates must be fp32 [N, 2], got {coordinates.dtype} {tuple(coordinates.shape)}')
+        if coordinates.requires_grad:
+            raise ValueError('the planes take no gradient with respect to the coordinates')
         return PackedQuery.apply(coordinates.contiguous(), self.grid, self.descriptors, self.node_bitmap,
                                  self.node_prefix, self.bitmap, self.input_width)
 
     @torch.no_grad()
     def _initialize_plane(self, level):
-        """Seeded N(0, std) draw over the dense plane, gathered at the retained nodes (odie/model.py:208-224)."""
+        """First opening of a level: N(0, feature_init_std) over the whole native plane ([points, max(2, F)], drawn
+        with torch's CUDA generator at plane_seed), kept at the closure nodes only."""
         if self.initialized_planes[level]:
-            raise RuntimeError('Each plane must be initialized exactly once')
-        item = self.layout['levels'][level]
-        level_seed = (self.config['seed'] + 1000003 * (level + 1)) % (2**31)
-        branch_seed = (level_seed + 104729 * 3) % (2**31)
-        generator = torch.Generator(device=self.grid.device).manual_seed(branch_seed)
-        dense = torch.empty((item['native_plane_points'], max(2, item['plane_dim'])), dtype=torch.float32,
-                            device=self.grid.device)
-        dense.normal_(0., self.config['feature_init_std'], generator=generator)
-        values = dense.index_select(0, item['nodes'].to(self.grid.device))[:, :item['plane_dim']].reshape(-1)
-        self.grid[item['plane_offset']:item['plane_offset'] + values.numel()].copy_(values)
+            raise RuntimeError(f'level {level} was already initialised')
+        entry = self.layout['levels'][level]
+        device = self.grid.device
+        draw = torch.empty((entry['native_plane_points'], max(2, entry['plane_dim'])), dtype=torch.float32,
+                           device=device)
+        draw.normal_(0., self.config['feature_init_std'],
+                     generator=torch.Generator(device=device).manual_seed(plane_seed(self.config['seed'], level)))
+        kept = draw.index_select(0, entry['nodes'].to(device))[:, :entry['plane_dim']].reshape(-1)
+        self.grid[entry['plane_offset']:entry['plane_offset'] + kept.numel()].copy_(kept)
         self.initialized_planes[level] = True
+
+    def _check_new_support(self, level, support):
+        resolution = self.config['resolutions'][level]
+        if level != self.active_prefix or not 2 <= level < self.n_levels:
+            raise ValueError(f'level {level} is not the next level to open (active prefix {self.active_prefix})')
+        if self.initialized_planes[level] or bool(self.supports[level].any()):
+            raise RuntimeError(f'level {level} is open already')
+        if support.device.type != 'cpu' or support.dtype != torch.bool or tuple(support.shape) != (resolution**2,):
+            raise ValueError(f'a support is a flat CPU bool tensor of R^2 = {resolution**2} cells')
+        nodes = int(plane_index_device(support.to(self.grid.device), resolution, with_nodes=False)[3])
+        if not 0 < nodes <= self.plane_node_caps[level]:
+            raise ValueError(f'the support closes over {nodes} nodes; level {level} takes 1..{self.plane_node_caps[level]}')
 
     @torch.no_grad()
     def activate_support(self, level, support):
-        """Open the next plane on a selected support without moving storage (odie/model.py:226-257)."""
-        if level != self.active_prefix or not 2 <= level < self.n_levels:
-            raise ValueError('Select the next unopened plane before advancing the prefix')
-        if self.initialized_planes[level] or bool(self.supports[level].any()):
-            raise RuntimeError('An opened support cannot be replaced or initialized again')
-        resolution = self.config['resolutions'][level]
-        if support.device.type != 'cpu' or support.dtype != torch.bool or tuple(support.shape) != (resolution**2,):
-            raise ValueError('New support must be a flat CPU bool R^2 tensor')
-        device = self.grid.device
-        count = int(plane_index_device(support.to(device), resolution, with_nodes=False)[3])
-        if not 0 < count <= self.plane_node_caps[level]:
-            raise ValueError('New support requires a nonempty complete closure within its cap')
-        storage = self.grid.data_ptr()
-        supports = list(self.supports)
-        supports[level] = support.clone()
-        # every level's closure, node index and cell bitmap rebuilt on the GPU (odie_plane_index)
-        layout = make_layout_device(self.config, [s.to(device) for s in supports], self.plane_dims,
-                                    self.plane_node_caps)
-        nodes = layout['levels'][level]['nodes']
-        for name in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap'):
-            setattr(self, name, layout.pop(name))
-        layout['supports'] = [s.cpu() for s in layout['supports']]
-        self.layout, self.supports = layout, layout['supports']
+        """Open `level` on the chosen cells: every level's index rebuilt on the GPU, the grid storage kept in place,
+        the new level's rows drawn once.  Returns the activation report."""
+        self._check_new_support(level, support)
+        device, storage = self.grid.device, self.grid.data_ptr()
+        supports = [s.to(device) for s in self.supports]
+        supports[level] = support.to(device)
+        self._install(make_layout_device(self.config, supports, self.plane_dims, self.plane_node_caps), device)
         self._initialize_plane(level)
         if self.grid.data_ptr() != storage:
-            raise AssertionError('Packed storage changed during plane activation')
-        points = layout['levels'][level]['native_plane_points']
+            raise AssertionError('opening a level moved the grid storage')
+        entry = self.layout['levels'][level]
         return {'level': level, 'initialized_once': True, 'grid_storage_unchanged': True,
-                'original_dense_f2_seed': (self.config['seed'] + 1000003 * (level + 1) + 104729 * 3) % (2**31),
-                'native_dense_draw_shape': [points, max(2, self.plane_dims[level])], 'selected_nodes': nodes.numel()}
+                'original_dense_f2_seed': plane_seed(self.config['seed'], level),
+                'native_dense_draw_shape': [entry['native_plane_points'], max(2, self.plane_dims[level])],
+                'selected_nodes': entry['nodes'].numel()}
 
     def set_active_prefix(self, prefix):
         if not isinstance(prefix, int) or not 2 <= prefix <= self.n_levels:
-            raise ValueError('Active prefix must be an integer between 2 and declared level count')
+            raise ValueError(f'the active prefix is an integer in 2..{self.n_levels}')
         self.active_prefix = prefix
         self.level_active.copy_(torch.arange(self.n_levels, device=self.grid.device) < prefix)
         self.feature_active.copy_((self.feature_levels < prefix).to(torch.float16))
 
+    def gates(self, raw, visible):
+        """Per-level weights of the decoder input: the router's sigmoid/softplus gate (1 for the first K levels,
+        and for every level while only those are open), zero for hidden or inactive levels."""
+        k = self.gate_coarse_levels_K
+        if self.gate is None:
+            return None
+        if self.active_prefix > k:
+            learned = router_weights(self.gate(raw)[:, :self.n_levels].float(),
+                                     self.config.get('router_output_activation', 'sigmoid'))
+            learned[:, :k] = 1.0
+        else:
+            learned = torch.ones(visible.shape, dtype=torch.float32, device=raw.device)
+        return learned * (visible & self.level_active).float()
+
     def forward(self, coordinates):
         raw, visible = self.query_features(coordinates)
         raw = raw * self.feature_active
-        if self.gate is None:
-            return self.decoder(raw).float()[:, :3]
-        if self.active_prefix > self.gate_coarse_levels_K:
-            own = router_weights(self.gate(raw)[:, :self.n_levels].float(),
-                                 self.config.get('router_output_activation', 'sigmoid'))
-            k = self.gate_coarse_levels_K
-            gates = torch.cat([torch.ones_like(own[:, :k]), own[:, k:]], dim=1)
-        else:
-            gates = torch.ones_like(visible, dtype=torch.float32)
-        effective = gates * (visible & self.level_active).float()
-        weights = effective.to(raw.dtype).index_select(1, self.feature_levels)
-        return self.decoder(raw * weights).float()[:, :3]
+        weights = self.gates(raw, visible)
+        if weights is not None:
+            raw = raw * weights.to(raw.dtype).index_select(1, self.feature_levels)
+        return self.decoder(raw).float()[:, :3]
 
     def storage_stats(self):
+        """Parameter and index storage (the key set of odie/model.py:281-314)."""
+        nbytes = lambda t: t.numel() * t.element_size()  # noqa: E731
         grid = self.grid.numel()
         gate = self.gate.params.numel() if self.gate is not None else 0
         heads = gate + self.decoder.params.numel()
-        node_bitmaps = self.node_bitmap.numel() * self.node_bitmap.element_size()
-        prefixes = self.node_prefix.numel() * self.node_prefix.element_size()
-        bitmaps = self.bitmap.numel() * self.bitmap.element_size()
-        descriptors = self.descriptors.numel() * self.descriptors.element_size()
-        gate_index = self.feature_levels.numel() * self.feature_levels.element_size()
-        flags = (self.level_active.numel() * self.level_active.element_size() +
-                 self.feature_active.numel() * self.feature_active.element_size())
-        return {'actual_params': grid + heads, 'grid_params': grid, 'head_params': heads, 'gate_params': gate,
-                'decoder_params': self.decoder.params.numel(), 'router_enabled': self.router_enabled,
-                'axis_params': 0, 'plane_params': grid, 'plane_caps': self.plane_node_caps,
-                'fp16_parameter_payload_bytes': 2 * (grid + heads), 'fp32_master_bytes': 4 * (grid + heads),
-                'adam_moment_bytes': 8 * (grid + heads), 'full_gradient_bytes': 4 * (grid + heads),
-                'index_bytes': node_bitmaps + prefixes, 'node_bitmap_bytes': node_bitmaps,
-                'node_prefix_bytes': prefixes, 'bitmap_bytes': bitmaps, 'descriptor_bytes': descriptors,
-                'runtime_index_bytes': node_bitmaps + prefixes + bitmaps + descriptors + gate_index + flags,
-                'active_flag_bytes': flags, 'input_width': self.input_width,
-                'native_input_padding': (self.input_width + 15) // 16 * 16, 'axis_mode': 'none',
-                'active_layers_from_update1': int(self.config.get('initial_active_prefix', 2)),
-                'active_prefix': self.active_prefix, 'gate_coarse_levels_K': int(self.config['coarse_levels']),
-                'full_cover_coarse_layers': self.config.get('full_cover_coarse_layers', [0, 1]),
-                'plane_dims': self.plane_dims, 'coordinate_version': COORDINATE_VERSION,
-                'layout_version': LAYOUT_VERSION, 'addressing_version': ADDRESSING_VERSION,
-                'query_cuda_launches': 1, 'backward_cuda_launches': 1,
-                'forward_precision': 'P01 FP32 geometry and FP16 interpolation chain',
-                'gradient_precision': 'FP16 feature gradient, FP32 interpolation weights and reductions',
-                'levels': [{k: v for k, v in level.items() if k != 'nodes'} for level in self.layout['levels']]}
+        words, prefixes = nbytes(self.node_bitmap), nbytes(self.node_prefix)
+        cells, descriptors = nbytes(self.bitmap), nbytes(self.descriptors)
+        flags = nbytes(self.level_active) + nbytes(self.feature_active)
+        stats = dict(actual_params=grid + heads, grid_params=grid, head_params=heads, gate_params=gate,
+                     decoder_params=self.decoder.params.numel(), router_enabled=self.router_enabled, axis_params=0,
+                     plane_params=grid, plane_caps=self.plane_node_caps)
+        for key, per_param in (('fp16_parameter_payload_bytes', 2), ('fp32_master_bytes', 4),
+                               ('adam_moment_bytes', 8), ('full_gradient_bytes', 4)):
+            stats[key] = per_param * (grid + heads)
+        stats.update(index_bytes=words + prefixes, node_bitmap_bytes=words, node_prefix_bytes=prefixes,
+                     bitmap_bytes=cells, descriptor_bytes=descriptors,
+                     runtime_index_bytes=words + prefixes + cells + descriptors + nbytes(self.feature_levels) + flags,
+                     active_flag_bytes=flags, input_width=self.input_width,
+                     native_input_padding=(self.input_width + 15) // 16 * 16, axis_mode='none',
+                     active_layers_from_update1=int(self.config.get('initial_active_prefix', 2)),
+                     active_prefix=self.active_prefix, gate_coarse_levels_K=int(self.config['coarse_levels']),
+                     full_cover_coarse_layers=self.config.get('full_cover_coarse_layers', [0, 1]),
+                     plane_dims=self.plane_dims, coordinate_version=COORDINATE_VERSION, layout_version=LAYOUT_VERSION,
+                     addressing_version=ADDRESSING_VERSION, query_cuda_launches=1, backward_cuda_launches=1,
+                     forward_precision='P01 FP32 geometry and FP16 interpolation chain',
+                     gradient_precision='FP16 feature gradient, FP32 interpolation weights and reductions',
+                     levels=[{k: v for k, v in entry.items() if k != 'nodes'} for entry in self.layout['levels']])
+        return stats
 
 
 class HashGrid(nn.Module):
-    """Hashed multiresolution grid with optional per-level gate (odie/hash_grid.py:8-80)."""
+    """Hashed multiresolution grid (the TCNN HashGrid of odie/hash_grid.py:8-80, with the published Instant-NGP
+    spatial hash) behind the same optional per-level gate and decoder as the planes; every level is open."""
 
     def __init__(self, config, supports, plane_dims, plane_node_caps):
         super().__init__()
         if supports or config['initial_active_prefix'] != config['n_levels']:
-            raise ValueError('HashGrid requires no supports and all levels active')
+            raise ValueError('a hash grid has no supports and trains every level from the start')
         self.config = deepcopy(config)
         self.router_enabled = config['router_enabled']
         self.n_levels = self.active_prefix = config['n_levels']
@@ -355,67 +400,80 @@ class HashGrid(nn.Module):
         self.plane_dims, self.plane_node_caps = list(plane_dims), list(plane_node_caps)
         self.supports = []
         self.records, total = hash_levels(config['hash_encoding'])
-        generator = torch.Generator().manual_seed(int(config['seed']))
-        self.grid = nn.Parameter(((torch.rand(total, generator=generator) * 2 - 1) * 1e-4).cuda())
-        self.register_buffer('feature_levels', torch.tensor(
-            [level for level, dim in enumerate(plane_dims) for _ in range(dim)], dtype=torch.int64, device='cuda'),
-            persistent=False)
         seed = int(config['seed'])
-        self.gate = (Head(self.input_width, self.n_levels, 32, 1, (seed + 2000003) % 2**31)
-                     if self.router_enabled else None)
+        table = (torch.rand(total, generator=torch.Generator().manual_seed(seed)) * 2 - 1) * 1e-4
+        self.grid = nn.Parameter(table.cuda())
+        columns = [l for l, dim in enumerate(plane_dims) for _ in range(dim)]
+        self.register_buffer('feature_levels', torch.tensor(columns, dtype=torch.int64, device='cuda'),
+                             persistent=False)
+        self.gate = Head(self.input_width, self.n_levels, 32, 1, (seed + 2000003) % 2**31) if self.router_enabled else None
         self.decoder = Head(self.input_width, 3, 64, 2, (seed + 4000037) % 2**31)
-        levels, offset = [], 0
-        for dim, cap in zip(plane_dims, plane_node_caps):
-            levels.append(dict(plane_offset=offset, plane_node_capacity=cap, plane_dim=dim))
-            offset += dim * cap
-        self.layout = dict(levels=levels)
+        offsets = np.cumsum([0] + [dim * cap for dim, cap in zip(plane_dims, plane_node_caps)])
+        self.layout = dict(levels=[dict(plane_offset=int(o), plane_node_capacity=cap, plane_dim=dim)
+                                   for o, dim, cap in zip(offsets[:-1], plane_dims, plane_node_caps)])
         gate = self.gate.params.numel() if self.gate is not None else 0
-        if self.grid.numel() != offset or self.decoder.params.numel() != config['decoder_parameters'] or \
-                gate != config['gate_parameters']:
-            raise RuntimeError('Actual allocation differs from the reference HashGrid budget')
+        expected = (int(offsets[-1]), config['decoder_parameters'], config['gate_parameters'])
+        if (self.grid.numel(), self.decoder.params.numel(), gate) != expected:
+            raise RuntimeError('the hash grid or its heads differ from the configured budget')
 
     def set_active_prefix(self, prefix):
         if prefix != self.n_levels:
-            raise ValueError('The no-on-demand model always trains every level')
+            raise ValueError('a hash grid always trains every level')
 
     def forward(self, coordinates):
         raw = HashQuery.apply(coordinates.contiguous(), self.grid, self.records, self.input_width)
         if self.gate is not None:
             weights = router_weights(self.gate(raw)[:, :self.n_levels].float(), self.config['router_output_activation'])
-            k = self.gate_coarse_levels_K
-            if k:
-                weights = torch.cat((torch.ones_like(weights[:, :k]), weights[:, k:]), dim=1)
+            weights[:, :self.gate_coarse_levels_K] = 1.0
             raw = raw * weights.to(raw.dtype).index_select(1, self.feature_levels)
         return self.decoder(raw).float()[:, :3]
 
     def storage_stats(self):
         grid, decoder = self.grid.numel(), self.decoder.params.numel()
         gate = self.gate.params.numel() if self.gate is not None else 0
-        heads = gate + decoder
-        return dict(actual_params=grid + heads, grid_params=grid, head_params=heads, gate_params=gate,
-                    decoder_params=decoder, router_enabled=self.router_enabled, plane_caps=self.plane_node_caps,
-                    fp16_parameter_payload_bytes=2 * (grid + heads), input_width=self.input_width,
-                    layout_version='hash-grid-v1', addressing_version='instant-ngp-spatial-hash')
+        return dict(actual_params=grid + gate + decoder, grid_params=grid, head_params=gate + decoder,
+                    gate_params=gate, decoder_params=decoder, router_enabled=self.router_enabled,
+                    plane_caps=self.plane_node_caps, fp16_parameter_payload_bytes=2 * (grid + gate + decoder),
+                    input_width=self.input_width, layout_version='hash-grid-v1',
+                    addressing_version='instant-ngp-spatial-hash')
 
 
 class RoutedExperts(nn.Module):
-    """Routed multi-expert hash-grid encoding with a shared decoder (16 routed experts in the benchmark; no reference counterpart).
+    """Routed multi-expert hash-grid encoding with a shared decoder (no reference counterpart).
 
     A coarse shared hash grid (``router_encoding``) feeds the router MLP
-    (W -> 32 -> 32 -> 16 logits, top-1 over ``experts``); coordinate i is then
-    encoded by its expert's own hash grid (``hash_encoding``; the tables of all
-    experts are one flat fp32 parameter, expert-major) and the features, scaled
-    by the router probability rounded to fp16, go through the shared decoder
-    (W -> 64 -> 64 -> 3).  Training runs in the native runtime; this module's
-    forward is the evaluation/decode path.
+    (W -> 32 -> 32 -> 16 or 64 logits, top-1); coordinate i is then encoded by
+    its expert's own hash grid (``hash_encoding``; the tables of the experts held
+    here are one flat fp32 parameter, expert-major) and the features, scaled by
+    the router probability rounded to fp16, go through the shared decoder
+    (W -> 64 -> 64 -> 3).
+
+    Spatial expert ownership (``bands`` > 1): the full image of ``image_rows``
+    rows is cut into equal row bands, band b owns experts [b * per, (b + 1) *
+    per) with per = ``experts_per_band``, and a coordinate chooses among its
+    band's experts only.  A data-parallel rank holds bands [first_band,
+    first_band + bands_held) and only their expert tables; every expert's table
+    is seeded by its global number, so the model is the same however the bands
+    are split.  Training runs in the native runtime; this module's forward is the
+    evaluation/decode path.
     """
 
     def __init__(self, config):
         super().__init__()
         self.config = deepcopy(config)
-        self.experts = int(config['experts'])
-        if not 1 <= self.experts <= 16:
-            raise ValueError('experts must be within 1..16')
+        self.experts = int(config['experts'])  # of the whole model
+        self.bands = int(config.get('bands', 1))
+        self.per_band = int(config.get('experts_per_band', self.experts))
+        self.first_band = int(config.get('first_band', 0))
+        self.bands_held = int(config.get('bands_held', self.bands))
+        if self.per_band * self.bands != self.experts or not 1 <= self.experts <= 64:
+            raise ValueError('experts must be bands x experts_per_band, within 1..64')
+        if self.bands > 1 and self.per_band not in (8, 16):
+            raise ValueError('banded routing takes 8 or 16 experts per band')
+        if not (0 <= self.first_band and self.first_band + self.bands_held <= self.bands and self.bands_held >= 1):
+            raise ValueError('the bands held must lie within the bands')
+        self.image_rows = int(config.get('image_rows', 2))
+        self.experts_held = self.bands_held * self.per_band
         encoding, router_encoding = config['hash_encoding'], config['router_encoding']
         self.records, self.expert_total = hash_levels(encoding)
         self.router_records, router_total = hash_levels(router_encoding)
@@ -426,14 +484,21 @@ class RoutedExperts(nn.Module):
         if router_width != self.input_width:
             raise ValueError('router and expert encodings must have the same width')
         seed = int(config['seed'])
-        generator = torch.Generator().manual_seed(seed)
-        self.grid = nn.Parameter(((torch.rand(self.experts * self.expert_total, generator=generator) * 2 - 1)
-                                  * float(config.get('grid_init', 1e-4))).cuda())
-        self.router_grid = nn.Parameter(((torch.rand(router_total, generator=generator) * 2 - 1)
+        scale = float(config.get('grid_init', 1e-4))
+        first_expert = self.first_band * self.per_band
+        tables = [(torch.rand(self.expert_total, generator=torch.Generator().manual_seed(seed + 7919 * (e + 1))) * 2 - 1)
+                  * scale for e in range(first_expert, first_expert + self.experts_held)]
+        self.grid = nn.Parameter(torch.cat(tables).cuda())
+        self.router_grid = nn.Parameter(((torch.rand(router_total, generator=torch.Generator().manual_seed(seed)) * 2 - 1)
                                          * float(config.get('router_init', 1e-1))).cuda())
-        self.gate = Head(self.input_width, 16, 32, 2, (seed + 2000003) % 2**31)  # the router MLP
+        self.gate = Head(self.input_width, router_out(self.experts), 32, 2, (seed + 2000003) % 2**31)  # the router MLP
         self.decoder = Head(self.input_width, 3, 64, 2, (seed + 4000037) % 2**31)
         self.supports = []
+
+    @property
+    def banding(self):
+        """The router's banding (router.cuh Banding) for the bands held here."""
+        return dict(bands=self.bands, first_band=self.first_band, per_band=self.per_band, rows=self.image_rows)
 
     def set_active_prefix(self, prefix):
         if prefix != self.n_levels:
@@ -476,9 +541,10 @@ class RoutedExperts(nn.Module):
         return {'bitmap': self.allocation_bitmap.data_ptr(), 'cells': list(self.allocation_cells)}
 
     def route(self, coordinates):
+        """(local expert, probability, live logits) of full-image coordinates."""
         with torch.no_grad():
             features = HashQuery.apply(coordinates.contiguous(), self.router_grid, self.router_records, self.input_width)
-            return route(features, self.gate.params, self.experts)
+            return route(features, self.gate.params, self.experts_held, coordinates, self.banding)
 
     def forward(self, coordinates):
         expert, prob, _ = self.route(coordinates)
@@ -491,7 +557,8 @@ class RoutedExperts(nn.Module):
         grid, router_grid = self.grid.numel(), self.router_grid.numel()
         heads = self.gate.params.numel() + self.decoder.params.numel()
         return dict(actual_params=grid + router_grid + heads, grid_params=grid, router_grid_params=router_grid,
-                    head_params=heads, experts=self.experts, fp16_parameter_payload_bytes=2 * (grid + router_grid + heads),
+                    head_params=heads, experts=self.experts, experts_held=self.experts_held, bands=self.bands,
+                    fp16_parameter_payload_bytes=2 * (grid + router_grid + heads),
                     input_width=self.input_width, addressing_version='instant-ngp-spatial-hash')
 
 

@@ -1,12 +1,11 @@
 """Optimizer-like wrapper of the native training runtime (odie/native_backend.py).
 
-Same public surface as the reference's NativeOptimizer: param_groups, state,
-prepare_epoch, train_batch, release_graph, recaptures, build_manifest,
-state_summary, native_state_digest, close.  The step is one C-ABI call
-(odie_step) captured in a CUDA graph and replayed for every full batch.
-Differences from the reference: the batch is the configured batch size (not
-fixed at 65536) and the compile-time specialisation of the reference build
-(odie/build.py:26-30) is passed as JSON keys.
+The public surface the training loop uses (odie/native_backend.py): param_groups, state,
+prepare_epoch, train_batch, release_graph, recaptures, build_manifest, state_summary,
+native_state_digest, close.  A step is one C-ABI call (odie_step); prepare_epoch captures it,
+with the batch's loss, in a CUDA graph that every full batch replays.  The batch is the
+configured batch size (the reference fixes 65536), and the reference's compile-time
+specialisation (odie/build.py:26-30) is passed as JSON keys.
 """
 import contextlib
 import json
@@ -40,7 +39,7 @@ def target_bytes(target):
 
 
 class NativeOptimizer:
-    def __init__(self, model, target, shape, config, planes, half=True, batch=None, head_grad=None):
+    def __init__(self, model, target, shape, config, planes, half=True, batch=None, head_grad=None, router_grad=None):
         self.lib = _lib.library()
         self.model, self.target, self.config = model, target, config
         self.half = half
@@ -72,15 +71,24 @@ class NativeOptimizer:
         if config['representation'] in ('hash_grid', 'routed_experts'):
             settings['hash_encoding'] = config['hash_encoding']
         if experts:
-            settings.update(experts=model.experts, router_encoding=config['router_encoding'], router=0,
-                            router_grid=model.router_grid.data_ptr())
+            settings.update(experts=model.experts_held, router_encoding=config['router_encoding'], router=0,
+                            router_grid=model.router_grid.data_ptr(), bands=model.bands, first_band=model.first_band,
+                            experts_per_band=model.per_band)
+            if model.bands > 1:
+                settings.update(full_height=model.image_rows, row_offset=int(config.get('row_offset', 0)))
+            if router_grad is not None:
+                settings['router_grad'] = router_grad.data_ptr()
         self.handle = self.lib.odie_create(json.dumps(settings).encode())
         if not self.handle:
             raise RuntimeError(_lib.error())
         self.pointers = json.loads(self.lib.odie_pointers(self.handle))
-        self.fixed = torch.zeros(self.batch, device='cuda', dtype=torch.int64)
+        self.fixed = torch.zeros(self.batch, device='cuda', dtype=torch.int64)  # the captured step's ids
         self.squares = torch.empty(self.batch, device='cuda', dtype=torch.float32)
+        self.graph_loss = None
+        self._launched = False
         self.state = PlaneState(self, planes)
+        from .gpu_residual import attach_runtime
+        attach_runtime(model, self)  # the stage boundary decodes this model through the runtime
 
     def current_settings(self):
         rates = {g['name'] + '_lr': float(g['lr']) for g in self.param_groups}
@@ -126,55 +134,72 @@ class NativeOptimizer:
         return result
 
     def release_graph(self):
+        """Drop the captured step (after a synchronize, so no replay is still running)."""
         torch.cuda.synchronize()
         self.graph = self.key = None
         self.lib.odie_release_contexts(self.handle)
 
+    def _capture(self):
+        """Capture one full-batch step plus the loss of its squared errors as a CUDA graph on the runtime's stream.
+        The runtime allocates nothing after creation, so the capture needs no preparation beyond having run each
+        kernel once (CUDA loads a library's kernels lazily, on their first launch): the first capture of a runtime
+        is preceded by one step that updates nothing."""
+        if not self._launched:
+            with self.on_stream():
+                self.check(self.lib.odie_step(self.handle, self.fixed.data_ptr(), self.batch, 0))
+            self._launched = True
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            self.check(self.lib.odie_step(self.handle, self.fixed.data_ptr(), self.batch, 1))
+            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], self.batch * 4,
+                                          self.stream.cuda_stream))
+            loss = self.squares.sum(dtype=torch.float64) / self.batch
+        return graph, loss
+
     def prepare_epoch(self):
+        """Apply the model's current settings (active prefix, layout, allocation, learning rates) and, when they
+        changed, capture the step for them."""
         settings = self.current_settings()
-        key = tuple(settings.items())
+        key = json.dumps(settings, sort_keys=True)
         if key == self.key:
             return
         self.release_graph()
         self.check(self.lib.odie_configure(self.handle, json.dumps(settings).encode()))
-        for _ in range(3):
-            self.step_raw(self.fixed, update=False)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=self.stream):
-            self.check(self.lib.odie_step(self.handle, self.fixed.data_ptr(), self.fixed.numel(), 1))
-            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], self.batch * 4,
-                                          self.stream.cuda_stream))
-            self.graph_loss = self.squares.double().mean()
+        self.graph, self.graph_loss = self._capture()
         self.lib.odie_pin_contexts(self.handle)
-        self.graph, self.key = graph, key
+        self.key = key
         self.recaptures += 1
 
     def train_batch(self, ids):
+        """One step on pixel ids; returns the batch's mean squared error (a CUDA fp64 scalar)."""
+        n = ids.numel()
         with self.on_stream():
-            if ids.numel() == self.batch and self.graph is not None:
+            if self.graph is not None and n == self.batch:
                 self.fixed.copy_(ids)
                 self.graph.replay()
                 return self.graph_loss
-            self.check(self.lib.odie_step(self.handle, ids.data_ptr(), ids.numel(), 1))
-            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], ids.numel() * 4,
+            self.check(self.lib.odie_step(self.handle, ids.data_ptr(), n, 1))
+            self.check(self.lib.odie_copy(self.squares.data_ptr(), self.pointers['squares'], n * 4,
                                           self.stream.cuda_stream))
-            return self.squares[:ids.numel()].double().mean()
+            return self.squares[:n].sum(dtype=torch.float64) / n
 
     def state_summary(self, begin=-1, end=-1):
-        data = self.lib.odie_state(self.handle, begin, end)
-        if data is None:
+        """The runtime's optimizer-state summary: {'pristine'} for a grid range, or the state digest (begin < 0)."""
+        reply = self.lib.odie_state(self.handle, begin, end)
+        if reply is None:
             raise RuntimeError(_lib.error())
-        return json.loads(data)
+        return json.loads(reply)
 
     def native_state_digest(self):
         return json.dumps(self.state_summary(), sort_keys=True)
 
     def close(self):
-        if self.handle:
-            self.release_graph()
-            self.lib.odie_destroy(self.handle)
-            self.handle = None
+        if not self.handle:
+            return
+        self.release_graph()
+        self.lib.odie_destroy(self.handle)
+        self.handle = None
 
     def decode(self, begin, count, rgb=None, rgb8=None):
         """Decode pixel ids [begin, begin+count) into fp32 and/or u8 RGB device tensors."""

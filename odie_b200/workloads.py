@@ -16,14 +16,22 @@ U(-1e-4, 1e-4)), a top-1 router (W -> 32 -> 32 -> 16) over a coarse shared grid
 U(-0.1, 0.1) so that the initial routing already splits the image), and the
 shared 64-wide decoder, on the same 2040 x 1356 image with 2^20 coords.
 
+c4-experts: the gigapixel benchmark -- a 32768 x 32768 procedural image (fractal
+1/f^2 noise, sharp-edged Voronoi regions, a 64 x 64-cell texture atlas), 64 routed
+experts under a 50 MiB fp16 budget (T = 2^14 per expert level: 24.4 M parameters,
+46.5 MiB with the router grid and heads), owned spatially by 8 row bands of 8
+experts each (a coordinate chooses among its band's experts), 20 % of the 256 x
+256 tiles allocated, 2^22 coordinates per step and GPU.  Rank r of N holds bands
+[8r/N, 8(r+1)/N) and their experts; the model is the same at every N.
+
 c3-experts: the on-demand allocation benchmark -- a 4096 x 4096
 image (1/f^2 noise + 200 sharp polygons), 8 routed experts with T = 2^17, the
 residual of every 256 x 256 tile of the current model's decode, the top 30 %
 tiles allocated (the fine expert levels restricted to their cells), and 2^21
 coordinates per step, 70 % of them drawn from the allocated tiles.
 
-Multi-GPU (all workloads): rank r of N trains the model of row band r of the
-image (its own tables: spatial ownership); the heads are shared.
+Multi-GPU (c2, c3): rank r of N trains the model of row band r of the image (its
+own tables: spatial ownership); the heads are shared.  c4 splits one fixed model.
 """
 import math
 
@@ -32,7 +40,7 @@ import numpy as np
 import torch
 
 from . import layout as host_layout
-from .data import ByteTarget, pink_noise, synthetic_image
+from .data import ByteTarget, pink_noise, procedural_image, synthetic_image
 from .model import PackedXYPlanes, RoutedExperts
 from .parallel import band_rows
 
@@ -135,6 +143,38 @@ def c3_experts(seed=1729, batch=1 << 21, band=(0, 1), device='cuda'):
     rgb, shape = band_of(rgb.cpu(), shape, band)
     encoding = dict(EXPERT_ENCODING, log2_hashmap_size=17)
     return experts_config(experts=8, seed=seed + band[0], batch=batch, encoding=encoding), rgb, shape
+
+
+C4_SHAPE = (32768, 32768)
+C4_BANDS, C4_PER_BAND = 8, 8
+C4_TILE, C4_ALLOCATED = 256, 0.2
+C4_ENCODING = dict(EXPERT_ENCODING, log2_hashmap_size=14)
+C4_BUDGET_BYTES = 50 << 20
+
+
+def c4_experts(seed=1729, batch=1 << 22, band=(0, 1), shape=C4_SHAPE, bands=C4_BANDS, per_band=C4_PER_BAND,
+               encoding=None, device='cuda'):
+    """(config, rgb u8 [rows * W, 3] on the GPU, (rows, W)) of rank band[0] of band[1]: the rank holds image bands
+    [first, first + bands / ranks) -- their rows of the procedural image and their experts."""
+    rank, ranks = band
+    height, width = shape
+    if bands % ranks or height % bands:
+        raise ValueError('the ranks must split the bands, and the bands the rows, evenly')
+    held = bands // ranks
+    first = rank * held
+    band_rows = height // bands
+    row0, rows = first * band_rows, held * band_rows
+    rgb = procedural_image(shape, seed, row0, rows, device=device)
+    config = experts_config(experts=bands * per_band, seed=seed, batch=batch, encoding=encoding or C4_ENCODING)
+    config.update(bands=bands, experts_per_band=per_band, first_band=first, bands_held=held, image_rows=height,
+                  row_offset=row0)
+    return config, rgb, (rows, width)
+
+
+def fp16_payload_bytes(model):
+    """fp16 bytes of every parameter of the whole model (all experts, whichever rank holds them)."""
+    return 2 * (model.experts * model.expert_total + model.router_grid.numel() + model.gate.params.numel() +
+                model.decoder.params.numel())
 
 
 def allocated_ids(tiles, shape, count, generator, fraction=0.7, tile_px=C3_TILE):

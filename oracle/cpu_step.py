@@ -120,28 +120,43 @@ class CpuExpertStep(CpuStep):
     Same arithmetic as the CUDA path's definition: router MLP with fp16
     activations, top-1 of the fp16 logits, decoder input = fp16(features x
     fp16(p)); autograd through p (softmax probability) and both grids; Adam on
-    expert tables, router grid, router MLP and decoder."""
+    expert tables, router grid, router MLP and decoder.  banding (dict: bands,
+    first_band, per_band, rows = full-image height, row_offset): spatial expert
+    ownership, each coordinate choosing among its row band's experts."""
 
     def __init__(self, shape, rgb_u8, levels, expert_stride, experts, router_levels, grid, router_grid, router, decoder,
-                 width, lr=(1e-2, 1e-3, 1e-3)):
+                 width, lr=(1e-2, 1e-3, 1e-3), banding=None):
         super().__init__(shape, rgb_u8, levels, grid, router, decoder, width, router=True, lr=lr)
         self.router_levels, self.stride, self.experts = router_levels, expert_stride, experts
+        self.banding = dict(banding or dict(bands=1, first_band=0, per_band=experts, rows=shape[0], row_offset=0))
+        model_experts = self.banding['bands'] * self.banding['per_band']
+        self.router_rows = 16 if model_experts <= 16 else 64
         self.router_grid = torch.nn.Parameter(torch.from_numpy(router_grid.copy()))
         self.optimizer.add_param_group({'params': [self.router_grid], 'lr': lr[0]})
 
     def step(self, ids):
         height, width = self.shape
-        xy = torch.stack(((ids % width).float() * (1.0 / (width - 1)), (ids // width).float() * (1.0 / (height - 1))), 1)
+        b = self.banding
+        rows = ids // width + b.get('row_offset', 0)
+        xy = torch.stack(((ids % width).float() * (1.0 / (width - 1)), rows.float() * (1.0 / (b['rows'] - 1))), 1)
         target = self.rgb[ids].float() / 255.
         self.optimizer.zero_grad(set_to_none=True)
         W = self.width
         rin, _ = encode_levels(self.router_grid, self.router_levels, xy, W)
-        r1, r2, r3 = self._mats(self.gate, [(32, W), (32, 32), (16, 32)])
+        r1, r2, r3 = self._mats(self.gate, [(32, W), (32, 32), (self.router_rows, 32)])
         h = F.relu(F.linear(rin, r1.half().float())).half().float()
         h = F.relu(F.linear(h, r2.half().float())).half().float()
-        logits = F.linear(h, r3.half().float()).half().float()[:, :self.experts]
-        expert = logits.detach().argmax(1)
-        prob = torch.softmax(logits, 1).gather(1, expert[:, None])
+        per = b['per_band']
+        if b['bands'] > 1:
+            held = self.experts // per
+            band = (rows * b['bands'] // b['rows']).clamp(b['first_band'], b['first_band'] + held - 1)
+        else:
+            band = torch.zeros_like(ids)
+        live = band[:, None] * per + torch.arange(per)[None, :]
+        logits = F.linear(h, r3.half().float()).half().float().gather(1, live)
+        choice = logits.detach().argmax(1)
+        expert = (band - b['first_band']) * per + choice
+        prob = torch.softmax(logits, 1).gather(1, choice[:, None])
         raw, _ = encode_levels(self.grid, self.levels, xy, W, base=expert * self.stride)
         x = (raw * prob.half().float()).half().float()
         d1, d2, d3 = self._mats(self.decoder, [(64, W), (64, 64), (16, 64)])

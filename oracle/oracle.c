@@ -45,6 +45,19 @@ void oracle_coords(const int64_t* ids, int64_t n, int width, int height, float* 
     }
 }
 
+/* The same coordinates for the rows of a band of a taller image (no reference counterpart): local
+ * pixel id of an image whose rows are rows [row0, row0 + height) of a full image of `rows` rows;
+ * y = (row0 + id / width) * fl(1 / (rows - 1)).  row0 = 0, rows = height is oracle_coords. */
+void oracle_coords_frame(const int64_t* ids, int64_t n, int width, int row0, int rows, float* xy) {
+    const float ix = (float)(1.0 / (double)(width - 1));
+    const float iy = (float)(1.0 / (double)(rows - 1));
+    for (int64_t i = 0; i < n; ++i) {
+        uint32_t id = (uint32_t)ids[i];
+        xy[2 * i] = (float)(id % (uint32_t)width) * ix;
+        xy[2 * i + 1] = (float)((uint32_t)row0 + id / (uint32_t)width) * iy;
+    }
+}
+
 /* ------------------------------------------------------------------ a2 */
 /* geometry, odie/packed_kernels.cu:12-22 */
 static inline void geometry(float x, float y, float scale, int r, int* cell, float* w) {
@@ -576,15 +589,17 @@ void oracle_topk(const double* scores, int64_t count, int64_t k, int64_t* chosen
 }
 
 /* ------------------------------------------------------------------ router */
-/* Top-1 expert router (16 routed experts in the benchmark; no reference counterpart).
+/* Top-1 expert router (routed experts; no reference counterpart).
  * Input fp16 features [n x in_width]; weights fp16 row-major [out][in];
  * each layer: fp32 accumulation in ascending input order with fmaf, ReLU on
- * hidden layers, fp16 rounding of every layer's output.  Expert = argmax of the
- * fp16 logits over the first `experts` columns (lowest index on ties); prob =
- * softmax of the fp32 values of those fp16 logits, in the order: max, then
- * sum of expf(z - max) in ascending expert order, then expf(z* - max) / sum. */
+ * hidden layers, fp16 rounding of every layer's output.  Coordinate i chooses
+ * among the `live` logits starting at row first[i] (first NULL: row 0): choice =
+ * argmax of those fp16 logits relative to first[i] (lowest index on ties);
+ * prob = softmax of the fp32 values of those fp16 logits, in the order: max,
+ * then sum of expf(z - max) in ascending order, then 1 / sum.  logits_out:
+ * every row's fp16 logit, [n][out_width]. */
 void oracle_router(const uint16_t* x, int64_t n, int in_width, const uint16_t* w1, int hidden,
-                   const uint16_t* w2, const uint16_t* w3, int out_width, int experts,
+                   const uint16_t* w2, const uint16_t* w3, int out_width, const int32_t* first, int live,
                    int32_t* expert, float* prob, uint16_t* logits_out) {
     float h1[256], h2[256], z[256];
     for (int64_t i = 0; i < n; ++i) {
@@ -605,10 +620,11 @@ void oracle_router(const uint16_t* x, int64_t n, int in_width, const uint16_t* w
             z[o] = f_of_h(h_of(acc));
             if (logits_out) logits_out[i * out_width + o] = bits_of_h(h_of(acc));
         }
+        const float* zl = z + (first ? first[i] : 0);
         int best = 0;
-        for (int e = 1; e < experts; ++e) if (z[e] > z[best]) best = e;
+        for (int e = 1; e < live; ++e) if (zl[e] > zl[best]) best = e;
         float sum = 0.0f;
-        for (int e = 0; e < experts; ++e) sum += expf(z[e] - z[best]);
+        for (int e = 0; e < live; ++e) sum += expf(zl[e] - zl[best]);
         expert[i] = best;
         prob[i] = 1.0f / sum;
     }

@@ -61,10 +61,14 @@ def _hash_levels(records):
 
 
 # ---------------------------------------------------------------- wrappers
-def coords(ids, width, height):
+def coords(ids, width, height, row0=0, rows=None):
+    """Coordinates of local pixel ids; row0/rows place the image's rows in a taller full image."""
     ids = np.ascontiguousarray(ids, dtype=np.int64)
     xy = np.empty((ids.size, 2), dtype=np.float32)
-    lib().oracle_coords(_p(ids), C.c_int64(ids.size), width, height, _p(xy))
+    if row0 == 0 and rows in (None, height):
+        lib().oracle_coords(_p(ids), C.c_int64(ids.size), width, height, _p(xy))
+    else:
+        lib().oracle_coords_frame(_p(ids), C.c_int64(ids.size), width, row0, rows, _p(xy))
     return xy
 
 
@@ -263,7 +267,9 @@ def topk(scores, k):
     return chosen
 
 
-def router(x16, w1, w2, w3, hidden, experts):
+def router(x16, w1, w2, w3, hidden, experts, first=None):
+    """Top-1 routing.  first (int32 [n], optional): each coordinate's first live logit row; it then chooses among
+    `experts` rows from there and the returned choice is relative to it.  Returns (choice, prob, all logits)."""
     x = np.ascontiguousarray(x16, dtype=np.float16).view(np.uint16)
     n, in_width = x.shape
     out_width = np.asarray(w3).size // hidden
@@ -271,9 +277,21 @@ def router(x16, w1, w2, w3, hidden, experts):
     prob = np.empty(n, dtype=np.float32)
     logits = np.empty((n, out_width), dtype=np.uint16)
     ws = [np.ascontiguousarray(w, dtype=np.float16).view(np.uint16) for w in (w1, w2, w3)]
-    lib().oracle_router(_p(x), C.c_int64(n), in_width, _p(ws[0]), hidden, _p(ws[1]), _p(ws[2]), out_width, experts,
-                        _p(expert), _p(prob), _p(logits))
+    rows = None if first is None else np.ascontiguousarray(first, dtype=np.int32)
+    if rows is not None:
+        assert rows.shape == (n,) and rows.min(initial=0) >= 0 and rows.max(initial=0) + experts <= out_width
+    lib().oracle_router(_p(x), C.c_int64(n), in_width, _p(ws[0]), hidden, _p(ws[1]), _p(ws[2]), out_width,
+                        None if rows is None else _p(rows), experts, _p(expert), _p(prob), _p(logits))
     return expert, prob, logits.view(np.float16)
+
+
+def band_rows_of(ids, width, banding):
+    """Band of each local pixel id under spatial expert ownership (router.cuh Banding): the global row
+    row_offset + id // width, its band floor(row * bands / rows), clamped to the bands held."""
+    rows_global = banding.get('row_offset', 0) + np.asarray(ids, dtype=np.int64) // width
+    band = rows_global * banding['bands'] // banding['rows']
+    held = banding['experts'] // banding['per_band']
+    return np.clip(band, banding['first_band'], banding['first_band'] + held - 1)
 
 
 # ---------------------------------------------------------------- heads and the full step
@@ -365,7 +383,14 @@ def reference_step(rgb, ids, shape, grid, layout, gate_params, decoder_params, l
 
 
 # ---------------------------------------------------------------- routed experts
-ROUTER_SHAPES = lambda width: [(32, width), (32, 32), (16, 32)]  # noqa: E731  router W1, W2, W3
+def router_out(model_experts):
+    """Logit rows of the router MLP: 16 for up to 16 experts, else 64 (router.cuh router_out)."""
+    return 16 if model_experts <= 16 else 64
+
+
+def router_shapes(width, model_experts=16):
+    """Router W1, W2, W3 as (out, in)."""
+    return [(32, width), (32, 32), (router_out(model_experts), 32)]
 
 
 def expert_query(xy, tables16, expert, expert_stride, records, width, bitmap=None):
@@ -387,25 +412,40 @@ def expert_backward(xy, upstream, expert, expert_stride, records, params, bitmap
 
 
 def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, experts, router_table, router_records,
-                           router_params, decoder_params, width=32, bitmap=None):
+                           router_params, decoder_params, width=32, bitmap=None, banding=None, targets=None):
     """One routed-expert training step on the CPU (the restatement the CUDA path is checked against).
 
     Routing: router grid features -> router MLP with fp32 fma chains (bit-exact
-    definition, `router`), top-1 expert, probability p.  Decoder input =
-    fp16(expert features x fp16(p)).  Decoder, loss and fp16 rounding points as
-    in `reference_step`.  Backward: v = fp16(dz / 128); expert values =
-    fp16(v x fp16(p)); dp = sum_c v_c f_c; dz_j = dp p (delta_je - p_j) with p_j
-    the softmax of the fp16 logits; da = fp16(fp16(dz_j) x 128); router backward
-    to dR; router values = fp16(dR / 128).  Head gradients (scale 16384) in the
-    order router W1, W2, W3 | decoder W1, W2, W3; grid gradients (scale 128) of
-    the expert tables and of the router grid.
+    definition, `router`), top-1 over the coordinate's live experts, probability
+    p.  banding (optional dict: bands, first_band, per_band, rows = full-image
+    height, row_offset): spatial expert ownership -- a coordinate of global row y
+    lies in band floor(y * bands / rows) and chooses among logit rows
+    [band * per_band, (band + 1) * per_band); its local expert is (band -
+    first_band) * per_band + choice.  Without banding every coordinate chooses
+    among all `experts`.  Decoder input = fp16(expert features x fp16(p)).
+    Decoder, loss and fp16 rounding points as in `reference_step`.  Backward:
+    v = fp16(dz / 128); expert values = fp16(v x fp16(p)); dp = sum_c v_c f_c;
+    dz_j = dp p (delta_je - p_j) with p_j the softmax of the live fp16 logits;
+    da = fp16(fp16(dz_j) x 128) in the live columns, 0 elsewhere; router
+    backward to dR; router values = fp16(dR / 128).  Head gradients (scale 16384)
+    in the order router W1, W2, W3 | decoder W1, W2, W3; grid gradients (scale
+    128) of the expert tables and of the router grid.  targets (optional u8 [n, 3]): the
+    pixels of `ids`, given instead of reading them from rgb (for images too large to copy to the host).
     """
     height, img_width = shape
-    xy = coords(ids, img_width, height)
-    target = target_u8(rgb, ids)
+    b = dict(banding or dict(bands=1, first_band=0, per_band=experts, rows=height, row_offset=0), experts=experts)
+    per = b['per_band']
+    n = len(ids)
+    xy = coords(ids, img_width, height, b.get('row_offset', 0), b['rows'])
+    target = target_u8(rgb, ids) if targets is None else target_u8(targets, np.arange(n))
     rin = hash_query(xy, router_table.astype(np.float16), router_records, width)
-    r1, r2, r3 = (_f16(w) for w in head_matrices(router_params, ROUTER_SHAPES(width)))
-    expert, prob, logits = router(rin, r1.reshape(-1), r2.reshape(-1), r3.reshape(-1), 32, experts)
+    r1, r2, r3 = (_f16(w) for w in head_matrices(router_params, router_shapes(width, b['bands'] * per)))
+    band = band_rows_of(ids, img_width, b) if b['bands'] > 1 else np.zeros(n, dtype=np.int64)
+    first_row = (band * per).astype(np.int32)
+    choice, prob, logits = router(rin, r1.reshape(-1), r2.reshape(-1), r3.reshape(-1), 32, per, first=first_row)
+    expert = ((band - b['first_band']) * per + choice).astype(np.int32)
+    live_cols = first_row[:, None] + np.arange(per)[None, :]
+    live_logits = np.take_along_axis(logits, live_cols, axis=1)
     feats = expert_query(xy, tables.astype(np.float16), expert, expert_stride, records, width, bitmap)
     ph = prob.astype(np.float16)
     weighted = _f16(feats.astype(np.float64) * ph.astype(np.float64)[:, None])
@@ -420,14 +460,14 @@ def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, expe
     v = _f16(dz.astype(np.float64) / 128)
     values = _f16(v.astype(np.float64) * ph.astype(np.float64)[:, None])
     dp = (v.astype(np.float64) * feats.astype(np.float64)).sum(1)
-    z = logits.astype(np.float64)[:, :experts]
+    z = live_logits.astype(np.float64)
     ez = np.exp(z - z.max(1, keepdims=True))
     pj = ez / ez.sum(1, keepdims=True)
     onehot = np.zeros_like(pj)
-    onehot[np.arange(len(expert)), expert] = 1
-    da = np.zeros((len(ids), 16))
-    da[:, :experts] = _f16(dp[:, None] * prob.astype(np.float64)[:, None] * (onehot - pj)).astype(np.float64) * 128
-    da = _f16(da)
+    onehot[np.arange(n), choice] = 1
+    da_live = _f16(_f16(dp[:, None] * prob.astype(np.float64)[:, None] * (onehot - pj)).astype(np.float64) * 128)
+    da = np.zeros((n, r3.shape[0]), dtype=np.float16)
+    np.put_along_axis(da, live_cols, da_live, axis=1)
     gh1 = _f16(np.maximum(_mm(rin, r1.T), 0))
     gh2 = _f16(np.maximum(_mm(gh1, r2.T), 0))
     dgh2 = _f16(np.where(gh2 > 0, _mm(da, r3), 0))
@@ -437,9 +477,9 @@ def reference_step_experts(rgb, ids, shape, tables, records, expert_stride, expe
     f64 = lambda a: a.astype(np.float64)  # noqa: E731
     head = [f64(dgh1).T @ f64(rin), f64(dgh2).T @ f64(gh1), f64(da).T @ f64(gh2),
             f64(dh1).T @ f64(weighted), f64(dh2).T @ f64(h1), f64(dy).T @ f64(h2)]
-    return dict(xy=xy, target=target, router_features=rin, expert=expert, prob=prob, logits=logits, raw=feats,
-                weighted=weighted, out=out, dy=dy, squares=squares, dz=dz, values=values.astype(np.float32),
-                dp=dp, da=da, router_values=router_values.astype(np.float32),
+    return dict(xy=xy, target=target, router_features=rin, expert=expert, band=band, prob=prob, logits=logits,
+                live_logits=live_logits, raw=feats, weighted=weighted, out=out, dy=dy, squares=squares, dz=dz,
+                values=values.astype(np.float32), dp=dp, da=da, router_values=router_values.astype(np.float32),
                 grid_grad=expert_backward(xy, values, expert, expert_stride, records, tables.size, bitmap),
                 router_grid_grad=hash_backward(xy, router_values, router_records, router_table.size),
                 head_grad=np.concatenate([g.reshape(-1) for g in head]))

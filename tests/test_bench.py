@@ -26,7 +26,7 @@ def test_reference_arm_line():
     line = run_bench('--impl', 'reference', '--steps', '1', '--warmup', '1')
     assert BASE_KEYS <= set(line)
     assert line['impl'] == 'reference' and line['unit'] == 'coords/s' and line['value'] > 0
-    assert line['higher_is_better'] is True and line['config']['workload'] == 'c2-experts'
+    assert line['higher_is_better'] is True and line['config']['workload'] == 'c4-experts'
     assert line['e2e'] == {'value': line['value'], 'unit': line['unit'], 'h2d_bytes_per_step': 0,
                            'd2h_bytes_per_step': 0}
     base = line['cpu_baseline']
@@ -34,7 +34,7 @@ def test_reference_arm_line():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize('workload', ['c2-experts', 'c2-planes', 'c3-experts'])
+@pytest.mark.parametrize('workload', ['c4-experts', 'c2-experts', 'c2-planes', 'c3-experts'])
 def test_our_arm_line(cuda, workload):
     batch = 1 << 16
     line = run_bench('--workload', workload, '--steps', '3', '--warmup', '3', '--batch', str(batch),
@@ -54,6 +54,12 @@ def test_our_arm_line(cuda, workload):
     assert line['decode']['value'] > 0
     first, last = line['loss_first_last']
     assert last == last and first == first, 'loss is NaN'
-    if workload == 'c3-experts':
+    if workload in ('c3-experts', 'c4-experts'):
         allocation = line['allocation']
-        assert allocation['tiles_allocated'] == round(0.3 * allocation['tiles_total'])
+        fraction = 0.3 if workload == 'c3-experts' else 0.2
+        assert allocation['tiles_allocated'] == round(fraction * allocation['tiles_total'])
+    if workload == 'c4-experts':
+        config = line['config']
+        assert config['experts'] == 64 and config['bands'] == 8 and config['image_hw'] == [32768, 32768]
+        assert config['fp16_payload_mib'] <= 50
+        assert line['decode']['launch_pixels'] == 1 << 24 and line['decode']['launches_per_pass'] == 64

@@ -14,7 +14,7 @@ import torch
 from oracle import oracle
 from odie_b200 import _lib
 from odie_b200 import selection as host
-from odie_b200.gpu_residual import DeviceScores, select_device
+from odie_b200.gpu_residual import ResidualAccumulator, select_device, select_live
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
@@ -111,11 +111,11 @@ def test_score_chunk_matches_reference_golden(cuda, golden, key):
     pred, u8, total = g[f'res_pred_{key}'], g[f'res_u8_{key}'], g[f'res_total_{key}']
     h, w = map(int, key.split('_')[0].split('x'))
     r = int(key.split('_')[1])
-    scores = DeviceScores((h, w), r)
+    scores = ResidualAccumulator((h, w), r)
     pred_d, u8_d = torch.from_numpy(pred).cuda(), torch.from_numpy(u8).cuda()
     for begin in range(0, h * w, 997):
         end = min(begin + 997, h * w)
-        scores.add(pred_d[begin:end], u8_d[begin:end], begin)
+        scores.accumulate(pred_d[begin:end], u8_d[begin:end], begin)
     assert np.array_equal(scores.totals.cpu().numpy(), total)
     assert np.array_equal(scores.counts, g[f'res_counts_{key}'])
 
@@ -125,11 +125,11 @@ def test_score_chunk_fp32_target(cuda):
     h, w, r = 40, 60, 17
     pred = rng.random((h * w, 3), dtype=np.float32)
     target = rng.random((h * w, 3), dtype=np.float32)
-    scores = DeviceScores((h, w), r)
-    scores.add(torch.from_numpy(pred).cuda(), torch.from_numpy(target).cuda(), 0)
+    scores = ResidualAccumulator((h, w), r)
+    scores.accumulate(torch.from_numpy(pred).cuda(), torch.from_numpy(target).cuda(), 0)
     expected = np.zeros(r * r)
-    oracle.score_chunk(pred, target, 0, h * w, w, r, 0, r * r, scores.xb.cpu().numpy(), scores.yb.cpu().numpy(),
-                       expected, False)
+    oracle.score_chunk(pred, target, 0, h * w, w, r, 0, r * r, scores.x_edges.cpu().numpy(),
+                       scores.y_edges.cpu().numpy(), expected, False)
     assert np.array_equal(scores.totals.cpu().numpy(), expected)
 
 
@@ -152,3 +152,49 @@ def test_tile_topk_bit_exact(cuda):
     assert np.array_equal(scores.cpu().numpy(), expected)
     assert np.array_equal(chosen.cpu().numpy(), oracle.topk(expected, k))
     assert selected.sum().item() == k
+
+
+def test_select_live_through_fused_decode(cuda):
+    """The stage boundary on a packed-plane model with its training runtime attached: the whole image decodes
+    through odie_decode in chunks, the residual totals equal the C oracle's over those very predictions bit for
+    bit, and the chosen support is the oracle's exact B2 greedy on them; the module path (no runtime) chooses
+    from its own predictions, within the fp16 tolerance of the fused ones."""
+    from odie_b200.data import ByteTarget
+    from odie_b200.model import PackedXYPlanes
+    from odie_b200.native_backend import NativeOptimizer
+    from tests.cases import close, plane_case, plane_config, random_image
+    shape = (97, 131)
+    resolutions, dims, supports, caps = plane_case(17, dense=10, packed=4, finest=64)
+    config = plane_config(resolutions, dims, 10, seed=17)
+    model = PackedXYPlanes(config, supports, dims, caps)
+    rgb = random_image(*shape, 17)
+    target = ByteTarget(torch.from_numpy(rgb).cuda())
+    planes = [torch.nn.Parameter(model.grid[l['plane_offset']:l['plane_offset'] + l['plane_node_capacity'] *
+                                            l['plane_dim']].detach()) for l in model.layout['levels']]
+    opt = NativeOptimizer(model, target, shape, config, planes, batch=2048)
+    ids = torch.randint(0, shape[0] * shape[1], (2048,), device='cuda', generator=torch.Generator('cuda').manual_seed(1))
+    for _ in range(5):
+        opt.train_batch(ids)
+    opt.call('sync_weights')
+    r, cap = resolutions[10], caps[10]  # the next level a stage boundary would open
+    metrics, support, record, counts, timing, totals = select_live(model, target, shape, r, cap, 2, 1000,
+                                                                   validate_scores=True)
+    assert timing['decode_path'] == 'fused odie_decode'
+    prediction = torch.empty((shape[0] * shape[1], 3), device='cuda')
+    opt.decode(0, shape[0] * shape[1], rgb=prediction)
+    torch.cuda.synchronize()
+    boxes = ResidualAccumulator(shape, r)
+    expected = np.zeros(r * r)
+    oracle.score_chunk(prediction.cpu().numpy(), rgb, 0, shape[0] * shape[1], shape[1], r, 0, r * r,
+                       boxes.x_edges.cpu().numpy(), boxes.y_edges.cpu().numpy(), expected, True)
+    assert np.array_equal(totals, expected), 'live residual totals differ from the oracle on the fused predictions'
+    chosen, nodes, iterations, used = oracle.select_benefit_cost(expected, r, cap)
+    assert np.array_equal(support, chosen) and record['iterations'] == iterations and record['closure_nodes'] == used
+    assert np.isfinite(metrics['mse']) and metrics['mse'] > 0
+    # the module path (no runtime attached) on the same weights
+    model._odie_runtime = None
+    metrics_m, _, _, _, timing_m, totals_m = select_live(model, target, shape, r, cap, 2, 1000, validate_scores=True)
+    assert timing_m['decode_path'] == 'module forward'
+    close(totals_m, totals, 2e-2, 1e-2, 'module-path residual totals')
+    close(metrics_m['mse'], metrics['mse'], 2e-3, 0.0, 'module-path mse')
+    opt.close()

@@ -20,7 +20,7 @@ from odie_b200.data import ByteTarget
 from odie_b200.evaluation import coordinates
 from odie_b200.model import PackedXYPlanes
 from odie_b200.native_backend import NativeOptimizer
-from tests.cases import close, layout_numpy, plane_case, plane_config, random_image
+from tests.cases import close, layout_numpy, plane_case, plane_config, random_image, FP16_QUANTUM, close_bound, scatter_bound
 
 pytestmark = pytest.mark.gpu
 SHAPE = (61, 47)
@@ -88,18 +88,21 @@ def test_step_gradients_match_oracle(cuda, router, k, activation, order):
                            f'{raw[tuple(diff[0])]} vs {ref["raw"][tuple(diff[0])]}')
     # fp16 network quantities
     squares = opt.copied('squares', (n,), torch.float32).cpu().numpy()
-    close(squares, ref['squares'], 2e-3, 2e-3, 'squares')
+    close(squares, ref['squares'], 2e-3, 1e-3, 'squares')
     values = read_rows(opt, 'gvals', n, W)
-    close(values.astype(np.float32), ref['values'], 2e-3, 2e-3, 'grid-gradient values')
+    close(values.astype(np.float32), ref['values'], 2e-3, 1e-3, 'grid-gradient values', quantum=FP16_QUANTUM)
     heads = opt.copied('head_grad', (opt.pointers['head_count'],), torch.float32).cpu().numpy()
-    close(heads, ref['head_grad'], 2e-3, 2e-3, 'head gradients')
+    close(heads, ref['head_grad'], 2e-3, 1e-3, 'head gradients')
     # the fp32 scatter, given the kernel's own fp16 values: fp32 tolerance
     grad = opt.copied('grid_grad', (model.grid.numel(),), torch.float32).cpu().numpy()
     lay = layout_numpy({k2: getattr(model, k2).cpu() for k2 in ('descriptors', 'node_bitmap', 'node_prefix', 'bitmap')})
-    scatter = oracle.query_backward(ref['xy'], values.astype(np.float16), lay['descriptors'], lay['node_bitmap'],
-                                    lay['node_prefix'], lay['bitmap'], grid.size)
-    close(grad, scatter, 1e-5, 1e-6, 'grid scatter')
-    close(grad, ref['grid_grad'], 2e-3, 2e-3, 'grid gradient end to end')
+    backward = lambda up: oracle.query_backward(ref['xy'], up, lay['descriptors'], lay['node_bitmap'],  # noqa: E731
+                                                lay['node_prefix'], lay['bitmap'], grid.size)
+    values16 = values.astype(np.float16)
+    close_bound(grad, backward(values16), scatter_bound(backward, values16), 'grid scatter')
+    # end to end: the values' own tolerance carried through the bilinear weights
+    close_bound(grad, ref['grid_grad'], scatter_bound(backward, ref['values'], 2e-3, 1e-3, FP16_QUANTUM),
+                'grid gradient end to end')
     opt.close()
 
 
@@ -167,7 +170,7 @@ def test_decode_matches_module_path(cuda):
     opt.decode(0, pixels, rgb=rgb32, rgb8=rgb8)
     with torch.no_grad():
         module = model(coordinates(SHAPE, torch.arange(pixels, device='cuda'))).float()
-    close(rgb32.cpu().numpy(), module.cpu().numpy(), 2e-3, 2e-3, 'decode vs module path')
+    close(rgb32.cpu().numpy(), module.cpu().numpy(), 2e-3, 1e-3, 'decode vs module path')
     expected8 = torch.round(rgb32.clamp(0, 1) * 255).to(torch.uint8)
     assert torch.equal(rgb8, expected8)
     opt.close()
