@@ -26,7 +26,15 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / '_ref'
-REFERENCE = Path(os.environ.get('ODIE_REFERENCE', '/root/reference'))
+
+
+def reference_root():
+    """The reference ODIE tree: $ODIE_REFERENCE, else a `reference` directory beside this repository."""
+    configured = os.environ.get('ODIE_REFERENCE')
+    return Path(configured) if configured else HERE.parent.parent / 'reference'
+
+
+REFERENCE = reference_root()
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 

@@ -2,7 +2,7 @@
 
 Run once, where the reference tree is present:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference]   (default: $ODIE_REFERENCE, else ../reference)
 
 The reference's CPU code for the hot path's integer/byte and fp64 parts is
 pure Python/NumPy/torch-CPU and runs here:
@@ -10,6 +10,7 @@ pure Python/NumPy/torch-CPU and runs here:
                      closure_nodes, select_benefit_cost (B2/E), select_mean_rank (B1)
   odie/model.py      plane_closure, make_node_index, make_layout
   odie/config.py     hash_grid_layout, resolve
+  odie/support_codec.py  encode_support (bitmap / DEFLATE mask storage of the fp16 checkpoint)
 The outputs are stored as small .npz fixtures beside this script so the tests
 (and the GPU box, which has no reference tree) can pin the oracle and the
 CUDA library against the reference itself.  Inputs are seeded synthetic data.
@@ -187,8 +188,34 @@ def configs(config):
     return out
 
 
+def support_codec():
+    """The reference's per-level mask encodings (odie/support_codec.py encode_support) of seeded masks: constant,
+    random, sparse, blocky (DEFLATE wins) and sizes that are not whole bytes.  Its optional JBIG1 bridge needs
+    libjbig; as the reference does when that bridge is unavailable, masks are then stored as bitmap / DEFLATE, so
+    the bridge is switched off here to record exactly that behaviour."""
+    import odie.support_codec as codec
+    codec.jbig_tool = lambda: None
+    rng = np.random.default_rng(1729)
+    masks = {'r1_one': np.ones(1, bool), 'r8_all': np.ones(64, bool), 'r9_none': np.zeros(81, bool),
+             'r37_random': rng.random(37 * 37) < .3, 'r64_sparse': rng.random(64 * 64) < .02,
+             'r5_single': np.eye(1, 25, 12, dtype=bool)[0], 'r3_pad': np.array([1, 0, 1, 1, 0, 0, 1, 0, 1], bool)}
+    blocky = np.zeros((100, 100), bool)
+    blocky[20:60, 30:90] = True
+    masks['r100_blocky'] = blocky.reshape(-1)
+    out = {}
+    for key, mask in masks.items():
+        record = codec.encode_support(torch.from_numpy(mask))
+        out[f'{key}_mask'] = mask.astype(np.uint8)
+        out[f'{key}_encoding'] = np.frombuffer(record['encoding'].encode(), dtype=np.uint8)
+        out[f'{key}_meta'] = np.array([record['num_cells'], record['resolution'], record['selected_count']], np.int64)
+        out[f'{key}_data'] = record['data'].numpy() if 'data' in record else np.zeros(0, np.uint8)
+    return out
+
+
 def main():
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle.build_ref import reference_root
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
     sel, model, config = reference_modules(root)
     fixtures = {
         'selection.npz': {**thresholds(sel), **pixel_cells(sel)},
@@ -196,6 +223,7 @@ def main():
         'greedy.npz': selections(sel),
         'layout.npz': {**closures(sel, model), **layouts(model)},
         'config.npz': configs(config),
+        'support_codec.npz': support_codec(),
     }
     for name, arrays in fixtures.items():
         np.savez_compressed(HERE / name, **arrays)
