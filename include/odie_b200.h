@@ -30,6 +30,12 @@ extern "C" {
  * bakes in at compile time (odie/build.py:26-30): "levels", "raw_width",
  * "router", "gate_k", "softplus", "rgb8", and "batch" (maximum coordinates per
  * step; the reference fixes 65536).
+ * "mode" takes the reference's bits (1 fused target, 4 half-precision grid
+ * gradients, 8 dirty-tile clearing, 16 parallel gate) and rejects others:
+ * targets are always read in the input kernel and the gate always runs fused in
+ * the heads kernel; grid gradients are always fp32 and Adam clears the entries
+ * it consumed, so bits 4 and 8 select nothing further ("half_grad" and
+ * "output" in odie_pointers are 0; "grid_gradient_precision" is "fp32").
  * Routed experts (no reference counterpart): "experts" (1..64 tables held)
  * with "hash_encoding" (one expert's grid; "grid" holds experts x its
  * parameters, expert-major), "router_encoding" (the coarse shared grid; fp32

@@ -59,12 +59,23 @@ struct Corner4 {
     int ix, iy;
     float w[4];
 };
+// floor(p) without the conversion unit (whose float/int conversions bound the gathers and scatters):
+// p + 1.5 x 2^23 rounded toward minus infinity is floor(p) + 1.5 x 2^23 exactly for |p| < 2^22 (the sum lies
+// in [2^23, 2^24), where fp32 spacing is 1), so its bits minus the constant's are floor(p) and the sum minus
+// the constant is floor(p) as a float.  Outside that range (coordinates far outside [0, 1], or NaN) the
+// integer lands outside [0, 2^22): off every grid, so level_on() hides the level.
+constexpr float FLOOR_MAGIC = 12582912.0f;  // 1.5 x 2^23
+constexpr int FLOOR_MAGIC_BITS = 0x4B400000;
+__device__ __forceinline__ float floor_split(float p, int& i) {
+    const float t = __fadd_rd(p, FLOOR_MAGIC);
+    i = __float_as_int(t) - FLOOR_MAGIC_BITS;
+    return __fsub_rn(t, FLOOR_MAGIC);  // exact: t and the constant share a binade
+}
 __device__ __forceinline__ Corner4 geometry(float x, float y, float scale) {
     Corner4 c;
     const float px = __fmaf_rn(scale, x, 0.5f), py = __fmaf_rn(scale, y, 0.5f);
-    c.ix = int(floorf(px));
-    c.iy = int(floorf(py));
-    const float fx = __fsub_rn(px, float(c.ix)), fy = __fsub_rn(py, float(c.iy));
+    const float bx = floor_split(px, c.ix), by = floor_split(py, c.iy);
+    const float fx = __fsub_rn(px, bx), fy = __fsub_rn(py, by);
     const float gx = __fsub_rn(1.0f, fx), gy = __fsub_rn(1.0f, fy);
     c.w[0] = __fmul_rn(gx, gy);
     c.w[1] = __fmul_rn(fx, gy);

@@ -40,17 +40,17 @@ struct RouterArgs {
 };
 
 // Band of a coordinate, clamped to the bands held here.  The global row is recovered exactly from
-// y = fl(row * fl(1 / (rows - 1))): its relative error is below 2^-22, so for rows < 2^20,
-// rint(y (rows - 1)) is the row.
+// y = fl(row * fl(1 / (rows - 1))): fl(y (rows - 1)) is within row x 2^-22 + 2^-24 of the row, below 1/2 for
+// rows < 2^20, so rounding it to the nearest integer gives the row.
 __host__ __device__ inline int band_of(const Banding& b, float y, int experts) {
     if (b.bands <= 1) return 0;
-    const double scaled = double(y) * double(b.rows - 1);
-    long long row = scaled > 0.0 ? (long long)(scaled + 0.5) : 0;
+    const float scaled = y * float(b.rows - 1);  // one fp32 product, as fl() above
+    int row = scaled > 0.0f ? int(scaled + 0.5f) : 0;  // scaled < 2^20: the sum is exact to well below 1/2
     row = row >= b.rows ? b.rows - 1 : row;
-    long long band = row * b.bands / b.rows;
-    const long long first = b.first_band, last = b.first_band + experts / b.per_band - 1;
+    int band = int((unsigned)row * (unsigned)b.bands / (unsigned)b.rows);  // row * bands < 2^26
+    const int first = b.first_band, last = b.first_band + experts / b.per_band - 1;
     band = band < first ? first : band > last ? last : band;
-    return int(band);
+    return band;
 }
 
 // Rejects a banding that the router and the heads cannot serve (throws std::invalid_argument).

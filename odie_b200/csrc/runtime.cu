@@ -151,7 +151,14 @@ struct Runtime {
         total = j.at("total").as_int();
         image_width = int(j.at("width").as_int());
         image_height = int(j.at("height").as_int());
+        // The reference's mode bits (odie/native/runtime.cu:93-143,256): 1 fused target, 4 half-precision grid
+        // gradients, 8 dirty-tile gradient clearing, 16 parallel gate.  Each names a path this runtime always
+        // takes or supersedes: the target is read inside the input kernel (1); the gate runs fused into the heads
+        // kernel (16); grid gradients accumulate in fp32 (4 asks for fp16 to halve the reference's atomic traffic;
+        // fp32 keeps the reference's fp32-path precision) and Adam clears exactly the entries it consumed, so no
+        // per-step clearing pass exists to restrict to dirty tiles (8).  Any other bit is rejected.
         mode = int(j.value("mode", 20));
+        ODIE_REQUIRE((mode & ~(1 | 4 | 8 | 16)) == 0, "mode: only the reference's bits 1, 4, 8 and 16 are defined");
         // The reference's warp-aggregation threshold; accepted for its JSON contract.  The scatter here
         // needs no threshold: it spreads equal addresses apart by its visiting order instead.
         warp_limit = int(j.value("warp_limit", 128));
@@ -717,6 +724,7 @@ struct Runtime {
           << ",\"decoder_grad\":" << (unsigned long long)(head_grad() + gate_count)
           << ",\"head_grad\":" << (unsigned long long)head_grad() << ",\"head_count\":" << head_count
           << ",\"gate_count\":" << gate_count << ",\"output\":0,\"raw\":" << (unsigned long long)raw.ptr
+          << ",\"mode\":" << mode << ",\"grid_gradient_precision\":\"fp32\""
           << ",\"dirty_count\":0,\"grid_half\":" << (unsigned long long)grid_half.ptr
           << ",\"head_half\":" << (unsigned long long)head_half.ptr << ",\"error_flag\":" << (unsigned long long)error_flag.ptr
           << ",\"capacity\":" << capacity << ",\"input_width\":" << input_width

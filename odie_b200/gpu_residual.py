@@ -42,6 +42,7 @@ class ResidualAccumulator:
     def accumulate(self, prediction, target_rows, first_pixel):
         """Add the residual of fp32 predictions [n, 3] for pixels [first_pixel, first_pixel + n); target_rows:
         the same pixels' u8 (or fp32) RGB."""
+        prediction, target_rows = prediction.contiguous(), target_rows.contiguous()  # read as packed [n, 3] rows
         width = self.shape[1]
         last_pixel = first_pixel + prediction.shape[0]
         top = int(self.row_cell[first_pixel // width])

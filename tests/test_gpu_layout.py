@@ -102,7 +102,7 @@ def test_activate_support_builds_the_host_layout_on_device(cuda):
     config = plane_config(resolutions, dims, 10, seed=9)
     model = PackedXYPlanes(config, supports, dims, caps)
     model.set_active_prefix(level)
-    with pytest.raises(ValueError, match='within its cap'):
+    with pytest.raises(ValueError, match='closes over'):
         model.activate_support(level, torch.ones(r * r, dtype=torch.bool))
     report = model.activate_support(level, support)
     new_supports = list(supports)

@@ -191,10 +191,18 @@ def test_select_live_through_fused_decode(cuda):
     chosen, nodes, iterations, used = oracle.select_benefit_cost(expected, r, cap)
     assert np.array_equal(support, chosen) and record['iterations'] == iterations and record['closure_nodes'] == used
     assert np.isfinite(metrics['mse']) and metrics['mse'] > 0
-    # the module path (no runtime attached) on the same weights
+    # the module path (no runtime attached) on the same weights: its totals are the oracle's on its own predictions,
+    # and those predictions are the fused ones within the fp16 decode tolerance
     model._odie_runtime = None
-    metrics_m, _, _, _, timing_m, totals_m = select_live(model, target, shape, r, cap, 2, 1000, validate_scores=True)
+    metrics_m, support_m, _, _, timing_m, totals_m = select_live(model, target, shape, r, cap, 2, 1000,
+                                                                 validate_scores=True)
     assert timing_m['decode_path'] == 'module forward'
-    close(totals_m, totals, 2e-2, 1e-2, 'module-path residual totals')
-    close(metrics_m['mse'], metrics['mse'], 2e-3, 0.0, 'module-path mse')
+    with torch.no_grad():
+        from odie_b200.evaluation import coordinates
+        module = model(coordinates(shape, torch.arange(shape[0] * shape[1], device='cuda'))).float()
+    expected_m = np.zeros(r * r)
+    oracle.score_chunk(module.cpu().numpy(), rgb, 0, shape[0] * shape[1], shape[1], r, 0, r * r,
+                       boxes.x_edges.cpu().numpy(), boxes.y_edges.cpu().numpy(), expected_m, True)
+    assert np.array_equal(totals_m, expected_m), 'module-path totals differ from the oracle on its own predictions'
+    close(module.cpu().numpy(), prediction.cpu().numpy(), 2e-3, 1e-3, 'module vs fused predictions')
     opt.close()

@@ -182,3 +182,21 @@ def test_create_rejects_invalid_settings(cuda):
                           grid_lr=1e-2, gate_lr=1e-3, decoder_lr=1e-3))
     assert lib.odie_create(bad.encode()) is None
     assert 'total' in _lib.error()
+
+
+def test_mode_bits(cuda):
+    """The reference's mode bits are accepted (their paths are always taken or superseded); other bits are refused
+    with a message."""
+    import json as _json
+    config, model, rgb, opt = setup(seed=5)
+    assert opt.pointers['mode'] == 20 and opt.pointers['grid_gradient_precision'] == 'fp32'
+    assert opt.pointers['half_grad'] == 0 and opt.pointers['output'] == 0
+    opt.close()
+    lib = _lib.library()
+    settings = dict(stream=torch.cuda.current_stream().cuda_stream, total=model.grid.numel(), width=SHAPE[1],
+                    height=SHAPE[0], mode=32, rgb=0, grid=model.grid.data_ptr(), decoder=model.decoder.params.data_ptr(),
+                    gate=model.gate.params.data_ptr(), levels=16, active=16, descriptors=model.descriptors.data_ptr(),
+                    node_bitmap=model.node_bitmap.data_ptr(), node_prefix=model.node_prefix.data_ptr(),
+                    bitmap=model.bitmap.data_ptr(), grid_lr=1e-2, gate_lr=1e-3, decoder_lr=1e-3)
+    assert not lib.odie_create(_json.dumps(settings).encode())
+    assert 'mode' in _lib.error()
