@@ -12,6 +12,8 @@ Workloads (odie_b200/workloads.py):
   c2-experts: 16 routed experts (T = 2^16) on a 2040 x 1356 image, 2^20 coords per step.
   c2-planes: the reference's own packed-plane method on the same image and batch.
   c3-experts: 8 routed experts (T = 2^17) on a 4096 x 4096 image with 30 % tile allocation, 2^21.
+  c1-hash: the single fp32 hash grid (T = 2^19, 16 levels, fp32 MLP 32-64-64-3 with a sigmoid output) on a
+    512 x 512 image, 2^18 uniform coordinates per step with bilinear targets, dense Adam (odie_hashgrid32_*).
 
 One JSON line on rank 0.  `value` is whole-job coords/s with inputs resident in HBM (device-timed
 with CUDA events, max over ranks); `e2e` is the same metric through the public API with the step's
@@ -41,8 +43,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = 'train coords/s (fwd+bwd+Adam) & decode Gpix/s at 1/2/4/8 B200'
 UNIT = 'coords/s'
-WORKLOADS = ('c4-experts', 'c2-experts', 'c2-planes', 'c3-experts')
-BATCHES = {'c4-experts': 1 << 22, 'c3-experts': 1 << 21, 'c2-experts': 1 << 20, 'c2-planes': 1 << 20}
+WORKLOADS = ('c4-experts', 'c2-experts', 'c2-planes', 'c3-experts', 'c1-hash')
+BATCHES = {'c4-experts': 1 << 22, 'c3-experts': 1 << 21, 'c2-experts': 1 << 20, 'c2-planes': 1 << 20, 'c1-hash': 1 << 18}
 DECODE_LAUNCH = 1 << 24  # pixels per decode launch of the gigapixel reconstruction
 CPU_WINDOW_ROWS = 1024   # rows of the gigapixel image the CPU legs sample from (their cost does not depend on it)
 
@@ -100,10 +102,18 @@ def c4_window(procedural=True):
 def cpu_step_of(name, batch, procedural=True):
     """The oracle's CPU restatement of one training step of the workload (same layout, seeded weights), and the
     (height, width) of the image window its coordinates are sampled from."""
-    from oracle.cpu_step import CpuExpertStep, CpuStep, hash_levels_for_cpu, plane_levels_for_cpu
+    from oracle.cpu_step import CpuExpertStep, CpuHashGrid32Step, CpuStep, hash_levels_for_cpu, plane_levels_for_cpu
     from odie_b200 import layout as host_layout
     from odie_b200 import workloads
     rng = np.random.default_rng(0)
+    if name == 'c1-hash':
+        from odie_b200.data import blobs_and_gratings
+        from odie_b200.hashgrid32 import c1_config, xavier_heads
+        records, total = host_layout.hash_levels(c1_config()['hash_encoding'])
+        image = blobs_and_gratings(512, 512, 1729).numpy()
+        step = CpuHashGrid32Step(image, records, (rng.random(total, dtype=np.float32) * 2 - 1) * 1e-4,
+                                 xavier_heads(1729).numpy())
+        return step, (512, 512)
     if name in ('c2-experts', 'c3-experts', 'c4-experts'):
         banding = None
         if name == 'c2-experts':
@@ -306,13 +316,19 @@ def cpu_legs(args, budget=10.0, threads_list=None):
     sample = 1 << 14
     pixels = shape[0] * shape[1]
     g = torch.Generator().manual_seed(1)
+
+    def one_step():
+        if args.workload == 'c1-hash':
+            step.step_uniform(sample)
+        else:
+            step.step(torch.randint(0, pixels, (sample,), generator=g))
     legs = []
     for threads in threads_list:
         torch.set_num_threads(threads)
-        step.step(torch.randint(0, pixels, (sample,), generator=g))  # warm-up
+        one_step()  # warm-up
         started, coords, steps = time.perf_counter(), 0, 0
         while time.perf_counter() - started < budget or steps < 2:
-            step.step(torch.randint(0, pixels, (sample,), generator=g))
+            one_step()
             coords += sample
             steps += 1
         seconds = time.perf_counter() - started
@@ -336,11 +352,17 @@ def run_reference(args):
     sample = 1 << 14
     g = torch.Generator().manual_seed(2)
     pixels = shape[0] * shape[1]
+
+    def one_step():
+        if args.workload == 'c1-hash':
+            step.step_uniform(sample)
+        else:
+            step.step(torch.randint(0, pixels, (sample,), generator=g))
     for _ in range(args.warmup):
-        step.step(torch.randint(0, pixels, (sample,), generator=g))
+        one_step()
     started = time.perf_counter()
     for _ in range(args.steps):
-        step.step(torch.randint(0, pixels, (sample,), generator=g))
+        one_step()
         steps += 1
         coords += sample
     seconds = time.perf_counter() - started
@@ -459,6 +481,9 @@ def main():
         args.batch = BATCHES[args.workload]
     if args.impl == 'reference':
         run_reference(args)
+        return
+    if args.workload == 'c1-hash':
+        main_c1(args)
         return
     rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
     local = int(os.environ.get('LOCAL_RANK', 0))
@@ -754,6 +779,189 @@ def main():
             line['sampler'] = sampler
         print(json.dumps(line), flush=True)
     opt.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def fma_peak(lib, iterations=1 << 16):
+    """Measured fp32 FMA throughput of this GPU (TFLOP/s; odie_fma_probe, best of 3)."""
+    sink = torch.zeros(1, device='cuda')
+    stream = torch.cuda.current_stream()
+    lib.odie_fma_probe(iterations, sink.data_ptr(), stream.cuda_stream)  # warm-up
+    best = float('inf')
+    for _ in range(3):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        flop = lib.odie_fma_probe(iterations, sink.data_ptr(), stream.cuda_stream)
+        end.record()
+        end.synchronize()
+        best = min(best, start.elapsed_time(end))
+    return flop / (best / 1e3) / 1e12
+
+
+def main_c1(args):
+    """c1-hash: the single fp32 hash grid through odie_hashgrid32_* (one GPU per process; each rank trains its
+    own replica on its own coordinates, no exchange)."""
+    rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    torch.cuda.set_device(local)
+    torch.cuda.set_stream(torch.cuda.Stream())
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
+    from odie_b200 import _lib
+    from odie_b200.hashgrid32 import HEAD_PARAMS, HashGrid32, HashGrid32Trainer, c1_config, c1_image
+    lib = _lib.library()
+    n = args.batch
+    config = c1_config(seed=1729 + rank, batch=n)
+    model = HashGrid32(config)
+    image = c1_image(1729)
+    trainer = HashGrid32Trainer(model, image, n)
+    seed = 1729 + rank
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for k in range(args.warmup):
+        trainer.step(step=k, seed=seed)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        barrier()
+        launches_before = lib.odie_launch_count()
+        start.record()
+        for k in range(args.steps):
+            trainer.step(step=args.warmup + k, seed=seed)
+        end.record()
+        launches = lib.odie_launch_count() - launches_before
+        barrier()
+    ms_t = torch.tensor([start.elapsed_time(end)], device='cuda')
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t)
+    value = world * n * args.steps / (ms / 1e3)
+    # stage times: CUDA events around each stage's launches (one stream, so each is its kernels' own time)
+    _lib.check(lib.odie_hashgrid32_profile(trainer.handle, 1))
+    for k in range(args.steps):
+        trainer.step(step=args.warmup + k, seed=seed)
+    report = json.loads(lib.odie_hashgrid32_profile_report(trainer.handle))
+    _lib.check(lib.odie_hashgrid32_profile(trainer.handle, 0))
+    # end to end: each step's coordinates from pinned host memory (uploaded on a copy stream one step ahead) and
+    # its mean loss read back to the host
+    host_xy = torch.rand((args.steps, n, 2), generator=torch.Generator().manual_seed(seed)).pin_memory()
+    device_xy = [torch.empty((n, 2), device='cuda') for _ in range(2)]
+    loss_host = torch.empty(args.steps, dtype=torch.float64).pin_memory()
+    main_stream, copy_stream = torch.cuda.current_stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    released = [torch.cuda.Event() for _ in range(2)]
+    squares = trainer.read('squares', n)
+
+    def upload(k):
+        with torch.cuda.stream(copy_stream):
+            if k >= 2:
+                copy_stream.wait_event(released[k % 2])
+            device_xy[k % 2].copy_(host_xy[k], non_blocking=True)
+            uploaded[k % 2].record(copy_stream)
+    def read_loss(k):
+        _lib.check(lib.odie_copy(squares.data_ptr(), int(trainer.buffers['squares']), 4 * n, main_stream.cuda_stream))
+        loss_host[k:k + 1].copy_((squares.sum(dtype=torch.float64) / n).reshape(1), non_blocking=True)
+    # warm-up of the loop's own operations (torch loads the reduction's kernels on first use)
+    upload(0)
+    main_stream.wait_event(uploaded[0])
+    trainer.step(step=0, xy=device_xy[0])
+    read_loss(0)
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    copy_stream.wait_event(e_start)
+    upload(0)
+    for k in range(args.steps):
+        if k + 1 < args.steps:
+            upload(k + 1)
+        main_stream.wait_event(uploaded[k % 2])
+        trainer.step(step=k, xy=device_xy[k % 2])
+        released[k % 2].record(main_stream)
+        read_loss(k)
+    e_end.record()
+    barrier()
+    e_ms = torch.tensor([e_start.elapsed_time(e_end)], device='cuda')
+    if dist is not None:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e = world * n * args.steps / (float(e_ms) / 1e3)
+    # decode of the whole image, fp32 RGB
+    pixels = image.shape[0] * image.shape[1]
+    rgb = torch.empty((pixels, 3), device='cuda')
+    trainer.decode(begin=0, n=pixels, out=rgb)
+    barrier()
+    d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    repeats = 20
+    d_start.record()
+    for _ in range(repeats):
+        trainer.decode(begin=0, n=pixels, out=rgb)
+    d_end.record()
+    barrier()
+    d_seconds = d_start.elapsed_time(d_end) / 1e3
+    if rank == 0:
+        hbm, _, _, peak_kind = peaks()
+        fma = fma_peak(lib)
+        flop_per_coord = 2 * 3 * (32 * 64 + 64 * 64 + 64 * 3)  # forward, data backward, weight gradients
+        total = model.total
+        work = {'fused_step': ('fp32', flop_per_coord * n),
+                'encode_backward': ('hbm', (8 + 4 * 32 + 16 * 4 * 8 * 2) * n),  # xy, dx rows, corner r+w
+                'reduce_partials': ('hbm', None),
+                'adam_grid': ('hbm', 40 * total),  # g, p, m, v, step read; p, m, v, step written; g cleared
+                'adam_heads': ('hbm', None)}
+        per_stage = {}
+        for k, v in report.items():
+            if not v['launches']:
+                continue
+            seconds = v['ms'] / args.steps / 1e3
+            bound, amount = work[k]
+            achieved = (amount / seconds / (1e12 if bound == 'fp32' else 1e9)) if amount else None
+            peak = fma if bound == 'fp32' else hbm
+            per_stage[k] = {'ms_per_step': v['ms'] / args.steps, 'bound': bound, 'algorithmic_per_step': amount,
+                            'achieved': achieved, 'unit': 'TFLOP/s' if bound == 'fp32' else 'GB/s',
+                            'frac': achieved / peak if achieved else None}
+        dominant = max(per_stage, key=lambda k: per_stage[k]['ms_per_step'])
+        d = per_stage[dominant]
+        roofline = {'kernel': dominant, 'bound': 'fp32 CUDA-core FMA' if d['bound'] == 'fp32' else 'hbm',
+                    'achieved': d['achieved'], 'peak': fma if d['bound'] == 'fp32' else hbm, 'unit': d['unit'],
+                    'frac': d['frac'], 'traffic': traffic_of('c1-hash', dominant),
+                    'peak_source': ('measured (odie_fma_probe, fp32 FMA)' if d['bound'] == 'fp32'
+                                    else f'{peak_kind} (HBM copy)'),
+                    'timing': 'stage events on one stream (kernel time)', 'stages': per_stage}
+        dec_bytes = 16 * 4 * 8 + 8 + 12
+        base = None
+        if world == 1 and not args.no_cpu_baseline:
+            legs = cpu_legs(args)
+            base = dict(legs[0], one_thread=legs[1])
+        losses = loss_host.numpy()
+        line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+                'warmup': args.warmup, 'ms_per_step': ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
+                'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+                'config': {'workload': 'c1-hash', 'image_hw': list(image.shape[:2]), 'global_batch': world * n,
+                           'batch_per_gpu': n, 'levels': 16, 'log2_hashmap_size': 19, 'grid_params': total,
+                           'head_params': HEAD_PARAMS, 'sampling': 'uniform (Philox on the device), bilinear targets',
+                           'parallelism': f'replicas{world} (each GPU its own model and coordinates)',
+                           'l2': 'per-step activations (dx rows 32 MB) and the 30.6 MB table; dense Adam state '
+                                 '92 MB: inputs larger than L2 across the step'},
+                'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': 8 * n, 'd2h_bytes_per_step': 8},
+                'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base,
+                'decode': {'value': pixels * repeats / d_seconds / 1e9, 'unit': 'Gpix/s', 'pixels': pixels,
+                           'roofline': {'bound': 'hbm', 'algorithmic_bytes_per_pixel': dec_bytes,
+                                        'achieved': pixels * repeats / d_seconds * dec_bytes / 1e9, 'peak': hbm,
+                                        'frac': pixels * repeats / d_seconds * dec_bytes / 1e9 / hbm,
+                                        'note': 'fp32 corner reads (L2-resident table) + fp32 RGB out'}},
+                'fma_peak_tflops': fma, 'loss_first_last': [float(losses[0]), float(losses[-1])],
+                'clocks': clocks.summary()}
+        print(json.dumps(line), flush=True)
+    trainer.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

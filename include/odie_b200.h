@@ -249,6 +249,10 @@ ODIE_API int odie_l2_probe(float* table, int64_t table_bytes, int mode, int64_t 
  * int32) = 2 when the wait ran out -- the code the heads kernel leaves in
  * its error flag -- and 0 if it completed.  The context stays usable. */
 ODIE_API int odie_wait_probe(uint32_t limit, int32_t* status, uint64_t stream);
+/* fp32 FMA throughput probe (no reference counterpart): one launch of 8 x SMs blocks of 256 threads, each
+ * running 8 independent fma chains of `iterations` steps; returns the launch's FLOP (-1 on bad input).
+ * The caller times it: the roofline denominator of the fp32 CUDA-core MLP. */
+ODIE_API int64_t odie_fma_probe(int iterations, float* sink, uint64_t stream);
 
 /* ------------------------------------------------------------------------
  * Tile top-k allocation (the allocation benchmark; no reference counterpart).
@@ -273,6 +277,48 @@ ODIE_API int odie_topk(const double* scores, int count, int k, int64_t* chosen, 
  * ------------------------------------------------------------------------ */
 ODIE_API int odie_procedural_image(uint64_t seed, int width, int height, int row0, int rows, uint8_t* rgb,
                    uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Single fp32 hash grid with an fp32 MLP (the hash-grid encoding of
+ * odie/hash_grid.py:8-80 with the layout of odie/config.py:83-94, in fp32:
+ * 16 levels x 2 features, MLP 32 -> 64 -> 64 -> 3, no biases, ReLU hidden
+ * layers, sigmoid output).
+ * odie_hashgrid32_create: JSON {"image": ptr f32[height][width][3],
+ * "width", "height", "grid": ptr f32[total], "heads": ptr f32[6336]
+ * (W1 [64][32] | W2 [64][64] | W3 [3][64], row-major [out][in]),
+ * "hash_encoding": {n_levels 16, n_features_per_level 2, log2_hashmap_size,
+ * base_resolution, per_level_scale}, optional "total" (checked), "capacity"
+ * (largest batch, default 2^18), "grid_lr", "head_lr" (1e-2), "beta1" (0.9),
+ * "beta2" (0.99), "eps" (1e-15)}.  Image, grid and heads stay caller-owned;
+ * Adam updates grid and heads in place.  NULL with odie_error() on bad input.
+ * odie_hashgrid32_step: one step on n coordinates: xy f32[n][2] on the device,
+ * or NULL for uniform coordinates in [0, 1)^2 drawn from Philox4x32-10 (key
+ * seed, counter (slot, step); x = (word0 >> 8) 2^-24, y = (word1 >> 8) 2^-24).
+ * Targets are the image bilinearly sampled at the coordinates; loss = mean
+ * of the 3 n squared errors.  update = 0 computes the gradients only
+ * (grid_grad accumulates until an update consumes it).  Every call runs on the
+ * stream it is given (0: the legacy default stream).
+ * odie_hashgrid32_update: the Adam update alone on the accumulated gradients.
+ * odie_hashgrid32_decode: fp32 RGB rgb[n][3] at xy f32[n][2], or at the pixel
+ * centres (col / (W - 1), row / (H - 1)) of pixels [begin, begin + n) when
+ * xy is NULL.
+ * odie_hashgrid32_pointers: JSON with the library-owned device buffers
+ * (grid_grad, head_grad, moments, steps, xy, dx, squares, error_flag), the
+ * handle's stream and the sizes.
+ * ------------------------------------------------------------------------ */
+ODIE_API void* odie_hashgrid32_create(const char* json);
+ODIE_API int odie_hashgrid32_step(void* handle, uint64_t seed, uint64_t step, int64_t n, const float* xy, int update,
+                   uint64_t stream);
+ODIE_API int odie_hashgrid32_update(void* handle, uint64_t stream);
+ODIE_API int odie_hashgrid32_decode(void* handle, int64_t begin, int64_t n, const float* xy, float* rgb,
+                   uint64_t stream);
+ODIE_API const char* odie_hashgrid32_pointers(void* handle);
+/* Stage timers of the steps (CUDA events on the step's stream): enable 1 / disable 0 (resets the record);
+ * report {stage: {"launches": k, "ms": total}} for fused_step, encode_backward, reduce_partials, adam_grid,
+ * adam_heads. */
+ODIE_API int odie_hashgrid32_profile(void* handle, int enable);
+ODIE_API const char* odie_hashgrid32_profile_report(void* handle);
+ODIE_API void odie_hashgrid32_destroy(void* handle);
 
 /* ------------------------------------------------------------------------
  * Allocation-free tile top-k (no counterpart in the reference).

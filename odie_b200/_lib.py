@@ -29,6 +29,7 @@ SIGNATURES = {
     'odie_step_stratified': (I32, [P, U64, U64, I32, I32]),
     'odie_stratified_ids': (I32, [U64, U64, I32, I32, I64, P, U64]),
     'odie_wait_probe': (I32, [C.c_uint32, P, U64]),
+    'odie_fma_probe': (I64, [I32, P, U64]),
     'odie_step_heads': (I32, [P]),
     'odie_grid_update': (I32, [P]),
     'odie_profile': (I32, [P, I32]),
@@ -61,6 +62,14 @@ SIGNATURES = {
     'odie_tile_topk_noalloc': (I32, [P, P, I32, I32, I32, I32, P, P, P, U64]),
     'odie_topk': (I32, [P, I32, I32, P, P, U64]),
     'odie_procedural_image': (I32, [U64, I32, I32, I32, I32, P, U64]),
+    'odie_hashgrid32_create': (P, [C.c_char_p]),
+    'odie_hashgrid32_step': (I32, [P, U64, U64, I64, P, I32, U64]),
+    'odie_hashgrid32_update': (I32, [P, U64]),
+    'odie_hashgrid32_decode': (I32, [P, I64, I64, P, P, U64]),
+    'odie_hashgrid32_pointers': (C.c_char_p, [P]),
+    'odie_hashgrid32_profile': (I32, [P, I32]),
+    'odie_hashgrid32_profile_report': (C.c_char_p, [P]),
+    'odie_hashgrid32_destroy': (None, [P]),
 }
 
 

@@ -12,7 +12,7 @@ from pathlib import Path
 PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 SOURCES = ['encode.cu', 'step.cu', 'mlp_tc.cu', 'router.cu', 'probe.cu', 'layout.cu', 'residual.cu', 'selection.cu',
-           'synth.cu', 'runtime.cu']
+           'synth.cu', 'hashgrid32.cu', 'runtime.cu']
 LIBRARY = PACKAGE / 'libodie_b200.so'
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 FLAGS = ['-O3', '-std=c++17', '-lineinfo', '--expt-relaxed-constexpr', '-Xcompiler', '-fPIC',

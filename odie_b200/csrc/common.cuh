@@ -29,10 +29,65 @@ struct CudaError : std::runtime_error {
     } while (0)
 
 void set_error(const std::string& message);  // thread-local, read by odie_error()
+// Runs f, turning an exception into status -1 and the thread's error message (every C-ABI entry point).
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
 void note_launch(int kernels = 1);          // counts this library's kernel launches (odie_launch_count)
 int sm_count();                              // cached multiprocessor count of the current device
 
 inline unsigned blocks_for(long long n, int threads) { return unsigned((n + threads - 1) / threads); }
+
+// Device buffer owned by the library (released with its owner).
+template <typename T>
+struct DeviceArray {
+    T* ptr = nullptr;
+    long long count = 0;
+    DeviceArray() = default;
+    DeviceArray(const DeviceArray&) = delete;
+    DeviceArray& operator=(const DeviceArray&) = delete;
+    ~DeviceArray() { release(); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        count = 0;
+    }
+    void allocate(long long n) {
+        release();
+        if (n <= 0) return;
+        ODIE_CUDA(cudaMalloc(&ptr, size_t(n) * sizeof(T)));
+        count = n;
+    }
+    void zero(cudaStream_t stream) {
+        if (count) ODIE_CUDA(cudaMemsetAsync(ptr, 0, size_t(count) * sizeof(T), stream));
+    }
+};
+
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011):
+// a counter-based generator, so slot j of step s has its own stream with no state to carry.
+struct Philox4 {
+    uint32_t v[4];
+};
+__device__ __forceinline__ Philox4 philox4x32_10(Philox4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        if (r > 0) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint32_t lo0 = 0xD2511F53u * c.v[0], hi0 = __umulhi(0xD2511F53u, c.v[0]);
+        const uint32_t lo1 = 0xCD9E8D57u * c.v[2], hi1 = __umulhi(0xCD9E8D57u, c.v[2]);
+        c = Philox4{{hi1 ^ c.v[1] ^ k0, lo1, hi0 ^ c.v[3] ^ k1, lo0}};
+    }
+    return c;
+}
 
 // ---------------------------------------------------------------- levels
 // One encoding level as the kernels see it (built on the host from the

@@ -9,6 +9,8 @@
 // gradient (odie/packed_kernels.cu:66-88, odie/native/runtime.cu:111-143) with
 // 8-byte vector reductions for F=2, one thread per coordinate in a scrambled
 // visiting order, and shared-memory pre-aggregation of coarse levels.
+#include <atomic>
+
 #include "encode.cuh"
 
 namespace odie {
@@ -182,9 +184,30 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
     for (int j = 0; j < W / 8; ++j) dst[j] = make_uint4(row[4 * j], row[4 * j + 1], row[4 * j + 2], row[4 * j + 3]);
 }
 
-__device__ __forceinline__ float upstream_value(const __half* __restrict__ up, const EncodeArgs& a, long long i, int col) {
-    if (a.row_major) return __half2float(up[i * a.width + col]);
-    return __half2float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
+// Gradient value of column col of coordinate i: fp16 rows (the fp16 network) or fp32 rows (the fp32 hash grid).
+__device__ __forceinline__ float as_float(__half v) { return __half2float(v); }
+__device__ __forceinline__ float as_float(float v) { return v; }
+template <typename U>
+__device__ __forceinline__ float upstream_value(const U* __restrict__ up, const EncodeArgs& a, long long i, int col) {
+    if (a.row_major) return as_float(up[i * a.width + col]);
+    return as_float(up[((long long)(col >> 1) * a.stride + i) * 2 + (col & 1)]);
+}
+// The value pairs of columns (2c0, 2c0 + 1) .. (2c0 + 6, 2c0 + 7) of row-major row i, 16-byte aligned:
+// one 16-byte load of fp16 values, two of fp32 ones.
+__device__ __forceinline__ void load_pairs4(const __half* __restrict__ up, long long i, int width, int c0, float (&u)[8]) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(up + i * width + 2 * c0));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        u[2 * g] = __half2float(lo_half(w[g]));
+        u[2 * g + 1] = __half2float(hi_half(w[g]));
+    }
+}
+__device__ __forceinline__ void load_pairs4(const float* __restrict__ up, long long i, int width, int c0, float (&u)[8]) {
+    const float4* src = reinterpret_cast<const float4*>(up + i * width + 2 * c0);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w;
+    u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
 }
 
 // Visiting order of the direct scatter kernel.  Training batches are often
@@ -272,10 +295,10 @@ __device__ __forceinline__ bool combine_lanes(float (&v)[8], long long key, int 
 // scrambled), each lane one coordinate over all its levels not in skip_levels
 // (those go through the shared-memory kernel below).  F=2 levels combine lanes
 // that share a cell before the 8-byte vector reductions.
-template <bool FROM_DESC>
+template <bool FROM_DESC, typename U>
 __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
                                                               const __grid_constant__ LevelTable table,
-                                                              const __half* __restrict__ upstream,
+                                                              const U* __restrict__ upstream,
                                                               float* __restrict__ grad, unsigned skip_levels,
                                                               uint32_t mask, int split) {
     const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -368,10 +391,11 @@ struct CoarseList {
 // coherence of the batch.
 constexpr int RUN_RES = 64;
 
+template <typename U>
 __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const EncodeArgs a,
                                                                      const __grid_constant__ LevelTable table,
                                                                      const __grid_constant__ CoarseList list,
-                                                                     const __half* __restrict__ upstream,
+                                                                     const U* __restrict__ upstream,
                                                                      float* __restrict__ grad) {
     extern __shared__ float acc[];
     const int experts = a.expert ? a.experts : 1;
@@ -477,11 +501,11 @@ __device__ __forceinline__ void runs_flush(const Level& d, float* tab, int e, in
     }
 }
 
-template <bool VEC, int KIND>
+template <bool VEC, int KIND, typename U>
 __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(const EncodeArgs a,
                                                                               const __grid_constant__ LevelTable table,
                                                                               const __grid_constant__ CoarseList list,
-                                                                              const __half* __restrict__ upstream,
+                                                                              const U* __restrict__ upstream,
                                                                               float* __restrict__ grad) {
     extern __shared__ float acc[];
     const int experts = a.expert ? a.experts : 1;
@@ -512,14 +536,8 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(c
                 valid = e >= 0 && e < experts;  // an id outside the tables would land outside shared memory
             }
             const float2 p = __ldg(coords + i);
-            uint32_t pairs[RUNS_GROUP];
-            if (VEC) {
-                const uint4 q = __ldg(reinterpret_cast<const uint4*>(upstream + i * a.width + 2 * c0));
-                pairs[0] = q.x;
-                pairs[1] = q.y;
-                pairs[2] = q.z;
-                pairs[3] = q.w;
-            }
+            float pairs[2 * RUNS_GROUP];
+            if (VEC) load_pairs4(upstream, i, a.width, c0, pairs);
 #pragma unroll
             for (int g = 0; g < RUNS_GROUP; ++g) {
                 const int c = c0 + g;
@@ -536,8 +554,8 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(c
                 }
                 float u0, u1;
                 if (VEC) {
-                    u0 = __half2float(lo_half(pairs[g]));
-                    u1 = __half2float(hi_half(pairs[g]));
+                    u0 = pairs[2 * g];
+                    u1 = pairs[2 * g + 1];
                 } else {
                     u0 = upstream_value(upstream, a, i, d.col);
                     u1 = upstream_value(upstream, a, i, d.col + 1);
@@ -628,35 +646,37 @@ static uint32_t visit_mask(long long n) {
     return size - 1;
 }
 
-template <int KIND>
+template <int KIND, typename U>
 static void set_runs_smem() {
-    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<true, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<true, KIND, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    COARSE_SMEM_FLOATS * 4));
-    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<false, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<false, KIND, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    COARSE_SMEM_FLOATS * 4));
 }
 
+template <typename U>
 struct RunsLaunch {
     const EncodeArgs& a;
     const LevelTable& table;
     const CoarseList& list;
-    const __half* upstream;
+    const U* upstream;
     float* grad;
     int blocks, smem;
     cudaStream_t stream;
 };
 
-template <int KIND>
-static void launch_runs(const RunsLaunch& l, bool vec) {
+template <int KIND, typename U>
+static void launch_runs(const RunsLaunch<U>& l, bool vec) {
     if (vec)
-        encode_backward_runs_kernel<true, KIND><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
-                                                                                            l.upstream, l.grad);
+        encode_backward_runs_kernel<true, KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
+                                                                                               l.upstream, l.grad);
     else
-        encode_backward_runs_kernel<false, KIND><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
-                                                                                             l.upstream, l.grad);
+        encode_backward_runs_kernel<false, KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
+                                                                                                l.upstream, l.grad);
 }
 
-void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
+template <typename U>
+static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U* upstream, float* grad,
                             cudaStream_t stream) {
     if (a.n <= 0 || a.levels <= 0) return;
     ODIE_REQUIRE(a.levels <= MAX_LEVELS, "at most 32 levels");
@@ -664,8 +684,8 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     const uint32_t mask = visit_mask(groups);
     const long long threads = 32 * (mask ? (long long)mask + 1 : groups);
     if (src.descriptors) {
-        encode_backward_kernel<true><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table, upstream,
-                                                                                  grad, 0u, mask, -1);
+        encode_backward_kernel<true, U><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table,
+                                                                                     upstream, grad, 0u, mask, -1);
         note_launch();
         return;
     }
@@ -688,17 +708,17 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
         skip |= 1u << l;
     }
     if (list.count) {
-        static unsigned long long configured = 0;
+        static std::atomic<unsigned long long> configured{0};  // per value type and device
         int device = 0;
         ODIE_CUDA(cudaGetDevice(&device));
-        if (!(configured >> device & 1ull)) {
-            ODIE_CUDA(cudaFuncSetAttribute(encode_backward_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (!(configured.load() >> device & 1ull)) {
+            ODIE_CUDA(cudaFuncSetAttribute(encode_backward_shared_kernel<U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            COARSE_SMEM_FLOATS * 4));
-            set_runs_smem<PLANE>();
-            set_runs_smem<HASH_DENSE>();
-            set_runs_smem<HASH_HASHED>();
-            set_runs_smem<-1>();
-            configured |= 1ull << device;
+            set_runs_smem<PLANE, U>();
+            set_runs_smem<HASH_DENSE, U>();
+            set_runs_smem<HASH_HASHED, U>();
+            set_runs_smem<-1, U>();
+            configured.fetch_or(1ull << device);
         }
         // runs kernel: every listed level has F = 2; the 16-byte value loads also need row-major values with
         // listed level c in columns (2c, 2c + 1) and 16-byte aligned rows
@@ -712,14 +732,14 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
             if (d.kind != kind) kind = -1;
         }
         if (pairs) {
-            const RunsLaunch l{a, src.table, list, upstream, grad, blocks, list.total * 4, stream};
+            const RunsLaunch<U> l{a, src.table, list, upstream, grad, blocks, list.total * 4, stream};
             if (kind == PLANE) launch_runs<PLANE>(l, vec);
             else if (kind == HASH_DENSE) launch_runs<HASH_DENSE>(l, vec);
             else if (kind == HASH_HASHED) launch_runs<HASH_HASHED>(l, vec);
             else launch_runs<-1>(l, vec);
         }
         else
-            encode_backward_shared_kernel<<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
+            encode_backward_shared_kernel<U><<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
         note_launch();
     }
     const int active = a.active < a.levels ? a.active : a.levels;
@@ -729,9 +749,18 @@ void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const _
     while (split < a.levels && src.table.level[split].kind == HASH_DENSE) ++split;
     for (int l = split; l < a.levels; ++l)
         if (src.table.level[l].kind != HASH_HASHED) split = -1;
-    encode_backward_kernel<false><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad, skip,
-                                                                               mask, split);
+    encode_backward_kernel<false, U><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad,
+                                                                                  skip, mask, split);
     note_launch();
+}
+
+void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
+                            cudaStream_t stream) {
+    encode_backward(a, src, upstream, grad, stream);
+}
+void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const float* upstream, float* grad,
+                            cudaStream_t stream) {
+    encode_backward(a, src, upstream, grad, stream);
 }
 
 }  // namespace odie

@@ -44,5 +44,8 @@ void launch_encode_forward(const EncodeArgs& a, const LevelSource& src, const fl
 // shared memory first.
 void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const __half* upstream, float* grad,
                             cudaStream_t stream);
+// The same with fp32 values (the fp32 hash grid's feature gradients, row-major).
+void launch_encode_backward(const EncodeArgs& a, const LevelSource& src, const float* upstream, float* grad,
+                            cudaStream_t stream);
 
 }  // namespace odie

@@ -45,6 +45,22 @@ __global__ void __launch_bounds__(256) l2_probe_kernel(float* table, uint32_t wo
     if (acc == 1234.5f) sink[0] = acc;  // keeps the loads alive
 }
 
+// fp32 FMA throughput: 8 independent fma chains per thread (enough to hide the pipe's latency at full
+// occupancy); the roofline denominator of the fp32 CUDA-core MLP.  2 x 8 x iterations FLOP per thread.
+__global__ void __launch_bounds__(256) fma_probe_kernel(int iterations, float* sink) {
+    float a[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = float(threadIdx.x + k) * 1e-3f;
+    const float b = 0.999f, c = 1e-4f;
+    for (int j = 0; j < iterations; ++j)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] = __fmaf_rn(a[k], b, c);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += a[k];
+    if (s == 1234.5f) sink[0] = s;  // keeps the chains alive
+}
+
 // The bounded mbarrier wait of the heads kernel, made to run out: one block waits on a barrier
 // that expects one arrival which nothing makes.  tc::bar_wait gives up after `limit` polls and
 // the block reports 2 (the heads kernel's "a wait ran out" code) instead of hanging.
@@ -66,6 +82,14 @@ void launch_wait_probe(uint32_t limit, int* status, cudaStream_t stream) {
     ODIE_REQUIRE(limit >= 1 && limit <= (1u << 20), "wait probe limit must be 1..2^20 polls");
     wait_probe_kernel<<<1, 128, 0, stream>>>(limit, status);
     note_launch();
+}
+
+long long launch_fma_probe(int iterations, float* sink, cudaStream_t stream) {
+    ODIE_REQUIRE(iterations >= 1 && iterations <= (1 << 24), "fma probe iterations must be 1..2^24");
+    const int blocks = 8 * sm_count();
+    fma_probe_kernel<<<blocks, 256, 0, stream>>>(iterations, sink);
+    note_launch();
+    return 2LL * 8 * iterations * blocks * 256;  // FLOP
 }
 
 void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,

@@ -52,29 +52,39 @@ int sm_count() {
     return cached[device];
 }
 
-template <typename T>
-struct DeviceArray {
-    T* ptr = nullptr;
-    long long count = 0;
-    DeviceArray() = default;
-    DeviceArray(const DeviceArray&) = delete;
-    DeviceArray& operator=(const DeviceArray&) = delete;
-    ~DeviceArray() { release(); }
-    void release() {
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        count = 0;
+// TCNN-style HashGrid layout restated from odie/config.py:83-94; returns the parameter count.
+long long hash_grid_table(const Json& enc, LevelTable& table, int& levels, int& F) {
+    levels = int(enc.at("n_levels").as_int());
+    F = int(enc.at("n_features_per_level").as_int());
+    const int log2t = int(enc.at("log2_hashmap_size").as_int());
+    const int base = int(enc.at("base_resolution").as_int());
+    const double growth = double(float(enc.at("per_level_scale").as_double()));
+    ODIE_REQUIRE(levels >= 2 && levels <= 16, "hash grid levels in [2, 16]");
+    ODIE_REQUIRE(F == 1 || F == 2 || F == 4, "hash grid features per level must be 1, 2 or 4");
+    ODIE_REQUIRE(levels * F <= 32, "the fused heads take at most 32 input features");
+    const float log_growth = float(std::log2(growth));
+    long long offset = 0;
+    for (int l = 0; l < levels; ++l) {
+        const float e = float(double(l) * double(log_growth));
+        const float p = float(std::pow(2.0, double(e)));
+        const float scale = float(double(float(double(p) * double(base))) - 1.0);
+        const int res = int(std::ceil(double(scale))) + 1;
+        const long long dense = ((long long)res * res + 7) / 8 * 8;
+        const long long cap = std::min(dense, 1LL << log2t);
+        Level& L = table.level[l];
+        L.scale = scale;
+        L.res = res;
+        L.points = int(cap);
+        L.offset = int(offset);
+        L.words = -1;
+        L.cells = -1;
+        L.F = F;
+        L.col = l * F;
+        L.kind = (long long)res * res > cap ? HASH_HASHED : HASH_DENSE;
+        offset += cap * F;
     }
-    void allocate(long long n) {
-        release();
-        if (n <= 0) return;
-        ODIE_CUDA(cudaMalloc(&ptr, size_t(n) * sizeof(T)));
-        count = n;
-    }
-    void zero(cudaStream_t stream) {
-        if (count) ODIE_CUDA(cudaMemsetAsync(ptr, 0, size_t(count) * sizeof(T), stream));
-    }
-};
+    return offset;
+}
 
 template <typename T>
 T* pointer_of(const Json& j, const char* key) {
@@ -281,38 +291,8 @@ struct Runtime {
         ODIE_CUDA(cudaStreamSynchronize(stream));
     }
 
-    // TCNN-style HashGrid layout restated from odie/config.py:83-94; returns the parameter count.
     static long long hash_layout(const Json& enc, LevelTable& table, int& levels, int& F) {
-        levels = int(enc.at("n_levels").as_int());
-        F = int(enc.at("n_features_per_level").as_int());
-        const int log2t = int(enc.at("log2_hashmap_size").as_int());
-        const int base = int(enc.at("base_resolution").as_int());
-        const double growth = double(float(enc.at("per_level_scale").as_double()));
-        ODIE_REQUIRE(levels >= 2 && levels <= 16, "hash grid levels in [2, 16]");
-        ODIE_REQUIRE(F == 1 || F == 2 || F == 4, "hash grid features per level must be 1, 2 or 4");
-        ODIE_REQUIRE(levels * F <= 32, "the fused heads take at most 32 input features");
-        const float log_growth = float(std::log2(growth));
-        long long offset = 0;
-        for (int l = 0; l < levels; ++l) {
-            const float e = float(double(l) * double(log_growth));
-            const float p = float(std::pow(2.0, double(e)));
-            const float scale = float(double(float(double(p) * double(base))) - 1.0);
-            const int res = int(std::ceil(double(scale))) + 1;
-            const long long dense = ((long long)res * res + 7) / 8 * 8;
-            const long long cap = std::min(dense, 1LL << log2t);
-            Level& L = table.level[l];
-            L.scale = scale;
-            L.res = res;
-            L.points = int(cap);
-            L.offset = int(offset);
-            L.words = -1;
-            L.cells = -1;
-            L.F = F;
-            L.col = l * F;
-            L.kind = (long long)res * res > cap ? HASH_HASHED : HASH_DENSE;
-            offset += cap * F;
-        }
-        return offset;
+        return hash_grid_table(enc, table, levels, F);
     }
 
     void build_hash_table(const Json& enc) {
@@ -781,17 +761,6 @@ struct Runtime {
     }
 };
 
-template <typename F>
-int guarded(F&& f) {
-    try {
-        f();
-        return 0;
-    } catch (const std::exception& e) {
-        set_error(e.what());
-        return -1;
-    }
-}
-
 LevelTable hash_levels_table(const odie_hash_level* host, int levels) {
     ODIE_REQUIRE(host && levels >= 1 && levels <= MAX_LEVELS, "1..32 hash levels required");
     LevelTable t{};
@@ -841,6 +810,7 @@ void launch_plane_index(const uint8_t* support, int resolution, unsigned long lo
 void launch_l2_probe(float* table, long long table_bytes, int mode, long long operations, float* sink,
                      cudaStream_t stream);
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t stream);
+long long launch_fma_probe(int iterations, float* sink, cudaStream_t stream);
 }  // namespace odie
 
 using odie::guarded;
@@ -1153,6 +1123,12 @@ int odie_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, int t
                                        reinterpret_cast<cudaStream_t>(stream));
         ODIE_CUDA(cudaGetLastError());
     });
+}
+
+int64_t odie_fma_probe(int iterations, float* sink, uint64_t stream) {
+    long long flop = -1;
+    guarded([&] { flop = odie::launch_fma_probe(iterations, sink, reinterpret_cast<cudaStream_t>(stream)); });
+    return flop;
 }
 
 int odie_wait_probe(uint32_t limit, int32_t* status, uint64_t stream) {

@@ -37,25 +37,6 @@ __global__ void input_batch_kernel(const int64_t* __restrict__ ids, long long n,
     input_of(i, (id < 0 || id > 0xffffffffLL) ? 0xffffffffu : uint32_t(id), rgb, rgb8, width, height, frame, xy, target);
 }
 
-// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011):
-// a counter-based generator, so slot j of step s has its own stream with no state to carry.
-struct Philox4 {
-    uint32_t v[4];
-};
-__device__ __forceinline__ Philox4 philox4x32_10(Philox4 c, uint32_t k0, uint32_t k1) {
-#pragma unroll
-    for (int r = 0; r < 10; ++r) {
-        if (r > 0) {
-            k0 += 0x9E3779B9u;
-            k1 += 0xBB67AE85u;
-        }
-        const uint32_t lo0 = 0xD2511F53u * c.v[0], hi0 = __umulhi(0xD2511F53u, c.v[0]);
-        const uint32_t lo1 = 0xCD9E8D57u * c.v[2], hi1 = __umulhi(0xCD9E8D57u, c.v[2]);
-        c = Philox4{{hi1 ^ c.v[1] ^ k0, lo1, hi0 ^ c.v[3] ^ k1, lo0}};
-    }
-    return c;
-}
-
 // Stratified pixel id of slot j (the reference's sampler, odie/data.py:63-80, with this generator):
 // stratum (j mod side, j / side); uv = r / side + stratum / side in fp32 (side a power of two, so the
 // quotients are exact), r = (philox word >> 8) 2^-24 in [0, 1); pixel = trunc(uv (W, H)) clamped.
@@ -130,7 +111,7 @@ __device__ __forceinline__ void adam_update(float& p, float& m, float& v, float 
     p = __fadd_rn(p, __fdiv_rn(__fmul_rn(-step_size, m), denom));
 }
 
-// One Adam segment: parameters, fp16 copy, moments, per-parameter steps, gradient, learning-rate table.
+// One Adam segment: parameters, fp16 copy (null: none), moments, per-parameter steps, gradient, learning-rate table.
 struct AdamSegment {
     float* master;
     __half* copy;
@@ -169,9 +150,11 @@ __device__ __forceinline__ void adam_at(const AdamSegment& a, long long q, float
         reinterpret_cast<float4*>(a.v)[q] = v4;
         reinterpret_cast<uint4*>(a.steps)[q] = s4;
         reinterpret_cast<float4*>(a.grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-        __half2* ch = reinterpret_cast<__half2*>(a.copy + 4 * q);
-        ch[0] = __floats2half2_rn(p4.x, p4.y);
-        ch[1] = __floats2half2_rn(p4.z, p4.w);
+        if (a.copy) {
+            __half2* ch = reinterpret_cast<__half2*>(a.copy + 4 * q);
+            ch[0] = __floats2half2_rn(p4.x, p4.y);
+            ch[1] = __floats2half2_rn(p4.z, p4.w);
+        }
         return;
     }
     const long long first = VEC ? 4 * q : q, last = VEC ? (4 * q + 4 < count ? 4 * q + 4 : count) : (q < count ? q + 1 : q);
@@ -183,7 +166,7 @@ __device__ __forceinline__ void adam_at(const AdamSegment& a, long long q, float
         float p = a.master[i], mi = a.m[i], vi = a.v[i];
         adam_update(p, mi, vi, gj, a.step_size[s - 1], bc2_sqrt[s - 1], beta1w, beta2, beta2w, eps);
         a.master[i] = p; a.m[i] = mi; a.v[i] = vi; a.grad[i] = 0.0f;
-        a.copy[i] = __float2half_rn(p);
+        if (a.copy) a.copy[i] = __float2half_rn(p);
     }
 }
 
@@ -270,7 +253,7 @@ void launch_reduce_partials(const float* partials, int blocks, int count, float*
 static bool adam_vec(const AdamSegment& a) {
     auto aligned = [](const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; };
     return aligned(a.master, 16) && aligned(a.m, 16) && aligned(a.v, 16) && aligned(a.steps, 16) && aligned(a.grad, 16) &&
-           aligned(a.copy, 8);
+           (!a.copy || aligned(a.copy, 8));
 }
 
 static void launch_adam_segments(const AdamSegment& s0, const AdamSegment& s1, float inv_scale, const float* bc2_sqrt,

@@ -7,8 +7,8 @@ TCNN, odie/optimizer.py:54-89), so its native step (odie/native/runtime.cu:
 of the fp16-rounded corner values, autograd's index_add scatter, F.linear heads
 with fp16 activations, the L2 loss with the reference's 128 x 128 loss scaling
 and torch.optim.Adam (betas 0.9/0.999, eps 1e-15).  CpuExpertStep restates the
-routed multi-expert step the same way.  Both run on all the
-host threads torch is given.
+routed multi-expert step the same way, CpuHashGrid32Step the single fp32 hash grid's.
+All run on the host threads torch is given.
 """
 import time
 
@@ -204,3 +204,57 @@ def time_steps(step, ids_batches, budget_seconds=20.0):
         if time.perf_counter() - started > budget_seconds:
             break
     return coords, time.perf_counter() - started
+
+
+class CpuHashGrid32Step:
+    """The single fp32 hash grid's step on the CPU: fp32 gathers (index_select), the fp32 MLP 32 -> 64 -> 64 -> 3
+    with a sigmoid output, bilinear targets, mean squared error, autograd's index_add scatter and dense
+    torch.optim.Adam (betas 0.9 / 0.99, eps 1e-15, lr 1e-2) over all 7.66 M table entries and the heads."""
+
+    def __init__(self, image, records, grid, heads, lr=1e-2, seed=0):
+        self.image = torch.from_numpy(np.ascontiguousarray(image, dtype=np.float32))
+        self.levels = hash_levels_for_cpu(records)
+        self.grid = torch.nn.Parameter(torch.from_numpy(np.array(grid, dtype=np.float32)))
+        self.heads = torch.nn.Parameter(torch.from_numpy(np.array(heads, dtype=np.float32)))
+        self.optimizer = torch.optim.Adam([self.grid, self.heads], lr=lr, betas=(.9, .99), eps=1e-15, foreach=False)
+        self.generator = torch.Generator().manual_seed(seed)
+
+    def features(self, xy):
+        cols = []
+        for lv in self.levels:
+            p = xy * lv['scale'] + 0.5
+            i = torch.floor(p)
+            f = p - i
+            ix, iy = i[:, 0].long(), i[:, 1].long()
+            fx, fy = f[:, 0], f[:, 1]
+            w = torch.stack(((1 - fx) * (1 - fy), fx * (1 - fy), (1 - fx) * fy, fx * fy), 1)
+            cx = torch.stack((ix, ix + 1, ix, ix + 1), 1)
+            cy = torch.stack((iy, iy, iy + 1, iy + 1), 1)
+            idx = ((cx ^ ((cy * 2654435761) & 0xffffffff)) & 0xffffffff) if lv['kind'] == 'hashed' else cx + cy * lv['res']
+            rows = lv['offset'] + 2 * (idx % lv['points'])
+            for c in range(2):
+                cols.append((w * self.grid.index_select(0, (rows + c).reshape(-1)).view(-1, 4)).sum(1))
+        return torch.stack(cols, 1)
+
+    def bilinear(self, xy):
+        h, w = self.image.shape[:2]
+        px, py = xy[:, 0] * (w - 1), xy[:, 1] * (h - 1)
+        x0, y0 = px.long().clamp(0, w - 2), py.long().clamp(0, h - 2)
+        fx, fy = (px - x0)[:, None], (py - y0)[:, None]
+        im = self.image
+        return (im[y0, x0] * (1 - fx) * (1 - fy) + im[y0, x0 + 1] * fx * (1 - fy) + im[y0 + 1, x0] * (1 - fx) * fy
+                + im[y0 + 1, x0 + 1] * fx * fy)
+
+    def step_uniform(self, n):
+        xy = torch.rand((n, 2), generator=self.generator)
+        target = self.bilinear(xy)
+        self.optimizer.zero_grad(set_to_none=True)
+        f = self.features(xy)
+        w = self.heads
+        h = F.relu(F.linear(f, w[:2048].view(64, 32)))
+        h = F.relu(F.linear(h, w[2048:6144].view(64, 64)))
+        y = torch.sigmoid(F.linear(h, w[6144:].view(3, 64)))
+        loss = ((y - target) ** 2).mean()
+        loss.backward()
+        self.optimizer.step()
+        return float(loss.detach())

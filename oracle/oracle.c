@@ -649,3 +649,108 @@ void oracle_allocation_bitmap(const uint8_t* tiles, int tiles_x, int tiles_y, in
         if (tiles[ty * tiles_x + tx]) bitmap[c >> 3] |= (uint8_t)(1u << (c & 7));
     }
 }
+
+/* ------------------------------------------------------------------ fp32 hash grid */
+/* The single fp32 hash grid with an fp32 MLP (the hash-grid encoding of odie/hash_grid.py:8-80 and the
+ * layout of odie/config.py:83-94, in fp32; the library's hashgrid32 kernels): 16 levels x 2 features,
+ * MLP 32 -> 64 -> 64 -> 3 without biases ([out][in] weights W1 | W2 | W3), ReLU hidden layers, sigmoid
+ * output.  Every dot product is one fmaf chain in ascending input order starting from zero. */
+
+/* Bilinear sample of an fp32 [height][width][3] image at (x, y): p = fl(x (W - 1)), corner
+ * min(trunc(p), W - 2), f = p - corner, weights (1-fx)(1-fy), fx(1-fy), (1-fx)fy, fx fy, sum
+ * w00 c00 then fmaf with the (1,0), (0,1), (1,1) corners. */
+void oracle_hg32_bilinear(const float* image, int width, int height, const float* xy, int64_t n, float* target) {
+    for (int64_t i = 0; i < n; ++i) {
+        const float px = xy[2 * i] * (float)(width - 1), py = xy[2 * i + 1] * (float)(height - 1);
+        int x0 = (int)px, y0 = (int)py;
+        x0 = x0 < 0 ? 0 : (x0 > width - 2 ? width - 2 : x0);
+        y0 = y0 < 0 ? 0 : (y0 > height - 2 ? height - 2 : y0);
+        const float fx = px - (float)x0, fy = py - (float)y0, gx = 1.0f - fx, gy = 1.0f - fy;
+        const float w00 = gx * gy, w10 = fx * gy, w01 = gx * fy, w11 = fx * fy;
+        const float* p00 = image + 3 * ((int64_t)y0 * width + x0);
+        const float* p01 = p00 + 3 * (int64_t)width;
+        for (int c = 0; c < 3; ++c) {
+            float s = w00 * p00[c];
+            s = fmaf(w10, p00[3 + c], s);
+            s = fmaf(w01, p01[c], s);
+            target[3 * i + c] = fmaf(w11, p01[3 + c], s);
+        }
+    }
+}
+
+/* fp32 features [n][2 levels]: per level the 4 corners' pairs, fmaf chain over the corners from zero. */
+void oracle_hg32_features(const float* xy, int64_t n, const float* grid, const HashLevel* lv, int levels, float* f) {
+    for (int64_t i = 0; i < n; ++i)
+        for (int l = 0; l < levels; ++l) {
+            const HashLevel* h = lv + l;
+            const float px = fmaf(h->scale, xy[2 * i], 0.5f), py = fmaf(h->scale, xy[2 * i + 1], 0.5f);
+            const int ix = (int)floorf(px), iy = (int)floorf(py);
+            const float fx = px - (float)ix, fy = py - (float)iy;
+            const float w[4] = {(1.0f - fx) * (1.0f - fy), fx * (1.0f - fy), (1.0f - fx) * fy, fx * fy};
+            float a0 = 0.0f, a1 = 0.0f;
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t idx = hash_index(h, ix + (k & 1), iy + (k >> 1));
+                a0 = fmaf(w[k], grid[h->offset + 2 * (int64_t)idx], a0);
+                a1 = fmaf(w[k], grid[h->offset + 2 * (int64_t)idx + 1], a1);
+            }
+            f[i * 2 * levels + 2 * l] = a0;
+            f[i * 2 * levels + 2 * l + 1] = a1;
+        }
+}
+
+/* Forward and backward of one batch: h1 = relu(W1 f), h2 = relu(W2 h1), z = W3 h2, y = 1 / (1 + e^-z),
+ * d = y - t, squares = fmaf chain of d^2 / 3, dz = ((s d) y)(1 - y) with s the loss scale (2 / 3n),
+ * dh2 = (fl(W3[0] dz0) then fmaf over the outputs) masked by h2 > 0, dh1 = (W2^T dh2) masked by h1 > 0,
+ * dx = W1^T dh1.  Arrays are row-major per coordinate. */
+void oracle_hg32_step(const float* f, const float* target, int64_t n, const float* w, float loss_scale, float* h1,
+                      float* h2, float* z, float* y, float* dz, float* squares, float* dh2, float* dh1, float* dx) {
+    const float* w1 = w;
+    const float* w2 = w + 64 * 32;
+    const float* w3 = w2 + 64 * 64;
+    for (int64_t i = 0; i < n; ++i) {
+        const float* fi = f + i * 32;
+        float* a = h1 + i * 64;
+        float* b = h2 + i * 64;
+        for (int o = 0; o < 64; ++o) {
+            float s = 0.0f;
+            for (int m = 0; m < 32; ++m) s = fmaf(w1[o * 32 + m], fi[m], s);
+            a[o] = s > 0.0f ? s : 0.0f;
+        }
+        for (int o = 0; o < 64; ++o) {
+            float s = 0.0f;
+            for (int j = 0; j < 64; ++j) s = fmaf(w2[o * 64 + j], a[j], s);
+            b[o] = s > 0.0f ? s : 0.0f;
+        }
+        float sq = 0.0f;
+        for (int c = 0; c < 3; ++c) {
+            float s = 0.0f;
+            for (int j = 0; j < 64; ++j) s = fmaf(w3[c * 64 + j], b[j], s);
+            z[3 * i + c] = s;
+            const float yc = 1.0f / (1.0f + expf(-s));
+            const float d = yc - target[3 * i + c];
+            sq = fmaf(d, d, sq);
+            y[3 * i + c] = yc;
+            dz[3 * i + c] = ((loss_scale * d) * yc) * (1.0f - yc);
+        }
+        squares[i] = sq / 3.0f;
+        float* g2 = dh2 + i * 64;
+        float* g1 = dh1 + i * 64;
+        const float* d = dz + 3 * i;
+        for (int j = 0; j < 64; ++j) {
+            float s = w3[j] * d[0];
+            s = fmaf(w3[64 + j], d[1], s);
+            s = fmaf(w3[128 + j], d[2], s);
+            g2[j] = b[j] > 0.0f ? s : 0.0f;
+        }
+        for (int j = 0; j < 64; ++j) {
+            float s = 0.0f;
+            for (int k = 0; k < 64; ++k) s = fmaf(w2[k * 64 + j], g2[k], s);
+            g1[j] = a[j] > 0.0f ? s : 0.0f;
+        }
+        for (int m = 0; m < 32; ++m) {
+            float s = 0.0f;
+            for (int j = 0; j < 64; ++j) s = fmaf(w1[j * 32 + m], g1[j], s);
+            dx[i * 32 + m] = s;
+        }
+    }
+}

@@ -523,3 +523,81 @@ def stratified_ids(seed, step, width, height, n):
     x = np.minimum((ux * np.float32(width)).astype(np.int64), width - 1)
     y = np.minimum((uy * np.float32(height)).astype(np.int64), height - 1)
     return y * width + x
+
+
+# ---------------------------------------------------------------- single fp32 hash grid
+def uniform_xy(seed, step, n):
+    """The fp32 hash grid's uniform coordinates: Philox4x32-10 with key = seed, counter = (slot, step);
+    x = (word0 >> 8) 2^-24, y = (word1 >> 8) 2^-24, in [0, 1)."""
+    j = np.arange(n, dtype=np.uint64)
+    words = philox4x32_10([j & 0xFFFFFFFF, j >> np.uint64(32), np.full(n, step & 0xFFFFFFFF, np.uint64),
+                           np.full(n, step >> 32, np.uint64)],
+                          [np.full(n, seed & 0xFFFFFFFF, np.uint64), np.full(n, seed >> 32, np.uint64)])
+    x = (words[0] >> np.uint32(8)).astype(np.float32) * np.float32(2.0 ** -24)
+    y = (words[1] >> np.uint32(8)).astype(np.float32) * np.float32(2.0 ** -24)
+    return np.stack([x, y], axis=1)
+
+
+def hg32_bilinear(image, xy):
+    """Bilinear fp32 targets [n, 3] of an fp32 [H, W, 3] image (oracle_hg32_bilinear)."""
+    image = np.ascontiguousarray(image, dtype=np.float32)
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    out = np.empty((xy.shape[0], 3), dtype=np.float32)
+    lib().oracle_hg32_bilinear(_p(image), image.shape[1], image.shape[0], _p(xy), C.c_int64(xy.shape[0]), _p(out))
+    return out
+
+
+def hg32_features(xy, grid, records):
+    """fp32 features [n, 2 levels] of the fp32 table (oracle_hg32_features)."""
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    grid = np.ascontiguousarray(grid, dtype=np.float32)
+    out = np.empty((xy.shape[0], 2 * len(records)), dtype=np.float32)
+    lib().oracle_hg32_features(_p(xy), C.c_int64(xy.shape[0]), _p(grid), _hash_levels(records), len(records), _p(out))
+    return out
+
+
+def hg32_step(image, xy, grid, weights, records, loss_scale=None):
+    """One step of the single fp32 hash grid restated: per-coordinate forward and backward in fp32 exactly as
+    the kernels round them (oracle_hg32_step), the weight and grid gradients summed in fp64.  Returns a dict
+    of every intermediate plus `head_grad` [6336] (W1 | W2 | W3) and `grid_grad` [grid size]."""
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    n = xy.shape[0]
+    loss_scale = np.float32(2.0 / (3.0 * n)) if loss_scale is None else np.float32(loss_scale)
+    target = hg32_bilinear(image, xy)
+    f = hg32_features(xy, grid, records)
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    out = {k: np.empty((n, d), dtype=np.float32) for k, d in
+           (('h1', 64), ('h2', 64), ('z', 3), ('y', 3), ('dz', 3), ('dh2', 64), ('dh1', 64), ('dx', 32))}
+    squares = np.empty(n, dtype=np.float32)
+    lib().oracle_hg32_step(_p(f), _p(target), C.c_int64(n), _p(w), C.c_float(loss_scale), _p(out['h1']),
+                           _p(out['h2']), _p(out['z']), _p(out['y']), _p(out['dz']), _p(squares), _p(out['dh2']),
+                           _p(out['dh1']), _p(out['dx']))
+    d = {k: v.astype(np.float64) for k, v in out.items()}
+    f64 = f.astype(np.float64)
+    head = np.concatenate([(d['dh1'].T @ f64).reshape(-1), (d['dh2'].T @ d['h1']).reshape(-1),
+                           (d['dz'].T @ d['h2']).reshape(-1)])
+    head_magnitude = np.concatenate([(np.abs(d['dh1']).T @ np.abs(f64)).reshape(-1),
+                                     (np.abs(d['dh2']).T @ np.abs(d['h1'])).reshape(-1),
+                                     (np.abs(d['dz']).T @ np.abs(d['h2'])).reshape(-1)])
+    params = int(sum(r['capacity'] * r['features'] for r in records))
+    grid_grad = hg32_scatter(xy, out['dx'], records, params)
+    grid_magnitude = hg32_scatter(xy, np.abs(out['dx']), records, params)
+    return dict(out, target=target, features=f, squares=squares, head_grad=head, head_magnitude=head_magnitude,
+                grid_grad=grid_grad, grid_magnitude=grid_magnitude, loss_scale=loss_scale)
+
+
+def hg32_scatter(xy, values, records, params):
+    """sum_k w_k v over every coordinate's corners, in fp64 (the fp32 hash grid's grid gradient)."""
+    xy = np.ascontiguousarray(xy, dtype=np.float32)
+    values = np.asarray(values, dtype=np.float64)
+    n, levels = xy.shape[0], len(records)
+    idx = np.empty((n, levels, 4), dtype=np.int32)
+    w = np.empty((n, levels, 4), dtype=np.float32)
+    lib().oracle_hash_indices(_p(xy), C.c_int64(n), _hash_levels(records), levels, _p(idx), _p(w))
+    grad = np.zeros(params, dtype=np.float64)
+    for l, r in enumerate(records):
+        rows = r['offset'] + 2 * idx[:, l, :].astype(np.int64)
+        weights = w[:, l, :].astype(np.float64)
+        for c in range(2):
+            np.add.at(grad, (rows + c).reshape(-1), (weights * values[:, 2 * l + c, None]).reshape(-1))
+    return grad
