@@ -23,11 +23,10 @@
 // GATE_EXPERTS (routed multi-expert encoding, no reference counterpart): the
 // decoder input is the routed expert's features times half(p), p the router
 // probability of that expert (chosen bit-exactly by router.cu).  Training
-// recomputes the router MLP on the tensor cores (R -> 32 -> 32 -> 16 logits)
-// for its backward: dp = sum_c v_c f_c, dz_j = dp p (delta_je - p_j), then the
-// router backward down to the router-grid gradient values.  The router
-// features of the next tile stream into a second shared-memory buffer with
-// cp.async while the current tile runs.
+// (experts_train3_kernel) recomputes the router MLP on the tensor cores
+// (R -> 32 -> 32 -> 16 or 64 logits) for its backward: dp = sum_c v_c f_c,
+// dz_j = dp p (delta_je - p_j), then the router backward down to the
+// router-grid gradient values; one CTA per SM keeps three tiles in flight.
 #include <atomic>
 
 #include "router.cuh"
@@ -103,7 +102,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_older() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 __device__ void stage_blocked(const __half* __restrict__ src, int rows, int cols, unsigned char* smem, int base) {
     for (int idx = threadIdx.x; idx < rows * cols; idx += blockDim.x) {
@@ -214,7 +212,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, S::g1);
         stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, S::g2);
     }
-    static_assert(!(EXPERTS && TRAIN), "routed-expert training runs in experts_train_kernel");
+    static_assert(!(EXPERTS && TRAIN), "routed-expert training runs in experts_train3_kernel");
     stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
@@ -718,65 +716,143 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
 }
 
-// ---------------------------------------------------------------- routed-expert training
-// TMEM columns of routed-expert training: T_ACC, T_DWD2, T_DWD1 and T_DW3T as above, then dWr3
-// [ROUT out][32 in] (M = 64 rows, N = 32) and one M = 64 accumulator holding dWr1 in rows 0-31 and
-// dWr2 in rows 32-63: 240 of the 256 columns, so two CTAs still share an SM.
-constexpr uint32_t T_DWR3 = 176, T_DWR12 = 208;
-static_assert(T_DWR12 + 32 <= TMEM_COLUMNS, "routed-expert accumulators fit the allocation");
+// ---------------------------------------------------------------- routed-expert training, three tiles per SM
+// Routed-expert training step of the heads (no reference counterpart).  Per 128-coordinate tile: router
+// recompute on the tensor cores (GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T); the logits come from router.cu,
+// which chose the expert on the CUDA cores), decoder forward on the gated input fp16(f x fp16(p)), loss
+// gradient, decoder backward, expert values v x fp16(p) with v = fp16(dz / 128) and dp = sum_c v_c f_c, logit
+// gradients dz_j = dp p (delta_je - p_j) over the coordinate's live experts, da = fp16(fp16(dz_j) x 128),
+// router backward down to the router-grid values fp16(dR / 128).  ROUT: router logit rows (16 or 64); LIVE:
+// logits per coordinate as router.cu stores them.
+// One CTA per SM runs three warpgroups, each its own stream of tiles through that phase chain, so while one
+// warpgroup converts an accumulator the tensor cores run the others' products.  The warpgroups share the staged weights and the weight-gradient accumulators in TMEM
+// (every product adds into them); each has its own per-tile accumulator, activation buffers, mbarriers and
+// named barrier.
+constexpr int E3_GROUPS = 3;
+constexpr int E3_THREADS = E3_GROUPS * TC_THREADS;
+constexpr uint32_t E3_TMEM_COLUMNS = 512;
+// TMEM columns: warpgroup g's per-tile accumulator at 64 g, then the shared weight-gradient accumulators
+// (M = 64 layout: rows 16 w .. 16 w + 15 in lanes 32 w .. 32 w + 15): dWd2, dWd1, dW3^T, dWr3, dWr1 | dWr2.
+constexpr uint32_t E3_DWD2 = 64 * E3_GROUPS, E3_DWD1 = E3_DWD2 + 64, E3_DW3T = E3_DWD1 + 32, E3_DWR3 = E3_DW3T + 16,
+                   E3_DWR12 = E3_DWR3 + 32, E3_DW_END = E3_DWR12 + 32;
+static_assert(E3_DW_END <= E3_TMEM_COLUMNS, "the three tiles' accumulators and the weight gradients fit TMEM");
 
-// Shared memory (bytes) of routed-expert training, decoder input width 32.  The router backward reuses the
-// decoder's buffers once the decoder's weight-gradient products have read them: dgh1 | zero | dgh2 is one
-// contiguous 96-column stretch, so the 64-column MN-major views [dgh1 | zero] and [zero | dgh2] feed dWr1
-// and dWr2 into the two halves of one M = 64 accumulator (the zero columns add exact zeros to the other half).
-struct ExpertSmem {
+// Shared memory (bytes): the weights once, then one region per warpgroup with the tile's activations.  The
+// router backward reuses the decoder's buffers once the decoder's weight-gradient products have read them:
+// dgh1 | zero | dgh2 is one contiguous 96-column stretch, so the 64-column MN-major views [dgh1 | zero] and
+// [zero | dgh2] feed dWr1 and dWr2 into the two halves of one M = 64 accumulator (the zero columns add exact
+// zeros to the other half).  The router features are single-buffered: the next tile's copy starts once the
+// last product that reads them has completed.
+struct E3Smem {
     static constexpr int W = 32, XB = 128 * W * 2;
-    static constexpr int g1 = 0;                    // [32 x 32] router W1
-    static constexpr int r2 = g1 + 32 * W * 2;      // [32 x 32] router W2
-    static constexpr int g2 = r2 + 32 * 32 * 2;     // [64 x 32] router W3 (ROUT rows, blocked for ROUT rows)
-    static constexpr int d1 = g2 + 64 * 32 * 2;     // [64 x 32] decoder W1
-    static constexpr int d2 = d1 + 64 * W * 2;      // [64 x 64]
-    static constexpr int d3 = d2 + 64 * 64 * 2;     // [16 x 64]
-    static constexpr int x = d3 + 16 * 64 * 2;      // [128 x 32] router features, buffer 0
-    static constexpr int x2 = x + XB;               // [128 x 32] router features, buffer 1
-    static constexpr int gh = x2 + XB;              // [128 x 32] router hidden 1
-    static constexpr int gh2 = gh + 8192;           // [128 x 32] router hidden 2
-    static constexpr int h1 = gh2 + 8192;           // [128 x 64] decoder hidden 1, then dh1
-    static constexpr int wx = h1 + 16384;           // [128 x 32] decoder input
-    static constexpr int dy = wx + XB;              // [128 x 16] output gradient
-    static constexpr int h2 = dy + 4096;            // [128 x 64] decoder hidden 2, then dh2
-    static constexpr int dgh1 = h1;                 // [128 x 32] router hidden-1 gradient (router backward)
-    static constexpr int zero = h1 + 8192;          // [128 x 32] zeros (router backward)
-    static constexpr int dgh2 = h1 + 16384;         // [128 x 32] router hidden-2 gradient (router backward)
-    static constexpr int da = h2;                   // [128 x 64] logit gradients, ROUT columns (router backward)
-    static constexpr int bar = h2 + 16384;          // mbarrier: data products of a phase
-    static constexpr int bar_dw = bar + 8;          // mbarrier: weight-gradient products of a phase
-    static constexpr int drain = bar_dw + 8;        // mbarrier: every issuing warp's products (error exit)
-    static constexpr int tmem = drain + 8;          // TMEM base address
-    static constexpr int total = tmem + 8;
+    static constexpr int g1 = 0;                     // [32 x 32] router W1
+    static constexpr int r2 = g1 + 32 * W * 2;       // [32 x 32] router W2
+    static constexpr int g2 = r2 + 32 * 32 * 2;      // [64 x 32] router W3 (ROUT rows)
+    static constexpr int d1 = g2 + 64 * 32 * 2;      // [64 x 32]
+    static constexpr int d2 = d1 + 64 * W * 2;       // [64 x 64]
+    static constexpr int d3 = d2 + 64 * 64 * 2;      // [16 x 64]
+    static constexpr int groups = d3 + 16 * 64 * 2;  // the first warpgroup's region
+    // offsets within a warpgroup's region
+    static constexpr int x = 0;                      // [128 x 32] router features
+    static constexpr int gh = x + XB;                // [128 x 32] router hidden 1
+    static constexpr int gh2 = gh + XB;              // [128 x 32] router hidden 2
+    static constexpr int h1 = gh2 + XB;              // [128 x 64] decoder hidden 1, then dh1
+    static constexpr int wx = h1 + 16384;            // [128 x 32] decoder input
+    static constexpr int dy = wx + XB;               // [128 x 16] output gradient
+    static constexpr int h2 = dy + 4096;             // [128 x 64] decoder hidden 2, then dh2
+    static constexpr int dgh1 = h1;                  // [128 x 32] router hidden-1 gradient
+    static constexpr int zero = h1 + 8192;           // [128 x 32] zeros
+    static constexpr int dgh2 = h1 + 16384;          // [128 x 32] router hidden-2 gradient
+    static constexpr int da = h2;                    // [128 x 64] logit gradients
+    static constexpr int bars = h2 + 16384;          // bar, bar_dw, drain
+    static constexpr int region = bars + 128;
+    static constexpr int tmem = groups + E3_GROUPS * region;  // TMEM base address
+    static constexpr int total = tmem + 16;
     static_assert(dgh2 == wx && dgh2 + 8192 == dy, "dgh1 | zero | dgh2 is one contiguous stretch ending at dy");
+    static_assert(total <= 232448, "fits the 227 KB a CTA may hold");
 };
 
-// Routed-expert training step of the heads (no reference counterpart), one CTA per 128-coordinate tile at a
-// time, persistent.  Per tile: router recompute on the tensor cores (GH1 = relu(R Wr1^T), GH2 = relu(GH1
-// Wr2^T); the logits come from router.cu, which chose the expert on the CUDA cores), decoder forward on the
-// gated input fp16(f x fp16(p)), loss gradient, decoder backward, expert values v x fp16(p) with
-// v = fp16(dz / 128) and dp = sum_c v_c f_c, logit gradients dz_j = dp p (delta_je - p_j) over the
-// coordinate's live experts, da = fp16(fp16(dz_j) x 128), router backward down to the router-grid values
-// fp16(dR / 128).  ROUT: router logit rows (16 or 64); LIVE: logits per coordinate as router.cu stores them.
+// A warpgroup's named barrier (id 1 + group; id 0 is __syncthreads) over its 128 threads.
+__device__ __forceinline__ void group_sync(int group) {
+    asm volatile("bar.sync %0, 128;\n" ::"r"(1 + group) : "memory");
+}
+__device__ __forceinline__ bool group_and(int group, bool value) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(out)
+        : "r"(uint32_t(value)), "r"(1 + group)
+        : "memory");
+    return out != 0;
+}
+
+// Issuer of one warpgroup: as Issuer, with the warpgroup's named barrier in place of __syncthreads.  A wait that
+// gives up ends the group's loop at the tile's end, for all its threads at once.
+struct GroupIssuer {
+    uint64_t* bar;
+    uint64_t* bar_dw;
+    int group, t;
+    uint32_t phase = 0, phase_dw = 0;
+    bool ok = true, fine = true;
+    __device__ void before_issue() {
+        tc::fence_async_smem();
+        tc::fence_before_sync();
+        group_sync(group);
+        if (t == 0) tc::fence_after_sync();
+    }
+    __device__ void complete() {
+        if (t == 0) tc::commit(bar);
+        wait_data();
+    }
+    __device__ void wait_data() {
+        fine = tc::bar_wait(bar, phase, WAIT_LIMIT) && fine;
+        phase ^= 1u;
+        tc::fence_after_sync();
+    }
+    __device__ void wait_dw() {
+        fine = tc::bar_wait(bar_dw, phase_dw, WAIT_LIMIT) && fine;
+        phase_dw ^= 1u;
+        tc::fence_after_sync();
+    }
+    __device__ bool settle() {
+        ok = group_and(group, fine);
+        return ok;
+    }
+};
+
+// 32 TMEM columns of a backward product, masked by the forward ReLU (bit c: column c), rounded to fp16 and
+// stored as chunks j0 .. j0 + 3 of row r; 16 columns at a time.
+__device__ __forceinline__ void masked_store32(uint32_t taddr, uint32_t mask, unsigned char* smem, int base, int r,
+                                               int j0) {
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+        float v[16];
+        tc::tmem_ld16(taddr + 16 * hlf, v);
+        const uint32_t m = mask >> (16 * hlf);
+        uint32_t h[8];
+#pragma unroll
+        for (int c = 0; c < 16; c += 2)
+            h[c / 2] = cvt_pair((m >> c & 1u) ? v[c] : 0.0f, (m >> (c + 1) & 1u) ? v[c + 1] : 0.0f);
+        store_chunk(smem, base, r, j0 + 2 * hlf, make_uint4(h[0], h[1], h[2], h[3]));
+        store_chunk(smem, base, r, j0 + 2 * hlf + 1, make_uint4(h[4], h[5], h[6], h[7]));
+    }
+}
+
 template <int ROUT, int LIVE>
-__global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpArgs a, int* error_flag) {
-    using S = ExpertSmem;
+__global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const MlpArgs a, int* error_flag) {
+    using S = E3Smem;
     constexpr int W = 32, PAIRS = W / 2, KW = W / 16;
     static_assert(ROUT == 16 || ROUT == 64, "the router has 16 or 64 logit rows");
     static_assert(LIVE == 8 || LIVE == 16, "8 or 16 live logits per coordinate");
     extern __shared__ __align__(128) unsigned char smem[];
-    const int t = threadIdx.x, warp = t >> 5;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
-    uint64_t* bar_dw = reinterpret_cast<uint64_t*>(smem + S::bar_dw);
-    uint64_t* drain = reinterpret_cast<uint64_t*>(smem + S::drain);
+    const int group = threadIdx.x >> 7, t = threadIdx.x & 127, warp = threadIdx.x >> 5, quad = warp & 3;
+    unsigned char* const mine = smem + S::groups + group * S::region;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(mine + S::bars);
+    uint64_t* bar_dw = bar + 1;
+    uint64_t* drain = bar + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
     const uint32_t sbase = tc::smem_u32(smem);
+    const uint32_t gbase = sbase + S::groups + uint32_t(group) * S::region;
 
     stage_blocked(a.gate_w, ROUTER_HIDDEN, W, smem, S::g1);
     stage_blocked(a.gate_w + ROUTER_HIDDEN * W, ROUTER_HIDDEN, ROUTER_HIDDEN, smem, S::r2);
@@ -786,12 +862,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
     if (t == 0) {
         tc::bar_init(bar, 1);
-        tc::bar_init(bar_dw, TC_THREADS / 32);  // one commit per warp: each warp issues part of every weight-gradient product
+        tc::bar_init(bar_dw, TC_THREADS / 32);  // one commit per warp of the group
         tc::bar_init(drain, TC_THREADS / 32);
         tc::fence_bar_init();
     }
     if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, TMEM_COLUMNS);
+        tc::tmem_alloc(tmem_slot, E3_TMEM_COLUMNS);
         tc::tmem_relinquish();
     }
     tc::fence_async_smem();
@@ -799,85 +875,71 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
-    {
-        // the weight-gradient accumulators start at zero; every product accumulates
+    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);  // this warp's TMEM lanes
+    const uint32_t acc = 64u * uint32_t(group);                      // this warpgroup's per-tile accumulator
+    if (group == 0) {  // the weight-gradient accumulators start at zero; every product accumulates
         float zero[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) zero[c] = 0.0f;
-        for (uint32_t col = T_DWD2; col < TMEM_COLUMNS; col += 16) tc::tmem_st16(lane_addr + col, zero);
+        for (uint32_t col = E3_DWD2; col < E3_DW_END; col += 16) tc::tmem_st16(lane_addr + col, zero);
         tc::tmem_wait_st();
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
     }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
 
-    Issuer is{bar, bar_dw};
-    uint32_t dw_accumulate = 0;  // 1 once a tile has added to the weight gradients
+    GroupIssuer is{bar, bar_dw, group, t};
+    bool added = false;  // this warpgroup has added a tile to the weight gradients
     const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
+    const long long stride = (long long)gridDim.x * E3_GROUPS;
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
     const int per = a.per_band;
 
-    // Inputs of a tile (loaded while the previous tile runs its backward products): the routed expert's
-    // feature row, target, probability, expert and the live logits.
-    uint32_t next_raw[PAIRS], next_lg[LIVE / 2];
-    float next_target[3] = {0.0f, 0.0f, 0.0f}, next_prob = 0.0f;
-    int next_expert = 0;
-    auto load_inputs = [&](long long tile) {
+    for (long long tile = (long long)blockIdx.x * E3_GROUPS + group; tile < tiles && is.ok; tile += stride) {
         const long long i = tile * TC_TILE + t;
-        const bool valid = tile < tiles && i < a.n;
+        const bool valid = i < a.n;
+        // ---- this tile's router features into x (the previous tile's last product, which read x, has completed)
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
+#pragma unroll
+            for (int j = 0; j < W / 8; ++j) cp_async16(gbase + S::x + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
+            cp_async_commit();
+        }
+        // ---- the routed expert's feature row, logits, target, probability and expert (read before use)
+        uint32_t raw[PAIRS], lg[LIVE / 2];
+        float target[3] = {0.0f, 0.0f, 0.0f}, prob = 0.0f;
+        int expert = 0;
 #pragma unroll
         for (int j = 0; j < PAIRS / 4; ++j) {
             const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.raw) + i * (PAIRS / 4) + j) : make_uint4(0, 0, 0, 0);
-            next_raw[4 * j] = q.x;
-            next_raw[4 * j + 1] = q.y;
-            next_raw[4 * j + 2] = q.z;
-            next_raw[4 * j + 3] = q.w;
+            raw[4 * j] = q.x;
+            raw[4 * j + 1] = q.y;
+            raw[4 * j + 2] = q.z;
+            raw[4 * j + 3] = q.w;
         }
 #pragma unroll
         for (int j = 0; j < LIVE / 8; ++j) {
             const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.logits) + i * (LIVE / 8) + j) : make_uint4(0, 0, 0, 0);
-            next_lg[4 * j] = q.x;
-            next_lg[4 * j + 1] = q.y;
-            next_lg[4 * j + 2] = q.z;
-            next_lg[4 * j + 3] = q.w;
+            lg[4 * j] = q.x;
+            lg[4 * j + 1] = q.y;
+            lg[4 * j + 2] = q.z;
+            lg[4 * j + 3] = q.w;
         }
+        if (valid) {
 #pragma unroll
-        for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
-        next_prob = valid ? __ldg(a.prob + i) : 0.0f;
-        next_expert = valid ? __ldg(a.expert + i) : 0;
-    };
-    // Router features of a tile (row-major [stride][W]): each row's W halves as W / 8 16-byte cp.async copies
-    // into the blocked layout of shared buffer `buf`.
-    auto prefetch_router = [&](long long tile, int buf) {
-        const long long i = tile * TC_TILE + t;
-        const bool valid = tile < tiles && i < a.n;
-        const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
-#pragma unroll
-        for (int j = 0; j < W / 8; ++j)
-            cp_async16(sbase + buf + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
-        cp_async_commit();
-    };
-    load_inputs(blockIdx.x);
-    int xbuf = S::x;  // router features of the current tile (alternates with S::x2)
-    prefetch_router(blockIdx.x, S::x);
-
-    for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
-        const long long i = tile * TC_TILE + t;
-        const bool valid = i < a.n;
-        // the other buffer was last read by the previous tile's router weight-gradient product, which has completed
-        prefetch_router(tile + gridDim.x, xbuf == S::x ? S::x2 : S::x);
-        cp_async_wait_older();  // this tile's features have landed
-        uint32_t raw[PAIRS], lg[LIVE / 2];
-#pragma unroll
-        for (int p = 0; p < PAIRS; ++p) raw[p] = next_raw[p];
-#pragma unroll
-        for (int p = 0; p < LIVE / 2; ++p) lg[p] = next_lg[p];
-        const float prob = next_prob, target[3] = {next_target[0], next_target[1], next_target[2]};
-        const int expert = next_expert;
-        const long long next_tile = tile + gridDim.x;
-
-        // ---- decoder input: the routed expert's features x half(p), one rounding per feature
+            for (int c = 0; c < 3; ++c) target[c] = __ldg(a.target + 3 * i + c);
+            prob = __ldg(a.prob + i);
+            expert = __ldg(a.expert + i);
+        }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T)
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
+        is.complete();
+        const uint32_t gh_mask = relu_store32(lane_addr + acc, mine, S::gh, t, 0);
+        // decoder input: the routed expert's features x half(p), one rounding per feature (registers have arrived)
         {
             const __half2 ph = __float2half2_rn(prob);
             uint32_t wx[PAIRS];
@@ -885,55 +947,39 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
             for (int p = 0; p < PAIRS; ++p) wx[p] = as_u32(__hmul2(as_half2(raw[p]), ph));
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
-                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+                store_chunk(mine, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
         }
-        // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T)
-        is.before_issue();
-        if (t == 0)
-            for (int s = 0; s < KW; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + xbuf, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
-        is.complete();
-        const uint32_t gh_mask = relu_store32(lane_addr + T_ACC, smem, S::gh, t, 0);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 2; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
         is.complete();
-        const uint32_t gh2_mask = relu_store32(lane_addr + T_ACC, smem, S::gh2, t, 0);
+        const uint32_t gh2_mask = relu_store32(lane_addr + acc, mine, S::gh2, t, 0);
         // ---- decoder hidden 1, hidden 2, output
-        uint32_t h1_mask[4], h2_mask[4];
+        uint32_t h1_mask[2], h2_mask[2];
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < KW; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 4; q += 2) {
-            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h1, t, 2 * q);
-            h1_mask[q] = m & 0xffffu;
-            h1_mask[q + 1] = m >> 16;
-        }
+        for (int q = 0; q < 2; ++q) h1_mask[q] = relu_store32(lane_addr + acc + 32 * q, mine, S::h1, t, 4 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 4; q += 2) {
-            const uint32_t m = relu_store32(lane_addr + T_ACC + 16 * q, smem, S::h2, t, 2 * q);
-            h2_mask[q] = m & 0xffffu;
-            h2_mask[q + 1] = m >> 16;
-        }
+        for (int q = 0; q < 2; ++q) h2_mask[q] = relu_store32(lane_addr + acc + 32 * q, mine, S::h2, t, 4 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::h2, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
         is.complete();
-        float out[16];
-        tc::tmem_ld16(lane_addr + T_ACC, out);
-        load_inputs(next_tile);  // prefetch: consumed at the start of the next tile
         // ---- loss gradient (odie/native/runtime.cu:53-63)
         {
+            float out[16];
+            tc::tmem_ld16(lane_addr + acc, out);
             float dy[16];
 #pragma unroll
             for (int c = 0; c < 16; ++c) dy[c] = 0.0f;
@@ -948,86 +994,79 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
                 }
                 a.squares[i] = __fdiv_rn(s, 3.0f);
             }
-            store_chunk(smem, S::dy, t, 0, pack8(dy));
-            store_chunk(smem, S::dy, t, 1, pack8(dy + 8));
+            store_chunk(mine, S::dy, t, 0, pack8(dy));
+            store_chunk(mine, S::dy, t, 1, pack8(dy + 8));
         }
-        uint32_t packed[32];
+        const int wq = t >> 5;  // warp within the group: it issues K-steps 2 wq, 2 wq + 1 of each weight-gradient product
         // ---- dh2 = DY Wd3 (B: Wd3 as MN-major); dW3^T += H2^T DY
         is.before_issue();
         if (t == 0) {
-            tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0),
-                    tc::idesc(128, 64, 0, 1), 0);
+            tc::mma(tmem + acc, tc::kmajor(gbase + S::dy, 128, 0), tc::mnmajor(sbase + S::d3, 16, 0), tc::idesc(128, 64, 0, 1), 0);
             tc::commit(bar);
         }
-        if ((t & 31) == 0) {  // every warp issues two of the eight K-steps of the weight-gradient product
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DW3T, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::dy, 128, s),
+        if ((t & 31) == 0) {
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DW3T, tc::mnmajor(gbase + S::h2, 128, s), tc::mnmajor(gbase + S::dy, 128, s),
                         tc::idesc(64, 16, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
-#pragma unroll
-        for (int q = 0; q < 4; q += 2)
-            masked_pack32(lane_addr + T_ACC + 16 * q, h2_mask[q] | (h2_mask[q + 1] << 16), packed + 8 * q);
         is.wait_dw();  // dW3 has read H2: dh2 may overwrite it
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            store_chunk(smem, S::h2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        for (int q = 0; q < 2; ++q) masked_store32(lane_addr + acc + 32 * q, h2_mask[q], mine, S::h2, t, 4 * q);
         // ---- dh1 = DH2 Wd2; dWd2 += DH2^T H1
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s),
-                        tc::idesc(128, 64, 0, 1), s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::h2, 128, s), tc::mnmajor(sbase + S::d2, 64, s), tc::idesc(128, 64, 0, 1), s > 0);
             tc::commit(bar);
         }
         if ((t & 31) == 0) {
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DWD2, tc::mnmajor(sbase + S::h2, 128, s), tc::mnmajor(sbase + S::h1, 128, s),
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DWD2, tc::mnmajor(gbase + S::h2, 128, s), tc::mnmajor(gbase + S::h1, 128, s),
                         tc::idesc(64, 64, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
-#pragma unroll
-        for (int q = 0; q < 4; q += 2)
-            masked_pack32(lane_addr + T_ACC + 16 * q, h1_mask[q] | (h1_mask[q + 1] << 16), packed + 8 * q);
         is.wait_dw();  // dWd2 has read H1: dh1 may overwrite it
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            store_chunk(smem, S::h1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        for (int q = 0; q < 2; ++q) masked_store32(lane_addr + acc + 32 * q, h1_mask[q], mine, S::h1, t, 4 * q);
         // ---- dz = DH1 Wd1; dWd1 += DH1^T WX
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 4; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s),
-                        tc::idesc(128, W, 0, 1), s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::h1, 128, s), tc::mnmajor(sbase + S::d1, 64, s), tc::idesc(128, W, 0, 1), s > 0);
             tc::commit(bar);
         }
         if ((t & 31) == 0) {
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DWD1, tc::mnmajor(sbase + S::h1, 128, s), tc::mnmajor(sbase + S::wx, 128, s),
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DWD1, tc::mnmajor(gbase + S::h1, 128, s), tc::mnmajor(gbase + S::wx, 128, s),
                         tc::idesc(64, W, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
-        float dzf[W];
-        tc::tmem_ld32(lane_addr + T_ACC, dzf);
         // ---- expert grid values v_c * half(p) and the probability gradient dp = sum_c v_c f_c
         uint32_t gv[PAIRS];
         float dp = 0.0f;
         {
             const __half2 ph = __float2half2_rn(prob);
 #pragma unroll
-            for (int p = 0; p < PAIRS; ++p) {
-                const __half2 v = grid_pair(dzf[2 * p], dzf[2 * p + 1]);
-                gv[p] = as_u32(__hmul2_rn(v, ph));
-                dp = __fmaf_rn(__low2float(v), __half2float(lo_half(raw[p])), dp);
-                dp = __fmaf_rn(__high2float(v), __half2float(hi_half(raw[p])), dp);
+            for (int hlf = 0; hlf < 2; ++hlf) {
+                float dzf[16];
+                tc::tmem_ld16(lane_addr + acc + 16 * hlf, dzf);
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    const int pp = 8 * hlf + p;
+                    const __half2 v = grid_pair(dzf[2 * p], dzf[2 * p + 1]);
+                    gv[pp] = as_u32(__hmul2_rn(v, ph));
+                    dp = __fmaf_rn(__low2float(v), __half2float(lo_half(raw[pp])), dp);
+                    dp = __fmaf_rn(__high2float(v), __half2float(hi_half(raw[pp])), dp);
+                }
             }
         }
         // ---- logit gradients: softmax of the router's fp16 logits over the coordinate's live experts
-        const int choice = expert % per;          // the chosen expert within its band
-        const int lo = (a.first_band + expert / per) * per;  // the band's first logit column
+        const int choice = expert % per;
+        const int lo = (a.first_band + expert / per) * per;
         float da[LIVE];
         {
             float z[LIVE], zmax = -INFINITY;
@@ -1043,80 +1082,69 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
                 sum = __fadd_rn(sum, z[j]);
             }
             const float dpp = __fmul_rn(dp, prob);
-            const float inv = __frcp_rn(sum);  // p_j = z_j / sum within an ulp; feeds only the fp16 logit gradients
+            const float inv = __frcp_rn(sum);
 #pragma unroll
             for (int j = 0; j < LIVE; j += 2) {
                 const float d0 = __fmul_rn(dpp, __fsub_rn(j == choice ? 1.0f : 0.0f, __fmul_rn(z[j], inv)));
                 const float d1 = __fmul_rn(dpp, __fsub_rn(j + 1 == choice ? 1.0f : 0.0f, __fmul_rn(z[j + 1], inv)));
-                // fp16(fp16(derivative) x 128): the scaling by 2^7 is exact unless it overflows, as in fp16 arithmetic
                 const __half2 h = __hmul2_rn(as_half2(cvt_pair(d0, d1)), __float2half2_rn(128.0f));
                 da[j] = j < per ? __low2float(h) : 0.0f;
                 da[j + 1] = j + 1 < per ? __high2float(h) : 0.0f;
             }
         }
         is.wait_dw();  // dWd1 has read WX and DH1: h1, wx, dy and h2 are free for the router backward
-        // DA row: the live gradients at the band's columns, zeros elsewhere; and this row of the zero block
         {
             const uint4 zero4 = make_uint4(0, 0, 0, 0);
             const uint4 first = pack8(da), second = LIVE == 16 ? pack8(da + 8) : zero4;
 #pragma unroll
             for (int c = 0; c < ROUT / 8; ++c)
-                store_chunk(smem, S::da, t, c, 8 * c == lo ? first : (LIVE == 16 && 8 * c == lo + 8) ? second : zero4);
+                store_chunk(mine, S::da, t, c, 8 * c == lo ? first : (LIVE == 16 && 8 * c == lo + 8) ? second : zero4);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) store_chunk(smem, S::zero, t, c, zero4);
+            for (int c = 0; c < 4; ++c) store_chunk(mine, S::zero, t, c, zero4);
         }
-        // ---- dgh2 = DA Wr3; dWr3 += DA^T GH2 (M = 64: rows past ROUT are never read)
+        // ---- dgh2 = DA Wr3; dWr3 += DA^T GH2
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < ROUT / 16; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::da, 128, s), tc::mnmajor(sbase + S::g2, ROUT, s),
-                        tc::idesc(128, 32, 0, 1), s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::da, 128, s), tc::mnmajor(sbase + S::g2, ROUT, s), tc::idesc(128, 32, 0, 1), s > 0);
             tc::commit(bar);
         }
         if ((t & 31) == 0) {
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DWR3, tc::mnmajor(sbase + S::da, 128, s), tc::mnmajor(sbase + S::gh2, 128, s),
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DWR3, tc::mnmajor(gbase + S::da, 128, s), tc::mnmajor(gbase + S::gh2, 128, s),
                         tc::idesc(64, 32, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
-        masked_pack32(lane_addr + T_ACC, gh2_mask, packed);
         is.wait_dw();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            store_chunk(smem, S::dgh2, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        masked_store32(lane_addr + acc, gh2_mask, mine, S::dgh2, t, 0);
         // ---- dgh1 = DGH2 Wr2; dWr2 (accumulator rows 32-63) += DGH2^T GH1 through the [zero | dgh2] view
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 2; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh2, 128, s), tc::mnmajor(sbase + S::r2, 32, s),
-                        tc::idesc(128, 32, 0, 1), s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::dgh2, 128, s), tc::mnmajor(sbase + S::r2, 32, s), tc::idesc(128, 32, 0, 1), s > 0);
             tc::commit(bar);
         }
         if ((t & 31) == 0) {
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DWR12, tc::mnmajor(sbase + S::zero, 128, s), tc::mnmajor(sbase + S::gh, 128, s),
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DWR12, tc::mnmajor(gbase + S::zero, 128, s), tc::mnmajor(gbase + S::gh, 128, s),
                         tc::idesc(64, 32, 1, 1), 1u);
             tc::commit(bar_dw);
         }
         is.wait_data();
-        masked_pack32(lane_addr + T_ACC, gh_mask, packed);
         is.wait_dw();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            store_chunk(smem, S::dgh1, t, j, make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]));
+        masked_store32(lane_addr + acc, gh_mask, mine, S::dgh1, t, 0);
         // ---- dR = DGH1 Wr1; dWr1 (accumulator rows 0-31) += DGH1^T R through the [dgh1 | zero] view;
         //      router grid values half(dR / 128)
         is.before_issue();
         if (t == 0) {
             for (int s = 0; s < 2; ++s)
-                tc::mma(tmem + T_ACC, tc::kmajor(sbase + S::dgh1, 128, s), tc::mnmajor(sbase + S::g1, 32, s),
-                        tc::idesc(128, W, 0, 1), s > 0);
+                tc::mma(tmem + acc, tc::kmajor(gbase + S::dgh1, 128, s), tc::mnmajor(sbase + S::g1, 32, s), tc::idesc(128, W, 0, 1), s > 0);
             tc::commit(bar);
         }
         if ((t & 31) == 0) {
-            for (int s = 2 * warp; s < 2 * warp + 2; ++s)
-                tc::mma(tmem + T_DWR12, tc::mnmajor(sbase + S::dgh1, 128, s), tc::mnmajor(sbase + xbuf, 128, s),
+            for (int s = 2 * wq; s < 2 * wq + 2; ++s)
+                tc::mma(tmem + E3_DWR12, tc::mnmajor(gbase + S::dgh1, 128, s), tc::mnmajor(gbase + S::x, 128, s),
                         tc::idesc(64, W, 1, 1), 1u);
             tc::commit(bar_dw);
         }
@@ -1124,84 +1152,86 @@ __global__ void __launch_bounds__(TC_THREADS, 2) experts_train_kernel(const MlpA
 #pragma unroll
         for (int q = 0; q < KW; ++q) {
             float v[16];
-            tc::tmem_ld16(lane_addr + T_ACC + 16 * q, v);
+            tc::tmem_ld16(lane_addr + acc + 16 * q, v);
             uint32_t rv[8];
 #pragma unroll
             for (int c = 0; c < 16; c += 2) rv[c / 2] = as_u32(grid_pair(v[c], v[c + 1]));
-            if (valid) {  // row-major [stride][W]: one 32-byte run per 16 columns
+            if (valid) {
                 uint4* dst = reinterpret_cast<uint4*>(a.router_gvals + i * W + 16 * q);
                 dst[0] = make_uint4(rv[0], rv[1], rv[2], rv[3]);
                 dst[1] = make_uint4(rv[4], rv[5], rv[6], rv[7]);
             }
         }
-        is.wait_dw();  // dWr1 has read R and DGH1
         if (valid) {
 #pragma unroll
-            for (int j = 0; j < PAIRS / 4; ++j)  // row-major [stride][W]: the coordinate's values in 16-byte runs
+            for (int j = 0; j < PAIRS / 4; ++j)
                 reinterpret_cast<uint4*>(a.gvals + i * W)[j] = make_uint4(gv[4 * j], gv[4 * j + 1], gv[4 * j + 2], gv[4 * j + 3]);
         }
+        is.wait_dw();  // dWr1 has read R and DGH1: the next tile may overwrite them
         if (!is.settle()) break;
-        dw_accumulate = 1;
-        xbuf = xbuf == S::x ? S::x2 : S::x;
+        added = true;
     }
     asm volatile("cp.async.wait_all;\n" ::: "memory");  // no copy outlives the block
 
     if (!is.ok) {
         if (t == 0) atomicExch(error_flag, 2);
-        // give the products every warp may still have in flight a bounded chance to land before TMEM is released
+        // give the products this group's warps may still have in flight a bounded chance to land
         if ((t & 31) == 0) tc::commit(drain);
         tc::bar_wait(drain, 0, WAIT_LIMIT);
     }
-    // ---- weight gradients: TMEM (M=64 layout: rows 16w..16w+15 in lanes 32w..32w+15) -> partials
-    constexpr int GP = router_params(W, ROUT), R2 = ROUTER_HIDDEN * W, R3 = R2 + ROUTER_HIDDEN * ROUTER_HIDDEN;
-    constexpr int P = GP + decoder_params(W);
-    float* part = a.partials + (long long)blockIdx.x * P;
-    float* dec = part + GP;
-    const int row = 16 * warp + (t & 31);
-    const bool holds = (t & 31) < 16;
-    const bool any = dw_accumulate && is.ok;
+    // ---- weight gradients: TMEM (M = 64 layout) -> this CTA's partials, by the first warpgroup
     tc::fence_before_sync();
-    __syncthreads();
+    const bool all_ok = __syncthreads_and(is.ok) != 0;
+    const bool any = __syncthreads_or(added) != 0;
     tc::fence_after_sync();
+    if (group == 0) {
+        constexpr int GP = router_params(W, ROUT), R2 = ROUTER_HIDDEN * W, R3 = R2 + ROUTER_HIDDEN * ROUTER_HIDDEN;
+        constexpr int P = GP + decoder_params(W);
+        float* part = a.partials + (long long)blockIdx.x * P;
+        float* dec = part + GP;
+        const int row = 16 * quad + (t & 31);
+        const bool holds = (t & 31) < 16;
+        const bool keep = any && all_ok;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {  // dWd2 [64][64]
-        float v[16];
-        tc::tmem_ld16(lane_addr + T_DWD2 + 16 * q, v);
-        if (holds)
-            for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + row * DEC_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
-    }
+        for (int q = 0; q < 4; ++q) {  // dWd2 [64][64]
+            float v[16];
+            tc::tmem_ld16(lane_addr + E3_DWD2 + 16 * q, v);
+            if (holds)
+                for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + row * DEC_HIDDEN + 16 * q + c] = keep ? v[c] : 0.0f;
+        }
 #pragma unroll
-    for (int q = 0; q < KW; ++q) {  // dWd1 [64][W]
-        float v[16];
-        tc::tmem_ld16(lane_addr + T_DWD1 + 16 * q, v);
-        if (holds)
-            for (int c = 0; c < 16; ++c) dec[row * W + 16 * q + c] = any ? v[c] : 0.0f;
-    }
-    {  // dW3 [16][64] from its transpose [64 in][16 out]
-        float v[16];
-        tc::tmem_ld16(lane_addr + T_DW3T, v);
-        if (holds)
-            for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN + c * DEC_HIDDEN + row] = any ? v[c] : 0.0f;
-    }
+        for (int q = 0; q < KW; ++q) {  // dWd1 [64][W]
+            float v[16];
+            tc::tmem_ld16(lane_addr + E3_DWD1 + 16 * q, v);
+            if (holds)
+                for (int c = 0; c < 16; ++c) dec[row * W + 16 * q + c] = keep ? v[c] : 0.0f;
+        }
+        {  // dW3 [16][64] from its transpose [64 in][16 out]
+            float v[16];
+            tc::tmem_ld16(lane_addr + E3_DW3T, v);
+            if (holds)
+                for (int c = 0; c < 16; ++c) dec[DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN + c * DEC_HIDDEN + row] = keep ? v[c] : 0.0f;
+        }
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {  // dWr1 [32][W] (rows 0-31) and dWr2 [32][32] (rows 32-63)
-        float v[16];
-        tc::tmem_ld16(lane_addr + T_DWR12 + 16 * q, v);
-        if (holds) {
-            float* dst = row < ROUTER_HIDDEN ? part + row * W : part + R2 + (row - ROUTER_HIDDEN) * ROUTER_HIDDEN;
-            for (int c = 0; c < 16; ++c) dst[16 * q + c] = any ? v[c] : 0.0f;
+        for (int q = 0; q < 2; ++q) {  // dWr1 [32][W] (rows 0-31) and dWr2 [32][32] (rows 32-63)
+            float v[16];
+            tc::tmem_ld16(lane_addr + E3_DWR12 + 16 * q, v);
+            if (holds) {
+                float* dst = row < ROUTER_HIDDEN ? part + row * W : part + R2 + (row - ROUTER_HIDDEN) * ROUTER_HIDDEN;
+                for (int c = 0; c < 16; ++c) dst[16 * q + c] = keep ? v[c] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {  // dWr3 [ROUT][32]
+            float v[16];
+            tc::tmem_ld16(lane_addr + E3_DWR3 + 16 * q, v);
+            if (holds && row < ROUT)
+                for (int c = 0; c < 16; ++c) part[R3 + row * ROUTER_HIDDEN + 16 * q + c] = keep ? v[c] : 0.0f;
         }
     }
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {  // dWr3 [ROUT][32]
-        float v[16];
-        tc::tmem_ld16(lane_addr + T_DWR3 + 16 * q, v);
-        if (holds && row < ROUT)
-            for (int c = 0; c < 16; ++c) part[R3 + row * ROUTER_HIDDEN + 16 * q + c] = any ? v[c] : 0.0f;
-    }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLUMNS);
+    if (warp == 0) tc::tmem_dealloc(tmem, E3_TMEM_COLUMNS);
 }
 
 // cudaFuncSetAttribute once per kernel and device (devices 0..63).
@@ -1219,8 +1249,8 @@ void set_smem(Kernel kernel, int bytes, std::atomic<unsigned long long>& configu
 template <int ROUT, int LIVE>
 void launch_experts(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t stream) {
     static std::atomic<unsigned long long> configured{0};
-    set_smem(experts_train_kernel<ROUT, LIVE>, ExpertSmem::total, configured);
-    experts_train_kernel<ROUT, LIVE><<<blocks, TC_THREADS, ExpertSmem::total, stream>>>(a, error_flag);
+    set_smem(experts_train3_kernel<ROUT, LIVE>, E3Smem::total, configured);
+    experts_train3_kernel<ROUT, LIVE><<<blocks, E3_THREADS, E3Smem::total, stream>>>(a, error_flag);
     note_launch();
 }
 
@@ -1262,6 +1292,14 @@ int mlp_tc_blocks(long long n) {
     const long long tiles = (n + TC_TILE - 1) / TC_TILE;
     long long blocks = 2LL * sm_count();
     if (blocks > tiles) blocks = tiles;
+    return blocks < 1 ? 1 : int(blocks);
+}
+
+int mlp_tc_train_blocks(long long n, GateMode gate) {
+    if (gate != GATE_EXPERTS) return mlp_tc_blocks(n);
+    const long long tiles = (n + TC_TILE - 1) / TC_TILE;
+    long long blocks = (tiles + E3_GROUPS - 1) / E3_GROUPS;  // one CTA per SM, three tiles in flight each
+    if (blocks > sm_count()) blocks = sm_count();
     return blocks < 1 ? 1 : int(blocks);
 }
 

@@ -573,7 +573,7 @@ struct Runtime {
             stage_end(slot);
         }
         const MlpArgs ma = mlp_args(n);
-        const int blocks = mlp_tc_blocks(n);
+        const int blocks = mlp_tc_train_blocks(n, gate_mode());
         slot = stage_begin(S_MLP);
         launch_mlp_tc_train(ma, input_width, gate_mode(), uniform, blocks, error_flag.ptr, stream);
         stage_end(slot);

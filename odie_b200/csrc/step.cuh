@@ -59,6 +59,8 @@ struct MlpArgs {
 // [levels][stride / 32]; stride is a multiple of 128.  A wait that runs out
 // sets *error_flag = 2 and the kernel returns.
 int mlp_tc_blocks(long long n);
+// CTAs of a training launch (the weight-gradient partials it writes): at most mlp_tc_blocks(n).
+int mlp_tc_train_blocks(long long n, GateMode gate);
 void launch_mlp_tc_train(const MlpArgs& args, int width, GateMode gate, bool uniform, int blocks, int* error_flag,
                          cudaStream_t stream);
 void launch_mlp_tc_decode(const MlpArgs& args, int width, GateMode gate, bool uniform, int* error_flag,
