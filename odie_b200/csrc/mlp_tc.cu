@@ -820,21 +820,38 @@ struct GroupIssuer {
     }
 };
 
-// 32 TMEM columns of a backward product, masked by the forward ReLU (bit c: column c), rounded to fp16 and
-// stored as chunks j0 .. j0 + 3 of row r; 16 columns at a time.
-__device__ __forceinline__ void masked_store32(uint32_t taddr, uint32_t mask, unsigned char* smem, int base, int r,
-                                               int j0) {
+// 32 TMEM columns through ReLU, rounded to fp16, stored as chunks j0 .. j0 + 3 of row r.
+__device__ __forceinline__ void relu_store32_plain(uint32_t taddr, unsigned char* smem, int base, int r, int j0) {
+    float v[32];
+    tc::tmem_ld32(taddr, v);
+    uint32_t h[16];
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) h[c / 2] = cvt_pair(v[c] > 0.0f ? v[c] : 0.0f, v[c + 1] > 0.0f ? v[c + 1] : 0.0f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        store_chunk(smem, base, r, j0 + q, make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]));
+}
+
+// 32 TMEM columns of a backward product kept where the layer's forward output -- the fp16 activations in
+// chunks j0 .. j0 + 3 of row r of buffer fwd -- is positive (the ReLU's derivative), rounded to fp16 and
+// stored as the same chunks of buffer dst (which may be fwd: each chunk is read before it is written).
+__device__ __forceinline__ void relu_grad_store32(uint32_t taddr, unsigned char* smem, int fwd, int dst, int r, int j0) {
+    const __half2 zero = __float2half2_rn(0.0f);
 #pragma unroll
     for (int hlf = 0; hlf < 2; ++hlf) {
         float v[16];
         tc::tmem_ld16(taddr + 16 * hlf, v);
-        const uint32_t m = mask >> (16 * hlf);
-        uint32_t h[8];
 #pragma unroll
-        for (int c = 0; c < 16; c += 2)
-            h[c / 2] = cvt_pair((m >> c & 1u) ? v[c] : 0.0f, (m >> (c + 1) & 1u) ? v[c + 1] : 0.0f);
-        store_chunk(smem, base, r, j0 + 2 * hlf, make_uint4(h[0], h[1], h[2], h[3]));
-        store_chunk(smem, base, r, j0 + 2 * hlf + 1, make_uint4(h[4], h[5], h[6], h[7]));
+        for (int q = 0; q < 2; ++q) {
+            const int j = j0 + 2 * hlf + q;
+            const uint4 a = *reinterpret_cast<const uint4*>(smem + fwd + tc::blocked(TC_TILE, r, 8 * j));
+            const uint32_t on[4] = {a.x, a.y, a.z, a.w};
+            uint32_t g[4];
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+                g[p] = cvt_pair(v[8 * q + 2 * p], v[8 * q + 2 * p + 1]) & __hgt2_mask(as_half2(on[p]), zero);
+            store_chunk(smem, dst, r, j, make_uint4(g[0], g[1], g[2], g[3]));
+        }
     }
 }
 
@@ -938,7 +955,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
             for (int s = 0; s < KW; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
         is.complete();
-        const uint32_t gh_mask = relu_store32(lane_addr + acc, mine, S::gh, t, 0);
+        relu_store32_plain(lane_addr + acc, mine, S::gh, t, 0);
         // decoder input: the routed expert's features x half(p), one rounding per feature (registers have arrived)
         {
             const __half2 ph = __float2half2_rn(prob);
@@ -954,23 +971,22 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
             for (int s = 0; s < 2; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
         is.complete();
-        const uint32_t gh2_mask = relu_store32(lane_addr + acc, mine, S::gh2, t, 0);
+        relu_store32_plain(lane_addr + acc, mine, S::gh2, t, 0);
         // ---- decoder hidden 1, hidden 2, output
-        uint32_t h1_mask[2], h2_mask[2];
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < KW; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 2; ++q) h1_mask[q] = relu_store32(lane_addr + acc + 32 * q, mine, S::h1, t, 4 * q);
+        for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + acc + 32 * q, mine, S::h1, t, 4 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
         is.complete();
 #pragma unroll
-        for (int q = 0; q < 2; ++q) h2_mask[q] = relu_store32(lane_addr + acc + 32 * q, mine, S::h2, t, 4 * q);
+        for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + acc + 32 * q, mine, S::h2, t, 4 * q);
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
@@ -1013,7 +1029,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
         is.wait_data();
         is.wait_dw();  // dW3 has read H2: dh2 may overwrite it
 #pragma unroll
-        for (int q = 0; q < 2; ++q) masked_store32(lane_addr + acc + 32 * q, h2_mask[q], mine, S::h2, t, 4 * q);
+        for (int q = 0; q < 2; ++q) relu_grad_store32(lane_addr + acc + 32 * q, mine, S::h2, S::h2, t, 4 * q);
         // ---- dh1 = DH2 Wd2; dWd2 += DH2^T H1
         is.before_issue();
         if (t == 0) {
@@ -1030,7 +1046,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
         is.wait_data();
         is.wait_dw();  // dWd2 has read H1: dh1 may overwrite it
 #pragma unroll
-        for (int q = 0; q < 2; ++q) masked_store32(lane_addr + acc + 32 * q, h1_mask[q], mine, S::h1, t, 4 * q);
+        for (int q = 0; q < 2; ++q) relu_grad_store32(lane_addr + acc + 32 * q, mine, S::h1, S::h1, t, 4 * q);
         // ---- dz = DH1 Wd1; dWd1 += DH1^T WX
         is.before_issue();
         if (t == 0) {
@@ -1117,7 +1133,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
         }
         is.wait_data();
         is.wait_dw();
-        masked_store32(lane_addr + acc, gh2_mask, mine, S::dgh2, t, 0);
+        relu_grad_store32(lane_addr + acc, mine, S::gh2, S::dgh2, t, 0);
         // ---- dgh1 = DGH2 Wr2; dWr2 (accumulator rows 32-63) += DGH2^T GH1 through the [zero | dgh2] view
         is.before_issue();
         if (t == 0) {
@@ -1133,7 +1149,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
         }
         is.wait_data();
         is.wait_dw();
-        masked_store32(lane_addr + acc, gh_mask, mine, S::dgh1, t, 0);
+        relu_grad_store32(lane_addr + acc, mine, S::gh, S::dgh1, t, 0);
         // ---- dR = DGH1 Wr1; dWr1 (accumulator rows 0-31) += DGH1^T R through the [dgh1 | zero] view;
         //      router grid values half(dR / 128)
         is.before_issue();
