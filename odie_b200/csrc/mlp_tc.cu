@@ -732,10 +732,13 @@ constexpr int E3_GROUPS = 3;
 constexpr int E3_THREADS = E3_GROUPS * TC_THREADS;
 constexpr uint32_t E3_TMEM_COLUMNS = 512;
 // TMEM columns: warpgroup g's per-tile accumulator at 64 g, then the shared weight-gradient accumulators
-// (M = 64 layout: rows 16 w .. 16 w + 15 in lanes 32 w .. 32 w + 15): dWd2, dWd1, dW3^T, dWr3, dWr1 | dWr2.
+// (M = 64 layout: rows 16 w .. 16 w + 15 in lanes 32 w .. 32 w + 15): dWd2, dWd1, dW3^T, dWr3, dWr1 | dWr2,
+// then a second 32-column accumulator per warpgroup.
 constexpr uint32_t E3_DWD2 = 64 * E3_GROUPS, E3_DWD1 = E3_DWD2 + 64, E3_DW3T = E3_DWD1 + 32, E3_DWR3 = E3_DW3T + 16,
                    E3_DWR12 = E3_DWR3 + 32, E3_DW_END = E3_DWR12 + 32;
-static_assert(E3_DW_END <= E3_TMEM_COLUMNS, "the three tiles' accumulators and the weight gradients fit TMEM");
+// then each warpgroup's second accumulator (32 columns): the router's hidden layers, computed beside the decoder's
+constexpr uint32_t E3_ACC2 = E3_DW_END;
+static_assert(E3_ACC2 + 32 * E3_GROUPS <= E3_TMEM_COLUMNS, "the three tiles' accumulators and the weight gradients fit TMEM");
 
 // Shared memory (bytes): the weights once, then one region per warpgroup with the tile's activations.  The
 // router backward reuses the decoder's buffers once the decoder's weight-gradient products have read them:
@@ -894,6 +897,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);  // this warp's TMEM lanes
     const uint32_t acc = 64u * uint32_t(group);                      // this warpgroup's per-tile accumulator
+    const uint32_t acc2 = E3_ACC2 + 32u * uint32_t(group);           // and its router-forward accumulator
     if (group == 0) {  // the weight-gradient accumulators start at zero; every product accumulates
         float zero[16];
 #pragma unroll
@@ -948,15 +952,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
             prob = __ldg(a.prob + i);
             expert = __ldg(a.expert + i);
         }
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
-        // ---- router recompute: GH1 = relu(R Wr1^T), GH2 = relu(GH1 Wr2^T)
-        is.before_issue();
-        if (t == 0)
-            for (int s = 0; s < KW; ++s)
-                tc::mma(tmem + acc, tc::kmajor(gbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
-        is.complete();
-        relu_store32_plain(lane_addr + acc, mine, S::gh, t, 0);
-        // decoder input: the routed expert's features x half(p), one rounding per feature (registers have arrived)
+        // decoder input: the routed expert's features x half(p), one rounding per feature
         {
             const __half2 ph = __float2half2_rn(prob);
             uint32_t wx[PAIRS];
@@ -966,27 +962,32 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
             for (int j = 0; j < W / 8; ++j)
                 store_chunk(mine, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
         }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        // ---- the router recompute and the decoder forward side by side (independent chains): GH1 = relu(R
+        //      Wr1^T) in acc2 with H1 = relu(WX Wd1^T) in acc, then GH2 = relu(GH1 Wr2^T) with H2 = relu(H1 Wd2^T)
         is.before_issue();
-        if (t == 0)
-            for (int s = 0; s < 2; ++s)
-                tc::mma(tmem + acc, tc::kmajor(gbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
-        is.complete();
-        relu_store32_plain(lane_addr + acc, mine, S::gh2, t, 0);
-        // ---- decoder hidden 1, hidden 2, output
-        is.before_issue();
-        if (t == 0)
+        if (t == 0) {
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem + acc2, tc::kmajor(gbase + S::x, 128, s), tc::kmajor(sbase + S::g1, 32, s), ID_G1, s > 0);
             for (int s = 0; s < KW; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
+        }
         is.complete();
+        relu_store32_plain(lane_addr + acc2, mine, S::gh, t, 0);
 #pragma unroll
         for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + acc + 32 * q, mine, S::h1, t, 4 * q);
         is.before_issue();
-        if (t == 0)
+        if (t == 0) {
+            for (int s = 0; s < 2; ++s)
+                tc::mma(tmem + acc2, tc::kmajor(gbase + S::gh, 128, s), tc::kmajor(sbase + S::r2, 32, s), ID_G1, s > 0);
             for (int s = 0; s < 4; ++s)
                 tc::mma(tmem + acc, tc::kmajor(gbase + S::h1, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
+        }
         is.complete();
+        relu_store32_plain(lane_addr + acc2, mine, S::gh2, t, 0);
 #pragma unroll
         for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + acc + 32 * q, mine, S::h2, t, 4 * q);
+        // ---- decoder output
         is.before_issue();
         if (t == 0)
             for (int s = 0; s < 4; ++s)
