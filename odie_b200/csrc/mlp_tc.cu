@@ -916,20 +916,14 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
     constexpr uint32_t ID_G1 = tc::idesc(128, 32, 0, 0), ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
     const int per = a.per_band;
 
-    for (long long tile = (long long)blockIdx.x * E3_GROUPS + group; tile < tiles && is.ok; tile += stride) {
+    // The routed expert's feature row, logits, target, probability and expert of a tile: read for the first tile
+    // here, then for the next tile once the current one has used them (during its router backward).
+    uint32_t raw[PAIRS], lg[LIVE / 2];
+    float target[3], prob;
+    int expert;
+    auto load_inputs = [&](long long tile) {
         const long long i = tile * TC_TILE + t;
-        const bool valid = i < a.n;
-        // ---- this tile's router features into x (the previous tile's last product, which read x, has completed)
-        {
-            const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
-#pragma unroll
-            for (int j = 0; j < W / 8; ++j) cp_async16(gbase + S::x + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
-            cp_async_commit();
-        }
-        // ---- the routed expert's feature row, logits, target, probability and expert (read before use)
-        uint32_t raw[PAIRS], lg[LIVE / 2];
-        float target[3] = {0.0f, 0.0f, 0.0f}, prob = 0.0f;
-        int expert = 0;
+        const bool valid = tile < tiles && i < a.n;
 #pragma unroll
         for (int j = 0; j < PAIRS / 4; ++j) {
             const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.raw) + i * (PAIRS / 4) + j) : make_uint4(0, 0, 0, 0);
@@ -946,11 +940,22 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
             lg[4 * j + 2] = q.z;
             lg[4 * j + 3] = q.w;
         }
-        if (valid) {
 #pragma unroll
-            for (int c = 0; c < 3; ++c) target[c] = __ldg(a.target + 3 * i + c);
-            prob = __ldg(a.prob + i);
-            expert = __ldg(a.expert + i);
+        for (int c = 0; c < 3; ++c) target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
+        prob = valid ? __ldg(a.prob + i) : 0.0f;
+        expert = valid ? __ldg(a.expert + i) : 0;
+    };
+    load_inputs((long long)blockIdx.x * E3_GROUPS + group);
+
+    for (long long tile = (long long)blockIdx.x * E3_GROUPS + group; tile < tiles && is.ok; tile += stride) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = i < a.n;
+        // ---- this tile's router features into x (the previous tile's last product, which read x, has completed)
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(a.router_in) + (valid ? i * (W / 8) : 0);
+#pragma unroll
+            for (int j = 0; j < W / 8; ++j) cp_async16(gbase + S::x + tc::blocked(TC_TILE, t, 8 * j), src + j, valid ? 16u : 0u);
+            cp_async_commit();
         }
         // decoder input: the routed expert's features x half(p), one rounding per feature
         {
@@ -1109,6 +1114,7 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
                 da[j + 1] = j + 1 < per ? __high2float(h) : 0.0f;
             }
         }
+        load_inputs(tile + stride);  // this tile's inputs are used up; the next tile's arrive during the router backward
         is.wait_dw();  // dWd1 has read WX and DH1: h1, wx, dy and h2 are free for the router backward
         {
             const uint4 zero4 = make_uint4(0, 0, 0, 0);
