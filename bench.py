@@ -369,7 +369,8 @@ def run_reference(args):
     value = coords / seconds
     line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': seconds / steps * 1e3, 'higher_is_better': True, 'scaling': 'weak',
-            'vs_baseline': None, 'dtype': 'f32/f16', 'data': 'synthetic', 'impl': 'reference',
+            'vs_baseline': None, 'dtype': 'f32' if args.workload == 'c1-hash' else 'f32/f16', 'data': 'synthetic',
+            'impl': 'reference',
             'config': {'workload': args.workload, 'batch_per_step': sample, 'full_batch': args.batch,
                        'note': 'bounded sample of the workload per step (full model and layout)'},
             'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port',
