@@ -594,6 +594,80 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(c
     }
 }
 
+// The runs scatter for the common case of the single-table grids (the router grid, the fp32 hash grid): no
+// expert ids, no cell that visibility can hide, value rows read 16 bytes per group.  The same runs and flushes
+// as encode_backward_runs_kernel, with each group's scales read once per run and no per-coordinate checks.
+template <int KIND, typename U>
+__global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_kernel(const EncodeArgs a,
+                                                                                    const __grid_constant__ LevelTable table,
+                                                                                    const __grid_constant__ CoarseList list,
+                                                                                    const U* __restrict__ upstream,
+                                                                                    float* __restrict__ grad) {
+    extern __shared__ float acc[];
+    for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
+    __syncthreads();
+    const long long chunk = (a.n + gridDim.x - 1) / gridDim.x;
+    const long long begin = (long long)blockIdx.x * chunk;
+    const long long end = begin + chunk < a.n ? begin + chunk : a.n;
+    const long long run = (chunk + blockDim.x - 1) / blockDim.x;
+    const long long first = begin + threadIdx.x * run;
+    const long long last = first + run < end ? first + run : end;
+    const float2* const coords = reinterpret_cast<const float2*>(a.coords);
+    for (int c0 = 0; c0 < list.count; c0 += RUNS_GROUP) {
+        const int here = list.count - c0 < RUNS_GROUP ? list.count - c0 : RUNS_GROUP;
+        int cx[RUNS_GROUP], cy[RUNS_GROUP];
+        float v[RUNS_GROUP][8], scale[RUNS_GROUP];
+        bool open = false;  // a run is open (the first coordinate has been seen)
+#pragma unroll
+        for (int g = 0; g < RUNS_GROUP; ++g) {
+            cx[g] = cy[g] = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[g][j] = 0.0f;
+            scale[g] = table.level[list.level[g < here ? c0 + g : c0]].scale;
+        }
+        for (long long i = first; i < last; ++i) {
+            const float2 p = __ldg(coords + i);
+            float pairs[2 * RUNS_GROUP];
+            load_pairs4(upstream, i, a.width, c0, pairs);
+#pragma unroll
+            for (int g = 0; g < RUNS_GROUP; ++g) {
+                if (g >= here) break;
+                const Corner4 geo = geometry(p.x, p.y, scale[g]);
+                if (open && (geo.ix != cx[g] || geo.iy != cy[g]))
+                    runs_flush<KIND>(table.level[list.level[c0 + g]], acc + list.offset[c0 + g], 0, cx[g], cy[g], v[g],
+                                     a.node_bitmap, a.node_prefix);
+                cx[g] = geo.ix;
+                cy[g] = geo.iy;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    v[g][2 * k] = __fmaf_rn(geo.w[k], pairs[2 * g], v[g][2 * k]);
+                    v[g][2 * k + 1] = __fmaf_rn(geo.w[k], pairs[2 * g + 1], v[g][2 * k + 1]);
+                }
+            }
+            open = true;
+        }
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int g = 0; g < RUNS_GROUP; ++g) {
+            if (g >= here) break;
+            const long long key = ((long long)cx[g] << 32) | uint32_t(cy[g]);
+            if (combine_lanes(v[g], key, open ? 0 : -1 - lane, open))
+                runs_flush<KIND>(table.level[list.level[c0 + g]], acc + list.offset[c0 + g], 0, cx[g], cy[g], v[g],
+                                 a.node_bitmap, a.node_prefix);
+        }
+    }
+    __syncthreads();
+    for (int c = 0; c < list.count; ++c) {
+        const Level d = table.level[list.level[c]];
+        const int per_table = d.points * d.F;
+        const float* tab = acc + list.offset[c];
+        for (int j = threadIdx.x; j < per_table; j += blockDim.x) {
+            const float v = tab[j];
+            if (v != 0.0f) red_add_f32(grad + d.offset + j, v);
+        }
+    }
+}
+
 }  // namespace
 
 constexpr int COARSE_SMEM_FLOATS = 27648;  // 108 KB of shared memory per block: two blocks per SM
@@ -652,6 +726,9 @@ static void set_runs_smem() {
                                    COARSE_SMEM_FLOATS * 4));
     ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<false, KIND, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    COARSE_SMEM_FLOATS * 4));
+    if (KIND == HASH_DENSE || KIND == HASH_HASHED || KIND == -1)
+        ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_plain_kernel<KIND, U>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, COARSE_SMEM_FLOATS * 4));
 }
 
 template <typename U>
@@ -666,7 +743,12 @@ struct RunsLaunch {
 };
 
 template <int KIND, typename U>
-static void launch_runs(const RunsLaunch<U>& l, bool vec) {
+static void launch_runs(const RunsLaunch<U>& l, bool vec, bool plain = false) {
+    if (KIND != PLANE && vec && plain) {
+        encode_backward_runs_plain_kernel<KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
+                                                                                               l.upstream, l.grad);
+        return;
+    }
     if (vec)
         encode_backward_runs_kernel<true, KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
                                                                                                l.upstream, l.grad);
@@ -732,11 +814,17 @@ static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U
             if (d.kind != kind) kind = -1;
         }
         if (pairs) {
+            // one table, no cell that visibility can hide: the runs kernel without per-coordinate checks
+            bool plain = !a.expert;
+            for (int c = 0; c < list.count; ++c) {
+                const Level& d = src.table.level[list.level[c]];
+                plain = plain && d.kind != PLANE && (d.cells < 0 || !a.bitmap);
+            }
             const RunsLaunch<U> l{a, src.table, list, upstream, grad, blocks, list.total * 4, stream};
             if (kind == PLANE) launch_runs<PLANE>(l, vec);
-            else if (kind == HASH_DENSE) launch_runs<HASH_DENSE>(l, vec);
-            else if (kind == HASH_HASHED) launch_runs<HASH_HASHED>(l, vec);
-            else launch_runs<-1>(l, vec);
+            else if (kind == HASH_DENSE) launch_runs<HASH_DENSE>(l, vec, plain);
+            else if (kind == HASH_HASHED) launch_runs<HASH_HASHED>(l, vec, plain);
+            else launch_runs<-1>(l, vec, plain);
         }
         else
             encode_backward_shared_kernel<U><<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
