@@ -1257,6 +1257,128 @@ __global__ void __launch_bounds__(E3_THREADS, 1) experts_train3_kernel(const Mlp
     if (warp == 0) tc::tmem_dealloc(tmem, E3_TMEM_COLUMNS);
 }
 
+// ---------------------------------------------------------------- routed-expert decode
+// Decode of the routed-expert model (no reference counterpart): decoder input fp16(features x fp16(p)), the
+// decoder's two ReLU layers and its output, fp16-rounded RGB out -- the decode variant of mlp_tc_kernel, with
+// only what decode needs resident: the decoder weights, the tile's input and one hidden buffer that holds the
+// first hidden layer and then the second (its product has read the first when the second is written).  38 KB of
+// shared memory and 64 TMEM columns per CTA, so four CTAs (four tiles in flight) share an SM.
+struct DecodeSmem {
+    static constexpr int W = 32;
+    static constexpr int d1 = 0;                   // [64 x 32]
+    static constexpr int d2 = d1 + 64 * W * 2;     // [64 x 64]
+    static constexpr int d3 = d2 + 64 * 64 * 2;    // [16 x 64]
+    static constexpr int wx = d3 + 16 * 64 * 2;    // [128 x 32] decoder input
+    static constexpr int h = wx + 128 * W * 2;     // [128 x 64] hidden 1, then hidden 2
+    static constexpr int bar = h + 16384;          // mbarrier: the products of a phase
+    static constexpr int drain = bar + 8;          // mbarrier: every warp's products (error exit)
+    static constexpr int tmem = drain + 8;
+    static constexpr int total = tmem + 8;
+};
+constexpr int DECODE_CTAS_PER_SM = 4;
+constexpr uint32_t DECODE_TMEM_COLUMNS = 64;
+
+__global__ void __launch_bounds__(TC_THREADS, DECODE_CTAS_PER_SM) experts_decode_kernel(const MlpArgs a, int* error_flag) {
+    using S = DecodeSmem;
+    constexpr int W = 32, PAIRS = W / 2, KW = W / 16;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int t = threadIdx.x, warp = t >> 5;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
+    uint64_t* drain = reinterpret_cast<uint64_t*>(smem + S::drain);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::tmem);
+    const uint32_t sbase = tc::smem_u32(smem);
+    stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
+    stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
+    if (t == 0) {
+        tc::bar_init(bar, 1);
+        tc::bar_init(drain, TC_THREADS / 32);
+        tc::fence_bar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, DECODE_TMEM_COLUMNS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
+    Issuer is{bar, bar};
+    const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
+    constexpr uint32_t ID_D1 = tc::idesc(128, 64, 0, 0), ID_D3 = tc::idesc(128, 16, 0, 0);
+    // the routed expert's feature row and probability of a tile, read one tile ahead
+    uint32_t raw[PAIRS];
+    float prob;
+    auto load_inputs = [&](long long tile) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = tile < tiles && i < a.n;
+#pragma unroll
+        for (int j = 0; j < PAIRS / 4; ++j) {
+            const uint4 q = valid ? __ldg(reinterpret_cast<const uint4*>(a.raw) + i * (PAIRS / 4) + j) : make_uint4(0, 0, 0, 0);
+            raw[4 * j] = q.x;
+            raw[4 * j + 1] = q.y;
+            raw[4 * j + 2] = q.z;
+            raw[4 * j + 3] = q.w;
+        }
+        prob = valid ? __ldg(a.prob + i) : 0.0f;
+    };
+    load_inputs(blockIdx.x);
+    for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
+        const long long i = tile * TC_TILE + t;
+        const bool valid = i < a.n;
+        {  // decoder input: the routed expert's features x half(p), one rounding per feature
+            const __half2 ph = __float2half2_rn(prob);
+            uint32_t wx[PAIRS];
+#pragma unroll
+            for (int p = 0; p < PAIRS; ++p) wx[p] = as_u32(__hmul2(as_half2(raw[p]), ph));
+#pragma unroll
+            for (int j = 0; j < W / 8; ++j)
+                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
+        }
+        load_inputs(tile + gridDim.x);  // the next tile's rows arrive while this one runs
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < KW; ++s)
+                tc::mma(tmem, tc::kmajor(sbase + S::wx, 128, s), tc::kmajor(sbase + S::d1, 64, s), ID_D1, s > 0);
+        is.complete();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + 32 * q, smem, S::h, t, 4 * q);
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem, tc::kmajor(sbase + S::h, 128, s), tc::kmajor(sbase + S::d2, 64, s), ID_D1, s > 0);
+        is.complete();  // the product has read hidden 1: hidden 2 may take its place
+#pragma unroll
+        for (int q = 0; q < 2; ++q) relu_store32_plain(lane_addr + 32 * q, smem, S::h, t, 4 * q);
+        is.before_issue();
+        if (t == 0)
+            for (int s = 0; s < 4; ++s)
+                tc::mma(tmem, tc::kmajor(sbase + S::h, 128, s), tc::kmajor(sbase + S::d3, 16, s), ID_D3, s > 0);
+        is.complete();
+        float out[16];
+        tc::tmem_ld16(lane_addr, out);
+        if (valid) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const float xo = __half2float(__float2half_rn(out[c]));
+                if (a.rgb) a.rgb[3 * i + c] = xo;
+                if (a.rgb8) a.rgb8[3 * i + c] = (uint8_t)__float2int_rn(__fmul_rn(fminf(fmaxf(xo, 0.0f), 1.0f), 255.0f));
+            }
+        }
+        if (!is.settle()) break;
+    }
+    if (!is.ok) {
+        if (t == 0) atomicExch(error_flag, 2);
+        if ((t & 31) == 0) tc::commit(drain);
+        tc::bar_wait(drain, 0, WAIT_LIMIT);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, DECODE_TMEM_COLUMNS);
+}
+
 // cudaFuncSetAttribute once per kernel and device (devices 0..63).
 template <typename Kernel>
 void set_smem(Kernel kernel, int bytes, std::atomic<unsigned long long>& configured) {
@@ -1274,6 +1396,16 @@ void launch_experts(const MlpArgs& a, int blocks, int* error_flag, cudaStream_t 
     static std::atomic<unsigned long long> configured{0};
     set_smem(experts_train3_kernel<ROUT, LIVE>, E3Smem::total, configured);
     experts_train3_kernel<ROUT, LIVE><<<blocks, E3_THREADS, E3Smem::total, stream>>>(a, error_flag);
+    note_launch();
+}
+
+void launch_experts_decode(const MlpArgs& a, int* error_flag, cudaStream_t stream) {
+    static std::atomic<unsigned long long> configured{0};
+    set_smem(experts_decode_kernel, DecodeSmem::total, configured);
+    const long long tiles = (a.n + TC_TILE - 1) / TC_TILE;
+    const long long resident = (long long)DECODE_CTAS_PER_SM * sm_count();
+    experts_decode_kernel<<<unsigned(tiles < resident ? tiles : resident), TC_THREADS, DecodeSmem::total, stream>>>(
+        a, error_flag);
     note_launch();
 }
 
@@ -1295,7 +1427,10 @@ void dispatch(const MlpArgs& a, int width, GateMode gate, bool uniform, int bloc
 #undef ODIE_TC
     if (gate == GATE_EXPERTS) {
         ODIE_REQUIRE(width == 32, "routed experts take 32 input features");
-        if (!TRAIN) return launch_tc<32, GATE_EXPERTS, false, true>(a, blocks, error_flag, stream);
+        if (!TRAIN) {
+            ODIE_REQUIRE(a.raw_rows, "routed-expert decode reads row-major feature rows");
+            return launch_experts_decode(a, error_flag, stream);
+        }
         const Banding b{a.model_experts / a.per_band, a.first_band, a.per_band, 2};
         check_banding(b, a.experts);
         ODIE_REQUIRE(a.logits && (a.live == 8 || a.live == 16) && a.live >= a.per_band,
