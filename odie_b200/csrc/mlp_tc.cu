@@ -27,6 +27,8 @@
 // (R -> 32 -> 32 -> 16 or 64 logits) for its backward: dp = sum_c v_c f_c,
 // dz_j = dp p (delta_je - p_j), then the router backward down to the
 // router-grid gradient values; one CTA per SM keeps three tiles in flight.
+// Decode (experts_decode_kernel) keeps only the decoder resident, four CTAs
+// per SM.  mlp_tc_kernel serves the per-level gate and the gate-free heads.
 #include <atomic>
 
 #include "router.cuh"
@@ -207,12 +209,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     const uint32_t sbase = tc::smem_u32(smem);
 
     constexpr bool ROUTER = GATE == GATE_LEVELS;   // the reference's per-level gate
-    constexpr bool EXPERTS = GATE == GATE_EXPERTS;  // routed experts
+    static_assert(GATE != GATE_EXPERTS, "routed experts train in experts_train3_kernel and decode in experts_decode_kernel");
     if (ROUTER) {
         stage_blocked(a.gate_w, GATE_HIDDEN, W, smem, S::g1);
         stage_blocked(a.gate_w + GATE_HIDDEN * W, GATE_OUT, GATE_HIDDEN, smem, S::g2);
     }
-    static_assert(!(EXPERTS && TRAIN), "routed-expert training runs in experts_train3_kernel");
     stage_blocked(a.decoder_w, DEC_HIDDEN, W, smem, S::d1);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W, DEC_HIDDEN, DEC_HIDDEN, smem, S::d2);
     stage_blocked(a.decoder_w + DEC_HIDDEN * W + DEC_HIDDEN * DEC_HIDDEN, DEC_OUT, DEC_HIDDEN, smem, S::d3);
@@ -260,7 +261,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     // backward products, so their global-memory latency is off the chain.
     uint32_t next_raw[PAIRS], next_vis = 0;
     float next_target[3] = {0.0f, 0.0f, 0.0f};
-    float next_prob = 0.0f;
     auto load_inputs = [&](long long tile) {
         const long long i = tile * TC_TILE + t;
         const bool valid = tile < tiles && i < a.n;
@@ -282,7 +282,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
 #pragma unroll
             for (int c = 0; c < 3; ++c) next_target[c] = valid ? __ldg(a.target + 3 * i + c) : 0.0f;
         }
-        if (EXPERTS) next_prob = valid ? __ldg(a.prob + i) : 0.0f;
     };
     // Visibility: lane l (< levels) loads this warp's word of level l; the
     // words are broadcast with shuffles when the bits are folded per row.
@@ -306,7 +305,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
     for (long long tile = blockIdx.x; tile < tiles && is.ok; tile += gridDim.x) {
         const long long i = tile * TC_TILE + t;
         const bool valid = i < a.n;
-        const float prob = next_prob;
         // ---- inputs: raw features (pad columns 1.0), visibility bits, target
         uint32_t raw[PAIRS];
         const __half one = __float2half_rn(1.0f);
@@ -320,7 +318,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
         const uint32_t visbits = next_vis;
         const float target[3] = {next_target[0], next_target[1], next_target[2]};
         const long long next_tile = tile + gridDim.x;
-        if (!EXPERTS) {
+        {
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
                 store_chunk(smem, S::x, t, j, make_uint4(raw[4 * j], raw[4 * j + 1], raw[4 * j + 2], raw[4 * j + 3]));
@@ -379,20 +377,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) mlp_tc_kernel(const MlpArgs a, 
                     }
                     wx[p] = pack_half2(h[0], h[1]);
                 }
-            }
-#pragma unroll
-            for (int j = 0; j < W / 8; ++j)
-                store_chunk(smem, S::wx, t, j, make_uint4(wx[4 * j], wx[4 * j + 1], wx[4 * j + 2], wx[4 * j + 3]));
-        }
-        if (EXPERTS) {
-            // ---- decoder input: the routed expert's features x half(p), one rounding per feature
-            const __half2 ph = __float2half2_rn(prob);
-            uint32_t wx[PAIRS];
-#pragma unroll
-            for (int p = 0; p < PAIRS; ++p) {
-                const __half2 f = __halves2half2(lo_half(raw[p]), hi_half(raw[p]));
-                const __half2 g = __hmul2(f, ph);
-                wx[p] = pack_half2(__low2half(g), __high2half(g));
             }
 #pragma unroll
             for (int j = 0; j < W / 8; ++j)
