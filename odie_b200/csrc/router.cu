@@ -220,9 +220,20 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_forward_kernel(const Ro
     }
     __syncthreads();
     // persistent blocks: the weights are staged once per block, then the block walks the coordinates,
-    // C x blockDim at a time (thread t: base + t, base + blockDim + t, ...)
-    for (long long base = (long long)blockIdx.x * C * blockDim.x; base < a.n; base += (long long)gridDim.x * C * blockDim.x)
+    // C x blockDim at a time (thread t: base + t, base + blockDim + t, ...); the next group's rows are
+    // prefetched into L2 while this group computes
+    const long long step = (long long)gridDim.x * C * blockDim.x;
+    for (long long base = (long long)blockIdx.x * C * blockDim.x; base < a.n; base += step) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const long long next = base + step + (long long)c * blockDim.x + threadIdx.x;
+            if (a.row_major && next < a.n) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.features + next * W));
+                if (BANDED) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.xy + 2 * next));
+            }
+        }
         route_group<C, W, BANDED>(a, w, act, base + threadIdx.x);
+    }
 }
 
 template <int W, int OUT, bool BANDED>
