@@ -161,27 +161,32 @@ __global__ void __launch_bounds__(256) encode_forward_rows_kernel(const EncodeAr
     if (i >= a.n) return;
     const float2 p = __ldg(reinterpret_cast<const float2*>(a.coords) + i);
     const long long base = a.expert ? (long long)__ldg(a.expert + i) * a.expert_stride : 0LL;
-    uint32_t row[W / 2];
-#pragma unroll 4
-    for (int l = 0; l < W / 2; ++l) {
-        __half2 acc = __float2half2_rn(0.0f);
-        if (l < a.levels && l < a.active) {
-            const Level d = table.level[l];
-            const Corner4 g = geometry(p.x, p.y, d.scale);
-            if (level_on(d, g, a.bitmap)) {
-                __half2 t[4];
-                if (KIND >= 0 || split < 0) corner_pairs<KIND>(a, d, g, base, params, t);
-                else if (l < split) corner_pairs<HASH_DENSE>(a, d, g, base, params, t);
-                else corner_pairs<HASH_HASHED>(a, d, g, base, params, t);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
-            }
-        }
-        row[l] = pack_half2(__low2half(acc), __high2half(acc));
-    }
     uint4* dst = reinterpret_cast<uint4*>(out + i * W);
+    // four levels at a time, each group's 16 bytes stored as soon as they are complete (the row never needs a
+    // dynamically indexed array)
+#pragma unroll 1
+    for (int l0 = 0; l0 < W / 2; l0 += 4) {
+        uint32_t row[4];
 #pragma unroll
-    for (int j = 0; j < W / 8; ++j) dst[j] = make_uint4(row[4 * j], row[4 * j + 1], row[4 * j + 2], row[4 * j + 3]);
+        for (int q = 0; q < 4; ++q) {
+            const int l = l0 + q;
+            __half2 acc = __float2half2_rn(0.0f);
+            if (l < a.levels && l < a.active) {
+                const Level d = table.level[l];
+                const Corner4 g = geometry(p.x, p.y, d.scale);
+                if (level_on(d, g, a.bitmap)) {
+                    __half2 t[4];
+                    if (KIND >= 0 || split < 0) corner_pairs<KIND>(a, d, g, base, params, t);
+                    else if (l < split) corner_pairs<HASH_DENSE>(a, d, g, base, params, t);
+                    else corner_pairs<HASH_HASHED>(a, d, g, base, params, t);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) acc = __hfma2(half2_dup(g.w[k]), t[k], acc);
+                }
+            }
+            row[q] = pack_half2(__low2half(acc), __high2half(acc));
+        }
+        dst[l0 / 4] = make_uint4(row[0], row[1], row[2], row[3]);
+    }
 }
 
 // Gradient value of column col of coordinate i: fp16 rows (the fp16 network) or fp32 rows (the fp32 hash grid).
