@@ -300,12 +300,23 @@ __device__ __forceinline__ bool combine_lanes(float (&v)[8], long long key, int 
 // scrambled), each lane one coordinate over all its levels not in skip_levels
 // (those go through the shared-memory kernel below).  F=2 levels combine lanes
 // that share a cell before the 8-byte vector reductions.
-template <bool FROM_DESC, typename U>
+// ROWS: the values are row-major rows of 32 (level l in columns 2l, 2l + 1, 16-byte aligned): each thread reads
+// its coordinate's row once with 16-byte loads into its own shared-memory row (odd word stride: no bank
+// conflicts) instead of two scattered loads per level.
+template <typename U>
+struct RowWords {
+    static constexpr int words = 32 * int(sizeof(U)) / 4;  // 16 for fp16 values, 32 for fp32
+    static constexpr int stride = words + 1;
+};
+
+template <bool FROM_DESC, typename U, bool ROWS>
 __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a, const int* desc,
                                                               const __grid_constant__ LevelTable table,
                                                               const U* __restrict__ upstream,
                                                               float* __restrict__ grad, unsigned skip_levels,
                                                               uint32_t mask, int split) {
+    using RW = RowWords<U>;
+    __shared__ uint32_t s_rows[ROWS ? 256 * RW::stride : 1];
     const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const long long i = visit(warp_id, mask) * 32 + lane;
@@ -321,6 +332,18 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
             base = (long long)e * a.expert_stride;
         }
     }
+    uint32_t* const my_row = s_rows + (ROWS ? threadIdx.x * RW::stride : 0);
+    if (ROWS) {
+        const uint4* src = reinterpret_cast<const uint4*>(upstream + (valid ? i : 0) * 32);
+#pragma unroll
+        for (int j = 0; j < RW::words / 4; ++j) {
+            const uint4 q = valid ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+            my_row[4 * j] = q.x;
+            my_row[4 * j + 1] = q.y;
+            my_row[4 * j + 2] = q.z;
+            my_row[4 * j + 3] = q.w;
+        }
+    }
     const int levels = a.active < a.levels ? a.active : a.levels;
 #pragma unroll 2
     for (int l = 0; l < levels; ++l) {
@@ -330,8 +353,21 @@ __global__ void __launch_bounds__(256) encode_backward_kernel(const EncodeArgs a
         const bool on = valid && level_on(d, g, a.bitmap);
         float* const level_grad = grad + d.offset + base;
         if (d.F == 2) {  // uniform
-            const float u0 = on ? upstream_value(upstream, a, i, d.col) : 0.0f;
-            const float u1 = on ? upstream_value(upstream, a, i, d.col + 1) : 0.0f;
+            float u0 = 0.0f, u1 = 0.0f;
+            if (ROWS) {
+                if (sizeof(U) == 2) {
+                    const uint32_t w = my_row[l];
+                    u0 = __half2float(lo_half(w));
+                    u1 = __half2float(hi_half(w));
+                } else {
+                    u0 = __uint_as_float(my_row[2 * l]);
+                    u1 = __uint_as_float(my_row[2 * l + 1]);
+                }
+                if (!on) u0 = u1 = 0.0f;
+            } else if (on) {
+                u0 = upstream_value(upstream, a, i, d.col);
+                u1 = upstream_value(upstream, a, i, d.col + 1);
+            }
             float v[8];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -771,8 +807,8 @@ static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U
     const uint32_t mask = visit_mask(groups);
     const long long threads = 32 * (mask ? (long long)mask + 1 : groups);
     if (src.descriptors) {
-        encode_backward_kernel<true, U><<<blocks_for(threads, 256), 256, 0, stream>>>(a, src.descriptors, src.table,
-                                                                                     upstream, grad, 0u, mask, -1);
+        encode_backward_kernel<true, U, false><<<blocks_for(threads, 256), 256, 0, stream>>>(
+            a, src.descriptors, src.table, upstream, grad, 0u, mask, -1);
         note_launch();
         return;
     }
@@ -842,8 +878,16 @@ static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U
     while (split < a.levels && src.table.level[split].kind == HASH_DENSE) ++split;
     for (int l = split; l < a.levels; ++l)
         if (src.table.level[l].kind != HASH_HASHED) split = -1;
-    encode_backward_kernel<false, U><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream, grad,
-                                                                                  skip, mask, split);
+    // the values as whole rows when every level is F = 2 at columns (2l, 2l + 1) of 16-byte aligned rows of 32
+    bool rows = a.row_major && a.width == 32 && (reinterpret_cast<uintptr_t>(upstream) & 15) == 0;
+    for (int l = 0; rows && l < a.levels; ++l) rows = src.table.level[l].F == 2 && src.table.level[l].col == 2 * l;
+    if (rows)
+        encode_backward_kernel<false, U, true><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table, upstream,
+                                                                                           grad, skip, mask, split);
+    else
+        encode_backward_kernel<false, U, false><<<blocks_for(threads, 256), 256, 0, stream>>>(a, nullptr, src.table,
+                                                                                            upstream, grad, skip, mask,
+                                                                                            split);
     note_launch();
 }
 
