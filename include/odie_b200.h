@@ -62,7 +62,10 @@ ODIE_API long long odie_launch_count(void);
 ODIE_API void* odie_create(const char* json);
 /* One fwd/bwd(/Adam when update) step over n int64 pixel ids. runtime.cu:322 */
 ODIE_API int odie_step(void* handle, uint64_t ids, int n, int update);
-/* JSON of internal device buffers ("squares", "grid_grad", "head_grad", ...). runtime.cu:323 */
+/* JSON of internal device buffers ("squares", "grid_grad", "head_grad", ...). runtime.cu:323
+ * "scatter_strategy": two device ints, the strategy the last step's router-grid
+ * and main grid scatters chose from the batch (0: per-block shared-memory
+ * tables, 1: global reductions for spatially coherent batches). */
 ODIE_API const char* odie_pointers(void* handle);
 /* {"pristine": bool} for a grid range, or {"hash_fnv1a64", "bytes"} of all
  * optimizer state when begin < 0. runtime.cu:324 */

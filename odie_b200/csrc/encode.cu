@@ -635,18 +635,52 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_kernel(c
     }
 }
 
+// Adds one cell's 8 corner sums straight to the gradient (two-float vector reductions: F = 2 entries are
+// adjacent and 8-byte aligned) and clears them.
+template <int KIND>
+__device__ __forceinline__ void runs_flush_global(const Level& d, float* grad, int ix, int iy, float (&v)[8]) {
+    Corner4 g;
+    g.ix = ix;
+    g.iy = iy;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int row = corner_row<KIND>(d, g, k, nullptr, nullptr);
+        red_add_v2(grad + d.offset + 2 * row, v[2 * k], v[2 * k + 1]);
+        v[2 * k] = 0.0f;
+        v[2 * k + 1] = 0.0f;
+    }
+}
+
+// The scatter strategy of the plain runs kernel, chosen per launch on the device by runs_probe_kernel.
+//
+// RUNS_SHARED: each block accumulates the listed levels in its shared-memory tables (shared-memory atomics)
+// and adds them to global memory at the end.  Needed when consecutive coordinates rarely share a cell
+// (uniform batches): every coordinate then flushes at every level, and global reductions into a coarse
+// level's few entries would serialise in L2.
+// RUNS_GLOBAL: no shared-memory tables; each flush goes straight to global memory.  On a spatially coherent
+// batch (the reference's stratified sampler) flushes are rare, and without the tables' shared-memory
+// allocation the L1 keeps the room that the runs' per-lane loads (each lane walks its own run, so one warp
+// load touches 32 lines) need to stay in flight: 2.7x faster on the routed-expert benchmark's router grid.
+constexpr int RUNS_SHARED = 0, RUNS_GLOBAL = 1;
+
 // The runs scatter for the common case of the single-table grids (the router grid, the fp32 hash grid): no
 // expert ids, no cell that visibility can hide, value rows read 16 bytes per group.  The same runs and flushes
 // as encode_backward_runs_kernel, with each group's scales read once per run and no per-coordinate checks.
-template <int KIND, typename U>
+// strategy: the device int runs_probe_kernel wrote (the kernel returns at once unless it names STRATEGY), or
+// null (RUNS_SHARED runs unconditionally).
+template <int KIND, typename U, int STRATEGY>
 __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_kernel(const EncodeArgs a,
                                                                                     const __grid_constant__ LevelTable table,
                                                                                     const __grid_constant__ CoarseList list,
                                                                                     const U* __restrict__ upstream,
-                                                                                    float* __restrict__ grad) {
+                                                                                    float* __restrict__ grad,
+                                                                                    const int* __restrict__ strategy) {
+    if (strategy && *strategy != STRATEGY) return;
     extern __shared__ float acc[];
-    for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
-    __syncthreads();
+    if (STRATEGY == RUNS_SHARED) {
+        for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
+        __syncthreads();
+    }
     const long long chunk = (a.n + gridDim.x - 1) / gridDim.x;
     const long long begin = (long long)blockIdx.x * chunk;
     const long long end = begin + chunk < a.n ? begin + chunk : a.n;
@@ -654,6 +688,11 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_ke
     const long long first = begin + threadIdx.x * run;
     const long long last = first + run < end ? first + run : end;
     const float2* const coords = reinterpret_cast<const float2*>(a.coords);
+    auto flush = [&](int c, int ix, int iy, float (&v)[8]) {
+        const Level& d = table.level[list.level[c]];
+        if (STRATEGY == RUNS_SHARED) runs_flush<KIND>(d, acc + list.offset[c], 0, ix, iy, v, a.node_bitmap, a.node_prefix);
+        else runs_flush_global<KIND>(d, grad, ix, iy, v);
+    };
     for (int c0 = 0; c0 < list.count; c0 += RUNS_GROUP) {
         const int here = list.count - c0 < RUNS_GROUP ? list.count - c0 : RUNS_GROUP;
         int cx[RUNS_GROUP], cy[RUNS_GROUP];
@@ -674,9 +713,7 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_ke
             for (int g = 0; g < RUNS_GROUP; ++g) {
                 if (g >= here) break;
                 const Corner4 geo = geometry(p.x, p.y, scale[g]);
-                if (open && (geo.ix != cx[g] || geo.iy != cy[g]))
-                    runs_flush<KIND>(table.level[list.level[c0 + g]], acc + list.offset[c0 + g], 0, cx[g], cy[g], v[g],
-                                     a.node_bitmap, a.node_prefix);
+                if (open && (geo.ix != cx[g] || geo.iy != cy[g])) flush(c0 + g, cx[g], cy[g], v[g]);
                 cx[g] = geo.ix;
                 cy[g] = geo.iy;
 #pragma unroll
@@ -692,20 +729,64 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_ke
         for (int g = 0; g < RUNS_GROUP; ++g) {
             if (g >= here) break;
             const long long key = ((long long)cx[g] << 32) | uint32_t(cy[g]);
-            if (combine_lanes(v[g], key, open ? 0 : -1 - lane, open))
-                runs_flush<KIND>(table.level[list.level[c0 + g]], acc + list.offset[c0 + g], 0, cx[g], cy[g], v[g],
-                                 a.node_bitmap, a.node_prefix);
+            if (combine_lanes(v[g], key, open ? 0 : -1 - lane, open)) flush(c0 + g, cx[g], cy[g], v[g]);
+        }
+    }
+    if (STRATEGY == RUNS_SHARED) {
+        __syncthreads();
+        for (int c = 0; c < list.count; ++c) {
+            const Level d = table.level[list.level[c]];
+            const int per_table = d.points * d.F;
+            const float* tab = acc + list.offset[c];
+            for (int j = threadIdx.x; j < per_table; j += blockDim.x) {
+                const float v = tab[j];
+                if (v != 0.0f) red_add_f32(grad + d.offset + j, v);
+            }
+        }
+    }
+}
+
+// Chooses the plain runs kernel's strategy from the batch: PROBE_PAIRS pairs of consecutive coordinates
+// (i, i + 1), one at a hashed position inside each of PROBE_PAIRS equal stretches of the batch (evenly spaced
+// positions would alias with a raster-ordered sampler's rows), give each listed level's rate of cell changes
+// r, the rate at which a run ends.  RUNS_GLOBAL when the runs are long -- on average over the levels at most one change in
+// PROBE_MEAN_RUN consecutive pairs -- and no level's expected flushes per table entry (n r / entries) exceed
+// PROBE_ENTRY_FLUSHES, so that global reductions neither serialise on a coarse level's few entries nor
+// outnumber what the shared-memory tables absorb; RUNS_SHARED otherwise.  Either strategy gives the same sums
+// up to the order of the fp32 additions.  One block; writes *strategy.
+constexpr int PROBE_THREADS = 512, PROBE_PAIRS = 4096, PROBE_MEAN_RUN = 8, PROBE_ENTRY_FLUSHES = 4096;
+__global__ void __launch_bounds__(PROBE_THREADS) runs_probe_kernel(const EncodeArgs a,
+                                                                   const __grid_constant__ LevelTable table,
+                                                                   const __grid_constant__ CoarseList list,
+                                                                   int* __restrict__ strategy) {
+    __shared__ int changes[MAX_LEVELS];
+    for (int c = threadIdx.x; c < MAX_LEVELS; c += blockDim.x) changes[c] = 0;
+    __syncthreads();
+    const long long pairs = a.n - 1 < PROBE_PAIRS ? a.n - 1 : PROBE_PAIRS;
+    const long long stretch = pairs > 0 ? (a.n - 1) / pairs : 1;  // >= 1
+    const float2* const coords = reinterpret_cast<const float2*>(a.coords);
+    for (long long j = threadIdx.x; j < pairs; j += blockDim.x) {
+        const uint32_t h = (uint32_t(j) * 0x9E3779B1u) >> 7;
+        const long long i = j * stretch + (long long)(h % uint64_t(stretch));  // <= pairs * stretch - 1 < n - 1
+        const float2 p = __ldg(coords + i), q = __ldg(coords + i + 1);
+        for (int c = 0; c < list.count; ++c) {
+            const float s = table.level[list.level[c]].scale;
+            const Corner4 g0 = geometry(p.x, p.y, s), g1 = geometry(q.x, q.y, s);
+            if (g0.ix != g1.ix || g0.iy != g1.iy) atomicAdd(&changes[c], 1);
         }
     }
     __syncthreads();
-    for (int c = 0; c < list.count; ++c) {
-        const Level d = table.level[list.level[c]];
-        const int per_table = d.points * d.F;
-        const float* tab = acc + list.offset[c];
-        for (int j = threadIdx.x; j < per_table; j += blockDim.x) {
-            const float v = tab[j];
-            if (v != 0.0f) red_add_f32(grad + d.offset + j, v);
+    if (threadIdx.x == 0) {
+        bool global = pairs > 0;
+        long long sum = 0;
+        for (int c = 0; c < list.count; ++c) {
+            sum += changes[c];
+            const double flushes_per_entry = double(a.n) * changes[c] / double(pairs > 0 ? pairs : 1) /
+                                             double(table.level[list.level[c]].points);
+            if (flushes_per_entry > PROBE_ENTRY_FLUSHES) global = false;
         }
+        if ((long long)PROBE_MEAN_RUN * sum > (long long)list.count * pairs) global = false;
+        *strategy = global ? RUNS_GLOBAL : RUNS_SHARED;
     }
 }
 
@@ -767,8 +848,8 @@ static void set_runs_smem() {
                                    COARSE_SMEM_FLOATS * 4));
     ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_kernel<false, KIND, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    COARSE_SMEM_FLOATS * 4));
-    if (KIND == HASH_DENSE || KIND == HASH_HASHED || KIND == -1)
-        ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_plain_kernel<KIND, U>,
+    if constexpr (KIND != PLANE)
+        ODIE_CUDA(cudaFuncSetAttribute(encode_backward_runs_plain_kernel<KIND, U, RUNS_SHARED>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, COARSE_SMEM_FLOATS * 4));
 }
 
@@ -783,12 +864,26 @@ struct RunsLaunch {
     cudaStream_t stream;
 };
 
+// The plain runs scatter, with the probe of its strategy when the call has a strategy int and the gradient
+// takes 8-byte vector reductions.  Returns the number of kernels launched.
 template <int KIND, typename U>
-static void launch_runs(const RunsLaunch<U>& l, bool vec, bool plain = false) {
-    if (KIND != PLANE && vec && plain) {
-        encode_backward_runs_plain_kernel<KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
-                                                                                               l.upstream, l.grad);
-        return;
+static int launch_runs_plain(const RunsLaunch<U>& l) {
+    const bool probe = l.a.strategy && l.a.n >= 2 && (reinterpret_cast<uintptr_t>(l.grad) & 7) == 0;
+    if (probe) {
+        runs_probe_kernel<<<1, PROBE_THREADS, 0, l.stream>>>(l.a, l.table, l.list, l.a.strategy);
+        encode_backward_runs_plain_kernel<KIND, U, RUNS_GLOBAL><<<l.blocks, RUNS_THREADS, 0, l.stream>>>(
+            l.a, l.table, l.list, l.upstream, l.grad, l.a.strategy);
+    }
+    encode_backward_runs_plain_kernel<KIND, U, RUNS_SHARED><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(
+        l.a, l.table, l.list, l.upstream, l.grad, probe ? l.a.strategy : nullptr);
+    return probe ? 3 : 1;
+}
+
+// Launches the runs scatter; returns the number of kernels launched.
+template <int KIND, typename U>
+static int launch_runs(const RunsLaunch<U>& l, bool vec, bool plain = false) {
+    if constexpr (KIND != PLANE) {
+        if (vec && plain) return launch_runs_plain<KIND>(l);
     }
     if (vec)
         encode_backward_runs_kernel<true, KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
@@ -796,6 +891,7 @@ static void launch_runs(const RunsLaunch<U>& l, bool vec, bool plain = false) {
     else
         encode_backward_runs_kernel<false, KIND, U><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(l.a, l.table, l.list,
                                                                                                 l.upstream, l.grad);
+    return 1;
 }
 
 template <typename U>
@@ -862,14 +958,16 @@ static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U
                 plain = plain && d.kind != PLANE && (d.cells < 0 || !a.bitmap);
             }
             const RunsLaunch<U> l{a, src.table, list, upstream, grad, blocks, list.total * 4, stream};
-            if (kind == PLANE) launch_runs<PLANE>(l, vec);
-            else if (kind == HASH_DENSE) launch_runs<HASH_DENSE>(l, vec, plain);
-            else if (kind == HASH_HASHED) launch_runs<HASH_HASHED>(l, vec, plain);
-            else launch_runs<-1>(l, vec, plain);
-        }
-        else
+            int launched;
+            if (kind == PLANE) launched = launch_runs<PLANE>(l, vec);
+            else if (kind == HASH_DENSE) launched = launch_runs<HASH_DENSE>(l, vec, plain);
+            else if (kind == HASH_HASHED) launched = launch_runs<HASH_HASHED>(l, vec, plain);
+            else launched = launch_runs<-1>(l, vec, plain);
+            note_launch(launched);
+        } else {
             encode_backward_shared_kernel<U><<<blocks, 512, list.total * 4, stream>>>(a, src.table, list, upstream, grad);
-        note_launch();
+            note_launch();
+        }
     }
     const int active = a.active < a.levels ? a.active : a.levels;
     if (list.count == active) return;  // every level took the shared-memory path

@@ -34,6 +34,10 @@ struct EncodeArgs {
     const int* expert = nullptr;
     long long expert_stride = 0;
     int experts = 1;  // number of expert tables (expert ids are < experts)
+    // One device int the backward may use to choose its scatter strategy on the device from the batch itself
+    // (spatially coherent batches: global reductions; incoherent ones: per-block shared-memory tables).  Null:
+    // the shared-memory tables always.  Calls that may run concurrently need distinct ints.
+    int* strategy = nullptr;
 };
 
 // Forward: table is fp32 (master) or fp16 (mirror); vis may be null.

@@ -143,6 +143,9 @@ struct Runtime {
     DeviceArray<__half> raw, gvals;
     DeviceArray<uint32_t> vis;
     DeviceArray<int> error_flag;
+    // the backward scatters' strategy ints (EncodeArgs::strategy): [0] the router grid's (side stream), [1] the
+    // main stream's
+    DeviceArray<int> scatter_strategy;
     DeviceArray<__half> router_half, router_in, router_gvals;
     DeviceArray<float> router_grad, router_m, router_v, prob;
     DeviceArray<uint32_t> router_steps;
@@ -256,6 +259,8 @@ struct Runtime {
         gvals.allocate((long long)input_width * capacity);
         vis.allocate((long long)levels * capacity / 32);  // bit-packed [levels][capacity / 32]
         error_flag.allocate(1);
+        scatter_strategy.allocate(2);
+        scatter_strategy.zero(stream);
         if (experts) {
             ODIE_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
             ODIE_CUDA(cudaEventCreateWithFlags(&fork_event, cudaEventDisableTiming));
@@ -411,6 +416,7 @@ struct Runtime {
         a.row_major = false;
         a.width = input_width;
         a.stride = capacity;
+        a.strategy = scatter_strategy.ptr + 1;
         return a;
     }
 
@@ -454,6 +460,7 @@ struct Runtime {
         a.active = router_levels;
         a.width = router_width;
         a.row_major = true;
+        a.strategy = scatter_strategy.ptr;
         return a;
     }
 
@@ -720,7 +727,7 @@ struct Runtime {
           << ",\"router_gvals\":" << (unsigned long long)router_gvals.ptr << ",\"prob\":" << (unsigned long long)prob.ptr
           << ",\"expert_ids\":" << (unsigned long long)expert_ids.ptr << ",\"router_m\":" << (unsigned long long)router_m.ptr
           << ",\"router_v\":" << (unsigned long long)router_v.ptr << ",\"router_steps\":" << (unsigned long long)router_steps.ptr
-          << "}";
+          << ",\"scatter_strategy\":" << (unsigned long long)scatter_strategy.ptr << "}";
         return o.str();
     }
 

@@ -126,3 +126,38 @@ def test_c2_planes_step_matches_oracle(cuda):
                 'grid gradient')
     check_adam(opt, model, grid, grad, config['grid_lr'])
     opt.close()
+
+
+@pytest.mark.parametrize('batch', ['coherent', 'uniform'])
+def test_router_scatter_strategy_matches_oracle(cuda, batch):
+    """The router-grid scatter chooses its strategy from the batch on the device: a raster-ordered 128 x 128 block
+    of pixels (consecutive coordinates share cells) takes global reductions (strategy 1), uniform pixel ids the
+    per-block shared-memory tables (strategy 0).  Either way the router grid gradient matches the oracle within the
+    fp32 summation bound."""
+    config, rgb, shape = workloads.c2_experts(batch=N)
+    model = RoutedExperts(config)
+    height, width = shape
+    if batch == 'coherent':
+        ys, xs = torch.meshgrid(torch.arange(128) + 300, torch.arange(128) + 700, indexing='ij')
+        ids = (ys * width + xs).reshape(-1).cuda()
+    else:
+        ids = torch.randint(0, height * width, (N,), generator=torch.Generator().manual_seed(5)).cuda()
+    rgb = rgb.cuda()
+    opt = NativeOptimizer(model, ByteTarget(rgb), shape, config, [model.grid], batch=N)
+    snapshot = [t.detach().cpu().numpy().copy() for t in (model.grid, model.router_grid, model.gate.params,
+                                                          model.decoder.params)]
+    opt.call('step_grads', ids.data_ptr(), N, 2)
+    torch.cuda.synchronize()
+    assert opt.copied('error_flag', (1,), torch.int32).item() == 0, 'a bounded device wait ran out'
+    strategy = int(opt.copied('scatter_strategy', (2,), torch.int32)[0])
+    assert strategy == (1 if batch == 'coherent' else 0), f'router scatter strategy {strategy}'
+    ref = oracle.reference_step_experts(None, ids.cpu().numpy(), shape, snapshot[0], model.records,
+                                        model.expert_total, model.experts_held, snapshot[1], model.router_records,
+                                        snapshot[2], snapshot[3], targets=rgb[ids].cpu().numpy())
+    cap = opt.pointers['capacity']
+    rows = opt.copied('router_gvals', (cap, 32), torch.float16)[:N].cpu().numpy()
+    close(rows.astype(np.float32), ref['router_values'], 2e-3, 1e-3, 'router grid values', quantum=FP16_QUANTUM)
+    router_backward = lambda up: oracle.hash_backward(ref['xy'], up, model.router_records, snapshot[1].size)  # noqa
+    close_bound(opt.copied('router_grad', (snapshot[1].size,), torch.float32).cpu().numpy(), ref['router_grid_grad'],
+                scatter_bound(router_backward, ref['router_values'], 2e-3, 1e-3, FP16_QUANTUM), 'router grid gradient')
+    opt.close()
