@@ -229,8 +229,14 @@ class Clocks:
 def per_coordinate(name, model):
     """Algorithmic work per coordinate of a training step's stages (the figures the roofline divides):
     encode forward 8 + 4 L F 2 + L F 2 B per encoding (fp16 tables, fp16 features), encode backward
-    8 + L F 2 + 8 L F 4 B per encoding (an fp32 atomic = read + write), router 64 + 8 B (+ 2 live B per
-    logit stored), heads 6 x sum(in x out) FLOP (forward, data and weight gradients)."""
+    8 + L F 2 B per encoding (the coordinate and its gradient values, read once; the touched table entries'
+    read + write, 8 B each, are added per step by the caller), router 64 + 8 B (+ 2 live B per logit stored),
+    heads 6 x sum(in x out) FLOP (forward, data and weight gradients).
+
+    The backward's figure is the least traffic any scatter needs.  Counting each of the 4 L F corner updates
+    of a coordinate as an fp32 read + write (8 L F 4 B more per encoding, the per-corner atomic algorithm)
+    would exceed what the kernels move: their runs add a cell's updates in registers and write each run once,
+    so that count is reported beside it (naive_atomics_per_step) but not divided."""
     L, F = model.n_levels, 2
     experts = name.endswith('experts')
     encodings = 2 if experts else 1  # the router grid and the routed expert
@@ -243,7 +249,7 @@ def per_coordinate(name, model):
     else:
         live, gate = 0, 32 * 32 + 32 * 16
     return {'encode_forward': ('hbm', encodings * (8 + 4 * L * F * 2 + L * F * 2)),
-            'encode_backward': ('hbm', encodings * (8 + L * F * 2 + 8 * L * F * 4)),
+            'encode_backward': ('hbm', encodings * (8 + L * F * 2)),
             'router': ('hbm', 64 + 8 + 2 * live) if experts else ('hbm', None),
             'mlp_train': ('tensor', 6 * (gate + decoder))}
 
@@ -717,6 +723,8 @@ def main():
                 work = work * args.batch
             if k == 'adam_grid':
                 work = adam_bytes(grid_params, touched)
+            if k == 'encode_backward':
+                work += 8 * touched  # each touched gradient entry read and written once
             if k == 'input_batch':
                 work = (8 + 3 + 8 + 12) * args.batch  # id, u8 target in; xy, fp32 target out
             achieved = (work / seconds / (1e12 if bound == 'tensor' else 1e9)) if work else None
@@ -725,6 +733,11 @@ def main():
                             'bound': bound, 'algorithmic_per_step': work, 'achieved': achieved,
                             'unit': 'TFLOP/s' if bound == 'tensor' else 'GB/s',
                             'frac': (achieved / peak) if achieved else None}
+            if k == 'encode_backward':
+                # the per-corner atomic algorithm's reductions, and their time at the probe's L2 reduction rate
+                atomics = (2 if experts else 1) * model.n_levels * 4 * args.batch
+                per_stage[k]['naive_atomics_per_step'] = atomics
+                per_stage[k]['naive_atomics_ms_at_l2_probe'] = atomics / (probe['gops']['red8'] * 1e9) * 1e3
         dominant = max(stages, key=lambda k: stages[k]['ms'])
         d = per_stage[dominant]
         peak = tensor_sustained if d['bound'] == 'tensor' else hbm
@@ -829,6 +842,11 @@ def main_c1(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    # a first step whose gradient is kept for inspection counts the table entries a step touches (the entries the
+    # scatter writes); its update then runs as a warm-up step's would
+    trainer.step(step=0, seed=seed, update=False)
+    touched = int(torch.count_nonzero(trainer.read('grid_grad', model.total)))
+    trainer.update()
     for k in range(args.warmup):
         trainer.step(step=k, seed=seed)
     barrier()
@@ -914,7 +932,8 @@ def main_c1(args):
         flop_per_coord = 2 * 3 * (32 * 64 + 64 * 64 + 64 * 3)  # forward, data backward, weight gradients
         total = model.total
         work = {'fused_step': ('fp32', flop_per_coord * n),
-                'encode_backward': ('hbm', (8 + 4 * 32 + 16 * 4 * 8 * 2) * n),  # xy, dx rows, corner r+w
+                # xy and the fp32 feature-gradient row read once, each touched table entry read and written once
+                'encode_backward': ('hbm', (8 + 4 * 32) * n + 8 * touched),
                 'reduce_partials': ('hbm', None),
                 'adam_grid': ('hbm', 40 * total),  # g, p, m, v, step read; p, m, v, step written; g cleared
                 'adam_heads': ('hbm', None)}
@@ -936,7 +955,8 @@ def main_c1(args):
                     'frac': d['frac'], 'traffic': traffic_of('c1-hash', dominant),
                     'peak_source': ('measured (odie_fma_probe, fp32 FMA)' if d['bound'] == 'fp32'
                                     else f'{peak_kind} (HBM copy)'),
-                    'timing': 'stage events on one stream (kernel time)', 'stages': per_stage}
+                    'timing': 'stage events on one stream (kernel time)', 'touched_params_per_step': touched,
+                    'stages': per_stage}
         dec_bytes = 16 * 4 * 8 + 8 + 12
         base = None
         if world == 1 and not args.no_cpu_baseline:

@@ -521,6 +521,7 @@ __global__ void __launch_bounds__(512) encode_backward_shared_kernel(const Encod
 // VEC: the gradient values are row-major and listed level c has columns
 // (2c, 2c + 1), so one 16-byte load brings a group's 4 value pairs.
 constexpr int RUNS_THREADS = 384;
+static_assert(RUNS_THREADS % (32 * 12) == 0, "1 to 4 warp groups of whole warps");
 constexpr int RUNS_GROUP = 4;
 
 // Adds one cell's 8 corner sums to the block's shared table of expert e and clears them.
@@ -681,11 +682,19 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_ke
         for (int j = threadIdx.x; j < list.total; j += blockDim.x) acc[j] = 0.0f;
         __syncthreads();
     }
+    // RUNS_GLOBAL: the block's threads form one warp group per group of RUNS_GROUP levels (up to four), side
+    // by side over the same runs, so that the groups' reads of a value row land close together in time and
+    // hit L1 (one pass after another re-read every row from DRAM: four passes over the router grid's rows
+    // moved 4x their bytes).  RUNS_SHARED: one group, the passes one after another.
+    const int passes = (list.count + RUNS_GROUP - 1) / RUNS_GROUP;
+    const int groups = STRATEGY == RUNS_GLOBAL ? (passes < 4 ? passes : 4) : 1;
+    const int per = blockDim.x / groups;  // RUNS_THREADS / groups: a multiple of 32, so warps stay whole
+    const int group = threadIdx.x / per;
     const long long chunk = (a.n + gridDim.x - 1) / gridDim.x;
     const long long begin = (long long)blockIdx.x * chunk;
     const long long end = begin + chunk < a.n ? begin + chunk : a.n;
-    const long long run = (chunk + blockDim.x - 1) / blockDim.x;
-    const long long first = begin + threadIdx.x * run;
+    const long long run = (chunk + per - 1) / per;
+    const long long first = begin + (threadIdx.x - group * per) * run;
     const long long last = first + run < end ? first + run : end;
     const float2* const coords = reinterpret_cast<const float2*>(a.coords);
     auto flush = [&](int c, int ix, int iy, float (&v)[8]) {
@@ -693,7 +702,7 @@ __global__ void __launch_bounds__(RUNS_THREADS, 2) encode_backward_runs_plain_ke
         if (STRATEGY == RUNS_SHARED) runs_flush<KIND>(d, acc + list.offset[c], 0, ix, iy, v, a.node_bitmap, a.node_prefix);
         else runs_flush_global<KIND>(d, grad, ix, iy, v);
     };
-    for (int c0 = 0; c0 < list.count; c0 += RUNS_GROUP) {
+    for (int c0 = group * RUNS_GROUP; c0 < list.count; c0 += groups * RUNS_GROUP) {
         const int here = list.count - c0 < RUNS_GROUP ? list.count - c0 : RUNS_GROUP;
         int cx[RUNS_GROUP], cy[RUNS_GROUP];
         float v[RUNS_GROUP][8], scale[RUNS_GROUP];
@@ -871,7 +880,10 @@ static int launch_runs_plain(const RunsLaunch<U>& l) {
     const bool probe = l.a.strategy && l.a.n >= 2 && (reinterpret_cast<uintptr_t>(l.grad) & 7) == 0;
     if (probe) {
         runs_probe_kernel<<<1, PROBE_THREADS, 0, l.stream>>>(l.a, l.table, l.list, l.a.strategy);
-        encode_backward_runs_plain_kernel<KIND, U, RUNS_GLOBAL><<<l.blocks, RUNS_THREADS, 0, l.stream>>>(
+        // no shared tables: four blocks per SM's worth of shorter chunks (two resident at 80 registers)
+        const long long spread = l.a.n / 1024 > 1 ? l.a.n / 1024 : 1;
+        const int blocks = int(spread < 4 * sm_count() ? spread : 4 * sm_count());
+        encode_backward_runs_plain_kernel<KIND, U, RUNS_GLOBAL><<<blocks, RUNS_THREADS, 0, l.stream>>>(
             l.a, l.table, l.list, l.upstream, l.grad, l.a.strategy);
     }
     encode_backward_runs_plain_kernel<KIND, U, RUNS_SHARED><<<l.blocks, RUNS_THREADS, l.smem, l.stream>>>(
