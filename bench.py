@@ -518,8 +518,11 @@ def main():
         shared, head_grad, router_grad = parallel.head_gradient_buffer(model, router_grid=c4)
     # c4 decodes in launches of 2^24 pixels: the runtime's buffers hold that many coordinates
     capacity = max(args.batch, args.decode_launch) if c4 else args.batch
+    # one GPU, routed experts: the runtime's pipeline mode (each step's backward branches overlap the next step's
+    # forward; odie_join before every stop event)
+    pipelined = world == 1 and experts
     opt = NativeOptimizer(model, w['target'], shape, config, w['planes'], batch=capacity, head_grad=head_grad,
-                          router_grad=router_grad)
+                          router_grad=router_grad, pipeline=pipelined)
     runtime = parallel.NativeRuntime(opt)
     overlap = runtime.side_stream() if world > 1 else None
     dp_step = parallel.DataParallelStep(runtime, shared, overlap_stream=overlap)
@@ -579,6 +582,7 @@ def main():
         start.record()
         for k in range(args.steps):
             step(ids[args.warmup + k])
+        opt.check(lib.odie_join(opt.handle))
         end.record()
         launches = lib.odie_launch_count() - launches_before
         barrier()
@@ -655,6 +659,7 @@ def main():
         released[buf].record(main_stream)
         read_loss(k)
     main_stream.wait_stream(loss_stream)  # the last loss has reached the host buffer
+    opt.check(lib.odie_join(opt.handle))
     e_end.record()
     barrier()
     e_ms = torch.tensor([e_start.elapsed_time(e_end)], device='cuda')
@@ -683,6 +688,7 @@ def main():
         s_events[2].record()
         for k in range(args.steps):
             opt.check(lib.odie_step_stratified(opt.handle, 7, k, args.batch, 1))
+        opt.check(lib.odie_join(opt.handle))
         s_events[3].record()
         barrier()
         sampler = {'torch_stratified_ms': s_events[0].elapsed_time(s_events[1]) / reps,
@@ -783,7 +789,9 @@ def main():
                                                          if args.sampling == 'stratified' else ' (iid)')
                                         + (', 70 % in the allocated tiles' if allocation else '')),
                            'l2': 'per-step inputs and activations (c4: > 1 GB) larger than L2; model tables '
-                                 'L2-resident'},
+                                 'L2-resident',
+                           'schedule': ('pipelined: each step\'s backward branches overlap the next step\'s forward '
+                                        '(odie_join before the stop event)' if pipelined else 'one step at a time')},
                 'e2e': {'value': e2e, 'unit': UNIT, 'h2d_bytes_per_step': args.batch * 8, 'd2h_bytes_per_step': 8},
                 'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': base, 'decode': decode,
                 'loss_first_last': [float(losses[0]), float(losses[-1])], 'clocks': clocks.summary()}

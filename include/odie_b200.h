@@ -94,6 +94,20 @@ ODIE_API int odie_step_grads(void* handle, uint64_t ids, int n, int update);
 ODIE_API int odie_step_heads(void* handle);
 ODIE_API int odie_grid_update(void* handle);
 
+/* Pipeline mode (no reference counterpart): with "pipeline": 1 in the create
+ * JSON (routed experts, library-owned head and router-grid gradients: one
+ * GPU), odie_step / odie_step_stratified with update return while the step's
+ * backward branches (router-grid scatter and the router grid's and heads'
+ * Adam; expert-table scatter and the expert tables' Adam) still run on the
+ * runtime's own streams; the next step's forward overlaps them as far as its
+ * data allow.  The step's loss ("squares") is ready in stream order as usual;
+ * the parameters are final once the runtime's stream has passed odie_join (or
+ * any other call on the handle, each of which joins first).  "xy", "target"
+ * and "expert_ids" of odie_pointers then alternate between two buffers.
+ * odie_join: the runtime's stream waits for those branches (a no-op outside
+ * pipeline mode). */
+ODIE_API int odie_join(void* handle);
+
 /* Stratified batches on the device (replaces the reference's per-step sampler,
  * odie/data.py:63-80, stratified_batches, which draws torch.rand and then
  * gathers targets in separate kernels): slot j of step `step` takes stratum

@@ -32,6 +32,7 @@ SIGNATURES = {
     'odie_fma_probe': (I64, [I32, P, U64]),
     'odie_step_heads': (I32, [P]),
     'odie_grid_update': (I32, [P]),
+    'odie_join': (I32, [P]),
     'odie_profile': (I32, [P, I32]),
     'odie_profile_report': (C.c_char_p, [P]),
     'odie_pointers': (C.c_char_p, [P]),

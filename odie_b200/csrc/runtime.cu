@@ -100,6 +100,22 @@ struct Runtime {
     // expert-table scatter (fork/join by events, so a captured graph keeps both branches).
     cudaStream_t side = nullptr;
     cudaEvent_t fork_event = nullptr, join_event = nullptr;
+    // Pipeline mode ("pipeline": 1; routed experts with library-owned gradients, i.e. one GPU): a training step
+    // (odie_step / odie_step_stratified with update) leaves the two branches of its backward running on the
+    // runtime's own streams -- the router-grid scatter, the head-gradient reduction and the router grid's and
+    // heads' Adam on `side`; the expert-table scatter and the expert tables' Adam on `tail` -- and returns.  The
+    // next step's input kernel starts at once; its router-grid gather and router forward wait only for the side
+    // branch (whose updates they read) and run while the tail still scatters; its expert gather waits for the
+    // tail.  Coordinates, targets and expert ids alternate between two buffers, so that a step never overwrites
+    // what the previous step's branches still read.  The step's forward and heads run on `front`, a stream of the
+    // device's highest priority (as is `side`, on the next step's critical path), so that the block scheduler
+    // gives them the SMs the tail frees rather than the tail's next blocks; the runtime's stream orders `front`
+    // after the caller's work (call_event) and waits for the heads (heads_done), so the step's loss is in the
+    // caller's stream order.  Every other call first makes the runtime's stream wait for both branches (join),
+    // as odie_join does; until then the parameters may still be changing.
+    bool pipeline = false, pending = false;
+    cudaStream_t tail = nullptr, front = nullptr;
+    cudaEvent_t heads_done = nullptr, side_done = nullptr, tail_done = nullptr, call_event = nullptr;
     int device = 0;
     long long total = 0, capacity = 65536;
     int image_width = 0, image_height = 0, mode = 0, warp_limit = 128;
@@ -150,6 +166,8 @@ struct Runtime {
     DeviceArray<float> router_grad, router_m, router_v, prob;
     DeviceArray<uint32_t> router_steps;
     DeviceArray<int> expert_ids;
+    DeviceArray<float> xy_alt, target_alt;  // pipeline mode: the second buffers
+    DeviceArray<int> expert_ids_alt;
     DeviceArray<__half> logits;
     std::vector<double> host_bc1, host_bc2;
     int partial_blocks = 0;
@@ -213,6 +231,9 @@ struct Runtime {
             router_total = hash_layout(j.at("router_encoding"), router_table, router_levels, rf);
             router_width = (router_levels * rf + 15) / 16 * 16;
         }
+        pipeline = j.value("pipeline", 0) != 0;
+        ODIE_REQUIRE(!pipeline || (experts && !external_head_grad && !external_router_grad),
+                     "pipeline mode needs routed experts with library-owned head and router-grid gradients");
         if (hash_mode) build_hash_table(j.at("hash_encoding"));
         else levels = int(j.value("levels", 16));
         if (experts) ODIE_REQUIRE(router_width == input_width && input_width == 32,
@@ -262,9 +283,21 @@ struct Runtime {
         scatter_strategy.allocate(2);
         scatter_strategy.zero(stream);
         if (experts) {
-            ODIE_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+            int least = 0, greatest = 0;
+            ODIE_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+            ODIE_CUDA(cudaStreamCreateWithPriority(&side, cudaStreamNonBlocking, pipeline ? greatest : least));
             ODIE_CUDA(cudaEventCreateWithFlags(&fork_event, cudaEventDisableTiming));
             ODIE_CUDA(cudaEventCreateWithFlags(&join_event, cudaEventDisableTiming));
+            if (pipeline) {
+                ODIE_CUDA(cudaStreamCreateWithPriority(&front, cudaStreamNonBlocking, greatest));
+                ODIE_CUDA(cudaStreamCreateWithPriority(&tail, cudaStreamNonBlocking, least));
+                for (cudaEvent_t* e : {&heads_done, &side_done, &tail_done, &call_event})
+                    ODIE_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+                xy_alt.allocate(2 * capacity);
+                target_alt.allocate(3 * capacity);
+                expert_ids_alt.allocate(capacity);
+                expert_ids_alt.zero(stream);
+            }
             router_half.allocate(router_total);
             router_grad.allocate(router_total);
             router_m.allocate(router_total);
@@ -332,6 +365,7 @@ struct Runtime {
     }
 
     void configure(const Json& j) {
+        join();
         active = int(j.at("active").as_int());
         ODIE_REQUIRE(active >= 2 && active <= levels, "invalid active prefix");
         if (!hash_mode) {
@@ -397,6 +431,7 @@ struct Runtime {
     }
 
     void sync_weights() {
+        join();
         launch_cast_half(grid, grid_half.ptr, total, stream);
         if (experts) launch_cast_half(router_grid, router_half.ptr, router_total, stream);
         if (gate_count) launch_cast_half(gate_master, head_half.ptr, gate_count, stream);
@@ -466,11 +501,14 @@ struct Runtime {
 
     // Routed experts, forward part shared by training and decode: router grid
     // features -> expert choice -> the chosen experts' features (raw).
-    void route_and_encode(long long n) {
+    // before_gather: an event the expert gather waits for (pipeline mode: the previous step's tail), or null;
+    // on: the stream of the gathers and the router (default: the runtime's)
+    void route_and_encode(long long n, cudaEvent_t before_gather = nullptr, cudaStream_t on = nullptr) {
+        const cudaStream_t s = on ? on : stream;
         LevelSource rsrc;
         rsrc.table = router_table;
         int slot = stage_begin(S_ENCODE_FWD);
-        launch_encode_forward(router_encode_args(n), rsrc, nullptr, router_half.ptr, router_in.ptr, nullptr, stream);
+        launch_encode_forward(router_encode_args(n), rsrc, nullptr, router_half.ptr, router_in.ptr, nullptr, s);
         stage_end(slot);
         RouterArgs ra;
         ra.features = router_in.ptr;
@@ -486,7 +524,7 @@ struct Runtime {
         ra.logits = logits.ptr;
         ra.live = live;
         slot = stage_begin(S_ROUTER);
-        launch_router_forward(ra, router_width, stream);
+        launch_router_forward(ra, router_width, s);
         stage_end(slot);
         LevelSource src;
         src.table = table;
@@ -495,8 +533,9 @@ struct Runtime {
         ea.expert_stride = expert_total;
         ea.experts = experts;
         ea.row_major = true;  // one row per coordinate: the per-coordinate gather over all levels
+        if (before_gather) ODIE_CUDA(cudaStreamWaitEvent(s, before_gather, 0));
         slot = stage_begin(S_ENCODE_FWD);
-        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, nullptr, stream);
+        launch_encode_forward(ea, src, nullptr, grid_half.ptr, raw.ptr, nullptr, s);
         stage_end(slot);
     }
 
@@ -512,6 +551,7 @@ struct Runtime {
     int recorded = 0;
 
     void profile(int mode) {
+        join();
         const bool enable = mode != 0;
         serial = mode == 2;
         ODIE_CUDA(cudaStreamSynchronize(stream));
@@ -536,6 +576,7 @@ struct Runtime {
         if (slot >= 0) ODIE_CUDA(cudaEventRecord(events[2 * slot + 1], on ? on : stream));
     }
     std::string profile_report() {
+        join();
         ODIE_CUDA(cudaStreamSynchronize(stream));
         double ms[S_COUNT] = {0};
         int launches[S_COUNT] = {0};
@@ -557,7 +598,63 @@ struct Runtime {
     struct Sampled {
         uint64_t seed, step;
     };
+    // pipeline mode: the runtime's stream waits for the branches the last step left running
+    void join() {
+        if (!pending) return;
+        ODIE_CUDA(cudaStreamWaitEvent(stream, side_done, 0));
+        ODIE_CUDA(cudaStreamWaitEvent(stream, tail_done, 0));
+        pending = false;
+    }
+
+    // One training step with update in pipeline mode (see `pipeline`).
+    void step_pipelined(const int64_t* ids, int n, const Sampled* sampled) {
+        ODIE_REQUIRE(n > 0 && n <= capacity, "invalid batch size for this runtime");
+        // the forward comes after the caller's work (its ids); from the router-grid gather on, also after the
+        // previous step's side branch, whose router-grid and head updates it reads
+        ODIE_CUDA(cudaEventRecord(call_event, stream));
+        ODIE_CUDA(cudaStreamWaitEvent(front, call_event, 0));
+        std::swap(xy.ptr, xy_alt.ptr);
+        std::swap(target.ptr, target_alt.ptr);
+        std::swap(expert_ids.ptr, expert_ids_alt.ptr);
+        if (sampled)
+            launch_stratified_batch(sampled->seed, sampled->step, n, rgb, rgb8, image_width, image_height, frame, xy.ptr,
+                                    target.ptr, front);
+        else
+            launch_input_batch(ids, n, rgb, rgb8, image_width, image_height, frame, xy.ptr, target.ptr, front);
+        if (pending) ODIE_CUDA(cudaStreamWaitEvent(front, side_done, 0));
+        // the expert gather reads the expert tables that the previous step's tail updates
+        route_and_encode(n, pending ? tail_done : nullptr, front);
+        const MlpArgs ma = mlp_args(n);
+        const int blocks = mlp_tc_train_blocks(n, gate_mode());
+        launch_mlp_tc_train(ma, input_width, gate_mode(), uniform, blocks, error_flag.ptr, front);
+        ODIE_CUDA(cudaEventRecord(heads_done, front));
+        ODIE_CUDA(cudaStreamWaitEvent(stream, heads_done, 0));  // the step's loss, in the caller's stream order
+        ODIE_CUDA(cudaStreamWaitEvent(side, heads_done, 0));
+        ODIE_CUDA(cudaStreamWaitEvent(tail, heads_done, 0));
+        LevelSource rsrc;
+        rsrc.table = router_table;
+        const EncodeArgs ra = router_encode_args(n);
+        launch_encode_backward(ra, rsrc, router_gvals.ptr, router_gradient(), side);
+        launch_reduce_partials(partials.ptr, blocks, head_count, head_grad(), side);
+        adam_router_grid(side);
+        adam_heads(side);
+        ODIE_CUDA(cudaEventRecord(side_done, side));
+        LevelSource src;
+        src.table = table;
+        EncodeArgs ea = encode_args(n);
+        ea.expert = expert_ids.ptr;
+        ea.expert_stride = expert_total;
+        ea.experts = experts;
+        ea.row_major = true;
+        launch_encode_backward(ea, src, gvals.ptr, grid_grad.ptr, tail);
+        adam_expert_tables(tail);
+        ODIE_CUDA(cudaEventRecord(tail_done, tail));
+        pending = true;
+        ODIE_CUDA(cudaGetLastError());
+    }
+
     void step_grads(const int64_t* ids, int n, int update, const Sampled* sampled = nullptr) {
+        join();
         ODIE_REQUIRE(n > 0 && n <= capacity, "invalid batch size for this runtime");
         int slot = stage_begin(S_INPUT);
         if (sampled)
@@ -636,10 +733,11 @@ struct Runtime {
     }
 
     // Adam of the grid tables (sparse: zero gradients are skipped), gradients at loss scale 128.
-    void adam_expert_tables() {
+    void adam_expert_tables(cudaStream_t on = nullptr) {
         AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
         launch_adam(grid, grid_half.ptr, grid_m.ptr, grid_v.ptr, grid_steps.ptr, grid_grad.ptr, total, 1.0f / 128.0f, t,
-                    float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), true, error_flag.ptr, stream);
+                    float(1.0 - BETA1), float(BETA2), float(1.0 - BETA2), float(EPS), true, error_flag.ptr,
+                    on ? on : stream);
     }
     void adam_router_grid(cudaStream_t on) {
         AdamTables t{table_step[0].ptr, table_bc2.ptr, TABLE_STEPS};
@@ -649,6 +747,7 @@ struct Runtime {
     }
 
     void grid_update() {
+        join();
         const int slot = stage_begin(S_ADAM_GRID);
         adam_expert_tables();
         if (experts && !external_router_grad) adam_router_grid(stream);  // a shared router grid: in step_heads
@@ -657,6 +756,7 @@ struct Runtime {
     }
 
     void step_heads(bool update) {
+        join();
         if (!update) return;
         if (experts && external_router_grad) {
             // the shared router grid: its summed gradient is ready once the caller's reduction has run
@@ -665,6 +765,12 @@ struct Runtime {
             stage_end(grid_slot);
         }
         const int slot = stage_begin(S_ADAM_HEADS);
+        adam_heads(stream);
+        stage_end(slot);
+        ODIE_CUDA(cudaGetLastError());
+    }
+
+    void adam_heads(cudaStream_t on) {
         // head gradients carry the 128 x 128 loss scale (odie/native/runtime.cu:59,300-309)
         const float inv = 1.0f / 16384.0f;
         // gate (or router) and decoder in one launch, each with its own master array and learning rate
@@ -672,12 +778,16 @@ struct Runtime {
         const AdamTables decoder_t{table_step[2].ptr, table_bc2.ptr, TABLE_STEPS};
         launch_adam2(gate_master, decoder_master, head_half.ptr, head_m.ptr, head_v.ptr, head_steps.ptr, head_grad(),
                      gate_count, decoder_count, inv, gate_t, decoder_t, float(1.0 - BETA1), float(BETA2),
-                     float(1.0 - BETA2), float(EPS), false, error_flag.ptr, stream);
-        stage_end(slot);
-        ODIE_CUDA(cudaGetLastError());
+                     float(1.0 - BETA2), float(EPS), false, error_flag.ptr, on);
     }
 
     ~Runtime() {
+        for (cudaStream_t s : {side, tail, front})
+            if (s) cudaStreamSynchronize(s);
+        for (cudaEvent_t e : {heads_done, side_done, tail_done, call_event})
+            if (e) cudaEventDestroy(e);
+        if (tail) cudaStreamDestroy(tail);
+        if (front) cudaStreamDestroy(front);
         for (auto& e : events) cudaEventDestroy(e);
         if (fork_event) cudaEventDestroy(fork_event);
         if (join_event) cudaEventDestroy(join_event);
@@ -685,6 +795,7 @@ struct Runtime {
     }
 
     void decode(long long begin, long long n, float* out_rgb, uint8_t* out_rgb8) {
+        join();
         LevelSource src;
         src.table = table;
         for (long long done = 0; done < n; done += capacity) {
@@ -732,6 +843,7 @@ struct Runtime {
     }
 
     std::string state(int begin, int end) {
+        join();
         ODIE_CUDA(cudaStreamSynchronize(stream));
         int flag = 0;
         ODIE_CUDA(cudaMemcpy(&flag, error_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost));
@@ -841,6 +953,10 @@ void* odie_create(const char* json) {
 int odie_step(void* handle, uint64_t ids, int n, int update) {
     return guarded([&] {
         auto* r = static_cast<Runtime*>(handle);
+        if (r->pipeline && update && !r->profiling) {
+            r->step_pipelined(reinterpret_cast<const int64_t*>(ids), n, nullptr);
+            return;
+        }
         r->step_grads(reinterpret_cast<const int64_t*>(ids), n, update != 0 ? 1 : 0);
         r->step_heads(update != 0);
     });
@@ -850,9 +966,17 @@ int odie_step_stratified(void* handle, uint64_t seed, uint64_t step, int n, int 
     return guarded([&] {
         auto* r = static_cast<Runtime*>(handle);
         const odie::Runtime::Sampled sampled{seed, step};
+        if (r->pipeline && update && !r->profiling) {
+            r->step_pipelined(nullptr, n, &sampled);
+            return;
+        }
         r->step_grads(nullptr, n, update != 0 ? 1 : 0, &sampled);
         r->step_heads(update != 0);
     });
+}
+
+int odie_join(void* handle) {
+    return guarded([&] { static_cast<Runtime*>(handle)->join(); });
 }
 
 int odie_stratified_ids(uint64_t seed, uint64_t step, int width, int height, int64_t n, int64_t* ids, uint64_t stream) {

@@ -39,8 +39,14 @@ def target_bytes(target):
 
 
 class NativeOptimizer:
-    def __init__(self, model, target, shape, config, planes, half=True, batch=None, head_grad=None, router_grad=None):
+    def __init__(self, model, target, shape, config, planes, half=True, batch=None, head_grad=None, router_grad=None,
+                 pipeline=False):
+        """pipeline: the runtime's pipeline mode (routed experts on one GPU): a step returns while its backward
+        branches still run on the runtime's own streams, and the next step's forward overlaps them; join() (or any
+        other call here, each of which joins first) makes the runtime's stream wait for them.  No CUDA graph is
+        captured in this mode."""
         self.lib = _lib.library()
+        self.pipeline = bool(pipeline)
         self.model, self.target, self.config = model, target, config
         self.half = half
         self.graph = self.key = None
@@ -78,6 +84,8 @@ class NativeOptimizer:
                 settings.update(full_height=model.image_rows, row_offset=int(config.get('row_offset', 0)))
             if router_grad is not None:
                 settings['router_grad'] = router_grad.data_ptr()
+        if self.pipeline:
+            settings['pipeline'] = 1
         self.handle = self.lib.odie_create(json.dumps(settings).encode())
         if not self.handle:
             raise RuntimeError(_lib.error())
@@ -126,8 +134,14 @@ class NativeOptimizer:
         with self.on_stream():
             self.check(self.lib.odie_step_stratified(self.handle, int(seed), int(step), int(n), int(update)))
 
+    def join(self):
+        """The runtime's stream (and the caller's) waits for the branches a pipelined step left running."""
+        with self.on_stream():
+            self.check(self.lib.odie_join(self.handle))
+
     def copied(self, name, shape, dtype):
         with self.on_stream():
+            self.check(self.lib.odie_join(self.handle))
             result = torch.empty(shape, device='cuda', dtype=dtype)
             self.check(self.lib.odie_copy(result.data_ptr(), self.pointers[name],
                                           result.numel() * result.element_size(), self.stream.cuda_stream))
@@ -166,7 +180,8 @@ class NativeOptimizer:
             return
         self.release_graph()
         self.check(self.lib.odie_configure(self.handle, json.dumps(settings).encode()))
-        self.graph, self.graph_loss = self._capture()
+        if not self.pipeline:  # a pipelined step leaves branches running past its end: nothing to capture
+            self.graph, self.graph_loss = self._capture()
         self.lib.odie_pin_contexts(self.handle)
         self.key = key
         self.recaptures += 1
