@@ -942,6 +942,7 @@ static void encode_backward(const EncodeArgs& a, const LevelSource& src, const U
         static std::atomic<unsigned long long> configured{0};  // per value type and device
         int device = 0;
         ODIE_CUDA(cudaGetDevice(&device));
+        ODIE_REQUIRE(device >= 0 && device < 64, "devices 0..63");  // one bit per device below
         if (!(configured.load() >> device & 1ull)) {
             ODIE_CUDA(cudaFuncSetAttribute(encode_backward_shared_kernel<U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            COARSE_SMEM_FLOATS * 4));

@@ -552,6 +552,7 @@ struct HashGrid32 {
             ODIE_CUDA(cudaMemcpy(step_size[g].ptr, host_step.data(), steps * 4, cudaMemcpyHostToDevice));
         }
         static std::atomic<unsigned long long> configured{0};
+        ODIE_REQUIRE(device >= 0 && device < 64, "devices 0..63");  // one bit per device below
         if (!(configured.load() >> device & 1ull)) {
             ODIE_CUDA(cudaFuncSetAttribute(hg32_train_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HgSmem::bytes));
             ODIE_CUDA(cudaFuncSetAttribute(hg32_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

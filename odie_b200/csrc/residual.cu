@@ -54,7 +54,7 @@ __global__ void score_cells_kernel(const float* __restrict__ prediction, const v
 // One block per tile, one thread per tile row (looping when tile > blockDim).
 __global__ void tile_rows_kernel(const float* __restrict__ prediction, const uint8_t* __restrict__ target, int height,
                                  int width, int tile, double* __restrict__ row_sums) {
-    const int tiles_x = (width + tile - 1) / tile;
+    const int tiles_x = int(((long long)width + tile - 1) / tile);  // widened: width + tile may pass INT_MAX
     const int tx = blockIdx.x % tiles_x, ty = blockIdx.x / tiles_x;
     const int x0 = tx * tile, x1 = min(x0 + tile, width);
     for (int r = threadIdx.x; r < tile; r += blockDim.x) {
