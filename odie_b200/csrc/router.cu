@@ -23,8 +23,9 @@ constexpr int ROUTER_THREADS = 128;
 // as packed fma chains (fma.rn.f32x2: two IEEE fp32 fused multiply-adds, each
 // rounded exactly as __fmaf_rn) over the input broadcast as {x_k, x_k}; the
 // weights sit in shared memory pair-interleaved, {W[o][k], W[o + 1][k]}, and each
-// weight load serves all of the thread's coordinates (the kernel is bound by shared-memory loads).
-constexpr int ROUTER_PER_THREAD = 4;
+// weight load serves all of the thread's coordinates.  Two coordinates per thread keep 96 registers, so 20
+// warps share an SM; four halved the weight loads but held 168 registers (12 warps) and ran 3.5 % slower.
+constexpr int ROUTER_PER_THREAD = 2;
 
 using f32x2 = unsigned long long;
 __device__ __forceinline__ f32x2 pack2(float a, float b) {
